@@ -1,0 +1,149 @@
+"""ctypes bindings to the CPU checkers (test infrastructure).
+
+* ``oracle()``  -> oracle/liboracle.so, the C restatement (oracle/xp_oracle.c)
+* ``ref()``     -> oracle/_ref/libxpref.so, the reference's own kernels and host
+                   engine compiled from source (None when it was not built)
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+_ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
+_REF = os.path.join(ROOT, "oracle", "_ref", "libxpref.so")
+
+f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+
+_o = None
+_r = None
+
+
+def oracle():
+    global _o
+    if _o is None:
+        lib = C.CDLL(_ORACLE)
+        lib.xo_gen_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, f32p]
+        lib.xo_gen_tokens.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint32, u32p]
+        lib.xo_uniform.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
+        lib.xo_uniform.restype = C.c_float
+        lib.xo_f32_to_f16.argtypes = [C.c_float]
+        lib.xo_f32_to_f16.restype = C.c_uint16
+        lib.xo_f16_to_f32.argtypes = [C.c_uint16]
+        lib.xo_f16_to_f32.restype = C.c_float
+        lib.xo_quantise.argtypes = [C.c_float, C.c_float]
+        lib.xo_quantise.restype = C.c_uint32
+        lib.xo_best_bf16_scale.argtypes = [f32p, C.c_float]
+        lib.xo_best_bf16_scale.restype = C.c_float
+        lib.xo_pack_km4bf16.argtypes = [f32p, C.c_uint32, C.c_uint32, u32p, u32p]
+        lib.xo_mv_km4_bs.argtypes = [f32p, f32p, u32p, u32p, C.c_uint32, C.c_uint32]
+        lib.xo_mv_km4_bs_split.argtypes = [f32p, f32p, u32p, u32p, C.c_uint32, C.c_uint32, C.c_uint32]
+        lib.xo_rmsnorm_gemma.argtypes = [f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.c_float]
+        lib.xo_rmsnorm_heads_gemma.argtypes = [f32p, f32p, f32p, C.c_uint32, C.c_uint32, C.c_float]
+        lib.xo_rope.argtypes = [f32p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]
+        lib.xo_geglu.argtypes = [f32p, f32p, f32p, C.c_uint32]
+        lib.xo_attention.argtypes = [f32p, f32p, C.c_void_p, C.c_void_p, C.c_int, C.c_uint32,
+                                     C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float]
+        lib.xo_argmax.argtypes = [f32p, C.c_uint32, C.POINTER(C.c_float)]
+        lib.xo_argmax.restype = C.c_uint32
+        lib.xo_topk.argtypes = [f32p, C.c_uint32, C.c_uint32, f32p, u32p]
+        lib.xo_topk.restype = C.c_uint32
+        lib.xo_sample.argtypes = [f32p, C.c_uint32, C.c_float, C.c_uint32, C.c_float, C.c_float]
+        lib.xo_sample.restype = C.c_uint32
+        _o = lib
+    return _o
+
+
+class _Arg(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("size", C.c_uint32), ("is_buffer", C.c_int)]
+
+
+def ref():
+    """The reference build, or None if oracle/_ref was not built."""
+    global _r
+    if _r is None:
+        if not os.path.exists(_REF):
+            return None
+        lib = C.CDLL(_REF)
+        lib.xpref_launch.argtypes = [C.c_char_p, C.c_char_p, C.c_uint32, C.POINTER(_Arg), C.c_uint32, C.c_int]
+        lib.xpref_last_error.restype = C.c_char_p
+        lib.xpref_pack_km4bf16.argtypes = [f32p, C.c_uint32, C.c_uint32, u32p, u32p, C.c_void_p]
+        lib.xpref_best_bf16_scale.argtypes = [f32p, C.c_float]
+        lib.xpref_best_bf16_scale.restype = C.c_float
+        lib.xpref_plan_weight_bytes.restype = C.c_uint64
+        lib.xpref_plan_dispatches.restype = C.c_uint32
+        lib.xpref_session_create.argtypes = [C.c_char_p, C.c_char_p, C.c_uint32, C.c_int, C.c_float,
+                                             C.c_uint32, C.c_float, C.c_uint64]
+        lib.xpref_session_create.restype = C.c_void_p
+        lib.xpref_session_error.restype = C.c_char_p
+        lib.xpref_session_destroy.argtypes = [C.c_void_p]
+        lib.xpref_session_prefill.argtypes = [C.c_void_p, u32p, C.c_uint32]
+        lib.xpref_session_step.argtypes = [C.c_void_p]
+        lib.xpref_session_step.restype = C.c_int64
+        lib.xpref_session_logits.argtypes = [C.c_void_p, f32p, C.c_uint32]
+        lib.xpref_session_position.argtypes = [C.c_void_p]
+        lib.xpref_session_position.restype = C.c_uint32
+        _r = lib
+    return _r
+
+
+def ref_launch(name, grid, *args, module=None, threads=0):
+    """Run one reference kernel over `grid` work items. numpy arrays are
+    buffers (modified in place); Python ints are uint32, floats fp32, and
+    (value, ctype) tuples give an explicit POD type."""
+    lib = ref()
+    keep = []
+    arr = (_Arg * max(1, len(args)))()
+    for i, a in enumerate(args):
+        if isinstance(a, np.ndarray):
+            assert a.flags.c_contiguous
+            arr[i] = _Arg(a.ctypes.data, 0, 1)
+            keep.append(a)
+        else:
+            if isinstance(a, tuple):
+                v = a[1](a[0])
+            elif isinstance(a, float):
+                v = C.c_float(a)
+            else:
+                v = C.c_uint32(a)
+            keep.append(v)
+            arr[i] = _Arg(C.addressof(v), C.sizeof(v), 0)
+    rc = lib.xpref_launch(module.encode() if module else None, name.encode(), grid, arr, len(args), threads)
+    if rc != 0:
+        raise RuntimeError(f"ref kernel {name}: {lib.xpref_last_error().decode()}")
+
+
+def gen_normal(seed, stream, n, sigma, offset=0):
+    out = np.empty(n, np.float32)
+    oracle().xo_gen_normal(seed, stream, offset, n, sigma, out)
+    return out
+
+
+def gen_tokens(seed, stream, n, vocab):
+    out = np.empty(n, np.uint32)
+    oracle().xo_gen_tokens(seed, stream, n, vocab, out)
+    return out
+
+
+def pack(w_cols_rows, rows, cols, impl="oracle"):
+    """fp32 [cols][rows] -> (words uint32[cols*rows/8], scales uint32[cols*rows/64])."""
+    w = np.ascontiguousarray(w_cols_rows, np.float32).reshape(-1)
+    words = np.zeros(cols * rows // 8, np.uint32)
+    scales = np.zeros(cols * rows // 64, np.uint32)
+    if impl == "oracle":
+        rc = oracle().xo_pack_km4bf16(w, rows, cols, words, scales)
+    else:
+        rc = ref().xpref_pack_km4bf16(w, rows, cols, words, scales, None)
+    assert rc == 0
+    return words, scales
+
+
+def mv(x, words, scales, rows, cols, split=1):
+    out = np.empty(cols, np.float32)
+    if split > 1:
+        oracle().xo_mv_km4_bs_split(out, np.ascontiguousarray(x, np.float32), words, scales, rows, cols, split)
+    else:
+        oracle().xo_mv_km4_bs(out, np.ascontiguousarray(x, np.float32), words, scales, rows, cols)
+    return out
