@@ -1,0 +1,266 @@
+/* xp_cuda.h -- C ABI of the B200 (sm_100a) Gemma-3 int4 decode path.
+ *
+ * This is the drop-in boundary for the reference's operator surface
+ * (badnikhil/Xpose, "Vulkore"): the kernel entry points of
+ * kernels/llm_matvec.cl, kernels/llm_transformer.cl and kernels/llm_sampling.cl
+ * that examples/llm/decode.cpp drives, the runtime calls it makes on them
+ * (include/vulkore/{context,buffer,program,launch,sync}.hpp), and the engine
+ * unit of work, DecodeSession (examples/llm/decode.hpp:605-676).
+ *
+ * Plain pointers and sizes only. Device pointers are CUDA device addresses;
+ * `stream` is a cudaStream_t (NULL = legacy default stream). Every call
+ * returns an xp_status; on failure xp_last_error() holds a message naming the
+ * kernel and argument, in the form the reference's vulkore::Error uses
+ * (src/launch.cpp:21-131). Not thread-safe per context; one context per
+ * thread per device (the reference's Context is single-threaded too,
+ * agent-docs/vulkore-core.md:76-77).
+ */
+#ifndef XP_CUDA_H
+#define XP_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status --------------------------------------------------------------- */
+typedef enum xp_status {
+    XP_OK = 0,
+    XP_TIMEOUT = 1,           /* Fence::wait timed out (include/vulkore/sync.hpp:25-28) */
+    XP_ERR_INVALID = -1,      /* bad argument value (null, size, shape) */
+    XP_ERR_NO_KERNEL = -2,    /* Program::kernel: unknown name (include/vulkore/program.hpp:107) */
+    XP_ERR_ARITY = -3,        /* launch: wrong argument count (src/launch.cpp:63-74) */
+    XP_ERR_ARG_KIND = -4,     /* launch: buffer where a POD is expected or vice versa (:85-111) */
+    XP_ERR_ARG_SIZE = -5,     /* launch: POD size mismatch (:112-121) */
+    XP_ERR_GRID = -6,         /* launch: zero grid or too many groups (:21-35) */
+    XP_ERR_CUDA = -7,         /* a CUDA runtime error */
+    XP_ERR_OOM = -8,
+    XP_ERR_KV_FULL = -9,      /* decode: KV cache is full (decode.cpp:1823-1826) */
+    XP_ERR_STATE = -10,       /* decode_step before prefill (decode.cpp:1821-1822), spent Batch */
+    XP_ERR_DEVICE = -11,      /* device lost / kernel fault */
+    XP_ERR_NO_DEVICE = -12,
+    XP_ERR_UNSUPPORTED = -13  /* shape outside what the kernels implement */
+} xp_status;
+
+const char* xp_last_error(void);
+const char* xp_status_name(int status);
+/* Library / device info. */
+const char* xp_version(void);
+int xp_device_count(void);
+
+/* ---- context and buffers (include/vulkore/context.hpp, buffer.hpp) -------- */
+typedef struct xp_context xp_context;
+typedef enum xp_usage { XP_DEVICE_LOCAL = 0, XP_HOST_VISIBLE = 1 } xp_usage;
+
+xp_status xp_context_create(int device, xp_context** out);
+xp_status xp_context_destroy(xp_context* ctx);
+/* The stream all Batch submissions and typed launches of this context use. */
+void* xp_context_stream(xp_context* ctx);
+xp_status xp_context_device_name(xp_context* ctx, char* buf, size_t n);
+xp_status xp_context_wait_idle(xp_context* ctx);
+
+/* ctx.alloc<T>(n, Usage) (include/vulkore/context.hpp:55-60). HOST_VISIBLE is
+ * pinned, mapped host memory; the returned pointer is its device alias and
+ * *host_ptr (if non-null) the host view. */
+xp_status xp_alloc(xp_context* ctx, size_t bytes, xp_usage usage, void** dptr, void** host_ptr);
+xp_status xp_free(xp_context* ctx, void* dptr);
+/* Buffer::upload/download (include/vulkore/buffer.hpp:83-92); synchronous. */
+xp_status xp_upload(xp_context* ctx, void* dst, size_t dst_offset, const void* src, size_t bytes);
+xp_status xp_download(xp_context* ctx, void* dst, const void* src, size_t src_offset, size_t bytes);
+
+/* ---- kernel registry (include/vulkore/program.hpp:96-110) -------------------
+ * Kernels are looked up by (module path, entry-point name). Module paths are
+ * the reference's: "kernels/llm_matvec.spv", "kernels/llm_transformer.spv",
+ * "kernels/llm_sampling.spv" (a bare file name also matches). An unknown name
+ * returns XP_ERR_NO_KERNEL and the message lists the module's kernels. */
+typedef int32_t xp_kernel;
+xp_status xp_kernel_lookup(const char* module, const char* name, xp_kernel* out);
+xp_status xp_kernel_info(xp_kernel k, const char** module, const char** name, uint32_t* nargs);
+/* argument i: kind 1 = buffer (device pointer), 0 = POD of `size` bytes */
+xp_status xp_kernel_arg(xp_kernel k, uint32_t i, int* kind, uint32_t* size, const char** arg_name);
+int xp_kernel_count(void);
+
+typedef struct xp_grid { uint32_t x, y, z; } xp_grid; /* GLOBAL thread counts */
+typedef struct xp_arg {
+    const void* ptr;  /* kind 1: the device pointer VALUE; kind 0: address of the POD */
+    uint32_t size;    /* POD byte size (ignored for buffers) */
+    int32_t kind;     /* 1 buffer, 0 POD */
+} xp_arg;
+
+/* vulkore::launch (include/vulkore/launch.hpp:148-160): validate the arguments
+ * against the kernel's signature, then enqueue it on `stream`. */
+xp_status xp_launch(xp_kernel k, xp_grid grid, const xp_arg* args, uint32_t nargs, void* stream);
+
+/* ---- Batch / Fence (include/vulkore/launch.hpp:165-213, sync.hpp:15-50) ----
+ * A Batch records launches; submit() captures them into one CUDA graph (the
+ * counterpart of one vkQueueSubmit), instantiates it, or updates the cached
+ * executable graph in place when the node list matches, and launches it. */
+typedef struct xp_batch xp_batch;
+typedef struct xp_fence xp_fence;
+xp_status xp_batch_create(xp_context* ctx, xp_batch** out);
+xp_status xp_batch_add(xp_batch* b, xp_kernel k, xp_grid grid, const xp_arg* args, uint32_t nargs);
+xp_status xp_batch_size(xp_batch* b, uint32_t* n);
+xp_status xp_batch_submit(xp_batch* b, xp_fence** out);  /* the Batch is spent afterwards */
+xp_status xp_batch_destroy(xp_batch* b);
+/* XP_OK when signaled, XP_TIMEOUT on timeout, XP_ERR_DEVICE on a device error */
+xp_status xp_fence_wait(xp_fence* f, uint64_t timeout_ns);
+xp_status xp_fence_destroy(xp_fence* f);                  /* drains first */
+
+/* ---- typed entry points, reference names and argument order --------------
+ * Each replaces the same-named entry point of the cited .cl file; `grid` is
+ * chosen by the library. Matvec convention (kernels/llm.cl:11-19): rows = K
+ * inputs, cols = N outputs, out[j] = sum_k in[k] * W[k][j]. */
+/* kernels/llm_matvec.cl:422-434 */
+xp_status xp_mv_km4_bs(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
+                       uint32_t rows, uint32_t cols);
+/* kernels/llm_matvec.cl:439-456 (partial[p*cols + j], split over quads) */
+xp_status xp_mv_km4_bs_split(void* stream, float* partial, const float* in, const uint32_t* wq,
+                             const uint32_t* sc, uint32_t rows, uint32_t cols, uint32_t split);
+/* kernels/llm_matvec.cl:128-135 */
+xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t cols, uint32_t split);
+/* kernels/llm_transformer.cl:96-116 */
+xp_status xp_rmsnorm_sumsq(void* stream, float* partial, const float* in, uint32_t n, uint32_t nparts);
+xp_status xp_rmsnorm_apply_gemma(void* stream, float* out, const float* in, const float* w,
+                                 const float* partial, uint32_t n, uint32_t nparts, float eps);
+/* kernels/llm_transformer.cl:122-134 */
+xp_status xp_rmsnorm_heads_gemma(void* stream, float* out, const float* in, const float* w, uint32_t n_heads,
+                                 uint32_t head_dim, float eps);
+/* kernels/llm_transformer.cl:158-179 */
+xp_status xp_rope(void* stream, float* x, uint32_t n_heads, uint32_t head_dim, uint32_t pos, float theta);
+/* kernels/llm_transformer.cl:223-231 */
+xp_status xp_geglu(void* stream, float* out, const float* gate, const float* up, uint32_t n);
+/* kernels/llm_transformer.cl:564-568 */
+xp_status xp_add_residual(void* stream, float* x, const float* y, uint32_t n);
+/* kernels/llm_transformer.cl:590-595 */
+xp_status xp_kv_append(void* stream, float* cache, const float* src, uint32_t n, uint32_t pos);
+/* kernels/llm_transformer.cl:287-305, :318-335, :478-497 */
+xp_status xp_attention_scores(void* stream, float* scores, const float* q, const float* kcache, uint32_t n_heads,
+                              uint32_t kv_heads, uint32_t head_dim, uint32_t span, float scale,
+                              uint32_t kv_start);
+xp_status xp_softmax_rows(void* stream, float* x, uint32_t n_rows, uint32_t n_cols);
+xp_status xp_attention_apply(void* stream, float* out, const float* probs, const float* vcache, uint32_t n_heads,
+                             uint32_t kv_heads, uint32_t head_dim, uint32_t span, uint32_t kv_start);
+/* kernels/llm_sampling.cl:57-123 (three-level argmax; out[0] = index as float,
+ * out[1] = value; ties -> lowest index) */
+xp_status xp_argmax(void* stream, float* out, uint32_t* idx_out, const float* logits, uint32_t n);
+/* kernels/llm_sampling.cl:318-347 */
+xp_status xp_topk4_partial(void* stream, float* cval, uint32_t* cidx, const float* x, uint32_t n,
+                           uint32_t nparts);
+
+/* ---- fused B200 kernels (no single reference counterpart) -----------------
+ * Fused split-K flash-decode attention over an fp16 KV cache for one position
+ * (replaces rmsnorm_heads_gemma x2, rope x2, kv_append x2, attention_scores,
+ * softmax_rows, attention_apply: examples/llm/decode.cpp:1676-1731). n_heads
+ * must be 4, kv_heads 1, head_dim 256 (Gemma-3-1B). `pos` is a DEVICE
+ * pointer. `scratch` needs xp_attention_scratch_bytes(nsplit) bytes and must
+ * be zero-initialised once (the kernel leaves it reusable). */
+size_t xp_attention_scratch_bytes(uint32_t nsplit);
+xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, const float* k_raw,
+                              const float* v_raw, const float* q_norm, const float* k_norm, uint16_t* kcache_f16,
+                              uint16_t* vcache_f16, const uint32_t* pos_dev, uint32_t window, float theta,
+                              float eps, float scale, uint32_t nsplit, uint32_t max_seq, void* scratch);
+/* Exact top-k (k <= 64) + temperature + top-p + multinomial over n logits
+ * (replaces topk4_partial + host draw(), decode.cpp:1873-1917). `u` index for
+ * the seeded uniform is *pos_dev. Writes the chosen id to *token_dev and the
+ * k survivors (descending) to out_vals/out_idx when non-null. */
+size_t xp_sample_scratch_bytes(uint32_t n);
+xp_status xp_sample_topk(void* stream, uint32_t* token_dev, float* out_vals, uint32_t* out_idx,
+                         const float* logits, uint32_t n, uint32_t top_k, float temperature, float top_p,
+                         uint64_t seed, uint64_t seq_id, const uint32_t* pos_dev, void* scratch);
+
+/* ---- load path -------------------------------------------------------------- */
+/* Device twin of the reference packer (examples/llm/decode.cpp:101-229): fp32
+ * weights [cols][rows] (GGUF order) -> KM4 nibble plane (cols*rows/2 bytes)
+ * and bf16 scale plane (cols*rows/16 bytes). Bit-exact with the host packer.
+ * rows % 128 == 0, cols % 64 == 0. */
+xp_status xp_pack_km4bf16(void* stream, const float* w, uint32_t rows, uint32_t cols, uint32_t* words,
+                          uint32_t* scales);
+/* Seeded synthetic N(0, sigma) (Irwin-Hall(12)), identical to the test oracle. */
+xp_status xp_gen_normal(void* stream, float* out, uint64_t n, uint64_t offset, uint64_t seed, uint64_t stream_id,
+                        float sigma);
+/* Bandwidth probe with the reference's stream4 contract (llm_matvec.cl:370-378). */
+xp_status xp_stream4(void* stream, float* out, const void* src, uint32_t n_uint4, uint32_t threads);
+
+/* ---- decode session (examples/llm/decode.hpp:605-676) ----------------------- */
+typedef struct xp_session xp_session;
+
+typedef struct xp_model_config {
+    uint32_t n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim, vocab;
+    uint32_t max_seq;          /* KV capacity in positions */
+    uint32_t sliding_window;   /* 512 for Gemma 3 */
+    uint32_t global_every;     /* layer i is global iff (i+1) % global_every == 0 */
+    float rms_eps, rope_theta_global, rope_theta_local;
+    float embed_scale;         /* 0 -> sqrt(hidden) */
+    float attn_scale;          /* 0 -> 1/sqrt(head_dim) */
+} xp_model_config;
+
+typedef struct xp_sampling {
+    int greedy;               /* 1: argmax (SampleMode::Greedy); 0: temperature/top-k/top-p */
+    float temperature;
+    uint32_t top_k;           /* <= 64 on the device sampler; 0 -> 64 */
+    float top_p;
+    uint64_t seed;
+    uint64_t seq_id;          /* stream id of this sequence's uniforms */
+} xp_sampling;
+
+/* Random-init weights generated and packed on the device: every fp32 master
+ * tensor is N(0, 0.02) from the seeded generator with a fixed stream id per
+ * tensor (see xp_session_tensor_stream), norm weights N(0, 0.02) offsets, the
+ * LM head tied to the embedding. */
+xp_status xp_session_create_random(int device, const xp_model_config* cfg, const xp_sampling* sp, uint64_t seed,
+                                   xp_session** out);
+/* Host-provided weights: every pointer is HOST memory; packed planes in the
+ * reference layout, fp32 norm offsets, fp32 embedding [vocab][hidden].
+ * Per layer: wq,wk,wv,wo,gate,up,down words then scales. */
+typedef struct xp_layer_weights {
+    const uint32_t* words[7];
+    const uint32_t* scales[7];
+    const float* attn_norm;
+    const float* post_attn_norm;
+    const float* ffn_norm;
+    const float* post_ffn_norm;
+    const float* q_norm;
+    const float* k_norm;
+} xp_layer_weights;
+xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sampling* sp,
+                            const xp_layer_weights* layers, const uint32_t* lm_words, const uint32_t* lm_scales,
+                            const float* final_norm, const float* embed, xp_session** out);
+xp_status xp_session_destroy(xp_session* s);
+/* Stream id used for tensor (layer, which) by create_random; which: 0..6 the
+ * matrices q,k,v,o,gate,up,down; 7..12 the norms; layer = n_layers: 0 embed,
+ * 7 final norm. */
+uint64_t xp_session_tensor_stream(uint32_t layer, uint32_t which);
+/* DecodeSession::prefill (decode.cpp:1790-1817): one pass per token, logits
+ * only for the last one. Tokens are host memory. */
+xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n);
+/* DecodeSession::decode_step (decode.cpp:1819-1866): sample from the
+ * previous pass's logits, run the network on it, return the sampled id. */
+xp_status xp_session_decode_step(xp_session* s, uint32_t* token);
+/* Device-resident generation: n steps back to back with no host round trip
+ * (the sampled token feeds the next step on the device); tokens (host) may be
+ * NULL. Returns the device time in *ms if non-null. */
+xp_status xp_session_generate(xp_session* s, uint32_t n, uint32_t* tokens, float* ms);
+xp_status xp_session_reset(xp_session* s);            /* DecodeSession::reset */
+xp_status xp_session_position(xp_session* s, uint32_t* pos);
+xp_status xp_session_logits(xp_session* s, float* host_out, uint32_t n);  /* last_logits() */
+/* Current token buffer (the next input) and per-kernel counts. */
+xp_status xp_session_stats(xp_session* s, uint32_t* kernels_per_token, uint64_t* weight_bytes);
+/* Device pointers of internal buffers, for tests: name in {"x","logits","kcache0",...} */
+xp_status xp_session_debug_ptr(xp_session* s, const char* name, void** dptr, size_t* bytes);
+/* Roofline probe of the dominant kernel: replays a graph holding only the
+ * token's int4 matvecs (same kernels and launch shapes as the decode graph)
+ * `iters` times back to back and reports device ms, algorithmic bytes
+ * (nibbles + scales + activations) and launches per token. */
+xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per_token, uint64_t* bytes_per_token,
+                                    uint32_t* launches_per_token);
+/* CUDA events on the session stream: stop = 0 records the start, 1 the end
+ * and returns the elapsed device ms (brackets host-driven decode_step loops). */
+xp_status xp_session_timer(xp_session* s, int stop, float* ms);
+/* The device error word (bit 0: attention chunk overflow); cleared on read. */
+xp_status xp_session_error_word(xp_session* s, uint32_t* word);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -301,8 +301,13 @@ void xo_rope(float* x, uint32_t n_heads, uint32_t head_dim, uint32_t pos, float 
     for (uint32_t h = 0; h < n_heads; ++h)
         for (uint32_t d = 0; d < half; ++d) {
             const uint32_t base = h * head_dim + d;
+            /* theta^(-2d/hd) as in the reference, with log2 and exp2 each
+             * rounded once from double so every IEEE host and the device
+             * agree bit for bit (the reference's fp32 exp2/log2 builtins
+             * differ between drivers by an ulp). */
+            const float l2 = (float)log2((double)theta);
             const float frac = (float)(2u * d) / (float)head_dim;
-            const float inv = exp2f(-log2f(theta) * frac);
+            const float inv = (float)exp2((double)(-l2 * frac));
             const float ang = (float)pos * inv;
             const float c = cosf(ang), s = sinf(ang);
             const float lo = x[base], hi = x[base + half];

@@ -147,3 +147,98 @@ def mv(x, words, scales, rows, cols, split=1):
     else:
         oracle().xo_mv_km4_bs(out, np.ascontiguousarray(x, np.float32), words, scales, rows, cols)
     return out
+
+
+# ---- whole-model oracle (xo_forward) -----------------------------------------
+class XoQW(C.Structure):
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("wq", C.c_void_p), ("sc", C.c_void_p)]
+
+
+class XoLayer(C.Structure):
+    _fields_ = [(n, XoQW) for n in ("wq", "wk", "wv", "wo", "gate", "up", "down")] + \
+               [(n, C.c_void_p) for n in ("attn_norm", "post_attn_norm", "ffn_norm", "post_ffn_norm", "q_norm",
+                                          "k_norm")]
+
+
+class XoModel(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_layers", "hidden", "ffn", "n_heads", "n_kv_heads", "head_dim", "vocab",
+                                          "max_seq", "sliding_window", "global_every", "norm_parts")] + \
+               [(n, C.c_float) for n in ("rms_eps", "theta_global", "theta_local", "embed_scale", "attn_scale")] + \
+               [("kv_fp16", C.c_int), ("layers", C.POINTER(XoLayer)), ("lm_head", XoQW),
+                ("final_norm", C.c_void_p), ("embed", C.c_void_p)]
+
+
+class XoState(C.Structure):
+    _fields_ = [("kcache", C.POINTER(C.c_void_p)), ("vcache", C.POINTER(C.c_void_p))]
+
+
+def tensor_stream(layer, which):
+    """Same stream ids as xp_session_tensor_stream (engine random init)."""
+    return 0x1000 + layer * 32 + which
+
+
+class OracleModel:
+    """Random-init model built exactly as xp_session_create_random builds it
+    (same generator, same stream ids, same packer), run by xo_forward."""
+
+    def __init__(self, cfg, seed, kv_fp16=True):
+        o = oracle()
+        o.xo_forward.argtypes = [C.POINTER(XoModel), C.POINTER(XoState), C.c_uint32, C.c_uint32, C.c_void_p]
+        self.cfg = cfg
+        self.keep = []
+        H, V = cfg.hidden, cfg.vocab
+        L = (XoLayer * cfg.n_layers)()
+        self.layers_np = []
+        for l in range(cfg.n_layers):
+            lw = {"words": [], "scales": []}
+            for m, (rows, cols) in enumerate(cfg.matrix_shapes()):
+                w = gen_normal(seed, tensor_stream(l, m), rows * cols, 0.02)
+                words, scales = pack(w, rows, cols)
+                lw["words"].append(words)
+                lw["scales"].append(scales)
+                q = XoQW(rows, cols, words.ctypes.data, scales.ctypes.data)
+                setattr(L[l], ("wq", "wk", "wv", "wo", "gate", "up", "down")[m], q)
+            names = ("attn_norm", "post_attn_norm", "ffn_norm", "post_ffn_norm", "q_norm", "k_norm")
+            for n, name in enumerate(names):
+                v = gen_normal(seed, tensor_stream(l, 7 + n), H if n < 4 else cfg.head_dim, 0.02)
+                lw[name] = v
+                setattr(L[l], name, v.ctypes.data)
+            self.layers_np.append(lw)
+        self.embed = gen_normal(seed, tensor_stream(cfg.n_layers, 0), V * H, 0.02)
+        self.lm_words, self.lm_scales = pack(self.embed, H, V)
+        self.final_norm = gen_normal(seed, tensor_stream(cfg.n_layers, 7), H, 0.02)
+        m = XoModel()
+        for n in ("n_layers", "hidden", "ffn", "n_heads", "n_kv_heads", "head_dim", "vocab", "max_seq",
+                  "sliding_window", "global_every"):
+            setattr(m, n, getattr(cfg, n))
+        m.norm_parts = 64
+        m.rms_eps, m.theta_global, m.theta_local = cfg.rms_eps, cfg.rope_theta_global, cfg.rope_theta_local
+        m.embed_scale = cfg.embed_scale or float(np.float32(np.sqrt(np.float32(H))))
+        m.attn_scale = cfg.attn_scale or float(np.float32(1.0) / np.sqrt(np.float32(cfg.head_dim)))
+        m.kv_fp16 = int(kv_fp16)
+        m.layers = L
+        m.lm_head = XoQW(H, V, self.lm_words.ctypes.data, self.lm_scales.ctypes.data)
+        m.final_norm = self.final_norm.ctypes.data
+        m.embed = self.embed.ctypes.data
+        self.model = m
+        self.L = L
+        kvd = cfg.n_kv_heads * cfg.head_dim
+        dt = np.uint16 if kv_fp16 else np.float32
+        self.kc = [np.zeros(cfg.max_seq * kvd, dt) for _ in range(cfg.n_layers)]
+        self.vc = [np.zeros(cfg.max_seq * kvd, dt) for _ in range(cfg.n_layers)]
+        kp = (C.c_void_p * cfg.n_layers)(*[a.ctypes.data for a in self.kc])
+        vp = (C.c_void_p * cfg.n_layers)(*[a.ctypes.data for a in self.vc])
+        self.state = XoState(C.cast(kp, C.POINTER(C.c_void_p)), C.cast(vp, C.POINTER(C.c_void_p)))
+        self.keep += [kp, vp]
+
+    def weights_dict(self):
+        """The packed weights in the layout DecodeSession.from_weights takes."""
+        return {"layers": self.layers_np, "lm_words": self.lm_words, "lm_scales": self.lm_scales,
+                "final_norm": self.final_norm, "embed": self.embed}
+
+    def forward(self, token, pos, want_logits=True):
+        out = np.empty(self.cfg.vocab, np.float32) if want_logits else None
+        rc = oracle().xo_forward(C.byref(self.model), C.byref(self.state), token, pos,
+                                 out.ctypes.data if want_logits else None)
+        assert rc == 0
+        return out

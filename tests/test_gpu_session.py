@@ -1,0 +1,109 @@
+"""The decode engine (one CUDA graph per token) against the oracle's
+record_token restatement on a small random-init model with the Gemma-3
+head layout, built from the same seeded generator and stream ids."""
+import numpy as np
+import pytest
+
+import oracle_lib as O
+
+pytestmark = pytest.mark.gpu
+pytest.importorskip("torch")
+from gpu_util import rel_l2  # noqa: E402
+from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling  # noqa: E402
+
+SMALL = DecodeConfig(n_layers=3, hidden=256, ffn=512, vocab=4096, max_seq=64, sliding_window=16, global_every=3)
+
+
+def _check_logits(got, want, tol=2e-3):
+    assert rel_l2(got, want) < tol, rel_l2(got, want)
+
+
+def test_session_greedy_matches_oracle():
+    cfg = SMALL
+    seed = 7
+    om = O.OracleModel(cfg, seed)
+    sess = DecodeSession.random(cfg, Sampling(greedy=True), seed=seed)
+    prompt = O.gen_tokens(seed, 500, 12, cfg.vocab)
+    sess.prefill(prompt)
+    want = None
+    for p, t in enumerate(prompt):
+        want = om.forward(int(t), p, want_logits=(p == len(prompt) - 1))
+    _check_logits(sess.last_logits(), want)
+    pos = len(prompt)
+    # teacher-forced greedy: both sides consume the engine's token
+    for step in range(24):
+        top2 = np.sort(want)[-2:]
+        tok = sess.decode_step()
+        if top2[1] - top2[0] > 1e-4:
+            assert tok == int(np.argmax(want))
+        want = om.forward(tok, pos)
+        pos += 1
+        _check_logits(sess.last_logits(), want)
+    assert sess.position() == pos
+
+
+def test_session_from_host_weights_matches_random_init():
+    cfg = SMALL
+    om = O.OracleModel(cfg, 11)
+    a = DecodeSession.random(cfg, Sampling(), seed=11)
+    b = DecodeSession.from_weights(cfg, om.weights_dict(), Sampling())
+    prompt = O.gen_tokens(11, 9, 5, cfg.vocab)
+    a.prefill(prompt)
+    b.prefill(prompt)
+    assert np.array_equal(a.last_logits(), b.last_logits())
+    for _ in range(5):
+        assert a.decode_step() == b.decode_step()
+
+
+def test_session_generate_matches_steps():
+    cfg = SMALL
+    a = DecodeSession.random(cfg, Sampling(), seed=3)
+    b = DecodeSession.random(cfg, Sampling(), seed=3)
+    prompt = O.gen_tokens(3, 1, 6, cfg.vocab)
+    a.prefill(prompt)
+    b.prefill(prompt)
+    steps = [a.decode_step() for _ in range(20)]
+    toks, ms = b.generate(20)
+    assert list(toks) == steps
+    assert ms > 0
+    assert np.array_equal(a.last_logits(), b.last_logits())
+
+
+def test_session_sampling_matches_oracle():
+    cfg = SMALL
+    sp = Sampling(greedy=False, temperature=1.0, top_k=64, top_p=0.95, seed=99, seq_id=3)
+    om = O.OracleModel(cfg, 5)
+    sess = DecodeSession.random(cfg, sp, seed=5)
+    prompt = O.gen_tokens(5, 2, 8, cfg.vocab)
+    sess.prefill(prompt)
+    want = None
+    for p, t in enumerate(prompt):
+        want = om.forward(int(t), p, want_logits=(p == len(prompt) - 1))
+    pos = len(prompt)
+    agree = 0
+    for step in range(16):
+        tok = sess.decode_step()
+        u = O.oracle().xo_uniform(sp.seed, sp.seq_id, pos - 1)
+        exp_tok = O.oracle().xo_sample(want, cfg.vocab, sp.temperature, sp.top_k, sp.top_p, u)
+        agree += tok == exp_tok
+        want = om.forward(tok, pos)
+        pos += 1
+    # logits agree to ~1e-6, so the draws agree except at a boundary within that
+    assert agree >= 15
+
+
+def test_session_errors():
+    cfg = SMALL
+    sess = DecodeSession.random(cfg, Sampling(), seed=1)
+    from xpose_b200 import XpError
+    with pytest.raises(XpError) as e:
+        sess.decode_step()
+    assert e.value.name == "XP_ERR_STATE"
+    with pytest.raises(XpError):
+        sess.prefill([cfg.vocab])  # out of vocabulary
+    sess.reset()
+    sess.prefill(O.gen_tokens(1, 1, cfg.max_seq, cfg.vocab))
+    with pytest.raises(XpError) as e:
+        sess.decode_step()
+    assert e.value.name == "XP_ERR_KV_FULL"
+    assert sess.error_word() == 0

@@ -1,0 +1,678 @@
+// DecodeSession on sm_100a: the reference's per-token op order
+// (examples/llm/decode.cpp:1634-1780) as five fused kernels per layer,
+// captured once into a CUDA graph with programmatic dependent launch.
+//
+//   qkv    : [residual + post-FFN norm of the previous layer] + attn norm ->
+//            int4 matvec q|k|v (cluster K-split)
+//   attn   : QK-norm + RoPE + fp16 KV append + split-K flash-decode + combine
+//   o      : int4 matvec (cluster K-split) on the attention output's limbs
+//   gateup : residual + post-attn norm + FFN norm -> gate|up matvec -> GeGLU
+//   down   : int4 matvec (cluster K-split) on hb's limbs
+// then final norm -> LM head (per-tile argmax) -> sampler. The token id and
+// the position live in device memory, so the same graph replays for every
+// position; a local layer's window is computed on the device from `pos`.
+#pragma once
+#include <cmath>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+#include "runtime.cuh"
+
+namespace xp {
+
+struct QW {
+    uint4* wq = nullptr;
+    uint2* sc = nullptr;
+    uint32_t rows = 0, cols = 0;
+};
+struct LayerDev {
+    QW m[7];          // q, k, v, o, gate, up, down
+    float* norm[6];   // attn, post_attn, ffn, post_ffn, q_norm, k_norm
+    __half* kc = nullptr;
+    __half* vc = nullptr;
+};
+
+inline int env_int(const char* name, int dflt) {
+    const char* v = std::getenv(name);
+    return v && *v ? std::atoi(v) : dflt;
+}
+
+// Smallest K-split (cluster size <= 8) that puts at least ~0.9 CTAs per SM
+// on the GPU, preferring splits that divide the block count evenly.
+inline uint32_t pick_ksplit(uint32_t tiles, uint32_t nblk) {
+    const uint32_t want = (uint32_t)(0.9 * sm_count());
+    uint32_t best = 1;
+    for (uint32_t ks = 1; ks <= 8; ++ks) {
+        if (nblk / ks < 2) break;
+        best = ks;
+        if (tiles * ks >= want && nblk % ks == 0) return ks;
+    }
+    for (uint32_t ks = 1; ks <= 8; ++ks)
+        if (tiles * ks >= want && nblk / ks >= 2) return ks;
+    return best;
+}
+
+}  // namespace xp
+
+using namespace xp;
+
+struct xp_session {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    xp_model_config cfg{};
+    xp_sampling sp{};
+    std::vector<LayerDev> L;
+    QW lm;
+    float* final_norm = nullptr;
+    float* embed = nullptr;
+    // activations
+    float *xa = nullptr, *xb = nullptr, *qr = nullptr, *kr = nullptr, *vr = nullptr, *att = nullptr;
+    float *oo = nullptr, *hb = nullptr, *dn = nullptr, *logits = nullptr, *amv = nullptr, *sample_out = nullptr;
+    uint32_t *ami = nullptr, *token = nullptr, *pos = nullptr, *hist = nullptr;
+    XBlk *att_xq = nullptr, *hb_xq = nullptr, *lm_xq = nullptr;
+    void* attn_scratch = nullptr;
+    void* samp_scratch = nullptr;
+    uint32_t* h_in = nullptr;
+    uint32_t* h_out = nullptr;
+    cudaGraphExec_t g_dev = nullptr, g_io = nullptr, g_prefill = nullptr;
+    cudaEvent_t ev_done = nullptr, ev_a = nullptr, ev_b = nullptr;
+    uint32_t host_pos = 0;
+    bool have_logits = false;
+    uint32_t kernels_per_token = 0;
+    uint64_t weight_bytes = 0;
+    uint32_t nsplit_global = 0, nsplit_local = 0;
+    uint32_t ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_down = 1;
+    bool pdl = true;
+    std::vector<void*> allocs;
+    uint32_t launches = 0;  // counted while recording
+    uint32_t mv_launches = 0;
+    uint64_t mv_token_bytes = 0;
+
+    ~xp_session() {
+        cudaSetDevice(device);
+        if (st) cudaStreamSynchronize(st);
+        for (cudaGraphExec_t g : {g_dev, g_io, g_prefill, g_mv})
+            if (g) cudaGraphExecDestroy(g);
+        for (cudaEvent_t e : {ev_done, ev_a, ev_b})
+            if (e) cudaEventDestroy(e);
+        for (void* p : allocs) cudaFree(p);
+        if (h_in) cudaFreeHost(h_in);
+        if (h_out) cudaFreeHost(h_out);
+        if (st) cudaStreamDestroy(st);
+    }
+
+    template <class T> xp_status alloc(T** p, size_t count) {
+        void* d = nullptr;
+        cudaError_t e = cudaMalloc(&d, count * sizeof(T) + 16);
+        if (e != cudaSuccess) return fail(XP_ERR_OOM, "decode: cudaMalloc(%zu) failed: %s", count * sizeof(T),
+                                          cudaGetErrorString(e));
+        cudaMemset(d, 0, count * sizeof(T) + 16);
+        allocs.push_back(d);
+        *p = static_cast<T*>(d);
+        return XP_OK;
+    }
+
+    uint32_t q_dim() const { return cfg.n_heads * cfg.head_dim; }
+    uint32_t kv_dim() const { return cfg.n_kv_heads * cfg.head_dim; }
+    bool is_global(uint32_t l) const { return cfg.global_every == 0 || (l + 1) % cfg.global_every == 0; }
+
+    // ---- recording one token ----------------------------------------------------------
+    cudaError_t rec_mv(const MvArgs& a, bool pdl_here, uint32_t max_ctas = 0) {
+        ++launches;
+        return launch_mv(a, st, pdl_here, max_ctas);
+    }
+
+    bool mv_only = false;       // record only the int4 matvecs (roofline profiling)
+    uint64_t mv_bytes = 0;      // algorithmic bytes of the recorded matvecs
+    cudaGraphExec_t g_mv = nullptr;
+
+    void count_mv(uint32_t rows, uint32_t cols, uint32_t nmat_same = 1) {
+        // nibbles + bf16 scales + activation read (4 B/elt) + output (4 B/elt)
+        mv_bytes += nmat_same * ((uint64_t)rows * cols / 2 + (uint64_t)rows * cols / 16 + (uint64_t)cols * 4);
+        mv_bytes += (uint64_t)rows * 4;
+    }
+
+    cudaError_t record_forward(bool want_logits, bool first_after_copy, bool advance_only_hist) {
+        const uint32_t H = cfg.hidden, F = cfg.ffn, QD = q_dim(), KVD = kv_dim();
+        const float embed_scale = cfg.embed_scale > 0 ? cfg.embed_scale : std::sqrt((float)H);
+        const float attn_scale = cfg.attn_scale > 0 ? cfg.attn_scale : 1.0f / std::sqrt((float)cfg.head_dim);
+        cudaError_t e = cudaSuccess;
+        bool pdl_next = pdl && !first_after_copy;
+        for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+            LayerDev& w = L[l];
+            // qkv
+            MvArgs a{};
+            a.m[0] = MvMat{w.m[0].wq, w.m[0].sc, qr, QD, 0};
+            a.m[1] = MvMat{w.m[1].wq, w.m[1].sc, kr, KVD, QD / 64};
+            a.m[2] = MvMat{w.m[2].wq, w.m[2].sc, vr, KVD, QD / 64 + KVD / 64};
+            a.nmat = 3;
+            a.ntiles = (QD + 2 * KVD) / 64;
+            a.K = H;
+            a.hidden = H;
+            a.ksplit = ks_qkv;
+            a.epi = EPI_STORE;
+            a.eps = cfg.rms_eps;
+            a.w_pre = w.norm[0];
+            a.x_out = xb;
+            if (l == 0) {
+                a.pro = PRO_EMBED_NORM;
+                a.embed = embed;
+                a.token = token;
+                a.embed_scale = embed_scale;
+            } else {
+                a.pro = PRO_RESID_NORM;
+                a.x = xa;
+                a.y = dn;
+                a.w_post = L[l - 1].norm[3];
+            }
+            if (mv_only) { a.pro = PRO_XQ; a.xq_in = lm_xq; }
+            if ((e = rec_mv(a, pdl_next)) != cudaSuccess) return e;
+            count_mv(H, QD); mv_bytes += (uint64_t)H * KVD * 2 * 9 / 16 + 2 * KVD * 4;
+            pdl_next = pdl;
+            // attention
+            AttnArgs t{};
+            t.q_raw = qr; t.k_raw = kr; t.v_raw = vr;
+            t.q_norm = w.norm[4]; t.k_norm = w.norm[5];
+            t.kcache = w.kc; t.vcache = w.vc;
+            t.pos = pos;
+            const bool glob = is_global(l);
+            t.window = glob ? 0 : cfg.sliding_window;
+            t.theta = glob ? cfg.rope_theta_global : cfg.rope_theta_local;
+            t.eps = cfg.rms_eps;
+            t.scale = attn_scale;
+            t.att = att;
+            t.att_xq = att_xq;
+            const uint32_t ns = glob ? nsplit_global : nsplit_local;
+            const uint32_t span_max = glob ? cfg.max_seq : std::min(cfg.max_seq, cfg.sliding_window);
+            if (!mv_only) {
+                ++launches;
+                if ((e = launch_attn(t, attn_scratch, ns, span_max, st, pdl)) != cudaSuccess) return e;
+            }
+            // o
+            MvArgs o{};
+            o.m[0] = MvMat{w.m[3].wq, w.m[3].sc, oo, H, 0};
+            o.nmat = 1;
+            o.ntiles = H / 64;
+            o.K = QD;
+            o.hidden = QD;
+            o.ksplit = ks_o;
+            o.pro = PRO_XQ;
+            o.xq_in = att_xq;
+            o.epi = EPI_STORE;
+            if ((e = rec_mv(o, pdl)) != cudaSuccess) return e;
+            count_mv(QD, H);
+            // gate / up + GeGLU
+            MvArgs g{};
+            g.m[0] = MvMat{w.m[4].wq, w.m[4].sc, nullptr, F, 0};
+            g.m[1] = MvMat{w.m[5].wq, w.m[5].sc, nullptr, F, 0};
+            g.nmat = 2;
+            g.ntiles = F / 64;
+            g.K = H;
+            g.hidden = H;
+            g.ksplit = ks_gu;
+            g.pro = PRO_RESID_NORM;
+            g.x = xb;
+            g.y = oo;
+            g.w_post = w.norm[1];
+            g.w_pre = w.norm[2];
+            g.x_out = xa;
+            g.eps = cfg.rms_eps;
+            g.epi = EPI_GEGLU;
+            g.hb = hb;
+            g.xq_out = hb_xq;
+            if (mv_only) { g.pro = PRO_XQ; g.xq_in = lm_xq; g.xq_out = nullptr; }
+            if ((e = rec_mv(g, pdl)) != cudaSuccess) return e;
+            count_mv(H, F, 2);
+            // down
+            MvArgs d{};
+            d.m[0] = MvMat{w.m[6].wq, w.m[6].sc, dn, H, 0};
+            d.nmat = 1;
+            d.ntiles = H / 64;
+            d.K = F;
+            d.hidden = F;
+            d.ksplit = ks_down;
+            d.pro = PRO_XQ;
+            d.xq_in = hb_xq;
+            d.epi = EPI_STORE;
+            if ((e = rec_mv(d, pdl)) != cudaSuccess) return e;
+            count_mv(F, H);
+        }
+        if (!want_logits) {
+            ++launches;
+            return launch_ex(advance_kernel, dim3(1), dim3(32), 0, st, 1, pdl, pos);
+        }
+        // final norm -> LM head -> sampler
+        if (!mv_only) ++launches;
+        if (!mv_only && (e = launch_ex(final_norm_xq_kernel, dim3(1), dim3(1024), (size_t)H * 4, st, 1, pdl, (const float*)xa,
+                           (const float*)dn, (const float*)L[cfg.n_layers - 1].norm[3], (const float*)final_norm, H,
+                           cfg.rms_eps, (float*)nullptr, lm_xq)) != cudaSuccess)
+            return e;
+        MvArgs h{};
+        h.m[0] = MvMat{lm.wq, lm.sc, logits, cfg.vocab, 0};
+        h.nmat = 1;
+        h.ntiles = cfg.vocab / 64;
+        h.K = H;
+        h.hidden = H;
+        h.ksplit = 1;
+        h.pro = PRO_XQ;
+        h.xq_in = lm_xq;
+        h.epi = EPI_ARGMAX;
+        h.am_val = amv;
+        h.am_idx = ami;
+        if ((e = rec_mv(h, pdl)) != cudaSuccess) return e;
+        count_mv(H, cfg.vocab);
+        if (mv_only) return cudaSuccess;
+        uint32_t* hp = advance_only_hist ? hist : hist;
+        if (sp.greedy) {
+            ++launches;
+            return launch_ex(greedy_final_kernel, dim3(1), dim3(1024), 0, st, 1, pdl, (const float*)amv,
+                             (const uint32_t*)ami, h.ntiles, token, sample_out, pos, hp);
+        }
+        launches += 2;
+        return launch_sample_topk(token, sample_out, pos, nullptr, nullptr, logits, cfg.vocab, sp.top_k,
+                                  sp.temperature, sp.top_p, sp.seed, sp.seq_id, samp_scratch, st, pdl, true, hp);
+    }
+
+    xp_status capture(cudaGraphExec_t* out, bool want_logits, bool io) {
+        cudaGraph_t graph = nullptr;
+        launches = 0;
+        XP_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = cudaSuccess;
+        if (io) e = cudaMemcpyAsync(token, h_in, 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = record_forward(want_logits, io, false);
+        if (e == cudaSuccess && io) e = cudaMemcpyAsync(h_out, token, 4, cudaMemcpyDeviceToHost, st);
+        cudaError_t ce = cudaStreamEndCapture(st, &graph);
+        if (e != cudaSuccess || ce != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            return fail(XP_ERR_CUDA, "decode: graph capture failed: %s",
+                        cudaGetErrorString(e != cudaSuccess ? e : ce));
+        }
+        cudaError_t ie = cudaGraphInstantiate(out, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return fail(XP_ERR_CUDA, "decode: cudaGraphInstantiate: %s", cudaGetErrorString(ie));
+        return XP_OK;
+    }
+
+    xp_status validate_cfg() {
+        const xp_model_config& c = cfg;
+        if (!c.n_layers || !c.hidden || !c.ffn || !c.vocab || !c.max_seq)
+            return fail(XP_ERR_INVALID, "decode: zero dimension in model config");
+        if (c.head_dim != 256 || c.n_heads != 4 || c.n_kv_heads != 1)
+            return fail(XP_ERR_UNSUPPORTED,
+                        "decode: the fused attention kernel implements Gemma-3-1B heads (4 q, 1 kv, head_dim 256); got %u/%u/%u",
+                        c.n_heads, c.n_kv_heads, c.head_dim);
+        if (c.hidden % 128 || c.ffn % 128 || c.vocab % 64)
+            return fail(XP_ERR_INVALID, "decode: hidden and ffn must be multiples of 128, vocab of 64");
+        if (!sp.greedy && (sp.top_k > 64 || c.vocab < 64))
+            return fail(XP_ERR_UNSUPPORTED, "decode: the device sampler supports top_k <= 64");
+        return XP_OK;
+    }
+
+    xp_status init_common() {
+        XP_CUDA_TRY(cudaSetDevice(device));
+        XP_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        XP_CUDA_TRY(cudaEventCreateWithFlags(&ev_done, cudaEventDisableTiming));
+        XP_CUDA_TRY(cudaEventCreate(&ev_a));
+        XP_CUDA_TRY(cudaEventCreate(&ev_b));
+        XP_CUDA_TRY(cudaHostAlloc(&h_in, 64, cudaHostAllocDefault));
+        XP_CUDA_TRY(cudaHostAlloc(&h_out, 64, cudaHostAllocDefault));
+        std::memset(h_in, 0, 64);
+        std::memset(h_out, 0, 64);
+        pdl = env_int("XP_PDL", 1) != 0;
+        const uint32_t H = cfg.hidden, F = cfg.ffn, QD = q_dim(), KVD = kv_dim();
+        xp_status s;
+#define A(p, n) if ((s = alloc(&p, n)) != XP_OK) return s
+        A(xa, H); A(xb, H); A(qr, QD); A(kr, KVD); A(vr, KVD); A(att, QD); A(oo, H); A(hb, F); A(dn, H);
+        A(logits, cfg.vocab); A(amv, cfg.vocab / 64); A(ami, cfg.vocab / 64); A(sample_out, 2);
+        A(token, 1); A(pos, 1); A(hist, (size_t)cfg.max_seq + 1);
+        A(att_xq, QD / 32); A(hb_xq, F / 32); A(lm_xq, H / 32);
+        nsplit_global = std::max<uint32_t>(1, std::min<uint32_t>((cfg.max_seq + 63) / 64, 2 * sm_count()));
+        const uint32_t lspan = std::min(cfg.max_seq, cfg.sliding_window ? cfg.sliding_window : cfg.max_seq);
+        nsplit_local = std::max<uint32_t>(1, std::min<uint32_t>((lspan + 31) / 32, 2 * sm_count()));
+        nsplit_global = (uint32_t)env_int("XP_NSPLIT_GLOBAL", (int)nsplit_global);
+        nsplit_local = (uint32_t)env_int("XP_NSPLIT_LOCAL", (int)nsplit_local);
+        unsigned char* scr = nullptr;
+        A(scr, attn_scratch_bytes(std::max(nsplit_global, nsplit_local)));
+        attn_scratch = scr;
+        unsigned char* ss = nullptr;
+        A(ss, sample_scratch_bytes(cfg.vocab));
+        samp_scratch = ss;
+        for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+            A(L[l].kc, (size_t)cfg.max_seq * KVD);
+            A(L[l].vc, (size_t)cfg.max_seq * KVD);
+        }
+#undef A
+        ks_qkv = (uint32_t)env_int("XP_KS_QKV", (int)pick_ksplit((QD + 2 * KVD) / 64, H / 32));
+        ks_o = (uint32_t)env_int("XP_KS_O", (int)pick_ksplit(H / 64, QD / 32));
+        ks_gu = (uint32_t)env_int("XP_KS_GU", (int)pick_ksplit(F / 64, H / 32));
+        ks_down = (uint32_t)env_int("XP_KS_DOWN", (int)pick_ksplit(H / 64, F / 32));
+        return XP_OK;
+    }
+
+    xp_status alloc_weights() {
+        const uint32_t H = cfg.hidden, F = cfg.ffn, QD = q_dim(), KVD = kv_dim();
+        const uint32_t shapes[7][2] = {{H, QD}, {H, KVD}, {H, KVD}, {QD, H}, {H, F}, {H, F}, {F, H}};
+        xp_status s;
+        weight_bytes = 0;
+        for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+            for (int m = 0; m < 7; ++m) {
+                QW& q = L[l].m[m];
+                q.rows = shapes[m][0];
+                q.cols = shapes[m][1];
+                if ((s = alloc(&q.wq, (size_t)q.rows * q.cols / 32)) != XP_OK) return s;
+                if ((s = alloc(&q.sc, (size_t)q.rows * q.cols / 128)) != XP_OK) return s;
+                weight_bytes += (size_t)q.rows * q.cols / 2 + (size_t)q.rows * q.cols / 16;
+            }
+            for (int n = 0; n < 6; ++n)
+                if ((s = alloc(&L[l].norm[n], n < 4 ? H : cfg.head_dim)) != XP_OK) return s;
+        }
+        lm.rows = H;
+        lm.cols = cfg.vocab;
+        if ((s = alloc(&lm.wq, (size_t)lm.rows * lm.cols / 32)) != XP_OK) return s;
+        if ((s = alloc(&lm.sc, (size_t)lm.rows * lm.cols / 128)) != XP_OK) return s;
+        weight_bytes += (size_t)lm.rows * lm.cols / 2 + (size_t)lm.rows * lm.cols / 16;
+        if ((s = alloc(&final_norm, H)) != XP_OK) return s;
+        if ((s = alloc(&embed, (size_t)cfg.vocab * H)) != XP_OK) return s;
+        return XP_OK;
+    }
+
+    xp_status build_graphs() {
+        xp_status s;
+        if ((s = capture(&g_dev, true, false)) != XP_OK) return s;
+        kernels_per_token = launches;
+        if ((s = capture(&g_io, true, true)) != XP_OK) return s;
+        if ((s = capture(&g_prefill, false, true)) != XP_OK) return s;
+        return XP_OK;
+    }
+
+    xp_status wait_prev() {
+        cudaError_t e = cudaEventSynchronize(ev_done);
+        if (e != cudaSuccess) return fail(XP_ERR_DEVICE, "decode: device error: %s", cudaGetErrorString(e));
+        return XP_OK;
+    }
+};
+
+extern "C" {
+
+uint64_t xp_session_tensor_stream(uint32_t layer, uint32_t which) { return 0x1000ull + layer * 32ull + which; }
+
+static xp_status session_common(int device, const xp_model_config* cfg, const xp_sampling* sp, xp_session** out,
+                                xp_session** made) {
+    if (!cfg || !out) return fail(XP_ERR_INVALID, "decode: null config or out");
+    if (device < 0 || device >= xp_device_count()) return fail(XP_ERR_NO_DEVICE, "decode: no CUDA device %d", device);
+    auto* s = new xp_session;
+    s->device = device;
+    s->cfg = *cfg;
+    if (sp) s->sp = *sp;
+    else { s->sp.greedy = 1; s->sp.temperature = 1.0f; s->sp.top_p = 1.0f; s->sp.seed = 1234; }
+    xp_status st = s->validate_cfg();
+    if (st == XP_OK) {
+        s->L.resize(cfg->n_layers);
+        st = s->init_common();
+    }
+    if (st == XP_OK) st = s->alloc_weights();
+    if (st != XP_OK) { delete s; return st; }
+    *made = s;
+    return XP_OK;
+}
+
+xp_status xp_session_create_random(int device, const xp_model_config* cfg, const xp_sampling* sp, uint64_t seed,
+                                   xp_session** out) {
+    xp_session* s = nullptr;
+    xp_status st = session_common(device, cfg, sp, out, &s);
+    if (st != XP_OK) return st;
+    const uint32_t H = s->cfg.hidden;
+    float* tmp = nullptr;
+    size_t maxe = 0;
+    for (int m = 0; m < 7; ++m) maxe = std::max(maxe, (size_t)s->L[0].m[m].rows * s->L[0].m[m].cols);
+    if ((st = s->alloc(&tmp, maxe)) != XP_OK) { delete s; return st; }
+    auto gen = [&](float* dst, size_t n, uint64_t stream) {
+        return xp_gen_normal(s->st, dst, n, 0, seed, stream, 0.02f);
+    };
+    for (uint32_t l = 0; l < s->cfg.n_layers && st == XP_OK; ++l) {
+        for (int m = 0; m < 7 && st == XP_OK; ++m) {
+            QW& q = s->L[l].m[m];
+            st = gen(tmp, (size_t)q.rows * q.cols, xp_session_tensor_stream(l, m));
+            if (st == XP_OK)
+                st = xp_pack_km4bf16(s->st, tmp, q.rows, q.cols, reinterpret_cast<uint32_t*>(q.wq),
+                                     reinterpret_cast<uint32_t*>(q.sc));
+        }
+        for (int n = 0; n < 6 && st == XP_OK; ++n)
+            st = gen(s->L[l].norm[n], n < 4 ? H : s->cfg.head_dim, xp_session_tensor_stream(l, 7 + n));
+    }
+    const uint32_t NL = s->cfg.n_layers;
+    if (st == XP_OK) st = gen(s->embed, (size_t)s->cfg.vocab * H, xp_session_tensor_stream(NL, 0));
+    if (st == XP_OK)
+        st = xp_pack_km4bf16(s->st, s->embed, H, s->cfg.vocab, reinterpret_cast<uint32_t*>(s->lm.wq),
+                             reinterpret_cast<uint32_t*>(s->lm.sc));
+    if (st == XP_OK) st = gen(s->final_norm, H, xp_session_tensor_stream(NL, 7));
+    if (st == XP_OK && cudaStreamSynchronize(s->st) != cudaSuccess) st = fail(XP_ERR_CUDA, "decode: weight init failed");
+    if (st == XP_OK) st = s->build_graphs();
+    if (st != XP_OK) { delete s; return st; }
+    *out = s;
+    return XP_OK;
+}
+
+xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sampling* sp,
+                            const xp_layer_weights* layers, const uint32_t* lm_words, const uint32_t* lm_scales,
+                            const float* final_norm, const float* embed, xp_session** out) {
+    if (!layers || !lm_words || !lm_scales || !final_norm || !embed)
+        return fail(XP_ERR_INVALID, "decode: null weight pointer");
+    xp_session* s = nullptr;
+    xp_status st = session_common(device, cfg, sp, out, &s);
+    if (st != XP_OK) return st;
+    const uint32_t H = s->cfg.hidden;
+    auto up = [&](void* dst, const void* src, size_t bytes) -> xp_status {
+        if (!src) return fail(XP_ERR_INVALID, "decode: null weight pointer");
+        XP_CUDA_TRY(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+        return XP_OK;
+    };
+    for (uint32_t l = 0; l < s->cfg.n_layers && st == XP_OK; ++l) {
+        for (int m = 0; m < 7 && st == XP_OK; ++m) {
+            QW& q = s->L[l].m[m];
+            st = up(q.wq, layers[l].words[m], (size_t)q.rows * q.cols / 2);
+            if (st == XP_OK) st = up(q.sc, layers[l].scales[m], (size_t)q.rows * q.cols / 16);
+        }
+        const float* nsrc[6] = {layers[l].attn_norm, layers[l].post_attn_norm, layers[l].ffn_norm,
+                                layers[l].post_ffn_norm, layers[l].q_norm, layers[l].k_norm};
+        for (int n = 0; n < 6 && st == XP_OK; ++n)
+            st = up(s->L[l].norm[n], nsrc[n], (size_t)(n < 4 ? H : s->cfg.head_dim) * 4);
+    }
+    if (st == XP_OK) st = up(s->lm.wq, lm_words, (size_t)H * s->cfg.vocab / 2);
+    if (st == XP_OK) st = up(s->lm.sc, lm_scales, (size_t)H * s->cfg.vocab / 16);
+    if (st == XP_OK) st = up(s->final_norm, final_norm, (size_t)H * 4);
+    if (st == XP_OK) st = up(s->embed, embed, (size_t)s->cfg.vocab * H * 4);
+    if (st == XP_OK) st = s->build_graphs();
+    if (st != XP_OK) { delete s; return st; }
+    *out = s;
+    return XP_OK;
+}
+
+xp_status xp_session_destroy(xp_session* s) {
+    delete s;
+    return XP_OK;
+}
+
+xp_status xp_session_reset(xp_session* s) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    cudaSetDevice(s->device);
+    XP_CUDA_TRY(cudaStreamSynchronize(s->st));
+    XP_CUDA_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
+    XP_CUDA_TRY(cudaStreamSynchronize(s->st));
+    s->host_pos = 0;
+    s->have_logits = false;
+    return XP_OK;
+}
+
+xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    if (n == 0) return XP_OK;
+    if (!tokens) return fail(XP_ERR_INVALID, "decode: null token array");
+    cudaSetDevice(s->device);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (s->host_pos >= s->cfg.max_seq)
+            return fail(XP_ERR_KV_FULL, "decode: prompt exceeds max_seq (%u)", s->cfg.max_seq);
+        if (tokens[i] >= s->cfg.vocab)
+            return fail(XP_ERR_INVALID, "decode: token id %u is outside the vocabulary", tokens[i]);
+        xp_status st = s->wait_prev();
+        if (st != XP_OK) return st;
+        *s->h_in = tokens[i];
+        const bool last = i + 1 == n;
+        XP_CUDA_TRY(cudaGraphLaunch(last ? s->g_io : s->g_prefill, s->st));
+        XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));
+        ++s->host_pos;
+    }
+    s->have_logits = true;
+    return s->wait_prev();
+}
+
+xp_status xp_session_decode_step(xp_session* s, uint32_t* token) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    if (s->host_pos == 0)
+        return fail(XP_ERR_STATE, "decode: decode_step() before prefill() — there is no context to condition on");
+    if (s->host_pos >= s->cfg.max_seq)
+        return fail(XP_ERR_KV_FULL, "decode: KV cache is full (max_seq %u)", s->cfg.max_seq);
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    const uint32_t t = *s->h_out;  // sampled from the previous pass's logits
+    *s->h_in = t;
+    XP_CUDA_TRY(cudaGraphLaunch(s->g_io, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));
+    ++s->host_pos;
+    if (token) *token = t;
+    return XP_OK;
+}
+
+xp_status xp_session_generate(xp_session* s, uint32_t n, uint32_t* tokens, float* ms) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    if (s->host_pos == 0) return fail(XP_ERR_STATE, "decode: generate() before prefill()");
+    if (s->host_pos + n > s->cfg.max_seq)
+        return fail(XP_ERR_KV_FULL, "decode: %u steps from position %u exceed max_seq %u", n, s->host_pos,
+                    s->cfg.max_seq);
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    const uint32_t p0 = s->host_pos;
+    XP_CUDA_TRY(cudaEventRecord(s->ev_a, s->st));
+    for (uint32_t i = 0; i < n; ++i) XP_CUDA_TRY(cudaGraphLaunch(s->g_dev, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_b, s->st));
+    XP_CUDA_TRY(cudaMemcpyAsync(s->h_out, s->token, 4, cudaMemcpyDeviceToHost, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));
+    XP_CUDA_TRY(cudaEventSynchronize(s->ev_done));
+    s->host_pos += n;
+    if (ms) XP_CUDA_TRY(cudaEventElapsedTime(ms, s->ev_a, s->ev_b));
+    if (tokens && n) {
+        // hist[p] holds the token sampled at the step that advanced to p; the
+        // first generated step consumed the token sampled before it (h_out of
+        // the previous pass), so tokens[i] = the input of step i.
+        std::vector<uint32_t> h(n + 1);
+        XP_CUDA_TRY(cudaMemcpy(h.data(), s->hist + p0, (size_t)(n + 1) * 4, cudaMemcpyDeviceToHost));
+        for (uint32_t i = 0; i < n; ++i) tokens[i] = h[i];
+    }
+    return XP_OK;
+}
+
+xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per_token, uint64_t* bytes_per_token,
+                                    uint32_t* launches_per_token) {
+    if (!s || iters == 0) return fail(XP_ERR_INVALID, "profile: bad arguments");
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    if (!s->g_mv) {
+        s->mv_only = true;
+        s->mv_bytes = 0;
+        st = s->capture(&s->g_mv, true, false);
+        s->mv_only = false;
+        if (st != XP_OK) return st;
+        s->mv_launches = s->launches;
+        s->mv_token_bytes = s->mv_bytes;
+    }
+    // the matvec-only graph reads lm_xq as its activation: make it valid limbs
+    XP_CUDA_TRY(cudaGraphLaunch(s->g_mv, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_a, s->st));
+    for (uint32_t i = 0; i < iters; ++i) XP_CUDA_TRY(cudaGraphLaunch(s->g_mv, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_b, s->st));
+    XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));
+    XP_CUDA_TRY(cudaEventSynchronize(s->ev_b));
+    float ms = 0;
+    XP_CUDA_TRY(cudaEventElapsedTime(&ms, s->ev_a, s->ev_b));
+    if (ms_per_token) *ms_per_token = ms / iters;
+    if (bytes_per_token) *bytes_per_token = s->mv_token_bytes;
+    if (launches_per_token) *launches_per_token = s->mv_launches;
+    return XP_OK;
+}
+
+xp_status xp_session_timer(xp_session* s, int stop, float* ms) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    cudaSetDevice(s->device);
+    if (!stop) {
+        XP_CUDA_TRY(cudaEventRecord(s->ev_a, s->st));
+        return XP_OK;
+    }
+    XP_CUDA_TRY(cudaEventRecord(s->ev_b, s->st));
+    XP_CUDA_TRY(cudaEventSynchronize(s->ev_b));
+    if (ms) XP_CUDA_TRY(cudaEventElapsedTime(ms, s->ev_a, s->ev_b));
+    return XP_OK;
+}
+
+xp_status xp_session_position(xp_session* s, uint32_t* p) {
+    if (!s || !p) return fail(XP_ERR_INVALID, "null argument");
+    *p = s->host_pos;
+    return XP_OK;
+}
+xp_status xp_session_logits(xp_session* s, float* out, uint32_t n) {
+    if (!s || !out) return fail(XP_ERR_INVALID, "null argument");
+    if (n != s->cfg.vocab) return fail(XP_ERR_INVALID, "decode: logits buffer holds %u, vocab is %u", n, s->cfg.vocab);
+    if (!s->have_logits) return fail(XP_ERR_STATE, "decode: no forward pass with logits yet");
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    XP_CUDA_TRY(cudaMemcpy(out, s->logits, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return XP_OK;
+}
+xp_status xp_session_stats(xp_session* s, uint32_t* kpt, uint64_t* wb) {
+    if (!s) return fail(XP_ERR_INVALID, "null session");
+    if (kpt) *kpt = s->kernels_per_token;
+    if (wb) *wb = s->weight_bytes;
+    return XP_OK;
+}
+xp_status xp_session_debug_ptr(xp_session* s, const char* name, void** d, size_t* bytes) {
+    if (!s || !name || !d) return fail(XP_ERR_INVALID, "null argument");
+    const std::string n(name);
+    const uint32_t H = s->cfg.hidden;
+    size_t b = 0;
+    void* p = nullptr;
+    if (n == "xa") { p = s->xa; b = H * 4; }
+    else if (n == "xb") { p = s->xb; b = H * 4; }
+    else if (n == "logits") { p = s->logits; b = (size_t)s->cfg.vocab * 4; }
+    else if (n == "att") { p = s->att; b = (size_t)s->q_dim() * 4; }
+    else if (n == "embed") { p = s->embed; b = (size_t)s->cfg.vocab * H * 4; }
+    else if (n == "token") { p = s->token; b = 4; }
+    else if (n == "pos") { p = s->pos; b = 4; }
+    else if (n.rfind("kcache", 0) == 0 || n.rfind("vcache", 0) == 0) {
+        const uint32_t l = (uint32_t)std::atoi(n.c_str() + 6);
+        if (l >= s->cfg.n_layers) return fail(XP_ERR_INVALID, "no layer %u", l);
+        p = n[0] == 'k' ? (void*)s->L[l].kc : (void*)s->L[l].vc;
+        b = (size_t)s->cfg.max_seq * s->kv_dim() * 2;
+    } else if (n.rfind("w", 0) == 0 && n.size() >= 3) {
+        // "w<m>_<l>" words of matrix m (0..6, 7 = lm head) in layer l; "s<m>_<l>" scales
+        return fail(XP_ERR_INVALID, "unknown buffer '%s'", name);
+    } else return fail(XP_ERR_INVALID, "unknown buffer '%s'", name);
+    *d = p;
+    if (bytes) *bytes = b;
+    return XP_OK;
+}
+xp_status xp_session_error_word(xp_session* s, uint32_t* w) {
+    if (!s || !w) return fail(XP_ERR_INVALID, "null argument");
+    cudaSetDevice(s->device);
+    XP_CUDA_TRY(cudaStreamSynchronize(s->st));
+    // the attention error word follows the ticket at the head of the scratch
+    uint32_t* err = static_cast<uint32_t*>(s->attn_scratch) + 1;
+    XP_CUDA_TRY(cudaMemcpy(w, err, 4, cudaMemcpyDeviceToHost));
+    XP_CUDA_TRY(cudaMemset(err, 0, 4));
+    return XP_OK;
+}
+
+}  // extern "C"
