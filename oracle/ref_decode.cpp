@@ -54,7 +54,7 @@ const char* xpref_session_error(void) { return g_sess_err.c_str(); }
 
 void* xpref_session_create(const char* gguf_path, const char* kernel_dir, uint32_t max_seq,
                            int greedy, float temperature, uint32_t top_k, float top_p,
-                           uint64_t seed) {
+                           uint64_t seed, uint32_t global_every) {
     try {
         Paths p;
         std::string kd = kernel_dir ? kernel_dir : "kernels";
@@ -70,6 +70,7 @@ void* xpref_session_create(const char* gguf_path, const char* kernel_dir, uint32
         c.sampling.top_k = top_k;
         c.sampling.top_p = top_p;
         c.sampling.seed = seed;
+        c.global_every = global_every;
         auto* h = new xpref_session;
         h->s = std::make_unique<DecodeSession>(p, c);
         return h;

@@ -75,7 +75,7 @@ def ref():
         lib.xpref_plan_weight_bytes.restype = C.c_uint64
         lib.xpref_plan_dispatches.restype = C.c_uint32
         lib.xpref_session_create.argtypes = [C.c_char_p, C.c_char_p, C.c_uint32, C.c_int, C.c_float,
-                                             C.c_uint32, C.c_float, C.c_uint64]
+                                             C.c_uint32, C.c_float, C.c_uint64, C.c_uint32]
         lib.xpref_session_create.restype = C.c_void_p
         lib.xpref_session_error.restype = C.c_char_p
         lib.xpref_session_destroy.argtypes = [C.c_void_p]
@@ -177,14 +177,21 @@ def tensor_stream(layer, which):
     return 0x1000 + layer * 32 + which
 
 
+def _roundtrip(w):
+    """Norm offsets as a GGUF file carries them: stored (1 + w), loaded back
+    as (1 + w) - 1 (examples/llm/decode.cpp:1490-1502), both in fp32."""
+    return ((np.float32(1.0) + w.astype(np.float32)).astype(np.float32) - np.float32(1.0)).astype(np.float32)
+
+
 class OracleModel:
     """Random-init model built exactly as xp_session_create_random builds it
     (same generator, same stream ids, same packer), run by xo_forward."""
 
-    def __init__(self, cfg, seed, kv_fp16=True):
+    def __init__(self, cfg, seed, kv_fp16=True, norm_roundtrip=False):
         o = oracle()
         o.xo_forward.argtypes = [C.POINTER(XoModel), C.POINTER(XoState), C.c_uint32, C.c_uint32, C.c_void_p]
         self.cfg = cfg
+        self.seed = seed
         self.keep = []
         H, V = cfg.hidden, cfg.vocab
         L = (XoLayer * cfg.n_layers)()
@@ -201,12 +208,16 @@ class OracleModel:
             names = ("attn_norm", "post_attn_norm", "ffn_norm", "post_ffn_norm", "q_norm", "k_norm")
             for n, name in enumerate(names):
                 v = gen_normal(seed, tensor_stream(l, 7 + n), H if n < 4 else cfg.head_dim, 0.02)
+                if norm_roundtrip:
+                    v = _roundtrip(v)
                 lw[name] = v
                 setattr(L[l], name, v.ctypes.data)
             self.layers_np.append(lw)
         self.embed = gen_normal(seed, tensor_stream(cfg.n_layers, 0), V * H, 0.02)
         self.lm_words, self.lm_scales = pack(self.embed, H, V)
         self.final_norm = gen_normal(seed, tensor_stream(cfg.n_layers, 7), H, 0.02)
+        if norm_roundtrip:
+            self.final_norm = _roundtrip(self.final_norm)
         m = XoModel()
         for n in ("n_layers", "hidden", "ffn", "n_heads", "n_kv_heads", "head_dim", "vocab", "max_seq",
                   "sliding_window", "global_every"):
@@ -242,3 +253,59 @@ class OracleModel:
                                  out.ctypes.data if want_logits else None)
         assert rc == 0
         return out
+
+
+def write_model_gguf(om, path, window=512):
+    """The OracleModel's fp32 master weights as a Gemma-3 GGUF the reference
+    engine loads (norms stored as 1 + w, tied output head)."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from gguf_writer import gemma3_meta, write_gguf
+    cfg = om.cfg
+    seed = om.seed
+    H = cfg.hidden
+    names = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+    norm_names = ("attn_norm", "post_attention_norm", "ffn_norm", "post_ffw_norm", "attn_q_norm", "attn_k_norm")
+    keys = ("attn_norm", "post_attn_norm", "ffn_norm", "post_ffn_norm", "q_norm", "k_norm")
+    tensors = [("token_embd.weight", (H, cfg.vocab), om.embed)]
+    for l in range(cfg.n_layers):
+        for m, (rows, cols) in enumerate(cfg.matrix_shapes()):
+            w = gen_normal(seed, tensor_stream(l, m), rows * cols, 0.02)
+            tensors.append((f"blk.{l}.{names[m]}.weight", (rows, cols), w))
+        for n in range(6):
+            v = om.layers_np[l][keys[n]]
+            tensors.append((f"blk.{l}.{norm_names[n]}.weight", (len(v),), np.float32(1.0) + v))
+    tensors.append(("output_norm.weight", (H,), np.float32(1.0) + om.final_norm))
+    write_gguf(path, gemma3_meta(cfg, cfg.rope_theta_global, window), tensors)
+
+
+class RefSession:
+    """The reference DecodeSession (examples/llm/decode.cpp) running on the CPU
+    stand-in runtime over the reference kernels, from a GGUF file."""
+
+    def __init__(self, gguf_path, max_seq, global_every, greedy=True):
+        self.lib = ref()
+        self.h = self.lib.xpref_session_create(gguf_path.encode(), b"kernels", max_seq, int(greedy), 1.0, 0, 1.0,
+                                               1234, global_every)
+        if not self.h:
+            raise RuntimeError(self.lib.xpref_session_error().decode())
+
+    def prefill(self, toks):
+        t = np.ascontiguousarray(toks, np.uint32)
+        assert self.lib.xpref_session_prefill(self.h, t, len(t)) == 0, self.lib.xpref_session_error()
+
+    def decode_step(self):
+        r = self.lib.xpref_session_step(self.h)
+        assert r >= 0, self.lib.xpref_session_error()
+        return int(r)
+
+    def logits(self, n):
+        out = np.empty(n, np.float32)
+        assert self.lib.xpref_session_logits(self.h, out, n) == 0
+        return out
+
+    def close(self):
+        if self.h:
+            self.lib.xpref_session_destroy(self.h)
+            self.h = None
