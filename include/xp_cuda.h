@@ -254,6 +254,10 @@ xp_status xp_session_debug_ptr(xp_session* s, const char* name, void** dptr, siz
  * (nibbles + scales + activations) and launches per token. */
 xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per_token, uint64_t* bytes_per_token,
                                     uint32_t* launches_per_token);
+/* Phase timeline of the last token (XP_TRACE=1 at session creation):
+ * out[0] = barriers; out[1] = start ns; out[2k], out[2k+1] = barrier k
+ * arrive / leave ns (CTA 0, %globaltimer); out[2*barriers+2] = end ns. */
+xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n);
 /* CUDA events on the session stream: stop = 0 records the start, 1 the end
  * and returns the elapsed device ms (brackets host-driven decode_step loops). */
 xp_status xp_session_timer(xp_session* s, int stop, float* ms);

@@ -125,6 +125,7 @@ _SIGS = {
     "xp_session_profile_matvec": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64),
                                             C.POINTER(C.c_uint32)]),
     "xp_session_timer": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_float)]),
+    "xp_session_trace": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
 }
 
 

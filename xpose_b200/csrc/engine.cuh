@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "runtime.cuh"
+#include "token_kernel.cuh"
 
 namespace xp {
 
@@ -86,6 +87,15 @@ struct xp_session {
     bool pdl = true;
     std::vector<void*> allocs;
     uint32_t launches = 0;  // counted while recording
+    // ---- persistent token kernel ----
+    bool use_tk = false;
+    TkArgs tk{};
+    size_t tk_smem = 0;
+    uint32_t tk_grid = 0;
+    TkLayer* tk_layers_dev = nullptr;
+    std::vector<TkLayer> tk_layers;
+    unsigned char* tk_head = nullptr;
+    uint64_t* tk_bar = nullptr;
     uint32_t mv_launches = 0;
     uint64_t mv_token_bytes = 0;
 
@@ -280,7 +290,8 @@ struct xp_session {
         XP_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         cudaError_t e = cudaSuccess;
         if (io) e = cudaMemcpyAsync(token, h_in, 4, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = record_forward(want_logits, io, false);
+        if (e == cudaSuccess) e = (use_tk && !mv_only) ? record_token_kernel(want_logits)
+                                                       : record_forward(want_logits, io, false);
         if (e == cudaSuccess && io) e = cudaMemcpyAsync(h_out, token, 4, cudaMemcpyDeviceToHost, st);
         cudaError_t ce = cudaStreamEndCapture(st, &graph);
         if (e != cudaSuccess || ce != cudaSuccess) {
@@ -292,6 +303,200 @@ struct xp_session {
         cudaGraphDestroy(graph);
         if (ie != cudaSuccess) return fail(XP_ERR_CUDA, "decode: cudaGraphInstantiate: %s", cudaGetErrorString(ie));
         return XP_OK;
+    }
+
+    // ---- token kernel plan -------------------------------------------------------------
+    static uint32_t largest_divisor_upto(uint32_t n, uint32_t cap) {
+        uint32_t best = 1;
+        for (uint32_t d = 1; d <= n && d <= cap; ++d)
+            if (n % d == 0) best = d;
+        return best;
+    }
+    static TkPhase mk_phase(uint32_t units, uint32_t nb, uint32_t cw, uint32_t nmat, uint32_t ks, uint32_t G) {
+        TkPhase p{};
+        p.units = units;
+        p.nb = nb;
+        p.cw = cw;
+        p.nmat = nmat;
+        p.ks = ks;
+        p.img_bytes = nmat * nb * cw * 18;
+        p.per_cta = (units + G - 1) / G;
+        return p;
+    }
+    static uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
+
+    // Returns false (and leaves the multi-kernel graph in charge) when the
+    // model does not fit the token kernel's one-unit-per-CTA phases.
+    bool plan_token_kernel() {
+        if (env_int("XP_ENGINE_MULTI", 0)) return false;
+        const uint32_t G = (uint32_t)sm_count();
+        const uint32_t H = cfg.hidden, F = cfg.ffn, QD = q_dim(), KVD = kv_dim();
+        const uint32_t nbH = H / 32, nbQ = QD / 32, nbF = F / 32;
+        if (H > 512 * TK_MAXJ || (H / 64) > G || QD + 2 * KVD > 512 * TK_MAXJ) return false;
+        if (cfg.vocab % 64) return false;
+        const uint32_t tq = (QD + 2 * KVD) / 64;
+        const uint32_t ksq = largest_divisor_upto(nbH, std::min<uint32_t>(TK_MAXP, G / tq));
+        const uint32_t kso = nbQ / 4;  // 128-dim K ranges (inside one 256-dim head)
+        const uint32_t to = H / 64;
+        const uint32_t ksd = largest_divisor_upto(nbF, std::min<uint32_t>(TK_MAXP, G / to));
+        if (tq * ksq > G || to * kso > G || to * ksd > G || tq == 0 || kso > (uint32_t)TK_MAXP) return false;
+        tk.qkv = mk_phase(tq * ksq, nbH / ksq, 64, 1, ksq, G);
+        tk.o = mk_phase(to * kso, 4, 64, 1, kso, G);
+        tk.gu = mk_phase(F / 16, nbH, 16, 2, 1, G);
+        tk.down = mk_phase(to * ksd, nbF / ksd, 64, 1, ksd, G);
+        tk.head = mk_phase(cfg.vocab / 64, nbH, 64, 1, 1, G);
+        if (tk.gu.per_cta > 3 || tk.down.nb > 4 * TK_WARPS) return false;
+        tk.chunk_max = (((cfg.max_seq + G - 1) / G) + 7) & ~7u;
+        uint32_t off = 0;
+        tk.off_qkv = off; off += al128(tk.qkv.img_bytes);
+        tk.off_o = off; off += al128(tk.o.img_bytes);
+        tk.off_gu = off; off += al128(tk.gu.per_cta * tk.gu.img_bytes);
+        tk.off_down = off; off += al128(tk.down.img_bytes);
+        tk.off_kv = off; off += al128(2 * tk.chunk_max * KVD * 2);
+        const uint32_t ring_bytes = off - tk.off_gu;
+        tk.head_ring = std::min<uint32_t>(TK_MAX_RING, ring_bytes / tk.head.img_bytes);
+        if (tk.head_ring == 0) return false;
+        tk.off_cqkv = off; off += al128(2 * H * 4);
+        tk.off_catt = off; off += al128(512 * 4);
+        tk.off_cgu = off; off += al128(2 * H * 4);
+        tk.off_rope = off; off += al128(512 * 4);
+        tk.off_xn = off; off += al128(std::max<uint32_t>(H, 128) * 4);
+        const uint32_t maxnb = std::max(std::max(std::max(tk.qkv.nb, tk.o.nb), std::max(tk.gu.nb, tk.down.nb)), tk.head.nb);
+        tk.off_xq = off; off += al128(maxnb * (uint32_t)sizeof(XBlk));
+        tk.off_q = off; off += al128(4 * 256 * 4 + 2 * 256 * 2);
+        tk.off_sc = off; off += al128(4 * tk.chunk_max * 4);
+        tk.off_red = off; off += al128(std::max<uint32_t>(4096, 64 + 16 * 64) * 4);
+        tk.off_misc = off; off += 512;
+        tk_smem = off;
+        if (tk_smem + 1024 > 227 * 1024) return false;
+        tk_grid = G;
+        return true;
+    }
+
+    xp_status repack(const QW& q, unsigned char* dst, const TkPhase& P, uint32_t mat, uint32_t tile0) {
+        RepackArgs r{};
+        r.words = q.wq;
+        r.sc = reinterpret_cast<const uint32_t*>(q.sc);
+        r.rows = q.rows;
+        r.cols = q.cols;
+        r.dst = dst;
+        r.img_bytes = P.img_bytes;
+        r.cw = P.cw;
+        r.nb = P.nb;
+        r.nmat = P.nmat;
+        r.mat = mat;
+        r.ks = P.ks;
+        r.tile0 = tile0;
+        const uint64_t total = (uint64_t)(q.rows / 32) * q.cols;
+        const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 32);
+        repack_units_kernel<<<blocks, 256, 0, st>>>(r);
+        XP_CUDA_TRY(cudaGetLastError());
+        return XP_OK;
+    }
+
+    xp_status setup_token_kernel() {
+        use_tk = plan_token_kernel();
+        if (!use_tk) return XP_OK;
+        const uint32_t G = tk_grid, H = cfg.hidden, QD = q_dim(), KVD = kv_dim();
+        xp_status e;
+        tk_layers.resize(cfg.n_layers);
+        for (uint32_t l = 0; l < cfg.n_layers; ++l) {
+            LayerDev& w = L[l];
+            TkLayer& t = tk_layers[l];
+            unsigned char *iq, *io, *ig, *id;
+            if ((e = alloc(&iq, (size_t)tk.qkv.units * tk.qkv.img_bytes)) != XP_OK) return e;
+            if ((e = alloc(&io, (size_t)tk.o.units * tk.o.img_bytes)) != XP_OK) return e;
+            if ((e = alloc(&ig, (size_t)tk.gu.units * tk.gu.img_bytes)) != XP_OK) return e;
+            if ((e = alloc(&id, (size_t)tk.down.units * tk.down.img_bytes)) != XP_OK) return e;
+            if ((e = repack(w.m[0], iq, tk.qkv, 0, 0)) != XP_OK) return e;
+            if ((e = repack(w.m[1], iq, tk.qkv, 0, QD / 64)) != XP_OK) return e;
+            if ((e = repack(w.m[2], iq, tk.qkv, 0, (QD + KVD) / 64)) != XP_OK) return e;
+            if ((e = repack(w.m[3], io, tk.o, 0, 0)) != XP_OK) return e;
+            if ((e = repack(w.m[4], ig, tk.gu, 0, 0)) != XP_OK) return e;
+            if ((e = repack(w.m[5], ig, tk.gu, 1, 0)) != XP_OK) return e;
+            if ((e = repack(w.m[6], id, tk.down, 0, 0)) != XP_OK) return e;
+            t.qkv = iq; t.o = io; t.gu = ig; t.down = id;
+            // per-phase constant vectors, contiguous for one bulk copy each
+            float *cq, *ca, *cgu;
+            if ((e = alloc(&cq, 2 * H)) != XP_OK) return e;
+            if ((e = alloc(&ca, 512)) != XP_OK) return e;
+            if ((e = alloc(&cgu, 2 * H)) != XP_OK) return e;
+            if (l > 0) XP_CUDA_TRY(cudaMemcpyAsync(cq, L[l - 1].norm[3], H * 4, cudaMemcpyDeviceToDevice, st));
+            XP_CUDA_TRY(cudaMemcpyAsync(cq + H, w.norm[0], H * 4, cudaMemcpyDeviceToDevice, st));
+            XP_CUDA_TRY(cudaMemcpyAsync(ca, w.norm[4], 256 * 4, cudaMemcpyDeviceToDevice, st));
+            XP_CUDA_TRY(cudaMemcpyAsync(ca + 256, w.norm[5], 256 * 4, cudaMemcpyDeviceToDevice, st));
+            XP_CUDA_TRY(cudaMemcpyAsync(cgu, w.norm[1], H * 4, cudaMemcpyDeviceToDevice, st));
+            XP_CUDA_TRY(cudaMemcpyAsync(cgu + H, w.norm[2], H * 4, cudaMemcpyDeviceToDevice, st));
+            t.c_qkv = cq; t.c_attn = ca; t.c_gu = cgu;
+            t.kc = w.kc;
+            t.vc = w.vc;
+            const bool glob = is_global(l);
+            t.window = glob ? 0 : cfg.sliding_window;
+            t.global = glob ? 1 : 0;
+        }
+        float* ch;
+        if ((e = alloc(&ch, 2 * H)) != XP_OK) return e;
+        XP_CUDA_TRY(cudaMemcpyAsync(ch, L[cfg.n_layers - 1].norm[3], H * 4, cudaMemcpyDeviceToDevice, st));
+        XP_CUDA_TRY(cudaMemcpyAsync(ch + H, final_norm, H * 4, cudaMemcpyDeviceToDevice, st));
+        tk.c_head = ch;
+        if ((e = alloc(&tk_head, (size_t)tk.head.units * tk.head.img_bytes)) != XP_OK) return e;
+        if ((e = repack(lm, tk_head, tk.head, 0, 0)) != XP_OK) return e;
+        if ((e = alloc(&tk_layers_dev, cfg.n_layers)) != XP_OK) return e;
+        XP_CUDA_TRY(cudaMemcpy(tk_layers_dev, tk_layers.data(), sizeof(TkLayer) * cfg.n_layers, cudaMemcpyHostToDevice));
+        float *qkvp, *attp, *atts, *op, *dnp, *amv2;
+        uint32_t* ami2;
+        if ((e = alloc(&qkvp, (size_t)tk.qkv.ks * (QD + 2 * KVD))) != XP_OK) return e;
+        if ((e = alloc(&attp, (size_t)G * 1024)) != XP_OK) return e;
+        if ((e = alloc(&atts, (size_t)G * 8)) != XP_OK) return e;
+        if ((e = alloc(&op, (size_t)tk.o.ks * H)) != XP_OK) return e;
+        if ((e = alloc(&dnp, (size_t)tk.down.ks * H)) != XP_OK) return e;
+        if ((e = alloc(&amv2, G)) != XP_OK) return e;
+        if ((e = alloc(&ami2, G)) != XP_OK) return e;
+        if ((e = alloc(&tk_bar, 4)) != XP_OK) return e;
+        if (env_int("XP_TRACE", 0)) {
+            if ((e = alloc(&tk.trace, 512 + 8 * 1024)) != XP_OK) return e;
+        }
+        tk.layers = tk_layers_dev;
+        tk.n_layers = cfg.n_layers;
+        tk.H = H; tk.F = cfg.ffn; tk.QD = QD; tk.KVD = KVD; tk.V = cfg.vocab;
+        tk.eps = cfg.rms_eps;
+        tk.embed_scale = cfg.embed_scale > 0 ? cfg.embed_scale : std::sqrt((float)H);
+        tk.attn_scale = cfg.attn_scale > 0 ? cfg.attn_scale : 1.0f / std::sqrt((float)cfg.head_dim);
+        tk.head_img = tk_head;
+        tk.theta_global = cfg.rope_theta_global;
+        tk.theta_local = cfg.rope_theta_local;
+        tk.embed = embed;
+        tk.x0 = xa; tk.x1 = xb;
+        tk.qkv_part = qkvp; tk.att_part = attp; tk.att_stat = atts; tk.o_part = op; tk.hb = hb; tk.dn_part = dnp;
+        tk.logits = logits; tk.am_val = amv2; tk.am_idx = ami2;
+        tk.token = token; tk.pos = pos; tk.hist = hist; tk.sample_out = sample_out;
+        tk.bar = tk_bar; tk.epoch = tk_bar + 1;
+        tk.err = static_cast<uint32_t*>(attn_scratch) + 1;
+        tk.greedy = sp.greedy;
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaStreamSynchronize(st));
+        return XP_OK;
+    }
+
+    cudaError_t record_token_kernel(bool want_logits) {
+        TkArgs a = tk;
+        a.want_logits = want_logits ? 1 : 0;
+        cudaLaunchConfig_t c = {};
+        c.gridDim = dim3(tk_grid);
+        c.blockDim = dim3(TK_THREADS);
+        c.dynamicSmemBytes = tk_smem;
+        c.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeCooperative;
+        at[0].val.cooperative = 1;
+        c.attrs = at;
+        c.numAttrs = 1;
+        ++launches;
+        cudaError_t e = cudaLaunchKernelEx(&c, token_kernel, a);
+        if (e != cudaSuccess || !want_logits || sp.greedy) return e;
+        launches += 2;
+        return launch_sample_topk(token, sample_out, pos, nullptr, nullptr, logits, cfg.vocab, sp.top_k,
+                                  sp.temperature, sp.top_p, sp.seed, sp.seq_id, samp_scratch, st, false, true, hist);
     }
 
     xp_status validate_cfg() {
@@ -448,6 +653,7 @@ xp_status xp_session_create_random(int device, const xp_model_config* cfg, const
                              reinterpret_cast<uint32_t*>(s->lm.sc));
     if (st == XP_OK) st = gen(s->final_norm, H, xp_session_tensor_stream(NL, 7));
     if (st == XP_OK && cudaStreamSynchronize(s->st) != cudaSuccess) st = fail(XP_ERR_CUDA, "decode: weight init failed");
+    if (st == XP_OK) st = s->setup_token_kernel();
     if (st == XP_OK) st = s->build_graphs();
     if (st != XP_OK) { delete s; return st; }
     *out = s;
@@ -483,6 +689,7 @@ xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sam
     if (st == XP_OK) st = up(s->lm.sc, lm_scales, (size_t)H * s->cfg.vocab / 16);
     if (st == XP_OK) st = up(s->final_norm, final_norm, (size_t)H * 4);
     if (st == XP_OK) st = up(s->embed, embed, (size_t)s->cfg.vocab * H * 4);
+    if (st == XP_OK) st = s->setup_token_kernel();
     if (st == XP_OK) st = s->build_graphs();
     if (st != XP_OK) { delete s; return st; }
     *out = s;
@@ -499,6 +706,7 @@ xp_status xp_session_reset(xp_session* s) {
     cudaSetDevice(s->device);
     XP_CUDA_TRY(cudaStreamSynchronize(s->st));
     XP_CUDA_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
+    if (s->tk_bar) XP_CUDA_TRY(cudaMemsetAsync(s->tk_bar, 0, 16, s->st));
     XP_CUDA_TRY(cudaStreamSynchronize(s->st));
     s->host_pos = 0;
     s->have_logits = false;
@@ -601,6 +809,16 @@ xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per
     if (ms_per_token) *ms_per_token = ms / iters;
     if (bytes_per_token) *bytes_per_token = s->mv_token_bytes;
     if (launches_per_token) *launches_per_token = s->mv_launches;
+    return XP_OK;
+}
+
+xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n) {
+    if (!s || !out) return fail(XP_ERR_INVALID, "null argument");
+    if (!s->use_tk || !s->tk.trace) return fail(XP_ERR_STATE, "trace: set XP_TRACE=1 before creating the session");
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    XP_CUDA_TRY(cudaMemcpy(out, s->tk.trace, (size_t)std::min<uint32_t>(n, 512 + 8 * 1024) * 8, cudaMemcpyDeviceToHost));
     return XP_OK;
 }
 

@@ -1,0 +1,103 @@
+// Primitives of the persistent token kernel: mbarriers, 1-D bulk async
+// copies (cp.async.bulk, no tensor map, no multicast), a bounded grid
+// barrier, and bounded waits that report through an error word instead of
+// hanging.
+#pragma once
+#include "common.cuh"
+
+namespace xp {
+
+constexpr uint32_t TK_ERR_ATTN_CHUNK = 1u;   // attention chunk larger than staged
+constexpr uint32_t TK_ERR_GRID_BAR = 2u;     // grid barrier wait ran out
+constexpr uint32_t TK_ERR_MBAR = 4u;         // bulk-copy wait ran out
+constexpr uint32_t TK_ERR_PLAN = 8u;         // a unit did not fit its slot
+
+// A wait of ~1 s on these loops is far beyond any phase (a token is < 1 ms).
+constexpr uint32_t TK_SPIN_LIMIT = 1u << 22;
+
+XP_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+XP_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+XP_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+XP_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+XP_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing on `bar`.
+XP_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+XP_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with `parity` to complete. On timeout sets the
+// error bit and returns (the data is then unspecified, the kernel finishes).
+XP_DEV void mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    uint32_t it = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (++it > TK_SPIN_LIMIT) {
+            atomicOr(err, TK_ERR_MBAR);
+            return;
+        }
+    }
+}
+
+XP_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Release-add: orders every prior write of the CTA (made visible to this
+// thread by the preceding bar.sync) before the increment, at GPU scope.
+XP_DEV void red_release_add_u64(uint64_t* p, uint64_t v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+XP_DEV uint64_t ld_acquire_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier over a monotonically increasing arrival counter: the
+// caller's k-th barrier of a launch waits for base + k * gridDim.x arrivals.
+// One CTA-wide bar.sync orders every thread's writes before thread 0's
+// release fence; thread 0's acquire load plus the closing bar.sync orders
+// every thread's later reads after the other CTAs' writes.
+XP_DEV void grid_barrier(uint64_t* counter, uint64_t target, uint32_t* err) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(reinterpret_cast<unsigned long long*>(counter), 1ull);
+        uint32_t it = 0;
+        while (ld_acquire_u64(counter) < target) {
+            if (++it > TK_SPIN_LIMIT) {
+                atomicOr(err, TK_ERR_GRID_BAR);
+                break;
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+}
+
+}  // namespace xp

@@ -1,0 +1,823 @@
+// Persistent token kernel: one cooperative launch decodes one position.
+//
+// Grid = one CTA per SM, all co-resident. The reference's per-token op order
+// (examples/llm/decode.cpp:1634-1780) runs as five phases per layer separated
+// by grid barriers:
+//
+//   QKV  : residual + post-FFN norm of layer l-1 (or the embedding), attention
+//          norm, then a K-split int4 matvec unit -> q|k|v partial sums
+//   ATTN : q/k/v = sum of partials, QK-norm + RoPE, fp16 KV append (CTA 0),
+//          one contiguous chunk of the attended window per CTA -> flash partials
+//   O    : combine the flash partials for this CTA's 128-dim K range, o-proj
+//          unit -> partial sums
+//   GU   : residual + post-attention norm, FFN norm, gate|up units of 16
+//          columns over all K -> GeGLU -> hb
+//   DOWN : hb limbs for this CTA's K range, down-proj unit -> partial sums
+//
+// then HEAD (residual + post-FFN + final norm, LM head tiles, per-CTA argmax)
+// and SAMPLE (CTA 0: lowest-index argmax, token, position).
+//
+// Everything a phase reads that does not depend on this token is in shared
+// memory before the phase starts:
+//   * weights live in a unit-major image made once at load time (each unit's
+//     nibbles and per-block bf16 scales contiguous), so a CTA's share of a
+//     phase is one cp.async.bulk copy into its slot;
+//   * the phase's norm weights are one contiguous vector per (layer, phase);
+//   * the KV rows a CTA attends to are staged one phase ahead;
+//   * RoPE cos/sin for this position are tabulated once per launch.
+// A slot is refilled for layer l+1 right after this CTA arrives at the
+// barrier that closes phase P of layer l, so every copy overlaps the barrier
+// wait and the other phases.
+#pragma once
+#include "attention.cuh"
+#include "common.cuh"
+#include "tk_primitives.cuh"
+#include "xq.cuh"
+
+namespace xp {
+
+constexpr int TK_THREADS = 512;
+constexpr int TK_WARPS = TK_THREADS / 32;
+constexpr int TK_MAXJ = 3;   // hidden <= 1536
+constexpr int TK_MAXP = 8;   // K-split partials per output <= 8
+constexpr int TK_NMB = 16;   // mbarriers
+constexpr int TK_OPV = 10;   // attention splits per thread loaded with the stats
+constexpr int TK_MB_QKV = 0, TK_MB_O = 1, TK_MB_GU = 2, TK_MB_DOWN = 3, TK_MB_KV = 4;
+constexpr int TK_MB_CQKV = 5, TK_MB_CATT = 6, TK_MB_CGU = 7, TK_MB_HEAD = 8;  // head ring: 8..15
+constexpr int TK_MAX_RING = TK_NMB - TK_MB_HEAD;
+
+struct TkPhase {
+    uint32_t units;      // units in the phase
+    uint32_t nb;         // 32-row blocks per unit
+    uint32_t cw;         // columns per unit
+    uint32_t nmat;       // matrices per unit image (2 for gate|up)
+    uint32_t ks;         // K chunks per column tile (unit = tile * ks + chunk)
+    uint32_t img_bytes;  // bytes of one unit image
+    uint32_t per_cta;    // most units any CTA takes
+};
+
+struct TkLayer {
+    const unsigned char* qkv;
+    const unsigned char* o;
+    const unsigned char* gu;
+    const unsigned char* down;
+    const float* c_qkv;   // [post_ffn of layer l-1 (zeros for l = 0) | attn_norm]   2H floats
+    const float* c_attn;  // [q_norm | k_norm]                                       512 floats
+    const float* c_gu;    // [post_attn_norm | ffn_norm]                              2H floats
+    __half* kc;
+    __half* vc;
+    uint32_t window;      // 0 = global layer
+    uint32_t global;      // RoPE table: 1 = global theta, 0 = local
+};
+
+struct TkArgs {
+    const TkLayer* layers;
+    uint32_t n_layers, H, F, QD, KVD, V;
+    float eps, embed_scale, attn_scale, theta_global, theta_local;
+    TkPhase qkv, o, gu, down, head;
+    const unsigned char* head_img;
+    const float* c_head;  // [post_ffn of the last layer | final_norm]  2H floats
+    const float* embed;
+    float* x0;          // residual after the FFN sublayer (written in QKV)
+    float* x1;          // residual after the attention sublayer (written in GU)
+    float* qkv_part;    // [qkv.ks][QD + 2 KVD]
+    float* att_part;    // [grid][4][256]
+    float* att_stat;    // [grid][4][2]
+    float* o_part;      // [o.ks][H]
+    float* hb;          // [F]
+    float* dn_part;     // [down.ks][H]
+    float* logits;      // [V]
+    float* am_val;      // [grid]
+    uint32_t* am_idx;   // [grid]
+    uint32_t* token;
+    uint32_t* pos;
+    uint32_t* hist;
+    float* sample_out;
+    uint64_t* bar;
+    uint64_t* epoch;
+    uint32_t* err;
+    uint64_t* trace;    // optional phase timeline (CTA 0)
+    int want_logits;
+    int greedy;
+    uint32_t chunk_max;
+    uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
+    uint32_t off_xn, off_xq, off_q, off_sc, off_red, off_misc;
+    uint32_t head_ring;
+};
+
+// ---- helpers -------------------------------------------------------------------
+
+// r = base + rmsnorm_gemma(sum_k part[k], w_post) (mode 1) or the scaled
+// embedding row (mode 0); x_out = r (CTA 0); xn = rmsnorm_gemma(r, w_pre).
+// w_post / w_pre are shared-memory vectors.
+XP_DEV void tk_norm_prologue(const TkArgs& a, int mode, const float* base, const float* part, uint32_t nparts,
+                             const float* w_post, const float* w_pre, float* x_out, float* xn, float* red) {
+    const uint32_t H = a.H;
+    const int tid = threadIdx.x;
+    float rv[TK_MAXJ];
+    if (mode == 0) {
+        const float* row = a.embed + (size_t)(*a.token) * H;
+#pragma unroll
+        for (int j = 0; j < TK_MAXJ; ++j) {
+            const uint32_t i = tid + j * TK_THREADS;
+            rv[j] = i < H ? row[i] * a.embed_scale : 0.0f;
+        }
+    } else {
+        // every global load of the prologue in flight at once, then summed in
+        // a fixed order
+        float ld[TK_MAXJ][TK_MAXP];
+        float bv[TK_MAXJ];
+#pragma unroll
+        for (int j = 0; j < TK_MAXJ; ++j) {
+            const uint32_t i = tid + j * TK_THREADS;
+            bv[j] = i < H ? base[i] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < TK_MAXP; ++k)
+                ld[j][k] = (i < H && (uint32_t)k < nparts) ? part[(size_t)k * H + i] : 0.0f;
+        }
+        float yv[TK_MAXJ];
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < TK_MAXJ; ++j) {
+            float s = 0.0f;
+#pragma unroll
+            for (int k = 0; k < TK_MAXP; ++k) s += ld[j][k];
+            yv[j] = s;
+            ss += s * s;
+        }
+        ss = block_sum(ss, red);
+        const float sc = rsqrtf(ss / (float)H + a.eps);
+#pragma unroll
+        for (int j = 0; j < TK_MAXJ; ++j) {
+            const uint32_t i = tid + j * TK_THREADS;
+            rv[j] = i < H ? bv[j] + yv[j] * sc * (1.0f + w_post[i]) : 0.0f;
+        }
+    }
+    float ss2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < TK_MAXJ; ++j) {
+        const uint32_t i = tid + j * TK_THREADS;
+        if (i < H && x_out && blockIdx.x == 0) x_out[i] = rv[j];
+        ss2 += rv[j] * rv[j];
+    }
+    ss2 = block_sum(ss2, red);
+    const float sc2 = rsqrtf(ss2 / (float)H + a.eps);
+#pragma unroll
+    for (int j = 0; j < TK_MAXJ; ++j) {
+        const uint32_t i = tid + j * TK_THREADS;
+        if (i < H) xn[i] = rv[j] * sc2 * (1.0f + w_pre[i]);
+    }
+    __syncthreads();
+}
+
+// Limbs of blocks [b0, b0+nb) of the smem vector v into xq[0..nb).
+XP_DEV void tk_prep(const float* v, uint32_t b0, uint32_t nb, XBlk* xq) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (uint32_t b = warp; b < nb; b += TK_WARPS) xq_prep_block(v[(b0 + b) * 32 + lane], &xq[b]);
+    __syncthreads();
+}
+
+XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
+    const int d = xq_dot(w, reinterpret_cast<const int4*>(X.w), X.bias);
+    return (float)d * (X.f * __uint_as_float((uint32_t)s << 16));
+}
+
+// A unit image of CW (64 or 32) columns over nb blocks: warp w takes blocks w,
+// w+16, ...; lane handles columns lane (and lane+32). Column sums -> red[0..CW).
+template <int CW>
+XP_DEV void tk_tile(const unsigned char* img, uint32_t nb, const XBlk* xq, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint4* nib = reinterpret_cast<const uint4*>(img);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(img + (size_t)nb * CW * 16);
+    float a0 = 0.0f, a1 = 0.0f;
+    for (uint32_t b = warp; b < nb; b += TK_WARPS) {
+        const XBlk& X = xq[b];
+        a0 += tk_dot(nib[b * CW + lane], sc[b * CW + lane], X);
+        if (CW == 64) a1 += tk_dot(nib[b * CW + lane + 32], sc[b * CW + lane + 32], X);
+    }
+    float* wr = red + 64;  // [16][CW] warp partials
+    wr[warp * CW + lane] = a0;
+    if (CW == 64) wr[warp * CW + lane + 32] = a1;
+    __syncthreads();
+    if (threadIdx.x < CW) {
+        float s = 0.0f;
+        const uint32_t nw = nb < (uint32_t)TK_WARPS ? nb : (uint32_t)TK_WARPS;
+        for (uint32_t w = 0; w < nw; ++w) s += wr[w * CW + threadIdx.x];
+        red[threadIdx.x] = s;
+    }
+    __syncthreads();
+}
+
+// Issue the bulk copies of this CTA's units of a phase into its slot. Thread 0
+// only. Returns whether anything was armed on `bar`.
+XP_DEV bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar) {
+    const uint32_t G = gridDim.x, c = blockIdx.x;
+    if (c >= P.units) return false;
+    uint32_t n = 0;
+    for (uint32_t u = c; u < P.units; u += G) ++n;
+    fence_proxy_async();
+    mbar_expect_tx(bar, n * P.img_bytes);
+    uint32_t i = 0;
+    for (uint32_t u = c; u < P.units; u += G, ++i)
+        bulk_g2s(slot + (size_t)i * P.img_bytes, imgs + (size_t)u * P.img_bytes, P.img_bytes, bar);
+    return true;
+}
+XP_DEV bool tk_issue_vec(const float* src, uint32_t n, unsigned char* slot, uint64_t* bar) {
+    fence_proxy_async();
+    mbar_expect_tx(bar, n * 4);
+    bulk_g2s(slot, src, n * 4, bar);
+    return true;
+}
+
+struct TkWin {
+    uint32_t kv_start, span, chunk, nsplit, j0, j1;
+};
+XP_DEV TkWin tk_window(uint32_t pos, uint32_t window) {
+    TkWin w;
+    const uint32_t seq = pos + 1;
+    w.kv_start = (window == 0 || seq <= window) ? 0 : seq - window;
+    w.span = seq - w.kv_start;
+    const uint32_t G = gridDim.x;
+    w.chunk = ((w.span + G - 1) / G + 7) & ~7u;
+    w.nsplit = (w.span + w.chunk - 1) / w.chunk;
+    w.j0 = w.kv_start + min(blockIdx.x * w.chunk, w.span);
+    w.j1 = w.kv_start + min((blockIdx.x + 1) * w.chunk, w.span);
+    return w;
+}
+
+// Stage the KV rows [j0, min(j1, pos)) of one layer (thread 0).
+XP_DEV bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigned char* kvs, uint64_t* bar) {
+    const TkWin w = tk_window(pos, L.window);
+    const uint32_t end = min(w.j1, pos);
+    if (w.j1 - w.j0 > a.chunk_max) { atomicOr(a.err, TK_ERR_ATTN_CHUNK); return false; }
+    if (end <= w.j0) return false;
+    const uint32_t rows = end - w.j0;
+    const uint32_t bytes = rows * a.KVD * 2;
+    fence_proxy_async();
+    mbar_expect_tx(bar, 2 * bytes);
+    bulk_g2s(kvs, L.kc + (size_t)w.j0 * a.KVD, bytes, bar);
+    bulk_g2s(kvs + (size_t)a.chunk_max * a.KVD * 2, L.vc + (size_t)w.j0 * a.KVD, bytes, bar);
+    return true;
+}
+
+// QK-norm + rotate-half RoPE of one 256-wide head held as 8 values per lane
+// (dims 4*lane..+3 and 128+4*lane..+3), weights and cos/sin from smem.
+XP_DEV void tk_qk_post(float v[8], const float* w, const float* cosT, const float* sinT, float eps) {
+    const int lane = threadIdx.x & 31;
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+    ss = warp_sum(ss);
+    const float sc = rsqrtf(ss / 256.0f + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t d = 4 * lane + i;
+        const float lo = v[i] * sc * (1.0f + w[d]);
+        const float hi = v[4 + i] * sc * (1.0f + w[128 + d]);
+        const float c = cosT[d], s = sinT[d];
+        v[i] = lo * c - hi * s;
+        v[4 + i] = lo * s + hi * c;
+    }
+}
+
+// ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    const uint32_t G = gridDim.x, c = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t* mb = reinterpret_cast<uint64_t*>(sm + a.off_misc);
+    float* red32 = reinterpret_cast<float*>(sm + a.off_misc + 8 * TK_NMB);
+    float* xn = reinterpret_cast<float*>(sm + a.off_xn);
+    XBlk* xq = reinterpret_cast<XBlk*>(sm + a.off_xq);
+    float* red = reinterpret_cast<float*>(sm + a.off_red);
+    unsigned char* s_qkv = sm + a.off_qkv;
+    unsigned char* s_o = sm + a.off_o;
+    unsigned char* s_gu = sm + a.off_gu;
+    unsigned char* s_down = sm + a.off_down;
+    unsigned char* s_kv = sm + a.off_kv;
+    const float* cq = reinterpret_cast<const float*>(sm + a.off_cqkv);
+    const float* ca = reinterpret_cast<const float*>(sm + a.off_catt);
+    const float* cg = reinterpret_cast<const float*>(sm + a.off_cgu);
+    float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128]
+    __shared__ uint32_t s_armed;  // bit i: mbarrier i armed for the current fill
+
+    const uint32_t pos = *a.pos;
+    const uint64_t base = *a.epoch;
+    const uint32_t L = a.n_layers, H = a.H;
+    uint32_t nbar = 0;
+    uint32_t par = 0;  // parity bit per mbarrier, identical in every thread
+
+    if (tid == 0) {
+        for (int i = 0; i < TK_NMB; ++i) mbar_init(&mb[i], 1);
+        fence_mbar_init();
+        s_armed = 0;
+    }
+    __syncthreads();
+    auto arm = [&](int i, bool armed) {  // thread 0
+        s_armed = armed ? (s_armed | (1u << i)) : (s_armed & ~(1u << i));
+    };
+    auto wait_slot = [&](int i) {
+        if (s_armed & (1u << i)) {
+            mbar_wait(&mb[i], (par >> i) & 1u, a.err);
+            par ^= 1u << i;
+        }
+    };
+    if (tid == 0) {
+        const TkLayer& L0 = a.layers[0];
+        arm(TK_MB_CQKV, tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]));
+        arm(TK_MB_QKV, tk_issue(L0.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]));
+        arm(TK_MB_CATT, tk_issue_vec(L0.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]));
+        arm(TK_MB_KV, tk_issue_kv(a, L0, pos, s_kv, &mb[TK_MB_KV]));
+        arm(TK_MB_O, tk_issue(L0.o, a.o, s_o, &mb[TK_MB_O]));
+        arm(TK_MB_CGU, tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]));
+        arm(TK_MB_GU, tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU]));
+        arm(TK_MB_DOWN, tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN]));
+    }
+    // RoPE table for this position: theta^(-2d/256) rounded once from double,
+    // angle pos * inv in fp32, full-precision sincos (llm_transformer.cl:158-179)
+    if (tid < 256) {
+        const uint32_t t = tid >> 7, d = tid & 127;
+        const float inv = rope_inv_freq(d, 256, t ? a.theta_global : a.theta_local);
+        float s, co;
+        sincosf((float)pos * inv, &s, &co);
+        rope[t * 256 + d] = co;
+        rope[t * 256 + 128 + d] = s;
+    }
+    if (a.trace && c == 0 && tid == 0) a.trace[1] = globaltimer_ns();
+    __syncthreads();
+
+#define TK_MARK(k) \
+    if (a.trace && c == 0 && tid == 0) a.trace[512 + nbar * 8 + (k)] = globaltimer_ns();
+    // Barrier split in two: arrive, let thread 0 issue refills for later
+    // phases while the other CTAs catch up, then wait.
+    auto bar_arrive = [&]() {
+        ++nbar;
+        __syncthreads();
+        if (tid == 0) {
+            if (a.trace && c == 0) a.trace[2 * nbar] = globaltimer_ns();
+            red_release_add_u64(a.bar, 1ull);
+        }
+    };
+    auto bar_wait = [&]() {
+        if (tid == 0) {
+            const uint64_t target = base + (uint64_t)nbar * G;
+            uint32_t it = 0;
+            // acquire load + the closing bar.sync order every thread's later
+            // reads after the other CTAs' released writes
+            while (ld_acquire_u64(a.bar) < target) {
+                if (++it > TK_SPIN_LIMIT) {
+                    atomicOr(a.err, TK_ERR_GRID_BAR);
+                    break;
+                }
+            }
+            if (a.trace && c == 0) a.trace[2 * nbar + 1] = globaltimer_ns();
+        }
+        __syncthreads();
+    };
+
+    const uint32_t QKVW = a.QD + 2 * a.KVD;
+    for (uint32_t l = 0; l < L; ++l) {
+        const TkLayer& Ly = a.layers[l];
+        const bool last = l + 1 == L;
+        // ============================ QKV ============================
+        wait_slot(TK_MB_CQKV);
+        if (l == 0) tk_norm_prologue(a, 0, nullptr, nullptr, 0, nullptr, cq + H, a.x0, xn, red32);
+        else tk_norm_prologue(a, 1, a.x1, a.dn_part, a.down.ks, cq, cq + H, a.x0, xn, red32);
+        TK_MARK(0)
+        if (c < a.qkv.units) {
+            const uint32_t tile = c / a.qkv.ks, kc = c % a.qkv.ks;
+            tk_prep(xn, kc * a.qkv.nb, a.qkv.nb, xq);
+            wait_slot(TK_MB_QKV);
+            TK_MARK(1)
+            tk_tile<64>(s_qkv, a.qkv.nb, xq, red);
+            if (tid < 64) a.qkv_part[(size_t)kc * QKVW + tile * 64 + tid] = red[tid];
+        }
+        bar_arrive();
+        if (tid == 0) {
+            if (!last) {
+                arm(TK_MB_QKV, tk_issue(a.layers[l + 1].qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]));
+                arm(TK_MB_CQKV, tk_issue_vec(a.layers[l + 1].c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]));
+            } else {
+                arm(TK_MB_QKV, false);
+                arm(TK_MB_CQKV, a.want_logits ? tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV])
+                                              : false);
+            }
+        }
+        bar_wait();
+
+        // ============================ ATTN ============================
+        const TkWin w = tk_window(pos, Ly.window);
+        // every CTA consumes the attention-constants fill (its mbarrier phase
+        // must be tracked even by CTAs with no keys this layer)
+        wait_slot(TK_MB_CATT);
+        {
+            const uint32_t n = w.j1 - w.j0;
+            float* qs = reinterpret_cast<float*>(sm + a.off_q);       // [4][256] pre-scaled
+            __half* kn = reinterpret_cast<__half*>(qs + 4 * 256);      // [256]
+            __half* vn = kn + 256;                                     // [256]
+            float* sc = reinterpret_cast<float*>(sm + a.off_sc);       // [4][chunk_max]
+            if (c < w.nsplit) {
+                // q|k|v = sum of the K-split partials, every load in flight at once
+                float* qkvs = red;  // [QKVW]
+                {
+                    float ld[TK_MAXJ][TK_MAXP];
+#pragma unroll
+                    for (int r = 0; r < TK_MAXJ; ++r) {
+                        const uint32_t i = tid + r * TK_THREADS;
+#pragma unroll
+                        for (int k = 0; k < TK_MAXP; ++k)
+                            ld[r][k] = (i < QKVW && (uint32_t)k < a.qkv.ks) ? a.qkv_part[(size_t)k * QKVW + i] : 0.0f;
+                    }
+#pragma unroll
+                    for (int r = 0; r < TK_MAXJ; ++r) {
+                        const uint32_t i = tid + r * TK_THREADS;
+                        float t = 0.0f;
+#pragma unroll
+                        for (int k = 0; k < TK_MAXP; ++k) t += ld[r][k];
+                        if (i < QKVW) qkvs[i] = t;
+                    }
+                }
+                __syncthreads();
+                TK_MARK(0)
+                if (warp < 6) {
+                    const uint32_t off = warp < 4 ? warp * 256 : (warp == 4 ? a.QD : a.QD + a.KVD);
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = qkvs[off + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4))];
+                    const float* cosT = rope + (Ly.global ? 256 : 0);
+                    const float* sinT = cosT + 128;
+                    if (warp < 4) {
+                        tk_qk_post(v, ca, cosT, sinT, a.eps);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            qs[warp * 256 + 4 * lane + i] = v[i] * a.attn_scale;
+                            qs[warp * 256 + 128 + 4 * lane + i] = v[4 + i] * a.attn_scale;
+                        }
+                    } else {
+                        if (warp == 4) tk_qk_post(v, ca + 256, cosT, sinT, a.eps);
+                        __half* dst = warp == 4 ? kn : vn;
+                        __half* cache = warp == 4 ? Ly.kc : Ly.vc;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
+                            dst[4 * lane + i] = lo;
+                            dst[128 + 4 * lane + i] = hi;
+                            if (c == 0) {
+                                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
+                                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
+                            }
+                        }
+                    }
+                }
+                TK_MARK(4)
+                wait_slot(TK_MB_KV);
+                TK_MARK(5)
+                __syncthreads();
+                TK_MARK(1)
+                const __half* ks = reinterpret_cast<const __half*>(s_kv);
+                const __half* vs = ks + (size_t)a.chunk_max * 256;
+                float q[4][8];
+#pragma unroll
+                for (int h = 0; h < 4; ++h)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) q[h][i] = qs[h * 256 + 8 * lane + i];
+                TK_MARK(6)
+                for (uint32_t jj = warp; jj < n; jj += TK_WARPS) {
+                    const uint32_t j = w.j0 + jj;
+                    const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(kn + 8 * lane)
+                                               : *reinterpret_cast<const uint4*>(ks + (size_t)jj * 256 + 8 * lane);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                    float kf[8];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __half22float2(h2[i]);
+                        kf[2 * i] = f.x;
+                        kf[2 * i + 1] = f.y;
+                    }
+                    float s4[4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        float acc = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc = fmaf(q[h][i], kf[i], acc);
+                        s4[h] = acc;
+                    }
+                    const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
+                    if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
+                }
+                __syncthreads();
+                TK_MARK(2)
+                if (warp < 4) {
+                    float m = -INFINITY;
+                    for (uint32_t jj = lane; jj < n; jj += 32) m = fmaxf(m, sc[warp * a.chunk_max + jj]);
+                    m = warp_max(m);
+                    float sum = 0.0f;
+                    for (uint32_t jj = lane; jj < n; jj += 32) {
+                        const float p = expf(sc[warp * a.chunk_max + jj] - m);
+                        sc[warp * a.chunk_max + jj] = p;
+                        sum += p;
+                    }
+                    sum = warp_sum(sum);
+                    if (lane == 0) {
+                        a.att_stat[((size_t)c * 4 + warp) * 2] = m;
+                        a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
+                    }
+                }
+                __syncthreads();
+                {
+                    const uint32_t dp = tid & 127, qr = tid >> 7;
+                    float acc[4][2] = {};
+                    for (uint32_t jj = qr; jj < n; jj += 4) {
+                        const uint32_t j = w.j0 + jj;
+                        const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vn)[dp]
+                                                    : reinterpret_cast<const __half2*>(vs + (size_t)jj * 256)[dp];
+                        const float2 vf = __half22float2(hv);
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            const float p = sc[h * a.chunk_max + jj];
+                            acc[h][0] = fmaf(p, vf.x, acc[h][0]);
+                            acc[h][1] = fmaf(p, vf.y, acc[h][1]);
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        red[(qr * 4 + h) * 256 + 2 * dp] = acc[h][0];
+                        red[(qr * 4 + h) * 256 + 2 * dp + 1] = acc[h][1];
+                    }
+                }
+                __syncthreads();
+                for (uint32_t i = tid; i < 4 * 256; i += TK_THREADS)
+                    a.att_part[(size_t)c * 1024 + i] = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
+                TK_MARK(3)
+            }
+        }
+        bar_arrive();
+        if (tid == 0) {
+            arm(TK_MB_KV, !last ? tk_issue_kv(a, a.layers[l + 1], pos, s_kv, &mb[TK_MB_KV]) : false);
+            arm(TK_MB_CATT, !last ? tk_issue_vec(a.layers[l + 1].c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT])
+                                  : false);
+        }
+        bar_wait();
+
+        // ============================ O ============================
+        if (c < a.o.units) {
+            const uint32_t tile = c / a.o.ks, kc = c % a.o.ks;
+            const uint32_t d0 = kc * a.o.nb * 32, nd = a.o.nb * 32, h = d0 / 256;
+            // the splits' statistics and this CTA's slice of their partials are
+            // loaded together (one round trip), then merged
+            const uint32_t d = tid % nd, g = tid / nd, ng = TK_THREADS / nd;
+            float pv[TK_OPV];
+#pragma unroll
+            for (int r = 0; r < TK_OPV; ++r) {
+                const uint32_t s_ = g + r * ng;
+                pv[r] = (g < ng && s_ < w.nsplit) ? a.att_part[(size_t)s_ * 1024 + d0 + d] : 0.0f;
+            }
+            float m = -INFINITY, l_ = 0.0f;
+            if ((uint32_t)tid < w.nsplit) {
+                m = a.att_stat[((size_t)tid * 4 + h) * 2];
+                l_ = a.att_stat[((size_t)tid * 4 + h) * 2 + 1];
+            }
+            float* wts = red;            // [nsplit] exp(m_s - M)
+            float* comb = red + 512;     // [4][nd]
+            float M = warp_max(m);
+            if (lane == 0) red32[warp] = M;
+            __syncthreads();
+            M = warp_max(lane < TK_WARPS ? red32[lane] : -INFINITY);
+            __syncthreads();
+            const float e = (uint32_t)tid < w.nsplit ? expf(m - M) : 0.0f;
+            if ((uint32_t)tid < w.nsplit) wts[tid] = e;
+            const float Lsum = block_sum(l_ * e, red32);
+            __syncthreads();
+            {
+                float acc = 0.0f;
+                if (g < ng) {
+#pragma unroll
+                    for (int r = 0; r < TK_OPV; ++r) {
+                        const uint32_t s_ = g + r * ng;
+                        if (s_ < w.nsplit) acc += pv[r] * wts[s_];
+                    }
+                    // splits beyond TK_OPV * ng (long windows): remaining loads
+                    for (uint32_t s_ = g + TK_OPV * ng; s_ < w.nsplit; s_ += ng)
+                        acc += a.att_part[(size_t)s_ * 1024 + d0 + d] * wts[s_];
+                    comb[g * nd + d] = acc;
+                }
+                __syncthreads();
+                if ((uint32_t)tid < nd) {
+                    float t = 0.0f;
+                    for (uint32_t gg = 0; gg < ng; ++gg) t += comb[gg * nd + tid];
+                    xn[tid] = t / Lsum;
+                }
+            }
+            __syncthreads();
+            TK_MARK(0)
+            tk_prep(xn, 0, a.o.nb, xq);
+            wait_slot(TK_MB_O);
+            TK_MARK(1)
+            tk_tile<64>(s_o, a.o.nb, xq, red);
+            if (tid < 64) a.o_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
+        }
+        bar_arrive();
+        if (tid == 0) arm(TK_MB_O, !last ? tk_issue(a.layers[l + 1].o, a.o, s_o, &mb[TK_MB_O]) : false);
+        bar_wait();
+
+        // ============================ GU ============================
+        wait_slot(TK_MB_CGU);
+        tk_norm_prologue(a, 1, a.x0, a.o_part, a.o.ks, cg, cg + H, a.x1, xn, red32);
+        TK_MARK(0)
+        if (c < a.gu.units) {
+            const uint32_t nb = a.gu.nb;
+            tk_prep(xn, 0, nb, xq);
+            wait_slot(TK_MB_GU);
+            TK_MARK(1)
+            uint32_t nu = 0;
+            for (uint32_t u = c; u < a.gu.units; u += G) ++nu;
+            // half-warp workers (16 lanes = 16 columns), each fixed on one
+            // (unit, matrix) pair and a stride of blocks, accumulating in a register
+            const uint32_t worker = tid >> 4, col = tid & 15, nwk = TK_THREADS / 16;
+            const uint32_t npair = nu * 2, wpp = nwk / npair;
+            const uint32_t p = worker / wpp, r = worker % wpp;
+            float acc = 0.0f;
+            if (p < npair) {
+                const uint32_t ui = p >> 1, m = p & 1;
+                const unsigned char* img = s_gu + (size_t)ui * a.gu.img_bytes;
+                const uint4* nib = reinterpret_cast<const uint4*>(img);
+                const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)2 * nb * 16 * 16);
+                for (uint32_t b = r; b < nb; b += wpp)
+                    acc += tk_dot(nib[(m * nb + b) * 16 + col], scl[(m * nb + b) * 16 + col], xq[b]);
+            }
+            float* wp = red;  // [npair * wpp][16]
+            if (p < npair) wp[(p * wpp + r) * 16 + col] = acc;
+            __syncthreads();
+            TK_MARK(2)
+            if ((uint32_t)tid < nu * 16) {
+                const uint32_t ui = tid / 16, cc = tid % 16;
+                float g = 0.0f, up = 0.0f;
+                for (uint32_t k = 0; k < wpp; ++k) {
+                    g += wp[((2 * ui) * wpp + k) * 16 + cc];
+                    up += wp[((2 * ui + 1) * wpp + k) * 16 + cc];
+                }
+                a.hb[(size_t)(c + ui * G) * 16 + cc] = gelu_tanh_ref(g) * up;
+            }
+        }
+        bar_arrive();
+        if (tid == 0) {
+            arm(TK_MB_GU, !last ? tk_issue(a.layers[l + 1].gu, a.gu, s_gu, &mb[TK_MB_GU]) : false);
+            arm(TK_MB_CGU, !last ? tk_issue_vec(a.layers[l + 1].c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU])
+                                 : false);
+        }
+        bar_wait();
+
+        // ============================ DOWN ============================
+        if (c < a.down.units) {
+            const uint32_t tile = c / a.down.ks, kc = c % a.down.ks, nb = a.down.nb;
+            // hb limbs for blocks [kc*nb, kc*nb + nb): all loads first
+            float hv[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t b = warp + r * TK_WARPS;
+                hv[r] = b < nb ? a.hb[(size_t)(kc * nb + b) * 32 + lane] : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t b = warp + r * TK_WARPS;
+                if (b < nb) xq_prep_block(hv[r], &xq[b]);
+            }
+            __syncthreads();
+            TK_MARK(0)
+            wait_slot(TK_MB_DOWN);
+            TK_MARK(1)
+            tk_tile<64>(s_down, nb, xq, red);
+            if (tid < 64) a.dn_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
+        }
+        bar_arrive();
+        if (tid == 0) {
+            if (!last) {
+                arm(TK_MB_DOWN, tk_issue(a.layers[l + 1].down, a.down, s_down, &mb[TK_MB_DOWN]));
+            } else {
+                arm(TK_MB_DOWN, false);
+                if (a.want_logits) {  // start the LM-head ring over the freed gu|down|kv slots
+                    for (uint32_t r = 0; r < a.head_ring; ++r) {
+                        const uint32_t t = c + r * G;
+                        bool armed = false;
+                        if (t < a.head.units) {
+                            fence_proxy_async();
+                            mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
+                            bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
+                                     a.head.img_bytes, &mb[TK_MB_HEAD + r]);
+                            armed = true;
+                        }
+                        arm(TK_MB_HEAD + r, armed);
+                    }
+                }
+            }
+        }
+        bar_wait();
+    }
+
+    // ============================ HEAD ============================
+    if (a.want_logits) {
+        wait_slot(TK_MB_CQKV);
+        tk_norm_prologue(a, 1, a.x1, a.dn_part, a.down.ks, cq, cq + H, nullptr, xn, red32);
+        tk_prep(xn, 0, a.head.nb, xq);
+        float bv = -INFINITY;
+        uint32_t bi = 0xFFFFFFFFu;
+        uint32_t i = 0;
+        for (uint32_t t = c; t < a.head.units; t += G, ++i) {
+            const uint32_t r = i % a.head_ring;
+            wait_slot(TK_MB_HEAD + r);
+            tk_tile<64>(s_gu + (size_t)r * a.head.img_bytes, a.head.nb, xq, red);
+            if (tid == 0) {  // refill this buffer while the argmax runs
+                const uint32_t tn = t + a.head_ring * G;
+                bool armed = false;
+                if (tn < a.head.units) {
+                    fence_proxy_async();
+                    mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
+                    bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)tn * a.head.img_bytes,
+                             a.head.img_bytes, &mb[TK_MB_HEAD + r]);
+                    armed = true;
+                }
+                arm(TK_MB_HEAD + r, armed);
+            }
+            if (warp == 0) {
+                float v0 = red[lane], v1 = red[lane + 32];
+                a.logits[(size_t)t * 64 + lane] = v0;
+                a.logits[(size_t)t * 64 + lane + 32] = v1;
+                uint32_t ix = t * 64 + lane;
+                if (v1 > v0) { v0 = v1; ix += 32; }
+                if (v0 > bv || (v0 == bv && ix < bi)) { bv = v0; bi = ix; }
+            }
+            __syncthreads();
+        }
+        if (warp == 0) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
+        }
+        bar_arrive();
+        bar_wait();
+        if (a.greedy && c == 0 && warp == 0) {
+            float v = -INFINITY;
+            uint32_t ix = 0xFFFFFFFFu;
+            for (uint32_t p = lane; p < G; p += 32) {
+                const float pv = a.am_val[p];
+                const uint32_t pi = a.am_idx[p];
+                if (pv > v || (pv == v && pi < ix)) { v = pv; ix = pi; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+                if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+            }
+            if (lane == 0) {
+                if (ix == 0xFFFFFFFFu) ix = 0;
+                *a.token = ix;
+                if (a.sample_out) { a.sample_out[0] = (float)ix; a.sample_out[1] = v; }
+                *a.pos = pos + 1;
+                if (a.hist) a.hist[pos + 1] = ix;
+            }
+        }
+    } else if (c == 0 && tid == 0) {
+        *a.pos = pos + 1;
+    }
+    if (c == 0 && tid == 0) {
+        *a.epoch = base + (uint64_t)nbar * G;
+        if (a.trace) { a.trace[0] = nbar; a.trace[2 * nbar + 2] = globaltimer_ns(); }
+    }
+#undef TK_MARK
+}
+
+// ---- load-time repack: reference KM4 + bf16-scale planes -> unit images ----------------
+// Unit u of a phase holds, for matrices m < nmat, nibbles[m][b][c] (uint4)
+// then scales[m][b][c] (bf16) for blocks b < nb and columns c < cw. The
+// dequantised weight of every (k, j) is unchanged: same nibble, same bf16.
+struct RepackArgs {
+    const uint4* words;    // reference nibble plane
+    const uint32_t* sc;    // reference scale plane (uint2 per quad and column)
+    uint32_t rows, cols;
+    unsigned char* dst;
+    uint32_t img_bytes, cw, nb, nmat, mat, ks, tile0;
+};
+__global__ void repack_units_kernel(const RepackArgs r) {
+    const uint32_t nblk = r.rows / 32;
+    const uint64_t total = (uint64_t)nblk * r.cols;
+    for (uint64_t id = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; id < total;
+         id += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t j = (uint32_t)(id % r.cols), b = (uint32_t)(id / r.cols);
+        const uint4 w = r.words[((size_t)(j / 64) * nblk + b) * 64 + (j % 64)];
+        const uint32_t sw = r.sc[((size_t)(b / 4) * r.cols + j) * 2 + ((b % 4) >> 1)];
+        const uint16_t s = (uint16_t)((b & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+        const uint32_t u = (r.tile0 + j / r.cw) * r.ks + b / r.nb;
+        const uint32_t bl = b % r.nb, cl = j % r.cw;
+        unsigned char* img = r.dst + (size_t)u * r.img_bytes;
+        const size_t e = ((size_t)r.mat * r.nb + bl) * r.cw + cl;
+        reinterpret_cast<uint4*>(img)[e] = w;
+        reinterpret_cast<uint16_t*>(img + (size_t)r.nmat * r.nb * r.cw * 16)[e] = s;
+    }
+}
+
+}  // namespace xp

@@ -173,6 +173,18 @@ class DecodeSession:
         check(lib().xp_session_timer(self._h, 1, C.byref(ms)))
         return ms.value
 
+    def trace(self):
+        """Phase timeline of the last token (XP_TRACE=1): list of
+        (arrive_ns, leave_ns) per grid barrier, relative to kernel start."""
+        buf = np.zeros(512 + 8 * 1024, np.uint64)
+        check(lib().xp_session_trace(self._h, buf.ctypes.data, len(buf)))
+        nb = int(buf[0])
+        t0 = int(buf[1])
+        bars = [(int(buf[2 * k]) - t0, int(buf[2 * k + 1]) - t0) for k in range(1, nb + 1)]
+        marks = [[(int(buf[512 + k * 8 + j]) - t0) if buf[512 + k * 8 + j] else None for j in range(8)]
+                 for k in range(nb + 1)]
+        return bars, int(buf[2 * nb + 2]) - t0, marks
+
     def error_word(self):
         w = C.c_uint32()
         check(lib().xp_session_error_word(self._h, C.byref(w)))
