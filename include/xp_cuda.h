@@ -103,6 +103,9 @@ xp_status xp_batch_add(xp_batch* b, xp_kernel k, xp_grid grid, const xp_arg* arg
 xp_status xp_batch_size(xp_batch* b, uint32_t* n);
 xp_status xp_batch_submit(xp_batch* b, xp_fence** out);  /* the Batch is spent afterwards */
 xp_status xp_batch_destroy(xp_batch* b);
+/* A fence signaled once everything enqueued on the context's stream so far
+ * has completed (vulkore::launch returns one, include/vulkore/launch.hpp:148). */
+xp_status xp_context_fence(xp_context* ctx, xp_fence** out);
 /* XP_OK when signaled, XP_TIMEOUT on timeout, XP_ERR_DEVICE on a device error */
 xp_status xp_fence_wait(xp_fence* f, uint64_t timeout_ns);
 xp_status xp_fence_destroy(xp_fence* f);                  /* drains first */

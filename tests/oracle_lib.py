@@ -12,6 +12,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 _ORACLE = os.path.join(ROOT, "oracle", "liboracle.so")
 _REF = os.path.join(ROOT, "oracle", "_ref", "libxpref.so")
+# the reference's engine compiled against include/xp (runs on libxp_cuda.so)
+_REF_GPU = os.path.join(ROOT, "oracle", "_ref", "libxpref_gpu.so")
 
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
@@ -60,15 +62,36 @@ class _Arg(C.Structure):
     _fields_ = [("ptr", C.c_void_p), ("size", C.c_uint32), ("is_buffer", C.c_int)]
 
 
+_rg = None
+
+
+def ref_gpu():
+    """The reference engine built on the B200 library (oracle/_ref/libxpref_gpu.so),
+    or None if it was not built."""
+    global _rg
+    if _rg is None:
+        if not os.path.exists(_REF_GPU):
+            return None
+        _rg = _configure(C.CDLL(_REF_GPU), kernels=False)
+    return _rg
+
+
 def ref():
     """The reference build, or None if oracle/_ref was not built."""
     global _r
     if _r is None:
         if not os.path.exists(_REF):
             return None
-        lib = C.CDLL(_REF)
+        _r = _configure(C.CDLL(_REF), kernels=True)
+    return _r
+
+
+def _configure(lib, kernels):
+    if kernels:
         lib.xpref_launch.argtypes = [C.c_char_p, C.c_char_p, C.c_uint32, C.POINTER(_Arg), C.c_uint32, C.c_int]
         lib.xpref_last_error.restype = C.c_char_p
+    # session and packer entry points (both builds)
+    if True:
         lib.xpref_pack_km4bf16.argtypes = [f32p, C.c_uint32, C.c_uint32, u32p, u32p, C.c_void_p]
         lib.xpref_best_bf16_scale.argtypes = [f32p, C.c_float]
         lib.xpref_best_bf16_scale.restype = C.c_float
@@ -85,8 +108,7 @@ def ref():
         lib.xpref_session_logits.argtypes = [C.c_void_p, f32p, C.c_uint32]
         lib.xpref_session_position.argtypes = [C.c_void_p]
         lib.xpref_session_position.restype = C.c_uint32
-        _r = lib
-    return _r
+    return lib
 
 
 def ref_launch(name, grid, *args, module=None, threads=0):
@@ -284,8 +306,8 @@ class RefSession:
     """The reference DecodeSession (examples/llm/decode.cpp) running on the CPU
     stand-in runtime over the reference kernels, from a GGUF file."""
 
-    def __init__(self, gguf_path, max_seq, global_every, greedy=True):
-        self.lib = ref()
+    def __init__(self, gguf_path, max_seq, global_every, greedy=True, lib=None):
+        self.lib = lib or ref()
         self.h = self.lib.xpref_session_create(gguf_path.encode(), b"kernels", max_seq, int(greedy), 1.0, 0, 1.0,
                                                1234, global_every)
         if not self.h:

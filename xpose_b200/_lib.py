@@ -81,6 +81,7 @@ _SIGS = {
     "xp_batch_size": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
     "xp_batch_submit": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "xp_batch_destroy": (C.c_int, [C.c_void_p]),
+    "xp_context_fence": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "xp_fence_wait": (C.c_int, [C.c_void_p, C.c_uint64]),
     "xp_fence_destroy": (C.c_int, [C.c_void_p]),
     "xp_mv_km4_bs": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 2),

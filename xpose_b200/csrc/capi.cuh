@@ -571,6 +571,19 @@ xp_status xp_batch_submit(xp_batch* b, xp_fence** out) {
     *out = f;
     return XP_OK;
 }
+xp_status xp_context_fence(xp_context* c, xp_fence** out) {
+    if (!c || !out) return fail(XP_ERR_INVALID, "xp_context_fence: null argument");
+    cudaSetDevice(c->device);
+    auto* f = new xp_fence;
+    f->device = c->device;
+    if (cudaEventCreateWithFlags(&f->ev, cudaEventDisableTiming) != cudaSuccess) {
+        delete f;
+        return fail(XP_ERR_CUDA, "cudaEventCreate failed");
+    }
+    XP_CUDA_TRY(cudaEventRecord(f->ev, c->stream));
+    *out = f;
+    return XP_OK;
+}
 xp_status xp_batch_destroy(xp_batch* b) {
     delete b;
     return XP_OK;
