@@ -163,6 +163,23 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
                               const float* v_raw, const float* q_norm, const float* k_norm, uint16_t* kcache_f16,
                               uint16_t* vcache_f16, const uint32_t* pos_dev, uint32_t window, float theta,
                               float eps, float scale, uint32_t nsplit, uint32_t max_seq, void* scratch);
+/* xp_attention_decode for callers that cannot allocate device memory (a host
+ * framework's arena they do not own, a memory-capped plugin, a path that must
+ * not call cudaMalloc): same arguments minus `scratch`, which lives instead in
+ * a fixed array inside the library (XP_ATTN_STATIC_SCRATCH_BYTES, enough for
+ * nsplit <= XP_ATTN_STATIC_MAX_NSPLIT, held on every GPU that loads the
+ * library until exit). Larger nsplit returns XP_ERR_INVALID. Runs on the
+ * current device; the first call on a device looks up the array's address, so
+ * make that first call before any stream capture. All calls share the one
+ * array: calls that overlap on the GPU race. Allocates nothing. No counterpart
+ * in the reference. */
+#define XP_ATTN_STATIC_MAX_NSPLIT 64u
+#define XP_ATTN_STATIC_SCRATCH_BYTES (64u + 64u * 4u * 256u * 4u + 64u * 8u * 4u)
+xp_status xp_attention_decode_static(void* stream, float* out, const float* q_raw, const float* k_raw,
+                                     const float* v_raw, const float* q_norm, const float* k_norm,
+                                     uint16_t* kcache_f16, uint16_t* vcache_f16, const uint32_t* pos_dev,
+                                     uint32_t window, float theta, float eps, float scale, uint32_t nsplit,
+                                     uint32_t max_seq);
 /* Exact top-k (k <= 64) + temperature + top-p + multinomial over n logits
  * (replaces topk4_partial + host draw(), decode.cpp:1873-1917). `u` index for
  * the seeded uniform is *pos_dev. Writes the chosen id to *token_dev and the
