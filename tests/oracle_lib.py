@@ -302,6 +302,35 @@ def write_model_gguf(om, path, window=512):
     write_gguf(path, gemma3_meta(cfg, cfg.rope_theta_global, window), tensors)
 
 
+def write_random_gguf(cfg, seed, path, window=512):
+    """The same seeded model as OracleModel(cfg, seed) written as a Gemma-3
+    GGUF one tensor at a time (a full-size model is 4 GB of fp32), for timing
+    the reference engine without holding the model twice in host memory."""
+    import os
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    from gguf_writer import gemma3_meta, write_gguf
+    H = cfg.hidden
+    names = ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")
+    norm_names = ("attn_norm", "post_attention_norm", "ffn_norm", "post_ffw_norm", "attn_q_norm", "attn_k_norm")
+
+    def normal(stream, n):
+        return lambda: gen_normal(seed, stream, n, 0.02)
+
+    def norm(stream, n):
+        return lambda: np.float32(1.0) + gen_normal(seed, stream, n, 0.02)
+
+    tensors = [("token_embd.weight", (H, cfg.vocab), normal(tensor_stream(cfg.n_layers, 0), cfg.vocab * H))]
+    for l in range(cfg.n_layers):
+        for m, (rows, cols) in enumerate(cfg.matrix_shapes()):
+            tensors.append((f"blk.{l}.{names[m]}.weight", (rows, cols), normal(tensor_stream(l, m), rows * cols)))
+        for n in range(6):
+            d = H if n < 4 else cfg.head_dim
+            tensors.append((f"blk.{l}.{norm_names[n]}.weight", (d,), norm(tensor_stream(l, 7 + n), d)))
+    tensors.append(("output_norm.weight", (H,), norm(tensor_stream(cfg.n_layers, 7), H)))
+    write_gguf(path, gemma3_meta(cfg, cfg.rope_theta_global, window), tensors)
+
+
 class RefSession:
     """The reference DecodeSession (examples/llm/decode.cpp) running on the CPU
     stand-in runtime over the reference kernels, from a GGUF file."""
