@@ -454,7 +454,7 @@ struct xp_session {
         if ((e = alloc(&ami2, G)) != XP_OK) return e;
         if ((e = alloc(&tk_bar, 4)) != XP_OK) return e;
         if (env_int("XP_TRACE", 0)) {
-            if ((e = alloc(&tk.trace, 512 + 8 * 1024)) != XP_OK) return e;
+            if ((e = alloc(&tk.trace, TK_TRACE_WORDS)) != XP_OK) return e;
         }
         tk.layers = tk_layers_dev;
         tk.n_layers = cfg.n_layers;
@@ -483,7 +483,7 @@ struct xp_session {
         a.want_logits = want_logits ? 1 : 0;
         cudaLaunchConfig_t c = {};
         c.gridDim = dim3(tk_grid);
-        c.blockDim = dim3(TK_THREADS);
+        c.blockDim = dim3(TK_BLOCK);
         c.dynamicSmemBytes = tk_smem;
         c.stream = st;
         cudaLaunchAttribute at[1];
@@ -818,7 +818,7 @@ xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n) {
     cudaSetDevice(s->device);
     xp_status st = s->wait_prev();
     if (st != XP_OK) return st;
-    XP_CUDA_TRY(cudaMemcpy(out, s->tk.trace, (size_t)std::min<uint32_t>(n, 512 + 8 * 1024) * 8, cudaMemcpyDeviceToHost));
+    XP_CUDA_TRY(cudaMemcpy(out, s->tk.trace, (size_t)std::min<uint32_t>(n, TK_TRACE_WORDS) * 8, cudaMemcpyDeviceToHost));
     return XP_OK;
 }
 

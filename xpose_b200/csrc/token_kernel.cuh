@@ -36,15 +36,26 @@
 
 namespace xp {
 
-constexpr int TK_THREADS = 512;
+constexpr int TK_THREADS = 512;              // compute threads (16 warps)
 constexpr int TK_WARPS = TK_THREADS / 32;
+constexpr int TK_BLOCK = TK_THREADS + 32;      // + one producer warp that issues every bulk copy
 constexpr int TK_MAXJ = 3;   // hidden <= 1536
 constexpr int TK_MAXP = 8;   // K-split partials per output <= 8
-constexpr int TK_NMB = 16;   // mbarriers
+constexpr int TK_NMB = 32;   // mbarriers
 constexpr int TK_OPV = 10;   // attention splits per thread loaded with the stats
 constexpr int TK_MB_QKV = 0, TK_MB_O = 1, TK_MB_GU = 2, TK_MB_DOWN = 3, TK_MB_KV = 4;
 constexpr int TK_MB_CQKV = 5, TK_MB_CATT = 6, TK_MB_CGU = 7, TK_MB_HEAD = 8;  // head ring: 8..15
-constexpr int TK_MAX_RING = TK_NMB - TK_MB_HEAD;
+constexpr int TK_MAX_RING = 8;
+// "empty" mbarriers: the compute warps arrive once they are done reading a
+// slot; the producer waits on them before refilling it
+constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME_DOWN = 20, TK_ME_HEAD = 21;
+static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_NMB, "mbarrier count");
+// Trace layout (u64 words, %globaltimer ns): [0] barriers, [1] start,
+// [2k, 2k+1] CTA 0 arrive/leave of barrier k, [512 + 8k + i] CTA 0 marks in
+// phase k, then per CTA c and barrier k < TK_TRACE_MAXBAR its arrive/leave at
+// TK_TRACE_CTA + (c * TK_TRACE_MAXBAR + k) * 2.
+constexpr uint32_t TK_TRACE_CTA = 512 + 8 * 1024, TK_TRACE_MAXBAR = 160, TK_TRACE_MAXCTA = 160;
+constexpr uint32_t TK_TRACE_WORDS = TK_TRACE_CTA + 2 * TK_TRACE_MAXBAR * TK_TRACE_MAXCTA;
 
 struct TkPhase {
     uint32_t units;      // units in the phase
@@ -106,6 +117,22 @@ struct TkArgs {
 };
 
 // ---- helpers -------------------------------------------------------------------
+// CTA barrier of the 16 compute warps only (named barrier 1); the producer
+// warp never joins it.
+XP_DEV void tk_sync() { asm volatile("bar.sync 1, %0;" ::"n"(TK_THREADS) : "memory"); }
+
+XP_DEV float tk_block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_sum(v);
+    tk_sync();
+    if (lane == 0) red[wid] = v;
+    tk_sync();
+    float t = lane < TK_WARPS ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+XP_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 // r = base + rmsnorm_gemma(sum_k part[k], w_post) (mode 1) or the scaled
 // embedding row (mode 0); x_out = r (CTA 0); xn = rmsnorm_gemma(r, w_pre).
@@ -145,7 +172,7 @@ XP_DEV void tk_norm_prologue(const TkArgs& a, int mode, const float* base, const
             yv[j] = s;
             ss += s * s;
         }
-        ss = block_sum(ss, red);
+        ss = tk_block_sum(ss, red);
         const float sc = rsqrtf(ss / (float)H + a.eps);
 #pragma unroll
         for (int j = 0; j < TK_MAXJ; ++j) {
@@ -160,21 +187,21 @@ XP_DEV void tk_norm_prologue(const TkArgs& a, int mode, const float* base, const
         if (i < H && x_out && blockIdx.x == 0) x_out[i] = rv[j];
         ss2 += rv[j] * rv[j];
     }
-    ss2 = block_sum(ss2, red);
+    ss2 = tk_block_sum(ss2, red);
     const float sc2 = rsqrtf(ss2 / (float)H + a.eps);
 #pragma unroll
     for (int j = 0; j < TK_MAXJ; ++j) {
         const uint32_t i = tid + j * TK_THREADS;
         if (i < H) xn[i] = rv[j] * sc2 * (1.0f + w_pre[i]);
     }
-    __syncthreads();
+    tk_sync();
 }
 
 // Limbs of blocks [b0, b0+nb) of the smem vector v into xq[0..nb).
 XP_DEV void tk_prep(const float* v, uint32_t b0, uint32_t nb, XBlk* xq) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (uint32_t b = warp; b < nb; b += TK_WARPS) xq_prep_block(v[(b0 + b) * 32 + lane], &xq[b]);
-    __syncthreads();
+    tk_sync();
 }
 
 XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
@@ -198,14 +225,14 @@ XP_DEV void tk_tile(const unsigned char* img, uint32_t nb, const XBlk* xq, float
     float* wr = red + 64;  // [16][CW] warp partials
     wr[warp * CW + lane] = a0;
     if (CW == 64) wr[warp * CW + lane + 32] = a1;
-    __syncthreads();
+    tk_sync();
     if (threadIdx.x < CW) {
         float s = 0.0f;
         const uint32_t nw = nb < (uint32_t)TK_WARPS ? nb : (uint32_t)TK_WARPS;
         for (uint32_t w = 0; w < nw; ++w) s += wr[w * CW + threadIdx.x];
         red[threadIdx.x] = s;
     }
-    __syncthreads();
+    tk_sync();
 }
 
 // Issue the bulk copies of this CTA's units of a phase into its slot. Thread 0
@@ -281,7 +308,7 @@ XP_DEV void tk_qk_post(float v[8], const float* w, const float* cosT, const floa
 }
 
 // ---------------------------------------------------------------------------------
-__global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
+__global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -299,40 +326,96 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
     const float* ca = reinterpret_cast<const float*>(sm + a.off_catt);
     const float* cg = reinterpret_cast<const float*>(sm + a.off_cgu);
     float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128]
-    __shared__ uint32_t s_armed;  // bit i: mbarrier i armed for the current fill
 
     const uint32_t pos = *a.pos;
     const uint64_t base = *a.epoch;
     const uint32_t L = a.n_layers, H = a.H;
     uint32_t nbar = 0;
-    uint32_t par = 0;  // parity bit per mbarrier, identical in every thread
+    uint32_t par = 0;  // parity bit per "full" mbarrier, identical in every compute thread
 
     if (tid == 0) {
         for (int i = 0; i < TK_NMB; ++i) mbar_init(&mb[i], 1);
         fence_mbar_init();
-        s_armed = 0;
     }
     __syncthreads();
-    auto arm = [&](int i, bool armed) {  // thread 0
-        s_armed = armed ? (s_armed | (1u << i)) : (s_armed & ~(1u << i));
-    };
-    auto wait_slot = [&](int i) {
-        if (s_armed & (1u << i)) {
-            mbar_wait(&mb[i], (par >> i) & 1u, a.err);
-            par ^= 1u << i;
+
+    // ---------------- producer warp: every bulk copy of the launch ----------------
+    // Each "full" mbarrier completes exactly once per fill, with the copy's
+    // bytes or, when this CTA has nothing to load, with a plain arrive, so the
+    // compute warps wait on every fill unconditionally. A slot is refilled
+    // for layer l+1 once the compute warps have arrived on its "empty"
+    // mbarrier at the grid barrier that closes the phase reading it.
+    if (warp == TK_WARPS) {
+        if (lane != 0) return;
+        uint32_t epar = 0;  // parity bit per "empty" mbarrier
+        auto fill = [&](bool issued, int i) {
+            if (!issued) mbar_arrive(&mb[i]);
+        };
+        auto wait_empty = [&](int i) {
+            mbar_wait(&mb[i], (epar >> i) & 1u, a.err);
+            epar ^= 1u << i;
+        };
+        {
+            const TkLayer& L0 = a.layers[0];
+            fill(tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
+            fill(tk_issue(L0.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
+            fill(tk_issue_vec(L0.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]), TK_MB_CATT);
+            fill(tk_issue_kv(a, L0, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
+            fill(tk_issue(L0.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
+            fill(tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
+            fill(tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
+            fill(tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN]), TK_MB_DOWN);
         }
-    };
-    if (tid == 0) {
-        const TkLayer& L0 = a.layers[0];
-        arm(TK_MB_CQKV, tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]));
-        arm(TK_MB_QKV, tk_issue(L0.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]));
-        arm(TK_MB_CATT, tk_issue_vec(L0.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]));
-        arm(TK_MB_KV, tk_issue_kv(a, L0, pos, s_kv, &mb[TK_MB_KV]));
-        arm(TK_MB_O, tk_issue(L0.o, a.o, s_o, &mb[TK_MB_O]));
-        arm(TK_MB_CGU, tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]));
-        arm(TK_MB_GU, tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU]));
-        arm(TK_MB_DOWN, tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN]));
+        for (uint32_t l = 0; l + 1 < L; ++l) {
+            const TkLayer& Ln = a.layers[l + 1];
+            wait_empty(TK_ME_QKV);
+            fill(tk_issue(Ln.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
+            fill(tk_issue_vec(Ln.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
+            wait_empty(TK_ME_ATT);
+            fill(tk_issue_kv(a, Ln, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
+            fill(tk_issue_vec(Ln.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]), TK_MB_CATT);
+            wait_empty(TK_ME_O);
+            fill(tk_issue(Ln.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
+            wait_empty(TK_ME_GU);
+            fill(tk_issue(Ln.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
+            fill(tk_issue_vec(Ln.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
+            wait_empty(TK_ME_DOWN);
+            fill(tk_issue(Ln.down, a.down, s_down, &mb[TK_MB_DOWN]), TK_MB_DOWN);
+        }
+        if (!a.want_logits) return;
+        // last layer: the head constants once QKV is done with its slot, the
+        // LM-head ring over the gu|down|kv slots once DOWN is done with them
+        wait_empty(TK_ME_QKV);
+        fill(tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
+        wait_empty(TK_ME_DOWN);
+        for (uint32_t r = 0; r < a.head_ring && c + r * G < a.head.units; ++r) {
+            fence_proxy_async();
+            mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
+            bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)(c + r * G) * a.head.img_bytes,
+                     a.head.img_bytes, &mb[TK_MB_HEAD + r]);
+        }
+        uint32_t i = 0;
+        for (uint32_t t = c; t < a.head.units; t += G, ++i) {
+            const uint32_t r = i % a.head_ring, tn = t + a.head_ring * G;
+            wait_empty(TK_ME_HEAD + r);
+            if (tn < a.head.units) {
+                fence_proxy_async();
+                mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
+                bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)tn * a.head.img_bytes,
+                         a.head.img_bytes, &mb[TK_MB_HEAD + r]);
+            }
+        }
+        return;
     }
+
+    // ---------------- compute warps ----------------
+    auto wait_slot = [&](int i) {
+        mbar_wait(&mb[i], (par >> i) & 1u, a.err);
+        par ^= 1u << i;
+    };
+    auto release_slot = [&](int i) {  // after a tk_sync: every compute thread is done with the slot
+        if (tid == 0) mbar_arrive(&mb[i]);
+    };
     // RoPE table for this position: theta^(-2d/256) rounded once from double,
     // angle pos * inv in fp32, full-precision sincos (llm_transformer.cl:158-179)
     if (tid < 256) {
@@ -344,17 +427,22 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
         rope[t * 256 + 128 + d] = s;
     }
     if (a.trace && c == 0 && tid == 0) a.trace[1] = globaltimer_ns();
-    __syncthreads();
+    tk_sync();
 
 #define TK_MARK(k) \
     if (a.trace && c == 0 && tid == 0) a.trace[512 + nbar * 8 + (k)] = globaltimer_ns();
-    // Barrier split in two: arrive, let thread 0 issue refills for later
-    // phases while the other CTAs catch up, then wait.
+    // Grid barrier split in two: arrive, release the phase's slots to the
+    // producer, then wait.
     auto bar_arrive = [&]() {
         ++nbar;
-        __syncthreads();
+        tk_sync();
         if (tid == 0) {
-            if (a.trace && c == 0) a.trace[2 * nbar] = globaltimer_ns();
+            if (a.trace) {
+                const uint64_t t = globaltimer_ns();
+                if (c == 0) a.trace[2 * nbar] = t;
+                if (nbar < TK_TRACE_MAXBAR && c < TK_TRACE_MAXCTA)
+                    a.trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
+            }
             red_release_add_u64(a.bar, 1ull);
         }
     };
@@ -370,15 +458,19 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                     break;
                 }
             }
-            if (a.trace && c == 0) a.trace[2 * nbar + 1] = globaltimer_ns();
+            if (a.trace) {
+                const uint64_t t = globaltimer_ns();
+                if (c == 0) a.trace[2 * nbar + 1] = t;
+                if (nbar < TK_TRACE_MAXBAR && c < TK_TRACE_MAXCTA)
+                    a.trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2 + 1] = t;
+            }
         }
-        __syncthreads();
+        tk_sync();
     };
 
     const uint32_t QKVW = a.QD + 2 * a.KVD;
     for (uint32_t l = 0; l < L; ++l) {
         const TkLayer& Ly = a.layers[l];
-        const bool last = l + 1 == L;
         // ============================ QKV ============================
         wait_slot(TK_MB_CQKV);
         if (l == 0) tk_norm_prologue(a, 0, nullptr, nullptr, 0, nullptr, cq + H, a.x0, xn, red32);
@@ -391,18 +483,11 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
             TK_MARK(1)
             tk_tile<64>(s_qkv, a.qkv.nb, xq, red);
             if (tid < 64) a.qkv_part[(size_t)kc * QKVW + tile * 64 + tid] = red[tid];
+        } else {
+            wait_slot(TK_MB_QKV);
         }
         bar_arrive();
-        if (tid == 0) {
-            if (!last) {
-                arm(TK_MB_QKV, tk_issue(a.layers[l + 1].qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]));
-                arm(TK_MB_CQKV, tk_issue_vec(a.layers[l + 1].c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]));
-            } else {
-                arm(TK_MB_QKV, false);
-                arm(TK_MB_CQKV, a.want_logits ? tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV])
-                                              : false);
-            }
-        }
+        release_slot(TK_ME_QKV);
         bar_wait();
 
         // ============================ ATTN ============================
@@ -437,7 +522,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                         if (i < QKVW) qkvs[i] = t;
                     }
                 }
-                __syncthreads();
+                tk_sync();
                 TK_MARK(0)
                 if (warp < 6) {
                     const uint32_t off = warp < 4 ? warp * 256 : (warp == 4 ? a.QD : a.QD + a.KVD);
@@ -472,7 +557,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                 TK_MARK(4)
                 wait_slot(TK_MB_KV);
                 TK_MARK(5)
-                __syncthreads();
+                tk_sync();
                 TK_MARK(1)
                 const __half* ks = reinterpret_cast<const __half*>(s_kv);
                 const __half* vs = ks + (size_t)a.chunk_max * 256;
@@ -505,7 +590,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                     const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
                     if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
                 }
-                __syncthreads();
+                tk_sync();
                 TK_MARK(2)
                 if (warp < 4) {
                     float m = -INFINITY;
@@ -523,7 +608,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                         a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
                     }
                 }
-                __syncthreads();
+                tk_sync();
                 {
                     const uint32_t dp = tid & 127, qr = tid >> 7;
                     float acc[4][2] = {};
@@ -545,18 +630,16 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                         red[(qr * 4 + h) * 256 + 2 * dp + 1] = acc[h][1];
                     }
                 }
-                __syncthreads();
+                tk_sync();
                 for (uint32_t i = tid; i < 4 * 256; i += TK_THREADS)
                     a.att_part[(size_t)c * 1024 + i] = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
                 TK_MARK(3)
+            } else {
+                wait_slot(TK_MB_KV);
             }
         }
         bar_arrive();
-        if (tid == 0) {
-            arm(TK_MB_KV, !last ? tk_issue_kv(a, a.layers[l + 1], pos, s_kv, &mb[TK_MB_KV]) : false);
-            arm(TK_MB_CATT, !last ? tk_issue_vec(a.layers[l + 1].c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT])
-                                  : false);
-        }
+        release_slot(TK_ME_ATT);
         bar_wait();
 
         // ============================ O ============================
@@ -581,13 +664,13 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
             float* comb = red + 512;     // [4][nd]
             float M = warp_max(m);
             if (lane == 0) red32[warp] = M;
-            __syncthreads();
+            tk_sync();
             M = warp_max(lane < TK_WARPS ? red32[lane] : -INFINITY);
-            __syncthreads();
+            tk_sync();
             const float e = (uint32_t)tid < w.nsplit ? expf(m - M) : 0.0f;
             if ((uint32_t)tid < w.nsplit) wts[tid] = e;
-            const float Lsum = block_sum(l_ * e, red32);
-            __syncthreads();
+            const float Lsum = tk_block_sum(l_ * e, red32);
+            tk_sync();
             {
                 float acc = 0.0f;
                 if (g < ng) {
@@ -601,23 +684,25 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                         acc += a.att_part[(size_t)s_ * 1024 + d0 + d] * wts[s_];
                     comb[g * nd + d] = acc;
                 }
-                __syncthreads();
+                tk_sync();
                 if ((uint32_t)tid < nd) {
                     float t = 0.0f;
                     for (uint32_t gg = 0; gg < ng; ++gg) t += comb[gg * nd + tid];
                     xn[tid] = t / Lsum;
                 }
             }
-            __syncthreads();
+            tk_sync();
             TK_MARK(0)
             tk_prep(xn, 0, a.o.nb, xq);
             wait_slot(TK_MB_O);
             TK_MARK(1)
             tk_tile<64>(s_o, a.o.nb, xq, red);
             if (tid < 64) a.o_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
+        } else {
+            wait_slot(TK_MB_O);
         }
         bar_arrive();
-        if (tid == 0) arm(TK_MB_O, !last ? tk_issue(a.layers[l + 1].o, a.o, s_o, &mb[TK_MB_O]) : false);
+        release_slot(TK_ME_O);
         bar_wait();
 
         // ============================ GU ============================
@@ -647,7 +732,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
             }
             float* wp = red;  // [npair * wpp][16]
             if (p < npair) wp[(p * wpp + r) * 16 + col] = acc;
-            __syncthreads();
+            tk_sync();
             TK_MARK(2)
             if ((uint32_t)tid < nu * 16) {
                 const uint32_t ui = tid / 16, cc = tid % 16;
@@ -658,13 +743,11 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                 }
                 a.hb[(size_t)(c + ui * G) * 16 + cc] = gelu_tanh_ref(g) * up;
             }
+        } else {
+            wait_slot(TK_MB_GU);
         }
         bar_arrive();
-        if (tid == 0) {
-            arm(TK_MB_GU, !last ? tk_issue(a.layers[l + 1].gu, a.gu, s_gu, &mb[TK_MB_GU]) : false);
-            arm(TK_MB_CGU, !last ? tk_issue_vec(a.layers[l + 1].c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU])
-                                 : false);
-        }
+        release_slot(TK_ME_GU);
         bar_wait();
 
         // ============================ DOWN ============================
@@ -682,35 +765,17 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                 const uint32_t b = warp + r * TK_WARPS;
                 if (b < nb) xq_prep_block(hv[r], &xq[b]);
             }
-            __syncthreads();
+            tk_sync();
             TK_MARK(0)
             wait_slot(TK_MB_DOWN);
             TK_MARK(1)
             tk_tile<64>(s_down, nb, xq, red);
             if (tid < 64) a.dn_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
+        } else {
+            wait_slot(TK_MB_DOWN);
         }
         bar_arrive();
-        if (tid == 0) {
-            if (!last) {
-                arm(TK_MB_DOWN, tk_issue(a.layers[l + 1].down, a.down, s_down, &mb[TK_MB_DOWN]));
-            } else {
-                arm(TK_MB_DOWN, false);
-                if (a.want_logits) {  // start the LM-head ring over the freed gu|down|kv slots
-                    for (uint32_t r = 0; r < a.head_ring; ++r) {
-                        const uint32_t t = c + r * G;
-                        bool armed = false;
-                        if (t < a.head.units) {
-                            fence_proxy_async();
-                            mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
-                            bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
-                                     a.head.img_bytes, &mb[TK_MB_HEAD + r]);
-                            armed = true;
-                        }
-                        arm(TK_MB_HEAD + r, armed);
-                    }
-                }
-            }
-        }
+        release_slot(TK_ME_DOWN);
         bar_wait();
     }
 
@@ -726,18 +791,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
             const uint32_t r = i % a.head_ring;
             wait_slot(TK_MB_HEAD + r);
             tk_tile<64>(s_gu + (size_t)r * a.head.img_bytes, a.head.nb, xq, red);
-            if (tid == 0) {  // refill this buffer while the argmax runs
-                const uint32_t tn = t + a.head_ring * G;
-                bool armed = false;
-                if (tn < a.head.units) {
-                    fence_proxy_async();
-                    mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
-                    bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)tn * a.head.img_bytes,
-                             a.head.img_bytes, &mb[TK_MB_HEAD + r]);
-                    armed = true;
-                }
-                arm(TK_MB_HEAD + r, armed);
-            }
+            release_slot(TK_ME_HEAD + r);  // the producer refills it while the argmax runs
             if (warp == 0) {
                 float v0 = red[lane], v1 = red[lane + 32];
                 a.logits[(size_t)t * 64 + lane] = v0;
@@ -746,7 +800,7 @@ __global__ void __launch_bounds__(TK_THREADS, 1) token_kernel(const TkArgs a) {
                 if (v1 > v0) { v0 = v1; ix += 32; }
                 if (v0 > bv || (v0 == bv && ix < bi)) { bv = v0; bi = ix; }
             }
-            __syncthreads();
+            tk_sync();
         }
         if (warp == 0) {
 #pragma unroll

@@ -73,6 +73,11 @@ class DecodeConfig:
                            self.rope_theta_global, self.rope_theta_local, self.embed_scale, self.attn_scale)
 
 
+# trace buffer layout of the token kernel (u64 words)
+TRACE_CTA, TRACE_MAXBAR, TRACE_MAXCTA = 512 + 8 * 1024, 160, 160
+TRACE_WORDS = TRACE_CTA + 2 * TRACE_MAXBAR * TRACE_MAXCTA
+
+
 def tensor_stream(layer, which):
     return lib().xp_session_tensor_stream(layer, which)
 
@@ -176,7 +181,7 @@ class DecodeSession:
     def trace(self):
         """Phase timeline of the last token (XP_TRACE=1): list of
         (arrive_ns, leave_ns) per grid barrier, relative to kernel start."""
-        buf = np.zeros(512 + 8 * 1024, np.uint64)
+        buf = np.zeros(TRACE_WORDS, np.uint64)
         check(lib().xp_session_trace(self._h, buf.ctypes.data, len(buf)))
         nb = int(buf[0])
         t0 = int(buf[1])
@@ -184,6 +189,16 @@ class DecodeSession:
         marks = [[(int(buf[512 + k * 8 + j]) - t0) if buf[512 + k * 8 + j] else None for j in range(8)]
                  for k in range(nb + 1)]
         return bars, int(buf[2 * nb + 2]) - t0, marks
+
+    def trace_ctas(self):
+        """Per-CTA (arrive_ns, leave_ns) of every grid barrier of the last
+        token (XP_TRACE=1), relative to kernel start: array [ctas, barriers, 2]."""
+        buf = np.zeros(TRACE_WORDS, np.uint64)
+        check(lib().xp_session_trace(self._h, buf.ctypes.data, len(buf)))
+        nb, t0 = int(buf[0]), int(buf[1])
+        per = buf[TRACE_CTA:].reshape(TRACE_MAXCTA, TRACE_MAXBAR, 2)[:, 1:nb + 1].astype(np.int64)
+        per = per[per[:, 0, 0] != 0]
+        return per - t0
 
     def error_word(self):
         w = C.c_uint32()
