@@ -335,25 +335,29 @@ struct xp_session {
         if (H > 512 * TK_MAXJ || (H / 64) > G || QD + 2 * KVD > 512 * TK_MAXJ) return false;
         if (cfg.vocab % 64) return false;
         const uint32_t tq = (QD + 2 * KVD) / 64;
-        const uint32_t ksq = largest_divisor_upto(nbH, std::min<uint32_t>(TK_MAXP, G / tq));
+        const uint32_t kmax = 8;  // K splits per column tile
+        const uint32_t ksq = largest_divisor_upto(nbH, std::min<uint32_t>(kmax, G / tq));
         const uint32_t kso = nbQ / 4;  // 128-dim K ranges (inside one 256-dim head)
         const uint32_t to = H / 64;
-        const uint32_t ksd = largest_divisor_upto(nbF, std::min<uint32_t>(TK_MAXP, G / to));
-        if (tq * ksq > G || to * kso > G || to * ksd > G || tq == 0 || kso > (uint32_t)TK_MAXP) return false;
+        const uint32_t ksd = largest_divisor_upto(nbF, std::min<uint32_t>(kmax, G / to));
+        if (tq * ksq > G || to * kso > G || to * ksd > G || tq == 0 || QD % 128) return false;
         tk.qkv = mk_phase(tq * ksq, nbH / ksq, 64, 1, ksq, G);
         tk.o = mk_phase(to * kso, 4, 64, 1, kso, G);
         tk.gu = mk_phase(F / 16, nbH, 16, 2, 1, G);
         tk.down = mk_phase(to * ksd, nbF / ksd, 64, 1, ksd, G);
         tk.head = mk_phase(cfg.vocab / 64, nbH, 64, 1, 1, G);
-        if (tk.gu.per_cta > 3 || tk.down.nb > 4 * TK_WARPS) return false;
-        tk.chunk_max = (((cfg.max_seq + G - 1) / G) + 7) & ~7u;
+        if (tk.gu.per_cta > 3 || tk.down.nb * 32 > std::max<uint32_t>(H, 128)) return false;
+        // attention: at most TK_SPLIT_CAP splits of at least chunk_min rows
+        tk.chunk_min = (uint32_t)std::max(8, env_int("XP_TK_CHUNK_MIN", 16));
+        tk.chunk_max = (std::max<uint32_t>(tk.chunk_min, (cfg.max_seq + TK_SPLIT_CAP - 1) / TK_SPLIT_CAP) + 7) & ~7u;
         uint32_t off = 0;
         tk.off_qkv = off; off += al128(tk.qkv.img_bytes);
         tk.off_o = off; off += al128(tk.o.img_bytes);
         tk.off_gu = off; off += al128(tk.gu.per_cta * tk.gu.img_bytes);
         tk.off_down = off; off += al128(tk.down.img_bytes);
-        tk.off_kv = off; off += al128(2 * tk.chunk_max * KVD * 2);
-        const uint32_t ring_bytes = off - tk.off_gu;
+        // KV rows of ATTN, then the flash-partial stage of O (512 B per split)
+        tk.off_kv = off; off += al128(std::max<uint32_t>(2 * tk.chunk_max * KVD * 2, TK_SPLIT_CAP * 512));
+        const uint32_t ring_bytes = off - tk.off_qkv;
         tk.head_ring = std::min<uint32_t>(TK_MAX_RING, ring_bytes / tk.head.img_bytes);
         if (tk.head_ring == 0) return false;
         tk.off_cqkv = off; off += al128(2 * H * 4);
@@ -443,13 +447,14 @@ struct xp_session {
         if ((e = repack(lm, tk_head, tk.head, 0, 0)) != XP_OK) return e;
         if ((e = alloc(&tk_layers_dev, cfg.n_layers)) != XP_OK) return e;
         XP_CUDA_TRY(cudaMemcpy(tk_layers_dev, tk_layers.data(), sizeof(TkLayer) * cfg.n_layers, cudaMemcpyHostToDevice));
-        float *qkvp, *attp, *atts, *op, *dnp, *amv2;
+        float *attp, *atts, *amv2;
+        long long *aq, *ao, *ad;
         uint32_t* ami2;
-        if ((e = alloc(&qkvp, (size_t)tk.qkv.ks * (QD + 2 * KVD))) != XP_OK) return e;
-        if ((e = alloc(&attp, (size_t)G * 1024)) != XP_OK) return e;
+        if ((e = alloc(&aq, (size_t)(QD + 2 * KVD))) != XP_OK) return e;
+        if ((e = alloc(&ao, (size_t)H)) != XP_OK) return e;
+        if ((e = alloc(&ad, (size_t)H)) != XP_OK) return e;
+        if ((e = alloc(&attp, (size_t)G * QD)) != XP_OK) return e;
         if ((e = alloc(&atts, (size_t)G * 8)) != XP_OK) return e;
-        if ((e = alloc(&op, (size_t)tk.o.ks * H)) != XP_OK) return e;
-        if ((e = alloc(&dnp, (size_t)tk.down.ks * H)) != XP_OK) return e;
         if ((e = alloc(&amv2, G)) != XP_OK) return e;
         if ((e = alloc(&ami2, G)) != XP_OK) return e;
         if ((e = alloc(&tk_bar, 4)) != XP_OK) return e;
@@ -467,7 +472,8 @@ struct xp_session {
         tk.theta_local = cfg.rope_theta_local;
         tk.embed = embed;
         tk.x0 = xa; tk.x1 = xb;
-        tk.qkv_part = qkvp; tk.att_part = attp; tk.att_stat = atts; tk.o_part = op; tk.hb = hb; tk.dn_part = dnp;
+        tk.acc_qkv = aq; tk.acc_o = ao; tk.acc_dn = ad;
+        tk.att_part = attp; tk.att_stat = atts; tk.hb = hb;
         tk.logits = logits; tk.am_val = amv2; tk.am_idx = ami2;
         tk.token = token; tk.pos = pos; tk.hist = hist; tk.sample_out = sample_out;
         tk.bar = tk_bar; tk.epoch = tk_bar + 1;

@@ -1,33 +1,37 @@
 // Persistent token kernel: one cooperative launch decodes one position.
 //
-// Grid = one CTA per SM, all co-resident. The reference's per-token op order
-// (examples/llm/decode.cpp:1634-1780) runs as five phases per layer separated
-// by grid barriers:
+// Grid = one CTA per SM, all co-resident; each CTA is 16 compute warps plus
+// one producer warp. The reference's per-token op order
+// (examples/llm/decode.cpp:1634-1780) runs as five steps per layer separated
+// by grid barriers, then one LM-head step:
 //
 //   QKV  : residual + post-FFN norm of layer l-1 (or the embedding), attention
-//          norm, then a K-split int4 matvec unit -> q|k|v partial sums
-//   ATTN : q/k/v = sum of partials, QK-norm + RoPE, fp16 KV append (CTA 0),
-//          one contiguous chunk of the attended window per CTA -> flash partials
-//   O    : combine the flash partials for this CTA's 128-dim K range, o-proj
-//          unit -> partial sums
+//          norm, then a K-split int4 matvec unit -> q|k|v sums
+//   ATTN : QK-norm + RoPE, fp16 KV append (CTA 0), one contiguous chunk of the
+//          attended window per CTA -> flash partials
+//   O    : combine the flash partials of this CTA's 128-dim K range, o-proj
+//          unit -> sums
 //   GU   : residual + post-attention norm, FFN norm, gate|up units of 16
 //          columns over all K -> GeGLU -> hb
-//   DOWN : hb limbs for this CTA's K range, down-proj unit -> partial sums
+//   DOWN : hb slice for this CTA's K range, down-proj unit -> sums
+//   HEAD : residual + post-FFN + final norm, LM-head tiles, per-CTA argmax;
+//          then CTA 0 picks the lowest-index maximum (greedy).
 //
-// then HEAD (residual + post-FFN + final norm, LM head tiles, per-CTA argmax)
-// and SAMPLE (CTA 0: lowest-index argmax, token, position).
-//
-// Everything a phase reads that does not depend on this token is in shared
-// memory before the phase starts:
-//   * weights live in a unit-major image made once at load time (each unit's
-//     nibbles and per-block bf16 scales contiguous), so a CTA's share of a
-//     phase is one cp.async.bulk copy into its slot;
-//   * the phase's norm weights are one contiguous vector per (layer, phase);
-//   * the KV rows a CTA attends to are staged one phase ahead;
-//   * RoPE cos/sin for this position are tabulated once per launch.
-// A slot is refilled for layer l+1 right after this CTA arrives at the
-// barrier that closes phase P of layer l, so every copy overlaps the barrier
-// wait and the other phases.
+// Design rules of this kernel, each measured on B200:
+//   * Code size. Every step's code runs once per layer, so a layer loop larger
+//     than the SM's instruction cache refetches all of it every layer (a cold
+//     ~150-instruction loop cost ~1 us). The layer loop is therefore ONE
+//     phase machine: the norm prologue, the limb prep and the 64-column tile
+//     loop each exist once and serve QKV, O, DOWN and HEAD.
+//   * K-split sums go through int64 fixed-point accumulators (2^-32 units,
+//     red.add): integer addition is order-independent, so the result is
+//     deterministic, and a consumer loads one vector instead of every partial.
+//   * Everything a step reads that does not depend on this token is in shared
+//     memory before the step starts: weights live in unit-major images (one
+//     bulk copy per CTA and step), per-step norm vectors are contiguous, the
+//     KV rows a CTA attends to are staged ahead, RoPE cos/sin are tabulated
+//     once per launch. The producer warp issues all of those copies, so no
+//     compute thread ever blocks on issuing one.
 #pragma once
 #include "attention.cuh"
 #include "common.cuh"
@@ -39,20 +43,25 @@ namespace xp {
 constexpr int TK_THREADS = 512;              // compute threads (16 warps)
 constexpr int TK_WARPS = TK_THREADS / 32;
 constexpr int TK_BLOCK = TK_THREADS + 32;      // + one producer warp that issues every bulk copy
-constexpr int TK_MAXJ = 3;   // hidden <= 1536
-constexpr int TK_MAXP = 8;   // K-split partials per output <= 8
+constexpr int TK_MAXJ = 3;   // hidden <= 1536, q|k|v width <= 1536
 constexpr int TK_NMB = 32;   // mbarriers
-constexpr int TK_OPV = 10;   // attention splits per thread loaded with the stats
+// "full" mbarriers: complete once per fill of a slot
 constexpr int TK_MB_QKV = 0, TK_MB_O = 1, TK_MB_GU = 2, TK_MB_DOWN = 3, TK_MB_KV = 4;
 constexpr int TK_MB_CQKV = 5, TK_MB_CATT = 6, TK_MB_CGU = 7, TK_MB_HEAD = 8;  // head ring: 8..15
 constexpr int TK_MAX_RING = 8;
 // "empty" mbarriers: the compute warps arrive once they are done reading a
 // slot; the producer waits on them before refilling it
 constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME_DOWN = 20, TK_ME_HEAD = 21;
-static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_NMB, "mbarrier count");
+constexpr int TK_MB_STAGE = 29;  // flash partials staged for the O combine
+static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "mbarrier count");
+constexpr int TK_SPLIT_CAP = 128;  // attention splits per layer (the O stage holds 512 B each)
+
+// steps of the phase machine
+constexpr uint32_t TK_S_QKV = 0, TK_S_ATTN = 1, TK_S_O = 2, TK_S_GU = 3, TK_S_DOWN = 4, TK_S_HEAD = 5;
+
 // Trace layout (u64 words, %globaltimer ns): [0] barriers, [1] start,
 // [2k, 2k+1] CTA 0 arrive/leave of barrier k, [512 + 8k + i] CTA 0 marks in
-// phase k, then per CTA c and barrier k < TK_TRACE_MAXBAR its arrive/leave at
+// step k, then per CTA c and barrier k < TK_TRACE_MAXBAR its arrive/leave at
 // TK_TRACE_CTA + (c * TK_TRACE_MAXBAR + k) * 2.
 constexpr uint32_t TK_TRACE_CTA = 512 + 8 * 1024, TK_TRACE_MAXBAR = 160, TK_TRACE_MAXCTA = 160;
 constexpr uint32_t TK_TRACE_WORDS = TK_TRACE_CTA + 2 * TK_TRACE_MAXBAR * TK_TRACE_MAXCTA;
@@ -89,17 +98,17 @@ struct TkArgs {
     const unsigned char* head_img;
     const float* c_head;  // [post_ffn of the last layer | final_norm]  2H floats
     const float* embed;
-    float* x0;          // residual after the FFN sublayer (written in QKV)
-    float* x1;          // residual after the attention sublayer (written in GU)
-    float* qkv_part;    // [qkv.ks][QD + 2 KVD]
-    float* att_part;    // [grid][4][256]
-    float* att_stat;    // [grid][4][2]
-    float* o_part;      // [o.ks][H]
-    float* hb;          // [F]
-    float* dn_part;     // [down.ks][H]
-    float* logits;      // [V]
-    float* am_val;      // [grid]
-    uint32_t* am_idx;   // [grid]
+    float* x0;            // residual after the FFN sublayer (written in QKV)
+    float* x1;            // residual after the attention sublayer (written in GU)
+    long long* acc_qkv;   // [QD + 2 KVD] fixed-point q|k|v sums
+    long long* acc_o;     // [H] fixed-point o-proj sums
+    long long* acc_dn;    // [H] fixed-point down-proj sums
+    float* att_part;      // [QD / 128][grid][128] flash partials, one 128-dim slice per O unit
+    float* att_stat;      // [grid][4][2] (max, sum) per split and head
+    float* hb;            // [F]
+    float* logits;        // [V]
+    float* am_val;        // [grid]
+    uint32_t* am_idx;     // [grid]
     uint32_t* token;
     uint32_t* pos;
     uint32_t* hist;
@@ -107,13 +116,14 @@ struct TkArgs {
     uint64_t* bar;
     uint64_t* epoch;
     uint32_t* err;
-    uint64_t* trace;    // optional phase timeline (CTA 0)
+    uint64_t* trace;      // optional timeline (XP_TRACE)
     int want_logits;
     int greedy;
-    uint32_t chunk_max;
+    uint32_t chunk_max;   // most KV rows one CTA attends to
+    uint32_t chunk_min;   // fewest KV rows per split
     uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
     uint32_t off_xn, off_xq, off_q, off_sc, off_red, off_misc;
-    uint32_t head_ring;
+    uint32_t head_ring;   // LM-head ring buffers laid from off_qkv on
 };
 
 // ---- helpers -------------------------------------------------------------------
@@ -127,81 +137,29 @@ XP_DEV float tk_block_sum(float v, float* red) {
     tk_sync();
     if (lane == 0) red[wid] = v;
     tk_sync();
-    float t = lane < TK_WARPS ? red[lane] : 0.0f;
+    const float t = lane < TK_WARPS ? red[lane] : 0.0f;
     return warp_sum(t);
 }
 XP_DEV void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// generic-proxy global writes of other CTAs (ordered before this thread by an
+// acquire) before this thread's async-proxy (bulk copy) reads
+XP_DEV void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
-// r = base + rmsnorm_gemma(sum_k part[k], w_post) (mode 1) or the scaled
-// embedding row (mode 0); x_out = r (CTA 0); xn = rmsnorm_gemma(r, w_pre).
-// w_post / w_pre are shared-memory vectors.
-XP_DEV void tk_norm_prologue(const TkArgs& a, int mode, const float* base, const float* part, uint32_t nparts,
-                             const float* w_post, const float* w_pre, float* x_out, float* xn, float* red) {
-    const uint32_t H = a.H;
-    const int tid = threadIdx.x;
-    float rv[TK_MAXJ];
-    if (mode == 0) {
-        const float* row = a.embed + (size_t)(*a.token) * H;
-#pragma unroll
-        for (int j = 0; j < TK_MAXJ; ++j) {
-            const uint32_t i = tid + j * TK_THREADS;
-            rv[j] = i < H ? row[i] * a.embed_scale : 0.0f;
-        }
-    } else {
-        // every global load of the prologue in flight at once, then summed in
-        // a fixed order
-        float ld[TK_MAXJ][TK_MAXP];
-        float bv[TK_MAXJ];
-#pragma unroll
-        for (int j = 0; j < TK_MAXJ; ++j) {
-            const uint32_t i = tid + j * TK_THREADS;
-            bv[j] = i < H ? base[i] : 0.0f;
-#pragma unroll
-            for (int k = 0; k < TK_MAXP; ++k)
-                ld[j][k] = (i < H && (uint32_t)k < nparts) ? part[(size_t)k * H + i] : 0.0f;
-        }
-        float yv[TK_MAXJ];
-        float ss = 0.0f;
-#pragma unroll
-        for (int j = 0; j < TK_MAXJ; ++j) {
-            float s = 0.0f;
-#pragma unroll
-            for (int k = 0; k < TK_MAXP; ++k) s += ld[j][k];
-            yv[j] = s;
-            ss += s * s;
-        }
-        ss = tk_block_sum(ss, red);
-        const float sc = rsqrtf(ss / (float)H + a.eps);
-#pragma unroll
-        for (int j = 0; j < TK_MAXJ; ++j) {
-            const uint32_t i = tid + j * TK_THREADS;
-            rv[j] = i < H ? bv[j] + yv[j] * sc * (1.0f + w_post[i]) : 0.0f;
-        }
+// Fixed point in units of 2^-32: |v| < 2^31 is exact to 2^-33. An
+// out-of-range (or NaN) value sets TK_ERR_RANGE and contributes 0.
+XP_DEV long long tk_fix(float v, uint32_t* err) {
+    const float s = v * 4294967296.0f;
+    if (!(fabsf(s) < 9.2e18f)) {
+        atomicOr(err, TK_ERR_RANGE);
+        return 0;
     }
-    float ss2 = 0.0f;
-#pragma unroll
-    for (int j = 0; j < TK_MAXJ; ++j) {
-        const uint32_t i = tid + j * TK_THREADS;
-        if (i < H && x_out && blockIdx.x == 0) x_out[i] = rv[j];
-        ss2 += rv[j] * rv[j];
-    }
-    ss2 = tk_block_sum(ss2, red);
-    const float sc2 = rsqrtf(ss2 / (float)H + a.eps);
-#pragma unroll
-    for (int j = 0; j < TK_MAXJ; ++j) {
-        const uint32_t i = tid + j * TK_THREADS;
-        if (i < H) xn[i] = rv[j] * sc2 * (1.0f + w_pre[i]);
-    }
-    tk_sync();
+    return __float2ll_rn(s);
 }
-
-// Limbs of blocks [b0, b0+nb) of the smem vector v into xq[0..nb).
-XP_DEV void tk_prep(const float* v, uint32_t b0, uint32_t nb, XBlk* xq) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t b = warp; b < nb; b += TK_WARPS) xq_prep_block(v[(b0 + b) * 32 + lane], &xq[b]);
-    tk_sync();
+XP_DEV float tk_unfix(long long x) { return __ll2float_rn(x) * 2.3283064365386963e-10f; }
+XP_DEV void red_add_s64(long long* p, long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
@@ -209,34 +167,34 @@ XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
     return (float)d * (X.f * __uint_as_float((uint32_t)s << 16));
 }
 
-// A unit image of CW (64 or 32) columns over nb blocks: warp w takes blocks w,
-// w+16, ...; lane handles columns lane (and lane+32). Column sums -> red[0..CW).
-template <int CW>
-XP_DEV void tk_tile(const unsigned char* img, uint32_t nb, const XBlk* xq, float* red) {
+// A unit image of 64 columns over nb blocks: warp w takes blocks w, w+16, ...;
+// lane handles columns lane and lane+32. Column sums -> red[0..64).
+XP_DEV void tk_tile64(const unsigned char* img, uint32_t nb, const XBlk* xq, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint4* nib = reinterpret_cast<const uint4*>(img);
-    const uint16_t* sc = reinterpret_cast<const uint16_t*>(img + (size_t)nb * CW * 16);
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(img + (size_t)nb * 64 * 16);
     float a0 = 0.0f, a1 = 0.0f;
     for (uint32_t b = warp; b < nb; b += TK_WARPS) {
         const XBlk& X = xq[b];
-        a0 += tk_dot(nib[b * CW + lane], sc[b * CW + lane], X);
-        if (CW == 64) a1 += tk_dot(nib[b * CW + lane + 32], sc[b * CW + lane + 32], X);
+        a0 += tk_dot(nib[b * 64 + lane], sc[b * 64 + lane], X);
+        a1 += tk_dot(nib[b * 64 + lane + 32], sc[b * 64 + lane + 32], X);
     }
-    float* wr = red + 64;  // [16][CW] warp partials
-    wr[warp * CW + lane] = a0;
-    if (CW == 64) wr[warp * CW + lane + 32] = a1;
+    float* wr = red + 64;  // [16][64] warp partials
+    wr[warp * 64 + lane] = a0;
+    wr[warp * 64 + lane + 32] = a1;
     tk_sync();
-    if (threadIdx.x < CW) {
+    if (threadIdx.x < 64) {
         float s = 0.0f;
         const uint32_t nw = nb < (uint32_t)TK_WARPS ? nb : (uint32_t)TK_WARPS;
-        for (uint32_t w = 0; w < nw; ++w) s += wr[w * CW + threadIdx.x];
+#pragma unroll 1
+        for (uint32_t w = 0; w < nw; ++w) s += wr[w * 64 + threadIdx.x];
         red[threadIdx.x] = s;
     }
     tk_sync();
 }
 
-// Issue the bulk copies of this CTA's units of a phase into its slot. Thread 0
-// only. Returns whether anything was armed on `bar`.
+// Issue the bulk copies of this CTA's units of a phase into its slot
+// (producer lane). Returns whether anything was armed on `bar`.
 XP_DEV bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar) {
     const uint32_t G = gridDim.x, c = blockIdx.x;
     if (c >= P.units) return false;
@@ -256,25 +214,28 @@ XP_DEV bool tk_issue_vec(const float* src, uint32_t n, unsigned char* slot, uint
     return true;
 }
 
+// The attended window of one layer and this CTA's split of it: chunks of at
+// least chunk_min rows (a multiple of 8), at most TK_SPLIT_CAP splits.
 struct TkWin {
     uint32_t kv_start, span, chunk, nsplit, j0, j1;
 };
-XP_DEV TkWin tk_window(uint32_t pos, uint32_t window) {
+XP_DEV TkWin tk_window(uint32_t pos, uint32_t window, uint32_t chunk_min) {
     TkWin w;
     const uint32_t seq = pos + 1;
     w.kv_start = (window == 0 || seq <= window) ? 0 : seq - window;
     w.span = seq - w.kv_start;
-    const uint32_t G = gridDim.x;
-    w.chunk = ((w.span + G - 1) / G + 7) & ~7u;
+    uint32_t ch = (w.span + TK_SPLIT_CAP - 1) / TK_SPLIT_CAP;
+    ch = ch > chunk_min ? ch : chunk_min;
+    w.chunk = (ch + 7) & ~7u;
     w.nsplit = (w.span + w.chunk - 1) / w.chunk;
     w.j0 = w.kv_start + min(blockIdx.x * w.chunk, w.span);
     w.j1 = w.kv_start + min((blockIdx.x + 1) * w.chunk, w.span);
     return w;
 }
 
-// Stage the KV rows [j0, min(j1, pos)) of one layer (thread 0).
+// Stage the KV rows [j0, min(j1, pos)) of one layer (producer lane).
 XP_DEV bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigned char* kvs, uint64_t* bar) {
-    const TkWin w = tk_window(pos, L.window);
+    const TkWin w = tk_window(pos, L.window, a.chunk_min);
     const uint32_t end = min(w.j1, pos);
     if (w.j1 - w.j0 > a.chunk_max) { atomicOr(a.err, TK_ERR_ATTN_CHUNK); return false; }
     if (end <= w.j0) return false;
@@ -287,28 +248,8 @@ XP_DEV bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigne
     return true;
 }
 
-// QK-norm + rotate-half RoPE of one 256-wide head held as 8 values per lane
-// (dims 4*lane..+3 and 128+4*lane..+3), weights and cos/sin from smem.
-XP_DEV void tk_qk_post(float v[8], const float* w, const float* cosT, const float* sinT, float eps) {
-    const int lane = threadIdx.x & 31;
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
-    ss = warp_sum(ss);
-    const float sc = rsqrtf(ss / 256.0f + eps);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t d = 4 * lane + i;
-        const float lo = v[i] * sc * (1.0f + w[d]);
-        const float hi = v[4 + i] * sc * (1.0f + w[128 + d]);
-        const float c = cosT[d], s = sinT[d];
-        v[i] = lo * c - hi * s;
-        v[4 + i] = lo * s + hi * c;
-    }
-}
-
 // ---------------------------------------------------------------------------------
-__global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
+__global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constant__ TkArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -321,7 +262,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
     unsigned char* s_o = sm + a.off_o;
     unsigned char* s_gu = sm + a.off_gu;
     unsigned char* s_down = sm + a.off_down;
-    unsigned char* s_kv = sm + a.off_kv;
+    unsigned char* s_kv = sm + a.off_kv;  // KV rows in ATTN, the flash-partial stage in O
     const float* cq = reinterpret_cast<const float*>(sm + a.off_cqkv);
     const float* ca = reinterpret_cast<const float*>(sm + a.off_catt);
     const float* cg = reinterpret_cast<const float*>(sm + a.off_cgu);
@@ -330,6 +271,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
     const uint32_t pos = *a.pos;
     const uint64_t base = *a.epoch;
     const uint32_t L = a.n_layers, H = a.H;
+    const uint32_t QKVW = a.QD + 2 * a.KVD;
     uint32_t nbar = 0;
     uint32_t par = 0;  // parity bit per "full" mbarrier, identical in every compute thread
 
@@ -339,12 +281,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
     }
     __syncthreads();
 
-    // ---------------- producer warp: every bulk copy of the launch ----------------
+    // ---------------- producer warp: every weight/constant/KV copy ----------------
     // Each "full" mbarrier completes exactly once per fill, with the copy's
     // bytes or, when this CTA has nothing to load, with a plain arrive, so the
     // compute warps wait on every fill unconditionally. A slot is refilled
     // for layer l+1 once the compute warps have arrived on its "empty"
-    // mbarrier at the grid barrier that closes the phase reading it.
+    // mbarrier at the grid barrier that closes the step reading it. The KV
+    // slot doubles as the O step's stage, so its refill waits for O.
     if (warp == TK_WARPS) {
         if (lane != 0) return;
         uint32_t epar = 0;  // parity bit per "empty" mbarrier
@@ -372,10 +315,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
             fill(tk_issue(Ln.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
             fill(tk_issue_vec(Ln.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
             wait_empty(TK_ME_ATT);
-            fill(tk_issue_kv(a, Ln, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
             fill(tk_issue_vec(Ln.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]), TK_MB_CATT);
             wait_empty(TK_ME_O);
             fill(tk_issue(Ln.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
+            fill(tk_issue_kv(a, Ln, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
             wait_empty(TK_ME_GU);
             fill(tk_issue(Ln.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
             fill(tk_issue_vec(Ln.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
@@ -384,26 +327,18 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
         }
         if (!a.want_logits) return;
         // last layer: the head constants once QKV is done with its slot, the
-        // LM-head ring over the gu|down|kv slots once DOWN is done with them
+        // LM-head ring over every weight slot once DOWN is done with them
         wait_empty(TK_ME_QKV);
         fill(tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
         wait_empty(TK_ME_DOWN);
-        for (uint32_t r = 0; r < a.head_ring && c + r * G < a.head.units; ++r) {
-            fence_proxy_async();
-            mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
-            bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)(c + r * G) * a.head.img_bytes,
-                     a.head.img_bytes, &mb[TK_MB_HEAD + r]);
-        }
         uint32_t i = 0;
         for (uint32_t t = c; t < a.head.units; t += G, ++i) {
-            const uint32_t r = i % a.head_ring, tn = t + a.head_ring * G;
-            wait_empty(TK_ME_HEAD + r);
-            if (tn < a.head.units) {
-                fence_proxy_async();
-                mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
-                bulk_g2s(s_gu + (size_t)r * a.head.img_bytes, a.head_img + (size_t)tn * a.head.img_bytes,
-                         a.head.img_bytes, &mb[TK_MB_HEAD + r]);
-            }
+            const uint32_t r = i % a.head_ring;
+            if (i >= a.head_ring) wait_empty(TK_ME_HEAD + r);
+            fence_proxy_async();
+            mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
+            bulk_g2s(s_qkv + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
+                     a.head.img_bytes, &mb[TK_MB_HEAD + r]);
         }
         return;
     }
@@ -413,9 +348,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
         mbar_wait(&mb[i], (par >> i) & 1u, a.err);
         par ^= 1u << i;
     };
-    auto release_slot = [&](int i) {  // after a tk_sync: every compute thread is done with the slot
-        if (tid == 0) mbar_arrive(&mb[i]);
-    };
+
     // RoPE table for this position: theta^(-2d/256) rounded once from double,
     // angle pos * inv in fp32, full-precision sincos (llm_transformer.cl:158-179)
     if (tid < 256) {
@@ -431,9 +364,390 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
 
 #define TK_MARK(k) \
     if (a.trace && c == 0 && tid == 0) a.trace[512 + nbar * 8 + (k)] = globaltimer_ns();
-    // Grid barrier split in two: arrive, release the phase's slots to the
-    // producer, then wait.
-    auto bar_arrive = [&]() {
+
+    const uint32_t nstep = 5 * L + (a.want_logits ? 1u : 0u);
+    float bv = -INFINITY;  // HEAD: this thread's best logit and its index (warp 0)
+    uint32_t bi = 0xFFFFFFFFu;
+#pragma unroll 1
+    for (uint32_t step = 0; step < nstep; ++step) {
+        const uint32_t l = step / 5;
+        const uint32_t k = l == L ? TK_S_HEAD : step - 5 * l;
+        const TkLayer& Ly = a.layers[l < L ? l : L - 1];
+
+        // ---------------- input of the step -> xn ----------------
+        if (k == TK_S_QKV || k == TK_S_GU || k == TK_S_HEAD) {
+            // r = base + rmsnorm_gemma(sum, w_post) (or the scaled embedding
+            // row); x_out = r (CTA 0); xn = rmsnorm_gemma(r, w_pre)
+            wait_slot(k == TK_S_GU ? TK_MB_CGU : TK_MB_CQKV);
+            const float* wv = k == TK_S_GU ? cg : cq;
+            const float* bsrc = k == TK_S_GU ? a.x0 : a.x1;
+            const long long* acc = k == TK_S_GU ? a.acc_o : a.acc_dn;
+            float* x_out = k == TK_S_QKV ? a.x0 : (k == TK_S_GU ? a.x1 : nullptr);
+            float rv[TK_MAXJ];
+            if (k == TK_S_QKV && l == 0) {
+                const float* row = a.embed + (size_t)(*a.token) * H;
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) {
+                    const uint32_t i = tid + j * TK_THREADS;
+                    rv[j] = i < H ? row[i] * a.embed_scale : 0.0f;
+                }
+            } else {
+                float yv[TK_MAXJ], bvv[TK_MAXJ];
+                float ss = 0.0f;
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) {
+                    const uint32_t i = tid + j * TK_THREADS;
+                    yv[j] = i < H ? tk_unfix(acc[i]) : 0.0f;
+                    bvv[j] = i < H ? bsrc[i] : 0.0f;
+                }
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) ss += yv[j] * yv[j];
+                ss = tk_block_sum(ss, red32);
+                const float sc = rsqrtf(ss / (float)H + a.eps);
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) {
+                    const uint32_t i = tid + j * TK_THREADS;
+                    rv[j] = i < H ? bvv[j] + yv[j] * sc * (1.0f + wv[i]) : 0.0f;
+                }
+            }
+            float ss2 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < TK_MAXJ; ++j) {
+                const uint32_t i = tid + j * TK_THREADS;
+                if (i < H && x_out && c == 0) x_out[i] = rv[j];
+                ss2 += rv[j] * rv[j];
+            }
+            ss2 = tk_block_sum(ss2, red32);
+            const float sc2 = rsqrtf(ss2 / (float)H + a.eps);
+#pragma unroll
+            for (int j = 0; j < TK_MAXJ; ++j) {
+                const uint32_t i = tid + j * TK_THREADS;
+                if (i < H) xn[i] = rv[j] * sc2 * (1.0f + wv[H + i]);
+            }
+        } else if (k == TK_S_O) {
+            // flash combine of this CTA's 128-dim slice over the splits: the
+            // slice of every split arrives in one bulk copy while each warp
+            // reduces the splits' statistics itself
+            const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            if (c < a.o.units) {
+                const uint32_t kc = c % a.o.ks, h = kc * 128 / 256;
+                const float* stage = reinterpret_cast<const float*>(s_kv);
+                if (tid == 0) {
+                    fence_proxy_async_all();
+                    mbar_expect_tx(&mb[TK_MB_STAGE], w.nsplit * 512);
+                    bulk_g2s(s_kv, a.att_part + (size_t)kc * G * 128, w.nsplit * 512, &mb[TK_MB_STAGE]);
+                }
+                float mv[TK_SPLIT_CAP / 32], lv[TK_SPLIT_CAP / 32];
+                float M = -INFINITY;
+#pragma unroll
+                for (int r = 0; r < TK_SPLIT_CAP / 32; ++r) {
+                    const uint32_t s_ = lane + 32 * r;
+                    mv[r] = s_ < w.nsplit ? a.att_stat[((size_t)s_ * 4 + h) * 2] : -INFINITY;
+                    lv[r] = s_ < w.nsplit ? a.att_stat[((size_t)s_ * 4 + h) * 2 + 1] : 0.0f;
+                    M = fmaxf(M, mv[r]);
+                }
+                M = warp_max(M);
+                float Ls = 0.0f;
+                float* wts = red + 1024;  // [TK_SPLIT_CAP]
+#pragma unroll
+                for (int r = 0; r < TK_SPLIT_CAP / 32; ++r) {
+                    const float e = mv[r] == -INFINITY ? 0.0f : expf(mv[r] - M);
+                    Ls += lv[r] * e;
+                    if (warp == 0) wts[lane + 32 * r] = e;
+                }
+                Ls = warp_sum(Ls);
+                wait_slot(TK_MB_STAGE);
+                tk_sync();
+                const uint32_t d = tid & 127, g = tid >> 7;
+                float acc = 0.0f;
+#pragma unroll 4
+                for (uint32_t s_ = g; s_ < w.nsplit; s_ += 4) acc += stage[s_ * 128 + d] * wts[s_];
+                red[g * 128 + d] = acc;
+                tk_sync();
+                if (tid < 128) xn[tid] = (red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / Ls;
+            }
+        } else if (k == TK_S_DOWN) {
+            if (c < a.down.units) {
+                const uint32_t kc = c % a.down.ks, n = a.down.nb * 32;
+#pragma unroll 1
+                for (uint32_t i = tid; i < n; i += TK_THREADS) xn[i] = a.hb[(size_t)kc * n + i];
+            }
+        } else {
+            // ================= ATTN =================
+            const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            wait_slot(TK_MB_CATT);
+            if (c < w.nsplit) {
+                const uint32_t n = w.j1 - w.j0;
+                float* qs = reinterpret_cast<float*>(sm + a.off_q);   // [4][256] pre-scaled
+                __half* kn = reinterpret_cast<__half*>(qs + 4 * 256);  // [256]
+                __half* vn = kn + 256;                                 // [256]
+                float* sc = reinterpret_cast<float*>(sm + a.off_sc);   // [4][chunk_max]
+                float* qkvs = red;                                     // [QKVW]
+#pragma unroll
+                for (int r = 0; r < TK_MAXJ; ++r) {
+                    const uint32_t i = tid + r * TK_THREADS;
+                    if (i < QKVW) qkvs[i] = tk_unfix(a.acc_qkv[i]);
+                }
+                tk_sync();
+                TK_MARK(0)
+                if (warp < 6) {
+                    // warps 0-3: q heads, 4: k, 5: v; a head held as 8 values
+                    // per lane (dims 4*lane..+3 and 128+4*lane..+3)
+                    const uint32_t off = warp < 4 ? warp * 256 : (warp == 4 ? a.QD : a.QD + a.KVD);
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[i] = qkvs[off + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4))];
+                    if (warp < 5) {
+                        // QK-norm + rotate-half RoPE
+                        const float* wq = warp < 4 ? ca : ca + 256;
+                        const float* cosT = rope + (Ly.global ? 256 : 0);
+                        const float* sinT = cosT + 128;
+                        float ss = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+                        ss = warp_sum(ss);
+                        const float scl = rsqrtf(ss / 256.0f + a.eps);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint32_t d = 4 * lane + i;
+                            const float lo = v[i] * scl * (1.0f + wq[d]);
+                            const float hi = v[4 + i] * scl * (1.0f + wq[128 + d]);
+                            v[i] = lo * cosT[d] - hi * sinT[d];
+                            v[4 + i] = lo * sinT[d] + hi * cosT[d];
+                        }
+                    }
+                    if (warp < 4) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            qs[warp * 256 + 4 * lane + i] = v[i] * a.attn_scale;
+                            qs[warp * 256 + 128 + 4 * lane + i] = v[4 + i] * a.attn_scale;
+                        }
+                    } else {
+                        __half* dst = warp == 4 ? kn : vn;
+                        __half* cache = warp == 4 ? Ly.kc : Ly.vc;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
+                            dst[4 * lane + i] = lo;
+                            dst[128 + 4 * lane + i] = hi;
+                            if (c == 0) {
+                                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
+                                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
+                            }
+                        }
+                    }
+                }
+                wait_slot(TK_MB_KV);
+                tk_sync();
+                TK_MARK(1)
+                const __half* ks = reinterpret_cast<const __half*>(s_kv);
+                const __half* vs = ks + (size_t)a.chunk_max * 256;
+                // scores: one key per warp, lane holds 8 dims of every head
+#pragma unroll 1
+                for (uint32_t jj = warp; jj < n; jj += TK_WARPS) {
+                    const uint32_t j = w.j0 + jj;
+                    const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(kn + 8 * lane)
+                                               : *reinterpret_cast<const uint4*>(ks + (size_t)jj * 256 + 8 * lane);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                    float kf[8];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __half22float2(h2[i]);
+                        kf[2 * i] = f.x;
+                        kf[2 * i + 1] = f.y;
+                    }
+                    float s4[4];
+#pragma unroll
+                    for (int hh = 0; hh < 4; ++hh) {
+                        const float4 qa = *reinterpret_cast<const float4*>(qs + hh * 256 + 8 * lane);
+                        const float4 qb = *reinterpret_cast<const float4*>(qs + hh * 256 + 8 * lane + 4);
+                        float acc = qa.x * kf[0];
+                        acc = fmaf(qa.y, kf[1], acc);
+                        acc = fmaf(qa.z, kf[2], acc);
+                        acc = fmaf(qa.w, kf[3], acc);
+                        acc = fmaf(qb.x, kf[4], acc);
+                        acc = fmaf(qb.y, kf[5], acc);
+                        acc = fmaf(qb.z, kf[6], acc);
+                        acc = fmaf(qb.w, kf[7], acc);
+                        s4[hh] = acc;
+                    }
+                    const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
+                    if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
+                }
+                tk_sync();
+                TK_MARK(2)
+                if (warp < 4) {
+                    float m = -INFINITY;
+#pragma unroll 1
+                    for (uint32_t jj = lane; jj < n; jj += 32) m = fmaxf(m, sc[warp * a.chunk_max + jj]);
+                    m = warp_max(m);
+                    float sum = 0.0f;
+#pragma unroll 1
+                    for (uint32_t jj = lane; jj < n; jj += 32) {
+                        const float p = expf(sc[warp * a.chunk_max + jj] - m);
+                        sc[warp * a.chunk_max + jj] = p;
+                        sum += p;
+                    }
+                    sum = warp_sum(sum);
+                    if (lane == 0) {
+                        a.att_stat[((size_t)c * 4 + warp) * 2] = m;
+                        a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
+                    }
+                }
+                tk_sync();
+                {
+                    const uint32_t dp = tid & 127, qr = tid >> 7;
+                    float acc[4][2] = {};
+#pragma unroll 2
+                    for (uint32_t jj = qr; jj < n; jj += 4) {
+                        const uint32_t j = w.j0 + jj;
+                        const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vn)[dp]
+                                                    : reinterpret_cast<const __half2*>(vs + (size_t)jj * 256)[dp];
+                        const float2 vf = __half22float2(hv);
+#pragma unroll
+                        for (int hh = 0; hh < 4; ++hh) {
+                            const float p = sc[hh * a.chunk_max + jj];
+                            acc[hh][0] = fmaf(p, vf.x, acc[hh][0]);
+                            acc[hh][1] = fmaf(p, vf.y, acc[hh][1]);
+                        }
+                    }
+#pragma unroll
+                    for (int hh = 0; hh < 4; ++hh) {
+                        red[(qr * 4 + hh) * 256 + 2 * dp] = acc[hh][0];
+                        red[(qr * 4 + hh) * 256 + 2 * dp + 1] = acc[hh][1];
+                    }
+                }
+                tk_sync();
+                // slice i / 128 of the partial goes where the O unit of that
+                // K range reads it: att_part[slice][c][i % 128]
+#pragma unroll 1
+                for (uint32_t i = tid; i < 4 * 256; i += TK_THREADS)
+                    a.att_part[((size_t)(i >> 7) * G + c) * 128 + (i & 127)] =
+                        red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
+                TK_MARK(3)
+            } else {
+                wait_slot(TK_MB_KV);
+            }
+            // the down-proj sums were consumed by this layer's QKV step
+            if (c == G - 1) {
+#pragma unroll 1
+                for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_dn[i] = 0;
+            }
+        }
+
+        if (k != TK_S_ATTN) {
+            // ---------------- limbs of xn: one shared prep ----------------
+            const TkPhase& P = k == TK_S_QKV ? a.qkv
+                             : k == TK_S_O   ? a.o
+                             : k == TK_S_GU  ? a.gu
+                             : k == TK_S_DOWN ? a.down : a.head;
+            const bool has = c < P.units;
+            const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
+            tk_sync();  // xn complete
+            if (has) {
+#pragma unroll 1
+                for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
+            }
+            tk_sync();
+            TK_MARK(0)
+
+            if (k == TK_S_GU) {
+                // ---------------- gate|up units -> GeGLU -> hb ----------------
+                wait_slot(TK_MB_GU);
+                TK_MARK(1)
+                if (has) {
+                    const uint32_t nb = P.nb;
+                    uint32_t nu = 0;
+                    for (uint32_t u = c; u < P.units; u += G) ++nu;
+                    // half-warp workers (16 lanes = 16 columns), each fixed on one
+                    // (unit, matrix) pair and a stride of blocks, accumulating in a register
+                    const uint32_t worker = tid >> 4, col = tid & 15, nwk = TK_THREADS / 16;
+                    const uint32_t npair = nu * 2, wpp = nwk / npair;
+                    const uint32_t p = worker / wpp, r = worker % wpp;
+                    float acc = 0.0f;
+                    if (p < npair) {
+                        const uint32_t ui = p >> 1, m = p & 1;
+                        const unsigned char* img = s_gu + (size_t)ui * P.img_bytes;
+                        const uint4* nib = reinterpret_cast<const uint4*>(img);
+                        const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)2 * nb * 16 * 16);
+                        for (uint32_t b = r; b < nb; b += wpp)
+                            acc += tk_dot(nib[(m * nb + b) * 16 + col], scl[(m * nb + b) * 16 + col], xq[b]);
+                    }
+                    float* wp = red;  // [npair * wpp][16]
+                    if (p < npair) wp[(p * wpp + r) * 16 + col] = acc;
+                    tk_sync();
+                    TK_MARK(2)
+                    if ((uint32_t)tid < nu * 16) {
+                        const uint32_t ui = tid / 16, cc = tid % 16;
+                        float gs = 0.0f, up = 0.0f;
+#pragma unroll 1
+                        for (uint32_t q = 0; q < wpp; ++q) {
+                            gs += wp[((2 * ui) * wpp + q) * 16 + cc];
+                            up += wp[((2 * ui + 1) * wpp + q) * 16 + cc];
+                        }
+                        a.hb[(size_t)(c + ui * G) * 16 + cc] = gelu_tanh_ref(gs) * up;
+                    }
+                }
+                // the q|k|v sums were consumed by this layer's ATTN step
+                if (c == G - 1) {
+#pragma unroll 1
+                    for (uint32_t i = tid; i < QKVW; i += TK_THREADS) a.acc_qkv[i] = 0;
+                }
+            } else {
+                // ---------------- 64-column tiles: QKV, O, DOWN (one), HEAD (ring) ----------------
+                const uint32_t ntile = k == TK_S_HEAD ? (P.units > c ? (P.units - c + G - 1) / G : 0) : (has ? 1 : 0);
+                const int full = k == TK_S_QKV ? TK_MB_QKV : (k == TK_S_O ? TK_MB_O : TK_MB_DOWN);
+                long long* acc = k == TK_S_QKV ? a.acc_qkv : (k == TK_S_O ? a.acc_o : a.acc_dn);
+                const uint32_t accw = k == TK_S_QKV ? QKVW : H;
+                const unsigned char* slot = k == TK_S_QKV ? s_qkv : (k == TK_S_O ? s_o : s_down);
+                if (ntile == 0 && k != TK_S_HEAD) wait_slot(full);
+#pragma unroll 1
+                for (uint32_t i = 0; i < ntile; ++i) {
+                    const uint32_t r = i % a.head_ring;
+                    const unsigned char* img = slot;
+                    if (k == TK_S_HEAD) {
+                        wait_slot(TK_MB_HEAD + r);
+                        img = s_qkv + (size_t)r * P.img_bytes;
+                    } else {
+                        wait_slot(full);
+                    }
+                    TK_MARK(1)
+                    tk_tile64(img, P.nb, xq, red);
+                    if (k == TK_S_HEAD) {
+                        if (tid == 0) mbar_arrive(&mb[TK_ME_HEAD + r]);  // the producer refills it
+                        if (warp == 0) {
+                            const uint32_t t = c + i * G;
+                            float v0 = red[lane], v1 = red[lane + 32];
+                            a.logits[(size_t)t * 64 + lane] = v0;
+                            a.logits[(size_t)t * 64 + lane + 32] = v1;
+                            uint32_t ix = t * 64 + lane;
+                            if (v1 > v0) { v0 = v1; ix += 32; }
+                            if (v0 > bv || (v0 == bv && ix < bi)) { bv = v0; bi = ix; }
+                        }
+                    } else if (tid < 64) {
+                        const uint32_t col = (c / P.ks) * 64 + tid;
+                        if (col < accw) red_add_s64(&acc[col], tk_fix(red[tid], a.err));
+                    }
+                }
+                TK_MARK(2)
+                if (k == TK_S_HEAD && warp == 0) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                    }
+                    if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
+                }
+                // the o-proj sums were consumed by this layer's GU step
+                if (k == TK_S_DOWN && c == G - 1) {
+#pragma unroll 1
+                    for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_o[i] = 0;
+                }
+            }
+        }
+
+        // ---------------- grid barrier; the step's slots go back to the producer ----------------
         ++nbar;
         tk_sync();
         if (tid == 0) {
@@ -444,10 +758,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
                     a.trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
             }
             red_release_add_u64(a.bar, 1ull);
-        }
-    };
-    auto bar_wait = [&]() {
-        if (tid == 0) {
+            if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
             const uint64_t target = base + (uint64_t)nbar * G;
             uint32_t it = 0;
             // acquire load + the closing bar.sync order every thread's later
@@ -466,353 +777,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const TkArgs a) {
             }
         }
         tk_sync();
-    };
-
-    const uint32_t QKVW = a.QD + 2 * a.KVD;
-    for (uint32_t l = 0; l < L; ++l) {
-        const TkLayer& Ly = a.layers[l];
-        // ============================ QKV ============================
-        wait_slot(TK_MB_CQKV);
-        if (l == 0) tk_norm_prologue(a, 0, nullptr, nullptr, 0, nullptr, cq + H, a.x0, xn, red32);
-        else tk_norm_prologue(a, 1, a.x1, a.dn_part, a.down.ks, cq, cq + H, a.x0, xn, red32);
-        TK_MARK(0)
-        if (c < a.qkv.units) {
-            const uint32_t tile = c / a.qkv.ks, kc = c % a.qkv.ks;
-            tk_prep(xn, kc * a.qkv.nb, a.qkv.nb, xq);
-            wait_slot(TK_MB_QKV);
-            TK_MARK(1)
-            tk_tile<64>(s_qkv, a.qkv.nb, xq, red);
-            if (tid < 64) a.qkv_part[(size_t)kc * QKVW + tile * 64 + tid] = red[tid];
-        } else {
-            wait_slot(TK_MB_QKV);
-        }
-        bar_arrive();
-        release_slot(TK_ME_QKV);
-        bar_wait();
-
-        // ============================ ATTN ============================
-        const TkWin w = tk_window(pos, Ly.window);
-        // every CTA consumes the attention-constants fill (its mbarrier phase
-        // must be tracked even by CTAs with no keys this layer)
-        wait_slot(TK_MB_CATT);
-        {
-            const uint32_t n = w.j1 - w.j0;
-            float* qs = reinterpret_cast<float*>(sm + a.off_q);       // [4][256] pre-scaled
-            __half* kn = reinterpret_cast<__half*>(qs + 4 * 256);      // [256]
-            __half* vn = kn + 256;                                     // [256]
-            float* sc = reinterpret_cast<float*>(sm + a.off_sc);       // [4][chunk_max]
-            if (c < w.nsplit) {
-                // q|k|v = sum of the K-split partials, every load in flight at once
-                float* qkvs = red;  // [QKVW]
-                {
-                    float ld[TK_MAXJ][TK_MAXP];
-#pragma unroll
-                    for (int r = 0; r < TK_MAXJ; ++r) {
-                        const uint32_t i = tid + r * TK_THREADS;
-#pragma unroll
-                        for (int k = 0; k < TK_MAXP; ++k)
-                            ld[r][k] = (i < QKVW && (uint32_t)k < a.qkv.ks) ? a.qkv_part[(size_t)k * QKVW + i] : 0.0f;
-                    }
-#pragma unroll
-                    for (int r = 0; r < TK_MAXJ; ++r) {
-                        const uint32_t i = tid + r * TK_THREADS;
-                        float t = 0.0f;
-#pragma unroll
-                        for (int k = 0; k < TK_MAXP; ++k) t += ld[r][k];
-                        if (i < QKVW) qkvs[i] = t;
-                    }
-                }
-                tk_sync();
-                TK_MARK(0)
-                if (warp < 6) {
-                    const uint32_t off = warp < 4 ? warp * 256 : (warp == 4 ? a.QD : a.QD + a.KVD);
-                    float v[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = qkvs[off + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4))];
-                    const float* cosT = rope + (Ly.global ? 256 : 0);
-                    const float* sinT = cosT + 128;
-                    if (warp < 4) {
-                        tk_qk_post(v, ca, cosT, sinT, a.eps);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            qs[warp * 256 + 4 * lane + i] = v[i] * a.attn_scale;
-                            qs[warp * 256 + 128 + 4 * lane + i] = v[4 + i] * a.attn_scale;
-                        }
-                    } else {
-                        if (warp == 4) tk_qk_post(v, ca + 256, cosT, sinT, a.eps);
-                        __half* dst = warp == 4 ? kn : vn;
-                        __half* cache = warp == 4 ? Ly.kc : Ly.vc;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
-                            dst[4 * lane + i] = lo;
-                            dst[128 + 4 * lane + i] = hi;
-                            if (c == 0) {
-                                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
-                                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
-                            }
-                        }
-                    }
-                }
-                TK_MARK(4)
-                wait_slot(TK_MB_KV);
-                TK_MARK(5)
-                tk_sync();
-                TK_MARK(1)
-                const __half* ks = reinterpret_cast<const __half*>(s_kv);
-                const __half* vs = ks + (size_t)a.chunk_max * 256;
-                float q[4][8];
-#pragma unroll
-                for (int h = 0; h < 4; ++h)
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) q[h][i] = qs[h * 256 + 8 * lane + i];
-                TK_MARK(6)
-                for (uint32_t jj = warp; jj < n; jj += TK_WARPS) {
-                    const uint32_t j = w.j0 + jj;
-                    const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(kn + 8 * lane)
-                                               : *reinterpret_cast<const uint4*>(ks + (size_t)jj * 256 + 8 * lane);
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-                    float kf[8];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 f = __half22float2(h2[i]);
-                        kf[2 * i] = f.x;
-                        kf[2 * i + 1] = f.y;
-                    }
-                    float s4[4];
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) acc = fmaf(q[h][i], kf[i], acc);
-                        s4[h] = acc;
-                    }
-                    const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
-                    if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
-                }
-                tk_sync();
-                TK_MARK(2)
-                if (warp < 4) {
-                    float m = -INFINITY;
-                    for (uint32_t jj = lane; jj < n; jj += 32) m = fmaxf(m, sc[warp * a.chunk_max + jj]);
-                    m = warp_max(m);
-                    float sum = 0.0f;
-                    for (uint32_t jj = lane; jj < n; jj += 32) {
-                        const float p = expf(sc[warp * a.chunk_max + jj] - m);
-                        sc[warp * a.chunk_max + jj] = p;
-                        sum += p;
-                    }
-                    sum = warp_sum(sum);
-                    if (lane == 0) {
-                        a.att_stat[((size_t)c * 4 + warp) * 2] = m;
-                        a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
-                    }
-                }
-                tk_sync();
-                {
-                    const uint32_t dp = tid & 127, qr = tid >> 7;
-                    float acc[4][2] = {};
-                    for (uint32_t jj = qr; jj < n; jj += 4) {
-                        const uint32_t j = w.j0 + jj;
-                        const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vn)[dp]
-                                                    : reinterpret_cast<const __half2*>(vs + (size_t)jj * 256)[dp];
-                        const float2 vf = __half22float2(hv);
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            const float p = sc[h * a.chunk_max + jj];
-                            acc[h][0] = fmaf(p, vf.x, acc[h][0]);
-                            acc[h][1] = fmaf(p, vf.y, acc[h][1]);
-                        }
-                    }
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        red[(qr * 4 + h) * 256 + 2 * dp] = acc[h][0];
-                        red[(qr * 4 + h) * 256 + 2 * dp + 1] = acc[h][1];
-                    }
-                }
-                tk_sync();
-                for (uint32_t i = tid; i < 4 * 256; i += TK_THREADS)
-                    a.att_part[(size_t)c * 1024 + i] = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
-                TK_MARK(3)
-            } else {
-                wait_slot(TK_MB_KV);
-            }
-        }
-        bar_arrive();
-        release_slot(TK_ME_ATT);
-        bar_wait();
-
-        // ============================ O ============================
-        if (c < a.o.units) {
-            const uint32_t tile = c / a.o.ks, kc = c % a.o.ks;
-            const uint32_t d0 = kc * a.o.nb * 32, nd = a.o.nb * 32, h = d0 / 256;
-            // the splits' statistics and this CTA's slice of their partials are
-            // loaded together (one round trip), then merged
-            const uint32_t d = tid % nd, g = tid / nd, ng = TK_THREADS / nd;
-            float pv[TK_OPV];
-#pragma unroll
-            for (int r = 0; r < TK_OPV; ++r) {
-                const uint32_t s_ = g + r * ng;
-                pv[r] = (g < ng && s_ < w.nsplit) ? a.att_part[(size_t)s_ * 1024 + d0 + d] : 0.0f;
-            }
-            float m = -INFINITY, l_ = 0.0f;
-            if ((uint32_t)tid < w.nsplit) {
-                m = a.att_stat[((size_t)tid * 4 + h) * 2];
-                l_ = a.att_stat[((size_t)tid * 4 + h) * 2 + 1];
-            }
-            float* wts = red;            // [nsplit] exp(m_s - M)
-            float* comb = red + 512;     // [4][nd]
-            float M = warp_max(m);
-            if (lane == 0) red32[warp] = M;
-            tk_sync();
-            M = warp_max(lane < TK_WARPS ? red32[lane] : -INFINITY);
-            tk_sync();
-            const float e = (uint32_t)tid < w.nsplit ? expf(m - M) : 0.0f;
-            if ((uint32_t)tid < w.nsplit) wts[tid] = e;
-            const float Lsum = tk_block_sum(l_ * e, red32);
-            tk_sync();
-            {
-                float acc = 0.0f;
-                if (g < ng) {
-#pragma unroll
-                    for (int r = 0; r < TK_OPV; ++r) {
-                        const uint32_t s_ = g + r * ng;
-                        if (s_ < w.nsplit) acc += pv[r] * wts[s_];
-                    }
-                    // splits beyond TK_OPV * ng (long windows): remaining loads
-                    for (uint32_t s_ = g + TK_OPV * ng; s_ < w.nsplit; s_ += ng)
-                        acc += a.att_part[(size_t)s_ * 1024 + d0 + d] * wts[s_];
-                    comb[g * nd + d] = acc;
-                }
-                tk_sync();
-                if ((uint32_t)tid < nd) {
-                    float t = 0.0f;
-                    for (uint32_t gg = 0; gg < ng; ++gg) t += comb[gg * nd + tid];
-                    xn[tid] = t / Lsum;
-                }
-            }
-            tk_sync();
-            TK_MARK(0)
-            tk_prep(xn, 0, a.o.nb, xq);
-            wait_slot(TK_MB_O);
-            TK_MARK(1)
-            tk_tile<64>(s_o, a.o.nb, xq, red);
-            if (tid < 64) a.o_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
-        } else {
-            wait_slot(TK_MB_O);
-        }
-        bar_arrive();
-        release_slot(TK_ME_O);
-        bar_wait();
-
-        // ============================ GU ============================
-        wait_slot(TK_MB_CGU);
-        tk_norm_prologue(a, 1, a.x0, a.o_part, a.o.ks, cg, cg + H, a.x1, xn, red32);
-        TK_MARK(0)
-        if (c < a.gu.units) {
-            const uint32_t nb = a.gu.nb;
-            tk_prep(xn, 0, nb, xq);
-            wait_slot(TK_MB_GU);
-            TK_MARK(1)
-            uint32_t nu = 0;
-            for (uint32_t u = c; u < a.gu.units; u += G) ++nu;
-            // half-warp workers (16 lanes = 16 columns), each fixed on one
-            // (unit, matrix) pair and a stride of blocks, accumulating in a register
-            const uint32_t worker = tid >> 4, col = tid & 15, nwk = TK_THREADS / 16;
-            const uint32_t npair = nu * 2, wpp = nwk / npair;
-            const uint32_t p = worker / wpp, r = worker % wpp;
-            float acc = 0.0f;
-            if (p < npair) {
-                const uint32_t ui = p >> 1, m = p & 1;
-                const unsigned char* img = s_gu + (size_t)ui * a.gu.img_bytes;
-                const uint4* nib = reinterpret_cast<const uint4*>(img);
-                const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)2 * nb * 16 * 16);
-                for (uint32_t b = r; b < nb; b += wpp)
-                    acc += tk_dot(nib[(m * nb + b) * 16 + col], scl[(m * nb + b) * 16 + col], xq[b]);
-            }
-            float* wp = red;  // [npair * wpp][16]
-            if (p < npair) wp[(p * wpp + r) * 16 + col] = acc;
-            tk_sync();
-            TK_MARK(2)
-            if ((uint32_t)tid < nu * 16) {
-                const uint32_t ui = tid / 16, cc = tid % 16;
-                float g = 0.0f, up = 0.0f;
-                for (uint32_t k = 0; k < wpp; ++k) {
-                    g += wp[((2 * ui) * wpp + k) * 16 + cc];
-                    up += wp[((2 * ui + 1) * wpp + k) * 16 + cc];
-                }
-                a.hb[(size_t)(c + ui * G) * 16 + cc] = gelu_tanh_ref(g) * up;
-            }
-        } else {
-            wait_slot(TK_MB_GU);
-        }
-        bar_arrive();
-        release_slot(TK_ME_GU);
-        bar_wait();
-
-        // ============================ DOWN ============================
-        if (c < a.down.units) {
-            const uint32_t tile = c / a.down.ks, kc = c % a.down.ks, nb = a.down.nb;
-            // hb limbs for blocks [kc*nb, kc*nb + nb): all loads first
-            float hv[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t b = warp + r * TK_WARPS;
-                hv[r] = b < nb ? a.hb[(size_t)(kc * nb + b) * 32 + lane] : 0.0f;
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const uint32_t b = warp + r * TK_WARPS;
-                if (b < nb) xq_prep_block(hv[r], &xq[b]);
-            }
-            tk_sync();
-            TK_MARK(0)
-            wait_slot(TK_MB_DOWN);
-            TK_MARK(1)
-            tk_tile<64>(s_down, nb, xq, red);
-            if (tid < 64) a.dn_part[(size_t)kc * H + tile * 64 + tid] = red[tid];
-        } else {
-            wait_slot(TK_MB_DOWN);
-        }
-        bar_arrive();
-        release_slot(TK_ME_DOWN);
-        bar_wait();
     }
 
-    // ============================ HEAD ============================
+    // ---------------- sample (greedy): lowest-index maximum over the CTAs ----------------
     if (a.want_logits) {
-        wait_slot(TK_MB_CQKV);
-        tk_norm_prologue(a, 1, a.x1, a.dn_part, a.down.ks, cq, cq + H, nullptr, xn, red32);
-        tk_prep(xn, 0, a.head.nb, xq);
-        float bv = -INFINITY;
-        uint32_t bi = 0xFFFFFFFFu;
-        uint32_t i = 0;
-        for (uint32_t t = c; t < a.head.units; t += G, ++i) {
-            const uint32_t r = i % a.head_ring;
-            wait_slot(TK_MB_HEAD + r);
-            tk_tile<64>(s_gu + (size_t)r * a.head.img_bytes, a.head.nb, xq, red);
-            release_slot(TK_ME_HEAD + r);  // the producer refills it while the argmax runs
-            if (warp == 0) {
-                float v0 = red[lane], v1 = red[lane + 32];
-                a.logits[(size_t)t * 64 + lane] = v0;
-                a.logits[(size_t)t * 64 + lane + 32] = v1;
-                uint32_t ix = t * 64 + lane;
-                if (v1 > v0) { v0 = v1; ix += 32; }
-                if (v0 > bv || (v0 == bv && ix < bi)) { bv = v0; bi = ix; }
-            }
-            tk_sync();
-        }
-        if (warp == 0) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
-        }
-        bar_arrive();
-        bar_wait();
         if (a.greedy && c == 0 && warp == 0) {
             float v = -INFINITY;
             uint32_t ix = 0xFFFFFFFFu;
