@@ -122,6 +122,30 @@ xp_status xp_mv_km4_bs_split(void* stream, float* partial, const float* in, cons
                              const uint32_t* sc, uint32_t rows, uint32_t cols, uint32_t split);
 /* kernels/llm_matvec.cl:128-135 */
 xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t cols, uint32_t split);
+
+/* ---- many matvecs in one launch ---------------------------------------------
+ * The reference submits a token's matvecs as mv_km4_bs dispatches recorded in
+ * one Batch (examples/llm/decode.cpp:1634-1780, include/vulkore/launch.hpp:
+ * 179-213); each job here computes exactly that kernel's output
+ * (kernels/llm_matvec.cl:422-434) from the same planes, and a plan runs all of
+ * its jobs in ONE persistent launch that streams the weights at HBM rate.
+ * A plan owns device memory (job table, activation limbs); create it once, run
+ * it any number of times on any stream of its device, destroy it last. Jobs
+ * may share an input vector; outputs must not overlap. rows % 128 == 0,
+ * cols % 64 == 0, at most 512 jobs. */
+typedef struct xp_mv_job {
+    float* out;              /* [cols] */
+    const float* in;         /* [rows] */
+    const uint32_t* wq;      /* nibble plane (uint4 per 32 rows x column) */
+    const uint32_t* sc;      /* bf16 scale plane (uint2 per 128 rows x column) */
+    uint32_t rows, cols;
+} xp_mv_job;
+typedef struct xp_mv_plan xp_mv_plan;
+xp_status xp_mv_plan_create(const xp_mv_job* jobs, uint32_t n, xp_mv_plan** plan);
+xp_status xp_mv_plan_run(xp_mv_plan* plan, void* stream);
+/* algorithmic bytes one run reads and writes (nibbles + scales + in + out) */
+xp_status xp_mv_plan_bytes(const xp_mv_plan* plan, uint64_t* bytes);
+void xp_mv_plan_destroy(xp_mv_plan* plan);
 /* kernels/llm_transformer.cl:96-116 */
 xp_status xp_rmsnorm_sumsq(void* stream, float* partial, const float* in, uint32_t n, uint32_t nparts);
 xp_status xp_rmsnorm_apply_gemma(void* stream, float* out, const float* in, const float* w,

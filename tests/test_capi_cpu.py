@@ -11,6 +11,8 @@ import numpy as np
 import pytest
 
 from xpose_b200._lib import LIB_PATH, XpError, exported_symbols, lib
+
+XP_ERR_INVALID = -1
 from xpose_b200.vulkore import Grid, Kernel, Program, _marshal, launch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -111,3 +113,19 @@ def test_no_device_is_reported_not_crashed():
 
 def test_fence_null_wait_is_signaled():
     assert lib().xp_fence_wait(None, 0) == 0
+
+
+def test_mv_plan_validation_on_host():
+    """xp_mv_plan_create checks every job before touching a device."""
+    class Job(C.Structure):
+        _fields_ = [("out", C.c_void_p), ("inp", C.c_void_p), ("wq", C.c_void_p), ("sc", C.c_void_p),
+                    ("rows", C.c_uint32), ("cols", C.c_uint32)]
+    plan = C.c_void_p()
+    bad_shape = (Job * 1)(Job(8, 8, 8, 8, 1152, 100))
+    assert lib().xp_mv_plan_create(C.cast(bad_shape, C.c_void_p), 1, C.byref(plan)) == XP_ERR_INVALID
+    assert b"multiple" in lib().xp_last_error()
+    null_ptr = (Job * 1)(Job(8, None, 8, 8, 1152, 64))
+    assert lib().xp_mv_plan_create(C.cast(null_ptr, C.c_void_p), 1, C.byref(plan)) == XP_ERR_INVALID
+    assert lib().xp_mv_plan_create(C.cast(null_ptr, C.c_void_p), 0, C.byref(plan)) == XP_ERR_INVALID
+    assert not plan.value
+    lib().xp_mv_plan_destroy(None)

@@ -87,6 +87,10 @@ _SIGS = {
     "xp_mv_km4_bs": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 2),
     "xp_mv_km4_bs_split": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 3),
     "xp_mv_reduce": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
+    "xp_mv_plan_create": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "xp_mv_plan_run": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "xp_mv_plan_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),
+    "xp_mv_plan_destroy": (None, [C.c_void_p]),
     "xp_rmsnorm_sumsq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     "xp_rmsnorm_apply_gemma": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 2 + [C.c_float]),
     "xp_rmsnorm_heads_gemma": (C.c_int, [C.c_void_p] + [C.c_void_p] * 3 + [C.c_uint32] * 2 + [C.c_float]),

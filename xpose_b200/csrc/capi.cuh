@@ -13,6 +13,7 @@
 #include <utility>
 #include <vector>
 
+#include "mv_stream.cuh"
 #include "ops.cuh"
 #include "runtime.cuh"
 
@@ -641,6 +642,137 @@ xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t 
     CHECK_PTR(out); CHECK_PTR(partial);
     ops::mv_reduce<<<(cols + 255) / 256, 256, 0, (cudaStream_t)stream>>>(out, partial, cols, split);
     return cuda_status(cudaGetLastError(), "mv_reduce");
+}
+struct xp_mv_plan {
+    int device = 0;
+    MvsJob* jobs = nullptr;
+    MvsSrc* src = nullptr;
+    XBlk* xq = nullptr;
+    uint32_t* next = nullptr;
+    float* part = nullptr;
+    uint32_t* arrive = nullptr;
+    uint32_t njobs = 0, nstrips = 0, nsrc = 0, nxq = 0, grid = 0;
+    bool smem_x = false;
+    uint64_t bytes = 0;
+};
+xp_status xp_mv_plan_create(const xp_mv_job* jobs, uint32_t n, xp_mv_plan** plan) {
+    CHECK_PTR(jobs); CHECK_PTR(plan);
+    *plan = nullptr;
+    if (n == 0 || n > MVS_MAXJOBS) return fail(XP_ERR_INVALID, "xp_mv_plan_create: %u jobs (1..%u)", n, MVS_MAXJOBS);
+    std::vector<MvsJob> hj(n);
+    std::vector<MvsSrc> hs;
+    std::vector<uint32_t> src_of(n);
+    uint32_t strips = 0, nxq = 0;
+    uint64_t bytes = 0;
+    size_t part_floats = 0, arrive_words = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const xp_mv_job& j = jobs[i];
+        if (!j.out || !j.in || !j.wq || !j.sc)
+            return fail(XP_ERR_INVALID, "xp_mv_plan_create: job %u has a null pointer", i);
+        if (j.rows == 0 || j.rows % 128 || j.cols == 0 || j.cols % 64)
+            return fail(XP_ERR_INVALID, "xp_mv_plan_create: job %u: rows must be a multiple of 128 and cols of 64 "
+                        "(got %u x %u)", i, j.rows, j.cols);
+        uint32_t k = 0;
+        while (k < hs.size() && !(hs[k].x == j.in && hs[k].nblk == j.rows / 32)) ++k;
+        if (k == hs.size()) {
+            hs.push_back(MvsSrc{j.in, j.rows / 32, nxq});
+            nxq += j.rows / 32;
+        }
+        src_of[i] = k;
+        // tall matrices split K into chunks of about MVS_CHUNK blocks so that
+        // every SM has work (down-proj: 18 groups, 216 blocks each)
+        const uint32_t nblk = j.rows / 32;
+        const uint32_t ks = std::max<uint32_t>(1, nblk / MVS_CHUNK);
+        const uint32_t cb = ((nblk + ks - 1) / ks + 3) & ~3u;
+        const uint32_t kspl = (nblk + cb - 1) / cb;
+        hj[i] = MvsJob{reinterpret_cast<const uint4*>(j.wq), reinterpret_cast<const uint2*>(j.sc), j.out, nullptr,
+                       nullptr, nblk, j.cols, strips, hs[k].off, kspl, cb};
+        strips += j.cols / 64 * kspl;
+        if (kspl > 1) { part_floats += (size_t)j.cols * kspl; arrive_words += j.cols / 64; }
+        bytes += (uint64_t)j.rows * j.cols / 2 + (uint64_t)j.rows * j.cols / 16 + 4ull * j.rows + 4ull * j.cols;
+    }
+    auto* p = new xp_mv_plan();
+    cudaGetDevice(&p->device);
+    auto cleanup = [&](const char* what, cudaError_t e) {
+        xp_mv_plan_destroy(p);
+        return fail(XP_ERR_OOM, "xp_mv_plan_create: %s: %s", what, cudaGetErrorString(e));
+    };
+    cudaError_t e;
+    if ((e = cudaMalloc(&p->xq, (size_t)nxq * sizeof(XBlk))) != cudaSuccess) return cleanup("limbs", e);
+    if (part_floats) {
+        if ((e = cudaMalloc(&p->part, part_floats * 4)) != cudaSuccess) return cleanup("partials", e);
+        if ((e = cudaMalloc(&p->arrive, arrive_words * 4)) != cudaSuccess) return cleanup("counters", e);
+        if ((e = cudaMemset(p->arrive, 0, arrive_words * 4)) != cudaSuccess) return cleanup("counters", e);
+        size_t po = 0, ao = 0;
+        for (auto& j : hj)
+            if (j.ksplit > 1) {
+                j.part = p->part + po;
+                j.arrive = p->arrive + ao;
+                po += (size_t)j.cols * j.ksplit;
+                ao += j.cols / 64;
+            }
+    }
+    if ((e = cudaMalloc(&p->jobs, n * sizeof(MvsJob))) != cudaSuccess) return cleanup("jobs", e);
+    if ((e = cudaMalloc(&p->src, hs.size() * sizeof(MvsSrc))) != cudaSuccess) return cleanup("sources", e);
+    if ((e = cudaMalloc(&p->next, 16)) != cudaSuccess) return cleanup("counter", e);
+    if ((e = cudaMemcpy(p->jobs, hj.data(), n * sizeof(MvsJob), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return cleanup("upload", e);
+    if ((e = cudaMemcpy(p->src, hs.data(), hs.size() * sizeof(MvsSrc), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return cleanup("upload", e);
+    p->njobs = n;
+    p->nstrips = strips;
+    p->nsrc = (uint32_t)hs.size();
+    p->nxq = nxq;
+    p->bytes = bytes;
+    p->smem_x = (size_t)nxq * sizeof(XBlk) <= MVS_SMEM_X_MAX;
+    int per_sm = 0;
+    if (p->smem_x) {
+        cudaFuncSetAttribute(mv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MVS_SMEM_X_MAX);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mv_stream_kernel<true>, MVS_THREADS,
+                                                      (size_t)nxq * sizeof(XBlk));
+    } else {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mv_stream_kernel<false>, MVS_THREADS, 0);
+    }
+    p->grid = (uint32_t)sm_count() * (uint32_t)std::max(per_sm, 1);
+    *plan = p;
+    return XP_OK;
+}
+xp_status xp_mv_plan_run(xp_mv_plan* p, void* stream) {
+    CHECK_PTR(p);
+    const cudaStream_t st = (cudaStream_t)stream;
+    mv_stream_prep_kernel<<<(p->nxq * 32 + 255) / 256, 256, 0, st>>>(p->src, p->nsrc, p->nxq, p->xq, p->next);
+    XP_CUDA_TRY(cudaGetLastError());
+    // the stream kernel launches while the limbs are prepared and waits for
+    // them (griddepcontrol.wait) after staging its job table
+    MvsArgs a{p->jobs, p->xq, p->njobs, p->nstrips, p->nxq, p->next};
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3(p->grid);
+    c.blockDim = dim3(MVS_THREADS);
+    c.dynamicSmemBytes = p->smem_x ? (size_t)p->nxq * sizeof(XBlk) : 0;
+    c.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = at;
+    c.numAttrs = 1;
+    const cudaError_t e = p->smem_x ? cudaLaunchKernelEx(&c, mv_stream_kernel<true>, a)
+                                    : cudaLaunchKernelEx(&c, mv_stream_kernel<false>, a);
+    return cuda_status(e, "mv_plan_run");
+}
+xp_status xp_mv_plan_bytes(const xp_mv_plan* p, uint64_t* bytes) {
+    CHECK_PTR(p); CHECK_PTR(bytes);
+    *bytes = p->bytes;
+    return XP_OK;
+}
+void xp_mv_plan_destroy(xp_mv_plan* p) {
+    if (!p) return;
+    cudaFree(p->jobs);
+    cudaFree(p->src);
+    cudaFree(p->xq);
+    cudaFree(p->next);
+    cudaFree(p->part);
+    cudaFree(p->arrive);
+    delete p;
 }
 xp_status xp_rmsnorm_sumsq(void* stream, float* partial, const float* in, uint32_t n, uint32_t nparts) {
     CHECK_PTR(partial); CHECK_PTR(in);
