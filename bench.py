@@ -21,6 +21,12 @@ roofline : the persistent token kernel (the only kernel of a decode step):
         average device duration.
 cpu_baseline : the CPU restatement of the same decode (oracle/, "port"),
         timed on this host's cores over a bounded sample.
+matvec : BASELINE configs 1 and 2 on the streaming int4 matvec
+        (xp_mv_plan_*: many matvecs in one persistent launch), timed with CUDA
+        events over whole plan runs (limb prep included): config 1 = W
+        6912x1152 N(0, 0.02) packed by the reference packer, x N(0, 1), seed 0,
+        64 distinct copies of W per run (289 MB > L2); config 2 = the session's
+        own per-token sweep (26 x q, k, v, o, gate, up, down + LM head, 567 MB).
 
 Under torchrun (N > 1) each rank decodes its own independent sequence on its
 own GPU (data-parallel replicas, weak scaling); value = all ranks' tokens /
@@ -52,15 +58,95 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--ncu-case", choices=["full", "small", "multi"], default=None,
+    ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
-                         "five-kernel graph path on the bench model")
+                         "five-kernel graph path on the bench model, 'matvec' = three runs of the config-1 "
+                         "matvec plan")
     return ap.parse_args()
 
 
+class MvJob(__import__("ctypes").Structure):
+    import ctypes as _C
+    _fields_ = [("out", _C.c_void_p), ("inp", _C.c_void_p), ("wq", _C.c_void_p), ("sc", _C.c_void_p),
+                ("rows", _C.c_uint32), ("cols", _C.c_uint32)]
+
+
+def config1_plan(copies=64, rows=1152, cols=6912):
+    """W (cols x rows) N(0, 0.02) packed by the reference
+    packer (device port, bit-exact), x N(0, 1), seed 0; `copies` distinct copies
+    of the packed planes in one matvec plan. Returns (plan, keep-alive list)."""
+    import ctypes as C
+    import torch
+    from xpose_b200._lib import check, lib
+    w = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+    x = torch.empty(rows, dtype=torch.float32, device="cuda")
+    check(lib().xp_gen_normal(None, w.data_ptr(), rows * cols, 0, 0, 1, 0.02))
+    check(lib().xp_gen_normal(None, x.data_ptr(), rows, 0, 0, 2, 1.0))
+    wq = torch.empty(rows * cols // 8, dtype=torch.int32, device="cuda")
+    sc = torch.empty(rows * cols // 64, dtype=torch.int32, device="cuda")
+    check(lib().xp_pack_km4bf16(None, w.data_ptr(), rows, cols, wq.data_ptr(), sc.data_ptr()))
+    del w
+    keep = [x]
+    jobs = []
+    for _ in range(copies):
+        cw, cs, out = wq.clone(), sc.clone(), torch.empty(cols, device="cuda")
+        keep += [cw, cs, out]
+        jobs.append(MvJob(out.data_ptr(), x.data_ptr(), cw.data_ptr(), cs.data_ptr(), rows, cols))
+    arr = (MvJob * len(jobs))(*jobs)
+    plan = C.c_void_p()
+    check(lib().xp_mv_plan_create(C.cast(arr, C.c_void_p), len(jobs), C.byref(plan)))
+    return plan, keep
+
+
+def matvec_bench(sess, peak):
+    """BASELINE configs 1 and 2 on the streaming matvec (GB/s of algorithmic bytes)."""
+    import ctypes as C
+    import torch
+    from xpose_b200._lib import check, lib
+    ms2, b2, _ = sess.profile_matvec(iters=20)
+    plan, keep = config1_plan()
+    try:
+        b1 = C.c_uint64()
+        check(lib().xp_mv_plan_bytes(plan, C.byref(b1)))
+        for _ in range(3):
+            check(lib().xp_mv_plan_run(plan, None))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 20
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            check(lib().xp_mv_plan_run(plan, None))
+        e1.record()
+        torch.cuda.synchronize()
+        ms1 = e0.elapsed_time(e1) / n
+    finally:
+        lib().xp_mv_plan_destroy(plan)
+        del keep
+
+    def entry(workload, nbytes, ms):
+        gbs = nbytes / ms / 1e6
+        return {"workload": workload, "bytes": int(nbytes), "us": round(ms * 1000.0, 2), "GB/s": round(gbs, 1),
+                "frac": round(gbs / peak, 4)}
+    return {"kernel": "mv_stream_kernel (xp_mv_plan_run: limb prep + one persistent streaming launch)",
+            "peak": peak, "unit": "GB/s",
+            "config1": entry("W 6912x1152 int4 matvec, 64 distinct weight copies per run", b1.value, ms1),
+            "config2": entry("per-token matvec sweep: 26 x (q, k, v, o, gate, up, down) + LM head", b2, ms2)}
+
+
 def ncu_case(which):
-    """A short, untimed decode used as the target of the ncu captures in profiles/."""
+    """A short, untimed run used as the target of the ncu captures in profiles/."""
+    if which == "matvec":
+        import torch
+        from xpose_b200._lib import check, lib
+        plan, keep = config1_plan()
+        for _ in range(3):
+            check(lib().xp_mv_plan_run(plan, None))
+        torch.cuda.synchronize()
+        lib().xp_mv_plan_destroy(plan)
+        print("ncu case matvec: 3 runs of the config-1 plan")
+        return 0
     from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling
     if which == "multi":
         os.environ["XP_ENGINE_MULTI"] = "1"
@@ -353,6 +439,13 @@ def main():
         except Exception as e:  # the checker arm must not hide the GPU result
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
 
+    mv = None
+    if rank == 0 and not args.no_matvec:
+        try:
+            mv = matvec_bench(sess, peak)
+        except Exception as e:  # a failure here must not hide the decode result
+            mv = {"error": str(e)}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K,
@@ -374,6 +467,7 @@ def main():
                          "avg_launch_us": round(ms_max / K * 1000.0, 2), "peak_kind": peak_kind},
             "clocks": clock_info,
             "cpu_baseline": cpu,
+            "matvec": mv,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

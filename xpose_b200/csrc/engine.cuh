@@ -104,6 +104,7 @@ struct xp_session {
         if (st) cudaStreamSynchronize(st);
         for (cudaGraphExec_t g : {g_dev, g_io, g_prefill, g_mv})
             if (g) cudaGraphExecDestroy(g);
+        if (mv_plan) xp_mv_plan_destroy(mv_plan);
         for (cudaEvent_t e : {ev_done, ev_a, ev_b})
             if (e) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
@@ -136,6 +137,8 @@ struct xp_session {
     bool mv_only = false;       // record only the int4 matvecs (roofline profiling)
     uint64_t mv_bytes = 0;      // algorithmic bytes of the recorded matvecs
     cudaGraphExec_t g_mv = nullptr;
+    xp_mv_plan* mv_plan = nullptr;  // the token's matvecs as one streaming plan (profiling)
+    float* mv_out = nullptr;
 
     void count_mv(uint32_t rows, uint32_t cols, uint32_t nmat_same = 1) {
         // nibbles + bf16 scales + activation read (4 B/elt) + output (4 B/elt)
@@ -794,27 +797,42 @@ xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per
     cudaSetDevice(s->device);
     xp_status st = s->wait_prev();
     if (st != XP_OK) return st;
-    if (!s->g_mv) {
-        s->mv_only = true;
-        s->mv_bytes = 0;
-        st = s->capture(&s->g_mv, true, false);
-        s->mv_only = false;
-        if (st != XP_OK) return st;
-        s->mv_launches = s->launches;
-        s->mv_token_bytes = s->mv_bytes;
+    if (!s->mv_plan) {
+        // the token's int4 matvecs as one streaming plan: 26 x (q, k, v, o,
+        // gate, up, down) + LM head, on the session's packed planes
+        const uint32_t H = s->cfg.hidden, F = s->cfg.ffn, QD = s->q_dim();
+        std::vector<xp_mv_job> jobs;
+        size_t outs = s->cfg.vocab;
+        for (uint32_t l = 0; l < s->cfg.n_layers; ++l)
+            for (int m = 0; m < 7; ++m) outs += s->L[l].m[m].cols;
+        if ((st = s->alloc(&s->mv_out, outs)) != XP_OK) return st;
+        size_t off = 0;
+        auto add = [&](const QW& q) {
+            const float* in = q.rows == H ? s->xa : (q.rows == F ? s->hb : s->att);
+            jobs.push_back(xp_mv_job{s->mv_out + off, in, reinterpret_cast<const uint32_t*>(q.wq),
+                                     reinterpret_cast<const uint32_t*>(q.sc), q.rows, q.cols});
+            off += q.cols;
+        };
+        for (uint32_t l = 0; l < s->cfg.n_layers; ++l)
+            for (int m = 0; m < 7; ++m) add(s->L[l].m[m]);
+        add(s->lm);
+        (void)QD;
+        if ((st = xp_mv_plan_create(jobs.data(), (uint32_t)jobs.size(), &s->mv_plan)) != XP_OK) return st;
     }
-    // the matvec-only graph reads lm_xq as its activation: make it valid limbs
-    XP_CUDA_TRY(cudaGraphLaunch(s->g_mv, s->st));
+    if ((st = xp_mv_plan_run(s->mv_plan, s->st)) != XP_OK) return st;
     XP_CUDA_TRY(cudaEventRecord(s->ev_a, s->st));
-    for (uint32_t i = 0; i < iters; ++i) XP_CUDA_TRY(cudaGraphLaunch(s->g_mv, s->st));
+    for (uint32_t i = 0; i < iters; ++i)
+        if ((st = xp_mv_plan_run(s->mv_plan, s->st)) != XP_OK) return st;
     XP_CUDA_TRY(cudaEventRecord(s->ev_b, s->st));
     XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));
     XP_CUDA_TRY(cudaEventSynchronize(s->ev_b));
     float ms = 0;
     XP_CUDA_TRY(cudaEventElapsedTime(&ms, s->ev_a, s->ev_b));
+    uint64_t b = 0;
+    xp_mv_plan_bytes(s->mv_plan, &b);
     if (ms_per_token) *ms_per_token = ms / iters;
-    if (bytes_per_token) *bytes_per_token = s->mv_token_bytes;
-    if (launches_per_token) *launches_per_token = s->mv_launches;
+    if (bytes_per_token) *bytes_per_token = b;
+    if (launches_per_token) *launches_per_token = 2;  // limbs + the streaming matvec
     return XP_OK;
 }
 

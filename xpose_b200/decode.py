@@ -164,8 +164,9 @@ class DecodeSession:
         return d.value, b.value
 
     def profile_matvec(self, iters=20):
-        """(ms per token, algorithmic bytes per token, launches per token) of
-        the token's int4 matvecs replayed alone."""
+        """(ms, algorithmic bytes, launches) of the token's int4 matvecs
+        (26 layers x q, k, v, o, gate, up, down + LM head, on this session's
+        packed planes) run alone as one streaming plan."""
         ms, b, n = C.c_float(), C.c_uint64(), C.c_uint32()
         check(lib().xp_session_profile_matvec(self._h, iters, C.byref(ms), C.byref(b), C.byref(n)))
         return ms.value, b.value, n.value
