@@ -123,6 +123,19 @@ xp_status xp_mv_km4_bs_split(void* stream, float* partial, const float* in, cons
 /* kernels/llm_matvec.cl:128-135 */
 xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t cols, uint32_t split);
 
+/* ---- one matrix, many sequences, on the tensor cores ------------------------
+ * out[s][j] = sum_k in[s][k] W[k][j] for s < n (<= 64): the skinny GEMM of
+ * batched decode, each row the value kernels/llm_matvec.cl:422-434 computes for
+ * that sequence (same planes, bf16 scales applied in fp32 per 32-row block).
+ * in is [n][rows], out [n][cols]; rows % 128 == 0, cols % 128 == 0. `scratch`
+ * (256-byte aligned, xp_mv_km4_bs_batch_scratch_bytes) is caller-owned; its
+ * 32-bit word at byte offset 256 is nonzero after a call whose tensor-core
+ * pipeline wait ran out. No counterpart entry in the reference (which
+ * dispatches mv_km4_bs once per sequence). */
+size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n);
+xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
+                             uint32_t rows, uint32_t cols, uint32_t n, void* scratch);
+
 /* ---- many matvecs in one launch ---------------------------------------------
  * The reference submits a token's matvecs as mv_km4_bs dispatches recorded in
  * one Batch (examples/llm/decode.cpp:1634-1780, include/vulkore/launch.hpp:

@@ -87,6 +87,8 @@ _SIGS = {
     "xp_mv_km4_bs": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 2),
     "xp_mv_km4_bs_split": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32] * 3),
     "xp_mv_reduce": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
+    "xp_mv_km4_bs_batch_scratch_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32]),
+    "xp_mv_km4_bs_batch": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
     "xp_mv_plan_create": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
     "xp_mv_plan_run": (C.c_int, [C.c_void_p, C.c_void_p]),
     "xp_mv_plan_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),

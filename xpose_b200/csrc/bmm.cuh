@@ -1,0 +1,350 @@
+// Batched int4 matvec on the 5th-generation tensor cores (tcgen05): N
+// activation vectors (sequences) times one KM4 + bf16-scale weight matrix,
+// out[n][j] = sum_k x[n][k] * W[k][j], the reference's mv_km4_bs
+// (kernels/llm_matvec.cl:422-434) for every sequence at once. This is the
+// skinny GEMM (M = weight columns, N = sequences, K = rows) of batched decode.
+//
+// Exactness. The reference dequantises (nibble - 8) * bf16(scale) in fp32. A
+// 16-bit MMA operand cannot hold that product exactly, so the tensor cores
+// multiply the exact integers (nibble - 8) in fp16 and the per-32-row block
+// scale is applied afterwards in fp32: one K = 32 block per accumulator, an
+// epilogue adds scale(j, b) * D_b to a register sum. The activation enters as
+// x / 2^e = hi + lo, two fp16 halves (about 22 significant bits), with one
+// power-of-two e per sequence applied at the end; hi and lo are two MMAs into
+// the same accumulator.
+//
+// CTA (320 threads) per work item = 128 output columns x one K range:
+//   warp 0   producer: bulk copies of the nibbles (2 x 1 KB per block, the
+//            reference plane read in place) and the prepared activations
+//   warp 1   MMA issuer (one thread) + TMEM owner (alloc/dealloc, 2N columns)
+//   warps 2-5  dequant: thread = column j, 32 nibbles -> fp16 A tile
+//   warps 6-9  epilogue: thread = column j, tcgen05.ld of the block's N sums,
+//            scale and accumulate; the item's result goes to out (one K
+//            range) or to int64 fixed-point sums (K split across CTAs)
+// Shared-memory operands use the K-major, no-swizzle canonical layout: 8 rows x
+// 16 bytes per core matrix. Within each 8-element K chunk the order is the
+// nibble extraction order (k0 k4 k1 k5 k2 k6 k3 k7) on both operands.
+//
+// Every wait is bounded and reports through an error word; no multicast.
+#pragma once
+#include "common.cuh"
+#include "tk_primitives.cuh"
+
+namespace xp {
+
+constexpr int BMM_THREADS = 320;
+constexpr int BMM_M = 128;           // output columns per tile
+constexpr int BMM_STAGES = 4;        // copy ring depth (blocks)
+constexpr int BMM_MAXN = 64;         // sequences per launch (N is 32 or 64)
+constexpr uint32_t BMM_ERR_WAIT = 64u;
+
+struct BmmArgs {
+    const uint4* wq;          // nibble plane of the matrix (reference layout)
+    const uint2* sc;          // bf16 scale plane
+    const unsigned char* xb;  // prepared activations: [nblk][hi, lo][chunk 4][N][16 B]
+    const float* xs;          // [N] per-sequence power-of-two scale 2^e
+    float* out;               // [N][cols] (ksplit == 1)
+    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1), zero at launch
+    uint32_t nblk, cols, N;   // N = padded sequence count (32 or 64)
+    uint32_t nreal;           // sequences actually present (rows of out)
+    uint32_t ksplit, cb;      // K ranges per tile, blocks per range
+    uint32_t nitems;          // (cols / 128) * ksplit
+    uint32_t* err;
+};
+
+// ---- tcgen05 helpers (PTX of the sm_100a tensor-core and TMEM instructions) ----
+XP_DEV uint64_t bmm_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    // K-major, SWIZZLE_NONE: start >> 4, leading (K) byte offset >> 4, stride
+    // (8-row group) byte offset >> 4, descriptor version 1 (bit 46)
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+XP_DEV uint32_t bmm_idesc(uint32_t n) {
+    // kind::f16: D f32 (bit 4), A = B = f16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24
+    return (1u << 4) | ((n >> 3) << 17) | ((uint32_t)(BMM_M >> 4) << 24);
+}
+XP_DEV void bmm_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+XP_DEV void bmm_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+XP_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+XP_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+XP_DEV void tmem_ld32(uint32_t taddr, float v[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// bounded wait that records the failure and returns
+XP_DEV void bmm_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    uint32_t it = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (++it > TK_SPIN_LIMIT) {
+            atomicOr(err, BMM_ERR_WAIT);
+            return;
+        }
+    }
+}
+
+// 8 nibbles (one word: k = 8c .. 8c+7) -> 8 fp16 (nibble - 8) in the order
+// k0 k4 k1 k5 k2 k6 k3 k7, exact (1024 + n - 1032 in fp16).
+XP_DEV uint4 bmm_unpack8(uint32_t w) {
+    const uint32_t magic = 0x64006400u;  // fp16 1024.0 in both halves
+    const __half2 bias = __halves2half2(__float2half_rn(1032.0f), __float2half_rn(1032.0f));
+    uint4 r;
+    uint32_t h;
+    h = (w & 0x000F000Fu) | magic;
+    *reinterpret_cast<__half2*>(&r.x) = __hsub2(*reinterpret_cast<__half2*>(&h), bias);
+    h = ((w >> 4) & 0x000F000Fu) | magic;
+    *reinterpret_cast<__half2*>(&r.y) = __hsub2(*reinterpret_cast<__half2*>(&h), bias);
+    h = ((w >> 8) & 0x000F000Fu) | magic;
+    *reinterpret_cast<__half2*>(&r.z) = __hsub2(*reinterpret_cast<__half2*>(&h), bias);
+    h = ((w >> 12) & 0x000F000Fu) | magic;
+    *reinterpret_cast<__half2*>(&r.w) = __hsub2(*reinterpret_cast<__half2*>(&h), bias);
+    return r;
+}
+
+// Activation prep, pass 1: per sequence the power-of-two 2^e >= max |x| (one
+// warp per sequence); also zeroes the fixed-point sums of this call.
+__global__ void bmm_scale_kernel(const float* x, uint32_t rows, uint32_t N, uint32_t Npad, float* xs, long long* acc,
+                                 size_t acc_n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; acc && i < acc_n; i += (size_t)gridDim.x * blockDim.x)
+        acc[i] = 0;
+    const uint32_t n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (n >= Npad) return;
+    float am = 0.0f;
+    if (n < N)
+        for (uint32_t i = lane; i < rows; i += 32) am = fmaxf(am, fabsf(x[(size_t)n * rows + i]));
+    am = warp_max(am);
+    // am = m 2^(eb-127), m in [1,2): 2^(eb-126) > am
+    const int eb = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+    if (lane == 0) xs[n] = eb > 0 && eb < 253 ? __uint_as_float((uint32_t)(eb + 1) << 23) : 1.0f;
+}
+// Pass 2: x / 2^e = hi + lo in fp16, written in the kernel's operand layout
+// and K order. One warp per (block, sequence).
+__global__ void bmm_prep_kernel(const float* x, uint32_t rows, uint32_t N, uint32_t Npad, const float* xs,
+                                unsigned char* xb) {
+    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const uint32_t nblk = rows / 32;
+    if (gw >= nblk * Npad) return;
+    const uint32_t b = gw / Npad, n = gw % Npad;
+    const float y = n < N ? x[(size_t)n * rows + b * 32 + lane] / xs[n] : 0.0f;  // exact: power of two
+    const __half hi = __float2half_rn(y);
+    const __half lo = __float2half_rn(y - __half2float(hi));
+    // element k = lane of the block: chunk c = k / 8, position of k in the
+    // extraction order k0 k4 k1 k5 k2 k6 k3 k7
+    const uint32_t c = lane >> 3, e = lane & 7, pos = (e & 3) * 2 + (e >> 2);
+    __half* base = reinterpret_cast<__half*>(xb + (size_t)b * 2 * 4 * Npad * 16);
+    base[((0 * 4 + c) * Npad + n) * 8 + pos] = hi;
+    base[((1 * 4 + c) * Npad + n) * 8 + pos] = lo;
+}
+
+XP_DEV void bmm_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
+    extern __shared__ __align__(1024) unsigned char bsm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t N = a.N;
+    const uint32_t xbytes = 2 * 4 * N * 16;   // activations per block
+    const uint32_t sbytes = 2048 + xbytes;    // one stage: nibbles + activations
+    // layout: [stages][nibbles 2 KB | activations] [A tiles 2 x 8 KB] [mbarriers] [tmem addr]
+    unsigned char* stage0 = bsm;
+    unsigned char* atile = bsm + BMM_STAGES * sbytes;
+    uint64_t* mb = reinterpret_cast<uint64_t*>(atile + 2 * 8192);
+    uint64_t* full = mb;                         // [STAGES] producer -> dequant, MMA
+    uint64_t* empty = mb + BMM_STAGES;           // [STAGES] dequant + MMA commit -> producer
+    uint64_t* afull = mb + 2 * BMM_STAGES;       // [2] dequant -> MMA
+    uint64_t* aempty = afull + 2;                // [2] MMA commit -> dequant
+    uint64_t* dfull = afull + 4;                 // [2] MMA commit -> epilogue
+    uint64_t* dempty = afull + 6;                // [2] epilogue -> MMA
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afull + 8);
+
+    if (tid == 0) {
+        for (int i = 0; i < BMM_STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 2);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&afull[i], 1);
+            mbar_init(&aempty[i], 1);
+            mbar_init(&dfull[i], 1);
+            mbar_init(&dempty[i], 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        const uint32_t ncols = 2 * N;  // two accumulator slots of N columns (64 or 128)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t G = gridDim.x;
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            uint32_t t = 0;  // global block counter of this CTA
+            for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
+                const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
+                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                for (uint32_t b = b0; b < b1; ++b, ++t) {
+                    const uint32_t s = t % BMM_STAGES;
+                    if (t >= BMM_STAGES) bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);
+                    unsigned char* st = stage0 + s * sbytes;
+                    fence_proxy_async();
+                    mbar_expect_tx(&full[s], 2048 + xbytes);
+                    // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups
+                    bulk_g2s(st, a.wq + ((size_t)(2 * tile) * a.nblk + b) * 64, 1024, &full[s]);
+                    bulk_g2s(st + 1024, a.wq + ((size_t)(2 * tile + 1) * a.nblk + b) * 64, 1024, &full[s]);
+                    bulk_g2s(st + 2048, a.xb + (size_t)b * xbytes, xbytes, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = bmm_idesc(N);
+            uint32_t t = 0;
+            for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
+                const uint32_t kc = item % a.ksplit;
+                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                for (uint32_t b = b0; b < b1; ++b, ++t) {
+                    const uint32_t s = t % BMM_STAGES, p = t & 1;
+                    bmm_wait(&afull[p], (t >> 1) & 1, a.err);           // A tile of block t dequantised
+                    bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);    // activations of block t landed
+                    if (t >= 2) bmm_wait(&dempty[p], ((t >> 1) - 1) & 1, a.err);  // epilogue done with slot p
+                    tc_fence_after();
+                    const uint32_t ab = smem_u32(atile + p * 8192);
+                    const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
+                    const uint32_t d = tmem + p * N;
+                    uint32_t acc = 0;
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+                        for (int hl = 0; hl < 2; ++hl) {
+                            // A: chunks 2kk, 2kk+1 of 128 columns (chunk stride 2 KB, 8-row groups 128 B)
+                            const uint64_t ad = bmm_desc(ab + kk * 4096, 2048, 128);
+                            // B: chunks 2kk, 2kk+1 of N sequences (chunk stride 16N B, 8-row groups 128 B)
+                            const uint64_t bd = bmm_desc(xbase + (hl * 4 + 2 * kk) * N * 16, N * 16, 128);
+                            bmm_mma(d, ad, bd, idesc, acc);
+                            acc = 1;
+                        }
+                    bmm_commit(&dfull[p]);   // accumulator of block t ready
+                    bmm_commit(&aempty[p]);  // A tile p free
+                    bmm_commit(&empty[s]);   // activations of stage s no longer read
+                }
+            }
+        }
+    } else if (warp < 6) {
+        // ------------------------------ dequant ------------------------------
+        const uint32_t j = tid - 64;  // column within the tile, 0..127
+        uint32_t t = 0;
+        for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
+            const uint32_t kc = item % a.ksplit;
+            const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+            for (uint32_t b = b0; b < b1; ++b, ++t) {
+                const uint32_t s = t % BMM_STAGES, p = t & 1;
+                bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);
+                const uint4 w = *reinterpret_cast<const uint4*>(stage0 + s * sbytes + (j >> 6) * 1024 + (j & 63) * 16);
+                // nibbles read: this thread no longer needs the stage
+                if (t >= 2) bmm_wait(&aempty[p], ((t >> 1) - 1) & 1, a.err);
+                unsigned char* at = atile + p * 8192 + j * 16;
+                *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8(w.x);
+                *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8(w.y);
+                *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8(w.z);
+                *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8(w.w);
+                fence_proxy_async();  // generic smem writes -> async-proxy MMA reads
+                asm volatile("bar.sync 2, 128;" ::: "memory");
+                if (j == 0) {
+                    bmm_arrive(&afull[p]);
+                    bmm_arrive(&empty[s]);
+                }
+            }
+        }
+    } else {
+        // ------------------------------ epilogue ------------------------------
+        const uint32_t q = warp & 3;                 // TMEM lane quadrant of this warp
+        const uint32_t j = q * 32 + lane;            // column within the tile
+        uint32_t t = 0;
+        for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
+            const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
+            const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+            const uint32_t col = tile * BMM_M + j;
+            float sum[BMM_MAXN];
+#pragma unroll
+            for (int n = 0; n < BMM_MAXN; ++n) sum[n] = 0.0f;
+            uint2 sw = __ldg(a.sc + (size_t)(b0 >> 2) * a.cols + col);
+            for (uint32_t b = b0; b < b1; ++b, ++t) {
+                const uint32_t p = t & 1;
+                if ((b & 3) == 0 && b != b0) sw = __ldg(a.sc + (size_t)(b >> 2) * a.cols + col);
+                const uint32_t word = (b & 2) ? sw.y : sw.x;
+                const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
+                bmm_wait(&dfull[p], (t >> 1) & 1, a.err);
+                tc_fence_after();
+#pragma unroll
+                for (int c0 = 0; c0 < BMM_MAXN; c0 += 32) {
+                    if ((uint32_t)c0 < N) {
+                        float v[32];
+                        tmem_ld32(tmem + ((q * 32) << 16) + p * N + c0, v);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) sum[c0 + i] = fmaf(scale, v[i], sum[c0 + i]);
+                    }
+                }
+                tc_fence_before();
+                asm volatile("bar.sync 3, 128;" ::: "memory");
+                if (tid == 192) bmm_arrive(&dempty[p]);
+            }
+#pragma unroll
+            for (int n = 0; n < BMM_MAXN; ++n) {
+                if ((uint32_t)n < a.nreal) {
+                    const float v = sum[n] * a.xs[n];
+                    if (a.ksplit == 1) {
+                        a.out[(size_t)n * a.cols + col] = v;
+                    } else {
+                        const float f = v * 4294967296.0f;
+                        long long fx = 0;
+                        if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
+                        else atomicOr(a.err, TK_ERR_RANGE);
+                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(a.acc + (size_t)n * a.cols + col),
+                                     "l"(fx) : "memory");
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        const uint32_t ncols = 2 * N;
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    }
+}
+
+// fixed-point sums -> fp32
+__global__ void bmm_finish_kernel(const long long* acc, float* out, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __ll2float_rn(acc[i]) * 2.3283064365386963e-10f;
+}
+
+}  // namespace xp

@@ -13,6 +13,7 @@
 #include <utility>
 #include <vector>
 
+#include "bmm.cuh"
 #include "mv_stream.cuh"
 #include "ops.cuh"
 #include "runtime.cuh"
@@ -643,6 +644,91 @@ xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t 
     ops::mv_reduce<<<(cols + 255) / 256, 256, 0, (cudaStream_t)stream>>>(out, partial, cols, split);
     return cuda_status(cudaGetLastError(), "mv_reduce");
 }
+// ---- batched matvec on tcgen05 -------------------------------------------------
+namespace {
+struct BmmPlan {
+    uint32_t npad, nblk, tiles, ksplit, cb, nitems;
+    size_t off_xs, off_err, off_xb, off_acc, bytes, smem;
+};
+BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
+    BmmPlan p{};
+    p.npad = n <= 32 ? 32 : 64;
+    p.nblk = rows / 32;
+    p.tiles = cols / BMM_M;
+    const uint32_t G = (uint32_t)sm_count();
+    p.ksplit = std::max<uint32_t>(1, std::min<uint32_t>(p.nblk, (G + p.tiles - 1) / p.tiles));
+    p.cb = (p.nblk + p.ksplit - 1) / p.ksplit;
+    p.ksplit = (p.nblk + p.cb - 1) / p.cb;
+    p.nitems = p.tiles * p.ksplit;
+    p.off_xs = 0;      // [64] per-sequence scales
+    p.off_err = 256;   // error word of the call
+    p.off_xb = 512;
+    p.off_acc = p.off_xb + (size_t)p.nblk * 2 * 4 * p.npad * 16;
+    p.bytes = p.off_acc + (p.ksplit > 1 ? (size_t)p.npad * cols * 8 : 0);
+    p.smem = (size_t)BMM_STAGES * (2048 + 2 * 4 * p.npad * 16) + 2 * 8192 + 8 * (2 * BMM_STAGES + 8) + 16;
+    return p;
+}
+}  // namespace
+size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n) {
+    if (rows == 0 || rows % 128 || cols == 0 || cols % 128 || n == 0 || n > BMM_MAXN) return 0;
+    return bmm_plan(rows, cols, n).bytes;
+}
+xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
+                             uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {
+    CHECK_PTR(out); CHECK_PTR(in); CHECK_PTR(wq); CHECK_PTR(sc); CHECK_PTR(scratch);
+    if (rows == 0 || rows % 128 || cols == 0 || cols % 128)
+        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: rows must be a multiple of 128 and cols of 128 (got %u x %u)",
+                    rows, cols);
+    if (n == 0 || n > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: 1..%d sequences (got %u)", BMM_MAXN, n);
+    if (reinterpret_cast<uintptr_t>(scratch) % 256)
+        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: scratch must be 256-byte aligned");
+    const BmmPlan p = bmm_plan(rows, cols, n);
+    const cudaStream_t st = (cudaStream_t)stream;
+    unsigned char* base = static_cast<unsigned char*>(scratch);
+    float* xs = reinterpret_cast<float*>(base + p.off_xs);
+    unsigned char* xb = base + p.off_xb;
+    long long* acc = p.ksplit > 1 ? reinterpret_cast<long long*>(base + p.off_acc) : nullptr;
+    const size_t acc_n = acc ? (size_t)p.npad * cols : 0;
+    const uint32_t sblocks = (uint32_t)std::max<size_t>((p.npad * 32 + 255) / 256, std::min<size_t>((acc_n + 255) / 256, 1024));
+    uint32_t* err = reinterpret_cast<uint32_t*>(base + p.off_err);
+    XP_CUDA_TRY(cudaMemsetAsync(err, 0, 4, st));
+    bmm_scale_kernel<<<sblocks, 256, 0, st>>>(in, rows, n, p.npad, xs, acc, acc_n);
+    XP_CUDA_TRY(cudaGetLastError());
+    bmm_prep_kernel<<<(p.nblk * p.npad * 32 + 255) / 256, 256, 0, st>>>(in, rows, n, p.npad, xs, xb);
+    XP_CUDA_TRY(cudaGetLastError());
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        XP_CUDA_TRY(cudaFuncSetAttribute(bmm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        attr_set[dev] = true;
+    }
+    BmmArgs a{};
+    a.wq = reinterpret_cast<const uint4*>(wq);
+    a.sc = reinterpret_cast<const uint2*>(sc);
+    a.xb = xb;
+    a.xs = xs;
+    a.out = out;
+    a.acc = acc;
+    a.nblk = p.nblk;
+    a.cols = cols;
+    a.N = p.npad;
+    a.nreal = n;
+    a.ksplit = p.ksplit;
+    a.cb = p.cb;
+    a.nitems = p.nitems;
+    a.err = err;
+    const uint32_t grid = std::min<uint32_t>(p.nitems, (uint32_t)sm_count());
+    bmm_kernel<<<grid, BMM_THREADS, p.smem, st>>>(a);
+    XP_CUDA_TRY(cudaGetLastError());
+    if (acc) {
+        // rows n >= the real sequence count are padding: convert only [n][cols]
+        bmm_finish_kernel<<<(uint32_t)(((size_t)n * cols + 255) / 256), 256, 0, st>>>(acc, out, (size_t)n * cols);
+        XP_CUDA_TRY(cudaGetLastError());
+    }
+    return XP_OK;
+}
+
 struct xp_mv_plan {
     int device = 0;
     MvsJob* jobs = nullptr;

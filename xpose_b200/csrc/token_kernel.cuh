@@ -40,10 +40,15 @@
 
 namespace xp {
 
-constexpr int TK_THREADS = 512;              // compute threads (16 warps)
+#ifndef XP_TK_THREADS
+#define XP_TK_THREADS 512
+#endif
+constexpr int TK_THREADS = XP_TK_THREADS;    // compute threads
 constexpr int TK_WARPS = TK_THREADS / 32;
 constexpr int TK_BLOCK = TK_THREADS + 32;      // + one producer warp that issues every bulk copy
-constexpr int TK_MAXJ = 3;   // hidden <= 1536, q|k|v width <= 1536
+constexpr int TK_MAXJ = (1536 + TK_THREADS - 1) / TK_THREADS;  // hidden and q|k|v width <= 1536
+constexpr int TK_GROUPS = TK_THREADS / 128;  // 128-thread groups (attention P.V, O combine)
+static_assert(TK_THREADS % 128 == 0 && TK_THREADS >= 256 && TK_THREADS <= 1024, "compute threads");
 constexpr int TK_NMB = 32;   // mbarriers
 // "full" mbarriers: complete once per fill of a slot
 constexpr int TK_MB_QKV = 0, TK_MB_O = 1, TK_MB_GU = 2, TK_MB_DOWN = 3, TK_MB_KV = 4;
@@ -383,46 +388,60 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             const float* bsrc = k == TK_S_GU ? a.x0 : a.x1;
             const long long* acc = k == TK_S_GU ? a.acc_o : a.acc_dn;
             float* x_out = k == TK_S_QKV ? a.x0 : (k == TK_S_GU ? a.x1 : nullptr);
-            float rv[TK_MAXJ];
-            if (k == TK_S_QKV && l == 0) {
+            // One block reduction for both norms: with u = y (1 + w_post) and
+            // s1 = rsqrt(sum y^2 / H + eps), r = b + s1 u and
+            // sum r^2 = sum b^2 + 2 s1 sum b u + s1^2 sum u^2.
+            float rv[TK_MAXJ], uv[TK_MAXJ];
+            float4 sums = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // y^2, b^2, b u, u^2
+            const bool emb = k == TK_S_QKV && l == 0;
+            if (emb) {
                 const float* row = a.embed + (size_t)(*a.token) * H;
 #pragma unroll
                 for (int j = 0; j < TK_MAXJ; ++j) {
                     const uint32_t i = tid + j * TK_THREADS;
                     rv[j] = i < H ? row[i] * a.embed_scale : 0.0f;
+                    uv[j] = 0.0f;
+                    sums.y += rv[j] * rv[j];
                 }
             } else {
-                float yv[TK_MAXJ], bvv[TK_MAXJ];
-                float ss = 0.0f;
 #pragma unroll
                 for (int j = 0; j < TK_MAXJ; ++j) {
                     const uint32_t i = tid + j * TK_THREADS;
-                    yv[j] = i < H ? tk_unfix(acc[i]) : 0.0f;
-                    bvv[j] = i < H ? bsrc[i] : 0.0f;
-                }
-#pragma unroll
-                for (int j = 0; j < TK_MAXJ; ++j) ss += yv[j] * yv[j];
-                ss = tk_block_sum(ss, red32);
-                const float sc = rsqrtf(ss / (float)H + a.eps);
-#pragma unroll
-                for (int j = 0; j < TK_MAXJ; ++j) {
-                    const uint32_t i = tid + j * TK_THREADS;
-                    rv[j] = i < H ? bvv[j] + yv[j] * sc * (1.0f + wv[i]) : 0.0f;
+                    const float y = i < H ? tk_unfix(acc[i]) : 0.0f;
+                    rv[j] = i < H ? bsrc[i] : 0.0f;
+                    uv[j] = i < H ? y * (1.0f + wv[i]) : 0.0f;
+                    sums.x += y * y;
+                    sums.y += rv[j] * rv[j];
+                    sums.z += rv[j] * uv[j];
+                    sums.w += uv[j] * uv[j];
                 }
             }
-            float ss2 = 0.0f;
+            sums.x = warp_sum(sums.x);
+            sums.y = warp_sum(sums.y);
+            sums.z = warp_sum(sums.z);
+            sums.w = warp_sum(sums.w);
+            if (lane == 0) reinterpret_cast<float4*>(red32)[warp] = sums;
+            tk_sync();
+            float4 t = lane < TK_WARPS ? reinterpret_cast<const float4*>(red32)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+            t.x = warp_sum(t.x);
+            t.y = warp_sum(t.y);
+            t.z = warp_sum(t.z);
+            t.w = warp_sum(t.w);
+            const float s1 = emb ? 0.0f : rsqrtf(t.x / (float)H + a.eps);
+            const float sc2 = rsqrtf((t.y + 2.0f * s1 * t.z + s1 * s1 * t.w) / (float)H + a.eps);
+            // limbs straight from registers: warp w holds blocks w, w + 16 and
+            // w + 32 in lane order
+            const TkPhase& P = k == TK_S_QKV ? a.qkv : (k == TK_S_GU ? a.gu : a.head);
+            const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
+            const bool has = c < P.units;
 #pragma unroll
             for (int j = 0; j < TK_MAXJ; ++j) {
                 const uint32_t i = tid + j * TK_THREADS;
-                if (i < H && x_out && c == 0) x_out[i] = rv[j];
-                ss2 += rv[j] * rv[j];
-            }
-            ss2 = tk_block_sum(ss2, red32);
-            const float sc2 = rsqrtf(ss2 / (float)H + a.eps);
-#pragma unroll
-            for (int j = 0; j < TK_MAXJ; ++j) {
-                const uint32_t i = tid + j * TK_THREADS;
-                if (i < H) xn[i] = rv[j] * sc2 * (1.0f + wv[H + i]);
+                const float r = rv[j] + s1 * uv[j];
+                if (i < H && x_out && c == 0) x_out[i] = r;
+                const uint32_t blk = warp + TK_WARPS * j;
+                if (has && blk >= b0 && blk < b0 + P.nb)
+                    xq_prep_block(r * sc2 * (1.0f + wv[H + (i < H ? i : 0)]), &xq[blk - b0]);
             }
         } else if (k == TK_S_O) {
             // flash combine of this CTA's 128-dim slice over the splits: the
@@ -461,10 +480,15 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 const uint32_t d = tid & 127, g = tid >> 7;
                 float acc = 0.0f;
 #pragma unroll 4
-                for (uint32_t s_ = g; s_ < w.nsplit; s_ += 4) acc += stage[s_ * 128 + d] * wts[s_];
+                for (uint32_t s_ = g; s_ < w.nsplit; s_ += TK_GROUPS) acc += stage[s_ * 128 + d] * wts[s_];
                 red[g * 128 + d] = acc;
                 tk_sync();
-                if (tid < 128) xn[tid] = (red[tid] + red[128 + tid] + red[256 + tid] + red[384 + tid]) / Ls;
+                if (tid < 128) {
+                    float t = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 128 + tid];
+                    xn[tid] = t / Ls;
+                }
             }
         } else if (k == TK_S_DOWN) {
             if (c < a.down.units) {
@@ -599,7 +623,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     const uint32_t dp = tid & 127, qr = tid >> 7;
                     float acc[4][2] = {};
 #pragma unroll 2
-                    for (uint32_t jj = qr; jj < n; jj += 4) {
+                    for (uint32_t jj = qr; jj < n; jj += TK_GROUPS) {
                         const uint32_t j = w.j0 + jj;
                         const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vn)[dp]
                                                     : reinterpret_cast<const __half2*>(vs + (size_t)jj * 256)[dp];
@@ -622,8 +646,12 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 // K range reads it: att_part[slice][c][i % 128]
 #pragma unroll 1
                 for (uint32_t i = tid; i < 4 * 256; i += TK_THREADS)
-                    a.att_part[((size_t)(i >> 7) * G + c) * 128 + (i & 127)] =
-                        red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
+                {
+                    float t = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 1024 + i];
+                    a.att_part[((size_t)(i >> 7) * G + c) * 128 + (i & 127)] = t;
+                }
                 TK_MARK(3)
             } else {
                 wait_slot(TK_MB_KV);
@@ -642,11 +670,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                              : k == TK_S_GU  ? a.gu
                              : k == TK_S_DOWN ? a.down : a.head;
             const bool has = c < P.units;
-            const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
-            tk_sync();  // xn complete
-            if (has) {
-#pragma unroll 1
-                for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
+            if (k == TK_S_O || k == TK_S_DOWN) {
+                tk_sync();  // xn complete
+                if (has) {
+                    for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[b * 32 + lane], &xq[b]);
+                }
             }
             tk_sync();
             TK_MARK(0)
