@@ -13,14 +13,18 @@
 // power-of-two e per sequence applied at the end; hi and lo are two MMAs into
 // the same accumulator.
 //
-// CTA (320 threads) per work item = 128 output columns x one K range:
+// CTA (448 threads) per work item = 128 output columns x one K range:
 //   warp 0   producer: bulk copies of the nibbles (2 x 1 KB per block, the
 //            reference plane read in place) and the prepared activations
-//   warp 1   MMA issuer (one thread) + TMEM owner (alloc/dealloc, 2N columns)
+//   warp 1   MMA issuer (one thread) + TMEM owner (alloc/dealloc, 4N columns)
 //   warps 2-5  dequant: thread = column j, 32 nibbles -> fp16 A tile
-//   warps 6-9  epilogue: thread = column j, tcgen05.ld of the block's N sums,
-//            scale and accumulate; the item's result goes to out (one K
-//            range) or to int64 fixed-point sums (K split across CTAs)
+//   warps 6-13 epilogue: thread = column j x half of the sequences,
+//            tcgen05.ld of the block's sums, scale and accumulate; the item's
+//            result goes to out (one K range) or to int64 fixed-point sums
+//            (K split across CTAs)
+// Four A tiles and four accumulator slots keep the MMA up to four blocks
+// ahead of the epilogue; two CTAs share an SM. Waiting warps poll with one
+// lane.
 // Shared-memory operands use the K-major, no-swizzle canonical layout: 8 rows x
 // 16 bytes per core matrix. Within each 8-element K chunk the order is the
 // nibble extraction order (k0 k4 k1 k5 k2 k6 k3 k7) on both operands.
@@ -32,9 +36,11 @@
 
 namespace xp {
 
-constexpr int BMM_THREADS = 320;
+constexpr int BMM_THREADS = 448;     // producer, MMA, 4 dequant, 8 epilogue warps
 constexpr int BMM_M = 128;           // output columns per tile
 constexpr int BMM_STAGES = 4;        // copy ring depth (blocks)
+constexpr int BMM_NA = 4;            // A tiles (dequantised blocks) in flight
+constexpr int BMM_ND = 4;            // TMEM accumulator slots in flight
 constexpr int BMM_MAXN = 64;         // sequences per launch (N is 32 or 64)
 constexpr uint32_t BMM_ERR_WAIT = 64u;
 
@@ -89,6 +95,19 @@ XP_DEV void tmem_ld32(uint32_t taddr, float v[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+XP_DEV void tmem_ld16(uint32_t taddr, float v[32]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+#pragma unroll
+    for (int i = 16; i < 32; ++i) v[i] = 0.0f;
+}
 // bounded wait that records the failure and returns
 XP_DEV void bmm_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
     uint32_t it = 0;
@@ -98,6 +117,13 @@ XP_DEV void bmm_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
             return;
         }
     }
+}
+
+// Warp-wide wait: lane 0 polls, the other lanes park at the warp barrier
+// (which also orders their later reads after lane 0's acquire).
+XP_DEV void bmm_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    if ((threadIdx.x & 31) == 0) bmm_wait(bar, parity, err);
+    __syncwarp();
 }
 
 // 8 nibbles (one word: k = 8c .. 8c+7) -> 8 fp16 (nibble - 8) in the order
@@ -157,7 +183,7 @@ XP_DEV void bmm_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-__global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
+__global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
     extern __shared__ __align__(1024) unsigned char bsm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t N = a.N;
@@ -166,30 +192,32 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
     // layout: [stages][nibbles 2 KB | activations] [A tiles 2 x 8 KB] [mbarriers] [tmem addr]
     unsigned char* stage0 = bsm;
     unsigned char* atile = bsm + BMM_STAGES * sbytes;
-    uint64_t* mb = reinterpret_cast<uint64_t*>(atile + 2 * 8192);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(atile + BMM_NA * 8192);
     uint64_t* full = mb;                         // [STAGES] producer -> dequant, MMA
     uint64_t* empty = mb + BMM_STAGES;           // [STAGES] dequant + MMA commit -> producer
-    uint64_t* afull = mb + 2 * BMM_STAGES;       // [2] dequant -> MMA
-    uint64_t* aempty = afull + 2;                // [2] MMA commit -> dequant
-    uint64_t* dfull = afull + 4;                 // [2] MMA commit -> epilogue
-    uint64_t* dempty = afull + 6;                // [2] epilogue -> MMA
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afull + 8);
+    uint64_t* afull = mb + 2 * BMM_STAGES;       // [NA] dequant -> MMA
+    uint64_t* aempty = afull + BMM_NA;           // [NA] MMA commit -> dequant
+    uint64_t* dfull = aempty + BMM_NA;           // [ND] MMA commit -> epilogue
+    uint64_t* dempty = dfull + BMM_ND;           // [ND] epilogue -> MMA
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + BMM_ND);
 
     if (tid == 0) {
         for (int i = 0; i < BMM_STAGES; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 2);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < BMM_NA; ++i) {
             mbar_init(&afull[i], 1);
             mbar_init(&aempty[i], 1);
+        }
+        for (int i = 0; i < BMM_ND; ++i) {
             mbar_init(&dfull[i], 1);
             mbar_init(&dempty[i], 1);
         }
         fence_mbar_init();
     }
     if (warp == 1) {
-        const uint32_t ncols = 2 * N;  // two accumulator slots of N columns (64 or 128)
+        const uint32_t ncols = BMM_ND * N;  // accumulator slots of N columns (128 or 256)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -229,14 +257,14 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
                 const uint32_t kc = item % a.ksplit;
                 const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
                 for (uint32_t b = b0; b < b1; ++b, ++t) {
-                    const uint32_t s = t % BMM_STAGES, p = t & 1;
-                    bmm_wait(&afull[p], (t >> 1) & 1, a.err);           // A tile of block t dequantised
+                    const uint32_t s = t % BMM_STAGES, p = t % BMM_NA, q = t % BMM_ND;
+                    bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);       // A tile of block t dequantised
                     bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);    // activations of block t landed
-                    if (t >= 2) bmm_wait(&dempty[p], ((t >> 1) - 1) & 1, a.err);  // epilogue done with slot p
+                    if (t >= BMM_ND) bmm_wait(&dempty[q], ((t / BMM_ND) - 1) & 1, a.err);  // slot q read
                     tc_fence_after();
                     const uint32_t ab = smem_u32(atile + p * 8192);
                     const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
-                    const uint32_t d = tmem + p * N;
+                    const uint32_t d = tmem + q * N;
                     uint32_t acc = 0;
 #pragma unroll
                     for (int kk = 0; kk < 2; ++kk)
@@ -249,7 +277,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
                             bmm_mma(d, ad, bd, idesc, acc);
                             acc = 1;
                         }
-                    bmm_commit(&dfull[p]);   // accumulator of block t ready
+                    bmm_commit(&dfull[q]);   // accumulator of block t ready
                     bmm_commit(&aempty[p]);  // A tile p free
                     bmm_commit(&empty[s]);   // activations of stage s no longer read
                 }
@@ -263,11 +291,10 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
             const uint32_t kc = item % a.ksplit;
             const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
             for (uint32_t b = b0; b < b1; ++b, ++t) {
-                const uint32_t s = t % BMM_STAGES, p = t & 1;
-                bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);
+                const uint32_t s = t % BMM_STAGES, p = t % BMM_NA;
+                bmm_wait_warp(&full[s], (t / BMM_STAGES) & 1, a.err);
                 const uint4 w = *reinterpret_cast<const uint4*>(stage0 + s * sbytes + (j >> 6) * 1024 + (j & 63) * 16);
-                // nibbles read: this thread no longer needs the stage
-                if (t >= 2) bmm_wait(&aempty[p], ((t >> 1) - 1) & 1, a.err);
+                if (t >= BMM_NA) bmm_wait_warp(&aempty[p], ((t / BMM_NA) - 1) & 1, a.err);
                 unsigned char* at = atile + p * 8192 + j * 16;
                 *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8(w.x);
                 *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8(w.y);
@@ -283,41 +310,47 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
         }
     } else {
         // ------------------------------ epilogue ------------------------------
-        const uint32_t q = warp & 3;                 // TMEM lane quadrant of this warp
-        const uint32_t j = q * 32 + lane;            // column within the tile
+        const uint32_t e = warp - 6;
+        const uint32_t q4 = warp & 3;                // TMEM lane quadrant of this warp
+        const uint32_t j = q4 * 32 + lane;           // column within the tile
+        const uint32_t half = e >> 2;                // sequences [half * N/2, +N/2)
+        const uint32_t nh = N / 2;                   // 16 or 32
         uint32_t t = 0;
         for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
             const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
             const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
             const uint32_t col = tile * BMM_M + j;
-            float sum[BMM_MAXN];
+            float sum[BMM_MAXN / 2];
 #pragma unroll
-            for (int n = 0; n < BMM_MAXN; ++n) sum[n] = 0.0f;
+            for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
+            // scales one quad ahead: the scale plane is read from HBM
             uint2 sw = __ldg(a.sc + (size_t)(b0 >> 2) * a.cols + col);
+            uint2 sw_next = b0 + 4 < b1 ? __ldg(a.sc + (size_t)((b0 >> 2) + 1) * a.cols + col) : sw;
             for (uint32_t b = b0; b < b1; ++b, ++t) {
-                const uint32_t p = t & 1;
-                if ((b & 3) == 0 && b != b0) sw = __ldg(a.sc + (size_t)(b >> 2) * a.cols + col);
+                const uint32_t q = t % BMM_ND;
+                if ((b & 3) == 0 && b != b0) {
+                    sw = sw_next;
+                    if (b + 4 < b1) sw_next = __ldg(a.sc + (size_t)((b >> 2) + 1) * a.cols + col);
+                }
                 const uint32_t word = (b & 2) ? sw.y : sw.x;
                 const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
-                bmm_wait(&dfull[p], (t >> 1) & 1, a.err);
+                bmm_wait_warp(&dfull[q], (t / BMM_ND) & 1, a.err);
                 tc_fence_after();
+                float v[32];
+                const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * N + half * nh;
+                if (nh == 32) tmem_ld32(taddr, v);
+                else tmem_ld16(taddr, v);
 #pragma unroll
-                for (int c0 = 0; c0 < BMM_MAXN; c0 += 32) {
-                    if ((uint32_t)c0 < N) {
-                        float v[32];
-                        tmem_ld32(tmem + ((q * 32) << 16) + p * N + c0, v);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) sum[c0 + i] = fmaf(scale, v[i], sum[c0 + i]);
-                    }
-                }
+                for (int i = 0; i < 32; ++i) sum[i] = fmaf(scale, v[i], sum[i]);
                 tc_fence_before();
-                asm volatile("bar.sync 3, 128;" ::: "memory");
-                if (tid == 192) bmm_arrive(&dempty[p]);
+                asm volatile("bar.sync 3, 256;" ::: "memory");
+                if (tid == 192) bmm_arrive(&dempty[q]);
             }
 #pragma unroll
-            for (int n = 0; n < BMM_MAXN; ++n) {
-                if ((uint32_t)n < a.nreal) {
-                    const float v = sum[n] * a.xs[n];
+            for (int i = 0; i < BMM_MAXN / 2; ++i) {
+                const uint32_t n = half * nh + i;
+                if ((uint32_t)i < nh && n < a.nreal) {
+                    const float v = sum[i] * a.xs[n];
                     if (a.ksplit == 1) {
                         a.out[(size_t)n * a.cols + col] = v;
                     } else {
@@ -336,7 +369,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 1) bmm_kernel(const BmmArgs a) {
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        const uint32_t ncols = 2 * N;
+        const uint32_t ncols = BMM_ND * N;
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
     }
 }

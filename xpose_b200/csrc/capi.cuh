@@ -657,7 +657,7 @@ BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     p.tiles = cols / BMM_M;
     const uint32_t G = (uint32_t)sm_count();
     p.ksplit = std::max<uint32_t>(1, std::min<uint32_t>(p.nblk, (G + p.tiles - 1) / p.tiles));
-    p.cb = (p.nblk + p.ksplit - 1) / p.ksplit;
+    p.cb = ((p.nblk + p.ksplit - 1) / p.ksplit + 3) & ~3u;  // whole quads
     p.ksplit = (p.nblk + p.cb - 1) / p.cb;
     p.nitems = p.tiles * p.ksplit;
     p.off_xs = 0;      // [64] per-sequence scales
@@ -665,10 +665,16 @@ BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     p.off_xb = 512;
     p.off_acc = p.off_xb + (size_t)p.nblk * 2 * 4 * p.npad * 16;
     p.bytes = p.off_acc + (p.ksplit > 1 ? (size_t)p.npad * cols * 8 : 0);
-    p.smem = (size_t)BMM_STAGES * (2048 + 2 * 4 * p.npad * 16) + 2 * 8192 + 8 * (2 * BMM_STAGES + 8) + 16;
+    p.smem = (size_t)BMM_STAGES * (2048 + 2 * 4 * p.npad * 16) + BMM_NA * 8192 + 8 * (2 * BMM_STAGES + 2 * BMM_NA + 2 * BMM_ND) + 16;
     return p;
 }
 }  // namespace
+#ifdef BMM_TRACE
+void xp_bmm_trace_read(unsigned long long* out) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(out, g_bmm_trace, sizeof(g_bmm_trace));
+}
+#endif
 size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n) {
     if (rows == 0 || rows % 128 || cols == 0 || cols % 128 || n == 0 || n > BMM_MAXN) return 0;
     return bmm_plan(rows, cols, n).bytes;
@@ -696,12 +702,12 @@ xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const ui
     XP_CUDA_TRY(cudaGetLastError());
     bmm_prep_kernel<<<(p.nblk * p.npad * 32 + 255) / 256, 256, 0, st>>>(in, rows, n, p.npad, xs, xb);
     XP_CUDA_TRY(cudaGetLastError());
-    static bool attr_set[64] = {};
+    static size_t attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-        XP_CUDA_TRY(cudaFuncSetAttribute(bmm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-        attr_set[dev] = true;
+    if (dev < 64 && attr_set[dev] < p.smem) {
+        XP_CUDA_TRY(cudaFuncSetAttribute(bmm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+        attr_set[dev] = p.smem;
     }
     BmmArgs a{};
     a.wq = reinterpret_cast<const uint4*>(wq);
@@ -718,7 +724,7 @@ xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const ui
     a.cb = p.cb;
     a.nitems = p.nitems;
     a.err = err;
-    const uint32_t grid = std::min<uint32_t>(p.nitems, (uint32_t)sm_count());
+    const uint32_t grid = std::min<uint32_t>(p.nitems, 2 * (uint32_t)sm_count());
     bmm_kernel<<<grid, BMM_THREADS, p.smem, st>>>(a);
     XP_CUDA_TRY(cudaGetLastError());
     if (acc) {
