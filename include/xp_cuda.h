@@ -315,6 +315,28 @@ xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per
  * out[0] = barriers; out[1] = start ns; out[2k], out[2k+1] = barrier k
  * arrive / leave ns (CTA 0, %globaltimer); out[2*barriers+2] = end ns. */
 xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n);
+
+/* ---- batched decode ---------------------------------------------------------
+ * nseq (<= 64) independent sequences advance one position together over the
+ * weights of session `s` (which must outlive the batch): per step every int4
+ * matvec is one tensor-core launch for all sequences (xp_mv_km4_bs_batch), the
+ * per-sequence norms, RoPE, fp16 KV append and attention run one CTA per
+ * sequence, and sampling is the batch-1 sampler per sequence with the uniform
+ * keyed (seed, seq0 + sequence, position). Each sequence computes what a
+ * DecodeSession (examples/llm/decode.cpp:1790-1866) computes for it alone; the
+ * reference has no batched engine. Calls follow its order: prefill feeds
+ * tokens [n][nseq] (position-major) one position at a time; step samples the
+ * previous pass's logits, returns those tokens and runs the network on them. */
+typedef struct xp_bdec xp_bdec;
+xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const xp_sampling* sp, uint64_t seq0,
+                         xp_bdec** out);
+xp_status xp_bdec_prefill(xp_bdec* b, const uint32_t* tokens, uint32_t n);
+xp_status xp_bdec_step(xp_bdec* b, uint32_t* tokens_out);
+/* n steps on the device without reading tokens back; device time in ms */
+xp_status xp_bdec_generate(xp_bdec* b, uint32_t n, float* ms);
+xp_status xp_bdec_logits(xp_bdec* b, float* out, size_t n);
+xp_status xp_bdec_position(xp_bdec* b, uint32_t* pos);
+void xp_bdec_destroy(xp_bdec* b);
 /* CUDA events on the session stream: stop = 0 records the start, 1 the end
  * and returns the elapsed device ms (brackets host-driven decode_step loops). */
 xp_status xp_session_timer(xp_session* s, int stop, float* ms);

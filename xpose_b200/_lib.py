@@ -89,6 +89,14 @@ _SIGS = {
     "xp_mv_reduce": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     "xp_mv_km4_bs_batch_scratch_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32]),
     "xp_mv_km4_bs_batch": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "xp_bdec_create": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(Sampling), C.c_uint64,
+                                 C.POINTER(C.c_void_p)]),
+    "xp_bdec_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "xp_bdec_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "xp_bdec_generate": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_float)]),
+    "xp_bdec_logits": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "xp_bdec_position": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32)]),
+    "xp_bdec_destroy": (None, [C.c_void_p]),
     "xp_mv_plan_create": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p)]),
     "xp_mv_plan_run": (C.c_int, [C.c_void_p, C.c_void_p]),
     "xp_mv_plan_bytes": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint64)]),

@@ -208,9 +208,8 @@ XP_DEV void bitonic_desc(uint64_t* k, uint32_t n) {
 
 // Phase 1: CTA b sorts its slice of `slice` logits (power of two) and emits
 // its best TK keys. Any global top-TK element is in its slice's top-TK.
-__global__ void topk_slice_kernel(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand) {
-    extern __shared__ uint64_t keys[];
-    pdl_wait();
+XP_DEV void topk_slice_body(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand,
+                            uint64_t* keys) {
     const uint32_t base = blockIdx.x * slice;
     for (uint32_t i = threadIdx.x; i < slice; i += blockDim.x) {
         const uint32_t g = base + i;
@@ -219,18 +218,25 @@ __global__ void topk_slice_kernel(const float* logits, uint32_t n, uint32_t slic
     bitonic_desc(keys, slice);
     for (uint32_t i = threadIdx.x; i < tk; i += blockDim.x) cand[(size_t)blockIdx.x * tk + i] = keys[i];
 }
+__global__ void topk_slice_kernel(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand) {
+    extern __shared__ uint64_t keys[];
+    pdl_wait();
+    topk_slice_body(logits, n, slice, tk, cand, keys);
+}
+// Batched decode: sequence blockIdx.y, logits [seq][n], candidates [seq][gridDim.x * tk].
+__global__ void topk_slice_batch_kernel(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand) {
+    extern __shared__ uint64_t keys[];
+    topk_slice_body(logits + (size_t)blockIdx.y * n, n, slice, tk, cand + (size_t)blockIdx.y * gridDim.x * tk, keys);
+}
 
 // Phase 2 (one CTA): exact top-k of the candidates, then decode.cpp:1873-1917's
 // draw(): weights exp((l - max)/T) in fp32, sums in double, top-p keeps the
 // crossing token, multinomial walk with r = u * sum, u from the seeded
 // counter generator keyed (seed, sequence, position).
-__global__ void topk_sample_kernel(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
-                                   float temperature, float top_p, uint64_t seed, uint64_t seq_id,
-                                   uint32_t* token, float* sample_out, uint32_t* pos, float* out_vals,
-                                   uint32_t* out_idx, const uint32_t* pos_read, uint32_t* hist) {
-    extern __shared__ uint64_t keys[];
-    __shared__ float w[256];
-    pdl_wait();
+XP_DEV void topk_sample_body(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
+                             float temperature, float top_p, uint64_t seed, uint64_t seq_id, uint32_t* token,
+                             float* sample_out, uint32_t* pos, float* out_vals, uint32_t* out_idx,
+                             const uint32_t* pos_read, uint32_t* hist, uint64_t* keys, float* w) {
     for (uint32_t i = threadIdx.x; i < ncand_pow2; i += blockDim.x) keys[i] = i < ncand ? cand[i] : 0ull;
     bitonic_desc(keys, ncand_pow2);
     uint32_t k = top_k ? min(top_k, ncand) : ncand;
@@ -269,6 +275,28 @@ __global__ void topk_sample_kernel(const uint64_t* cand, uint32_t ncand_pow2, ui
             if (hist) hist[p + 1] = chosen;
         }
     }
+}
+__global__ void topk_sample_kernel(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
+                                   float temperature, float top_p, uint64_t seed, uint64_t seq_id,
+                                   uint32_t* token, float* sample_out, uint32_t* pos, float* out_vals,
+                                   uint32_t* out_idx, const uint32_t* pos_read, uint32_t* hist) {
+    extern __shared__ uint64_t keys[];
+    __shared__ float w[256];
+    pdl_wait();
+    topk_sample_body(cand, ncand_pow2, ncand, top_k, temperature, top_p, seed, seq_id, token, sample_out, pos,
+                     out_vals, out_idx, pos_read, hist, keys, w);
+}
+// Batched decode: sequence blockIdx.x draws from its candidates with the
+// uniform keyed (seed, seq0 + sequence, pos[sequence]); positions are read,
+// not advanced.
+__global__ void topk_sample_batch_kernel(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
+                                         float temperature, float top_p, uint64_t seed, uint64_t seq0, uint32_t* tokens,
+                                         const uint32_t* pos) {
+    extern __shared__ uint64_t keys[];
+    __shared__ float w[256];
+    const uint32_t b = blockIdx.x;
+    topk_sample_body(cand + (size_t)b * ncand, ncand_pow2, ncand, top_k, temperature, top_p, seed, seq0 + b,
+                     tokens + b, nullptr, nullptr, nullptr, nullptr, pos + b, nullptr, keys, w);
 }
 
 }  // namespace xp

@@ -1,0 +1,229 @@
+// Batched decode: B independent sequences advance one position per step over
+// the same weights. The int4 matvecs run on the tensor cores (bmm.cuh); the
+// per-sequence work between them runs here, one CTA per sequence. Arithmetic
+// follows the reference's per-token ops (examples/llm/decode.cpp:1634-1780,
+// kernels/llm_transformer.cl) exactly as the batch-1 path does: gemma RMSNorm
+// x * rsqrt(mean(x^2) + eps) * (1 + w), QK-norm per head, rotate-half RoPE with
+// theta^(-2d/256) rounded once from double, fp16 KV cache, max-subtracted
+// softmax, tanh-approximate GeGLU.
+#pragma once
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace xp {
+
+constexpr int BK_THREADS = 512;
+
+// x[b] = embed[token[b]] * scale
+__global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, float scale, float* x, uint32_t H) {
+    const uint32_t b = blockIdx.x;
+    const float* row = embed + (size_t)tokens[b] * H;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)b * H + i] = row[i] * scale;
+}
+
+// mode 0: xn = rmsnorm_gemma(x, w_pre)
+// mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)
+__global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, const float* y, const float* w_post,
+                                                                 const float* w_pre, float* xn, uint32_t H, float eps,
+                                                                 int mode) {
+    __shared__ float red[32];
+    const uint32_t b = blockIdx.x;
+    float* xb = x + (size_t)b * H;
+    const float* yb = y + (size_t)b * H;
+    constexpr int J = 4;  // H <= 2048
+    float r[J];
+    if (mode == 1) {
+        float yv[J], ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const uint32_t i = threadIdx.x + j * BK_THREADS;
+            yv[j] = i < H ? yb[i] : 0.0f;
+            ss += yv[j] * yv[j];
+        }
+        ss = block_sum(ss, red);
+        const float sc = rsqrtf(ss / (float)H + eps);
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const uint32_t i = threadIdx.x + j * BK_THREADS;
+            r[j] = i < H ? xb[i] + yv[j] * sc * (1.0f + w_post[i]) : 0.0f;
+            if (i < H) xb[i] = r[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const uint32_t i = threadIdx.x + j * BK_THREADS;
+            r[j] = i < H ? xb[i] : 0.0f;
+        }
+    }
+    float ss2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) ss2 += r[j] * r[j];
+    ss2 = block_sum(ss2, red);
+    const float sc2 = rsqrtf(ss2 / (float)H + eps);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const uint32_t i = threadIdx.x + j * BK_THREADS;
+        if (i < H) xn[(size_t)b * H + i] = r[j] * sc2 * (1.0f + w_pre[i]);
+    }
+}
+
+__global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
+    if (threadIdx.x < B) pos[threadIdx.x] += 1;
+}
+
+__global__ void bk_geglu_kernel(const float* g, const float* u, float* hb, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) hb[i] = gelu_tanh_ref(g[i]) * u[i];
+}
+
+// One CTA per sequence: QK-norm + RoPE of the raw q (4 heads) and k, fp16 KV
+// append at pos[b], then 4-head attention over [kv_start, pos] of this
+// sequence's cache (window 0 = global). Dynamic smem: 4 * span_max floats.
+struct BkAttnArgs {
+    const float* q;        // [B][1024] raw
+    const float* k;        // [B][256]
+    const float* v;        // [B][256]
+    const float* qn;       // [256] q_norm weights
+    const float* kn;       // [256] k_norm weights
+    __half* kc;            // [B][max_seq][256]
+    __half* vc;
+    const uint32_t* pos;   // [B]
+    float* att;            // [B][1024]
+    uint32_t max_seq, window;
+    float theta, eps, scale;
+};
+__global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const BkAttnArgs a) {
+    extern __shared__ __align__(16) float bsm_f[];
+    __shared__ float qs[4 * 256];
+    __shared__ float red[4 * 4 * 256];  // P.V partials [4 groups][4 heads][256]
+    __shared__ __align__(16) __half knew[256], vnew[256];
+    __shared__ float cs[256];           // cos | sin for this position
+    const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t pos = a.pos[b];
+    const uint32_t seq = pos + 1;
+    const uint32_t kv_start = (a.window == 0 || seq <= a.window) ? 0 : seq - a.window;
+    const uint32_t span = seq - kv_start;
+    float* sc = bsm_f;  // [4][max_span]
+    const uint32_t ms = a.window ? min(a.window, a.max_seq) : a.max_seq;
+    if (tid < 128) {
+        const float inv = rope_inv_freq(tid, 256, a.theta);
+        float s, c;
+        sincosf((float)pos * inv, &s, &c);
+        cs[tid] = c;
+        cs[128 + tid] = s;
+    }
+    __syncthreads();
+    __half* kcb = a.kc + (size_t)b * a.max_seq * 256;
+    __half* vcb = a.vc + (size_t)b * a.max_seq * 256;
+    if (warp < 6) {
+        // warps 0-3: q heads, 4: k, 5: v; lane holds dims 4 lane..+3 and 128 + 4 lane..+3
+        const float* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
+        if (warp < 5) {
+            const float* w = warp < 4 ? a.qn : a.kn;
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+            ss = warp_sum(ss);
+            const float s = rsqrtf(ss / 256.0f + a.eps);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t d = 4 * lane + i;
+                const float lo = v[i] * s * (1.0f + w[d]);
+                const float hi = v[4 + i] * s * (1.0f + w[128 + d]);
+                v[i] = lo * cs[d] - hi * cs[128 + d];
+                v[4 + i] = lo * cs[128 + d] + hi * cs[d];
+            }
+        }
+        if (warp < 4) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                qs[warp * 256 + 4 * lane + i] = v[i] * a.scale;
+                qs[warp * 256 + 128 + 4 * lane + i] = v[4 + i] * a.scale;
+            }
+        } else {
+            __half* dst = warp == 4 ? knew : vnew;
+            __half* cache = warp == 4 ? kcb : vcb;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
+                dst[4 * lane + i] = lo;
+                dst[128 + 4 * lane + i] = hi;
+                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
+                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
+            }
+        }
+    }
+    __syncthreads();
+    // scores: one key per warp, lane holds 8 dims of every head
+    for (uint32_t jj = warp; jj < span; jj += BK_THREADS / 32) {
+        const uint32_t j = kv_start + jj;
+        const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(knew + 8 * lane)
+                                   : *reinterpret_cast<const uint4*>(kcb + (size_t)j * 256 + 8 * lane);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+        float kf[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h2[i]);
+            kf[2 * i] = f.x;
+            kf[2 * i + 1] = f.y;
+        }
+        float s4[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc = fmaf(qs[h * 256 + 8 * lane + i], kf[i], acc);
+            s4[h] = acc;
+        }
+        const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
+        if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * ms + jj] = tot;
+    }
+    __syncthreads();
+    __shared__ float sums[4];
+    if (warp < 4) {
+        float m = -INFINITY;
+        for (uint32_t jj = lane; jj < span; jj += 32) m = fmaxf(m, sc[warp * ms + jj]);
+        m = warp_max(m);
+        float sum = 0.0f;
+        for (uint32_t jj = lane; jj < span; jj += 32) {
+            const float p = expf(sc[warp * ms + jj] - m);
+            sc[warp * ms + jj] = p;
+            sum += p;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) sums[warp] = sum;
+    }
+    __syncthreads();
+    {
+        const uint32_t dp = tid & 127, qr = tid >> 7;
+        float acc[4][2] = {};
+        for (uint32_t jj = qr; jj < span; jj += 4) {
+            const uint32_t j = kv_start + jj;
+            const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vnew)[dp]
+                                        : reinterpret_cast<const __half2*>(vcb + (size_t)j * 256)[dp];
+            const float2 vf = __half22float2(hv);
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float p = sc[h * ms + jj];
+                acc[h][0] = fmaf(p, vf.x, acc[h][0]);
+                acc[h][1] = fmaf(p, vf.y, acc[h][1]);
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            red[(qr * 4 + h) * 256 + 2 * dp] = acc[h][0];
+            red[(qr * 4 + h) * 256 + 2 * dp + 1] = acc[h][1];
+        }
+    }
+    __syncthreads();
+    for (uint32_t i = tid; i < 1024; i += BK_THREADS) {
+        const float t = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
+        a.att[(size_t)b * 1024 + i] = t / sums[i >> 8];
+    }
+}
+
+}  // namespace xp

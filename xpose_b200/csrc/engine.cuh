@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "runtime.cuh"
+#include "batch.cuh"
 #include "token_kernel.cuh"
 
 namespace xp {
@@ -914,6 +915,246 @@ xp_status xp_session_error_word(xp_session* s, uint32_t* w) {
     uint32_t* err = static_cast<uint32_t*>(s->attn_scratch) + 1;
     XP_CUDA_TRY(cudaMemcpy(w, err, 4, cudaMemcpyDeviceToHost));
     XP_CUDA_TRY(cudaMemset(err, 0, 4));
+    return XP_OK;
+}
+
+}  // extern "C"
+
+// ============================================================================
+// Batched decode: B sequences over one session's weights (tensor-core matvecs)
+// ============================================================================
+struct xp_bdec {
+    xp_session* s = nullptr;
+    int device = 0;
+    cudaStream_t st = nullptr;
+    uint32_t B = 0, max_seq = 0;
+    xp_sampling sp{};
+    uint64_t seq0 = 0;
+    std::vector<void*> allocs;
+    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
+    float *g = nullptr, *u = nullptr, *hb = nullptr, *dn = nullptr, *logits = nullptr;
+    std::vector<__half*> kc, vc;
+    uint32_t *tokens = nullptr, *pos = nullptr, *h_tok = nullptr;
+    unsigned char* bscratch = nullptr;
+    uint64_t* cand = nullptr;
+    uint32_t ns = 0, nc = 0, p2 = 0;
+    cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    uint32_t h_pos = 0;  // every sequence is at the same position
+
+    ~xp_bdec() {
+        cudaSetDevice(device);
+        if (st) cudaStreamSynchronize(st);
+        for (cudaGraphExec_t ge : {g_fwd, g_step})
+            if (ge) cudaGraphExecDestroy(ge);
+        for (cudaEvent_t e : {ev_a, ev_b})
+            if (e) cudaEventDestroy(e);
+        for (void* p : allocs) cudaFree(p);
+        if (h_tok) cudaFreeHost(h_tok);
+        if (st) cudaStreamDestroy(st);
+    }
+    template <class T> xp_status alloc(T** p, size_t count) {
+        void* d = nullptr;
+        cudaError_t e = cudaMalloc(&d, count * sizeof(T) + 256);
+        if (e != cudaSuccess) return fail(XP_ERR_OOM, "batch: cudaMalloc(%zu) failed: %s", count * sizeof(T),
+                                          cudaGetErrorString(e));
+        cudaMemset(d, 0, count * sizeof(T) + 256);
+        allocs.push_back(d);
+        *p = static_cast<T*>(d);
+        return XP_OK;
+    }
+    cudaError_t mm(float* out, const float* in, const QW& w) {
+        const xp_status e = xp_mv_km4_bs_batch(st, out, in, reinterpret_cast<const uint32_t*>(w.wq),
+                                               reinterpret_cast<const uint32_t*>(w.sc), w.rows, w.cols, B, bscratch);
+        return e == XP_OK ? cudaSuccess : cudaErrorUnknown;
+    }
+    // one position for every sequence: tokens -> logits, pos += 1
+    cudaError_t forward() {
+        const xp_model_config& c = s->cfg;
+        const uint32_t H = c.hidden, F = c.ffn, L = c.n_layers;
+        const float escale = c.embed_scale > 0 ? c.embed_scale : std::sqrt((float)H);
+        const float ascale = c.attn_scale > 0 ? c.attn_scale : 1.0f / std::sqrt((float)c.head_dim);
+        cudaError_t e;
+        bk_embed_kernel<<<B, 256, 0, st>>>(tokens, s->embed, escale, x, H);
+        for (uint32_t l = 0; l < L; ++l) {
+            const LayerDev& W = s->L[l];
+            if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], xn, H, c.rms_eps, 0);
+            else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], xn, H, c.rms_eps, 1);
+            if ((e = mm(q, xn, W.m[0])) != cudaSuccess) return e;
+            if ((e = mm(k, xn, W.m[1])) != cudaSuccess) return e;
+            if ((e = mm(v, xn, W.m[2])) != cudaSuccess) return e;
+            BkAttnArgs aa{};
+            aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
+            aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = att; aa.max_seq = max_seq;
+            const bool glob = s->is_global(l);
+            aa.window = glob ? 0 : c.sliding_window;
+            aa.theta = glob ? c.rope_theta_global : c.rope_theta_local;
+            aa.eps = c.rms_eps;
+            aa.scale = ascale;
+            const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
+            bk_attn_kernel<<<B, BK_THREADS, (size_t)4 * ms * 4, st>>>(aa);
+            if ((e = mm(o, att, W.m[3])) != cudaSuccess) return e;
+            bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], xn, H, c.rms_eps, 1);
+            if ((e = mm(g, xn, W.m[4])) != cudaSuccess) return e;
+            if ((e = mm(u, xn, W.m[5])) != cudaSuccess) return e;
+            const size_t nf = (size_t)B * F;
+            bk_geglu_kernel<<<(uint32_t)((nf + 255) / 256), 256, 0, st>>>(g, u, hb, nf);
+            if ((e = mm(dn, hb, W.m[6])) != cudaSuccess) return e;
+        }
+        bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, xn, H, c.rms_eps, 1);
+        if ((e = mm(logits, xn, s->lm)) != cudaSuccess) return e;
+        bk_pos_inc_kernel<<<1, 64, 0, st>>>(pos, B);
+        return cudaGetLastError();
+    }
+    // tokens[b] = sample(logits[b]) with the uniform of (seed, seq0 + b, pos[b])
+    cudaError_t sample() {
+        const uint32_t V = s->cfg.vocab;
+        topk_slice_batch_kernel<<<dim3(ns, B), 256, TOPK_SLICE * 8, st>>>(logits, V, TOPK_SLICE, TOPK_TK, cand);
+        const uint32_t topk = sp.greedy ? 1u : (sp.top_k == 0 || sp.top_k > TOPK_TK ? TOPK_TK : sp.top_k);
+        topk_sample_batch_kernel<<<B, 1024, (size_t)p2 * 8, st>>>(cand, p2, nc, topk, sp.temperature, sp.top_p,
+                                                                sp.seed, seq0, tokens, pos);
+        return cudaGetLastError();
+    }
+    xp_status capture(cudaGraphExec_t* out, bool with_sample) {
+        cudaGraph_t gr = nullptr;
+        XP_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = with_sample ? sample() : cudaSuccess;
+        if (e == cudaSuccess) e = forward();
+        cudaError_t e2 = cudaStreamEndCapture(st, &gr);
+        if (e != cudaSuccess || e2 != cudaSuccess) {
+            if (gr) cudaGraphDestroy(gr);
+            return fail(XP_ERR_CUDA, "batch: graph capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+        }
+        e = cudaGraphInstantiate(out, gr, 0);
+        cudaGraphDestroy(gr);
+        if (e != cudaSuccess) return fail(XP_ERR_CUDA, "batch: graph instantiate failed: %s", cudaGetErrorString(e));
+        return XP_OK;
+    }
+};
+
+extern "C" {
+
+xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const xp_sampling* sp, uint64_t seq0,
+                          xp_bdec** out) {
+    if (!s || !sp || !out) return fail(XP_ERR_INVALID, "xp_bdec_create: null argument");
+    *out = nullptr;
+    if (nseq == 0 || nseq > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_bdec_create: 1..%d sequences (got %u)", BMM_MAXN, nseq);
+    if (max_seq == 0 || max_seq > s->cfg.max_seq)
+        return fail(XP_ERR_INVALID, "xp_bdec_create: max_seq %u (1..%u)", max_seq, s->cfg.max_seq);
+    if (s->cfg.hidden > 4 * BK_THREADS || s->cfg.hidden % 128 || s->cfg.ffn % 128 || s->cfg.vocab % 128)
+        return fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: hidden <= 2048 and hidden, ffn, vocab multiples of 128");
+    if ((size_t)4 * max_seq * 4 > 200 * 1024)
+        return fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: max_seq %u exceeds the attention kernel's score buffer", max_seq);
+    auto* b = new xp_bdec();
+    b->s = s;
+    b->device = s->device;
+    b->B = nseq;
+    b->max_seq = max_seq;
+    b->sp = *sp;
+    b->seq0 = seq0;
+    cudaSetDevice(b->device);
+    auto bail = [&](xp_status st) { delete b; return st; };
+    if (cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreate(&b->ev_a) != cudaSuccess || cudaEventCreate(&b->ev_b) != cudaSuccess)
+        return bail(fail(XP_ERR_CUDA, "xp_bdec_create: stream/event creation failed"));
+    const xp_model_config& c = s->cfg;
+    const size_t H = c.hidden, F = c.ffn, QD = s->q_dim(), KVD = s->kv_dim(), V = c.vocab;
+    xp_status e;
+#define BA(p, n) if ((e = b->alloc(&b->p, (n))) != XP_OK) return bail(e)
+    BA(x, nseq * H); BA(xn, nseq * H); BA(q, nseq * QD); BA(k, nseq * KVD); BA(v, nseq * KVD); BA(att, nseq * QD);
+    BA(o, nseq * H); BA(g, nseq * F); BA(u, nseq * F); BA(hb, nseq * F); BA(dn, nseq * H); BA(logits, nseq * V);
+    BA(tokens, nseq); BA(pos, nseq);
+#undef BA
+    b->kc.resize(c.n_layers);
+    b->vc.resize(c.n_layers);
+    for (uint32_t l = 0; l < c.n_layers; ++l) {
+        if ((e = b->alloc(&b->kc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
+        if ((e = b->alloc(&b->vc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
+    }
+    size_t sb = 0;
+    const uint32_t shapes[5][2] = {{(uint32_t)H, (uint32_t)QD}, {(uint32_t)H, (uint32_t)KVD}, {(uint32_t)QD, (uint32_t)H},
+                                   {(uint32_t)H, (uint32_t)F}, {(uint32_t)F, (uint32_t)H}};
+    for (auto& sh : shapes) sb = std::max(sb, xp_mv_km4_bs_batch_scratch_bytes(sh[0], sh[1], nseq));
+    sb = std::max(sb, xp_mv_km4_bs_batch_scratch_bytes((uint32_t)H, (uint32_t)V, nseq));
+    if (sb == 0) return bail(fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: a matrix shape is not supported by the batched matvec"));
+    if ((e = b->alloc(&b->bscratch, sb)) != XP_OK) return bail(e);
+    b->ns = (uint32_t)((V + TOPK_SLICE - 1) / TOPK_SLICE);
+    b->nc = b->ns * TOPK_TK;
+    b->p2 = pow2_ceil(b->nc);
+    if ((e = b->alloc(&b->cand, (size_t)nseq * b->nc)) != XP_OK) return bail(e);
+    if (cudaHostAlloc(&b->h_tok, (size_t)nseq * 4, cudaHostAllocDefault) != cudaSuccess)
+        return bail(fail(XP_ERR_OOM, "xp_bdec_create: pinned buffer"));
+    XP_CUDA_TRY(cudaFuncSetAttribute(bk_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    XP_CUDA_TRY(cudaFuncSetAttribute(topk_sample_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    // warm every kernel once outside capture (attributes, lazy loading)
+    if (b->forward() != cudaSuccess) return bail(fail(XP_ERR_CUDA, "xp_bdec_create: warm-up forward failed"));
+    XP_CUDA_TRY(cudaMemsetAsync(b->pos, 0, (size_t)nseq * 4, b->st));
+    XP_CUDA_TRY(cudaStreamSynchronize(b->st));
+    if ((e = b->capture(&b->g_fwd, false)) != XP_OK) return bail(e);
+    if ((e = b->capture(&b->g_step, true)) != XP_OK) return bail(e);
+    *out = b;
+    return XP_OK;
+}
+
+void xp_bdec_destroy(xp_bdec* b) { delete b; }
+
+xp_status xp_bdec_prefill(xp_bdec* b, const uint32_t* tokens, uint32_t n) {
+    if (!b || (!tokens && n)) return fail(XP_ERR_INVALID, "xp_bdec_prefill: null argument");
+    if (b->h_pos + n > b->max_seq) return fail(XP_ERR_KV_FULL, "xp_bdec_prefill: %u + %u > max_seq %u", b->h_pos, n, b->max_seq);
+    cudaSetDevice(b->device);
+    for (uint32_t t = 0; t < n; ++t) {
+        std::memcpy(b->h_tok, tokens + (size_t)t * b->B, (size_t)b->B * 4);
+        XP_CUDA_TRY(cudaMemcpyAsync(b->tokens, b->h_tok, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->st));
+        XP_CUDA_TRY(cudaGraphLaunch(b->g_fwd, b->st));
+        XP_CUDA_TRY(cudaStreamSynchronize(b->st));  // h_tok is reused
+        ++b->h_pos;
+    }
+    return XP_OK;
+}
+
+xp_status xp_bdec_step(xp_bdec* b, uint32_t* tokens_out) {
+    if (!b) return fail(XP_ERR_INVALID, "xp_bdec_step: null batch");
+    if (b->h_pos == 0) return fail(XP_ERR_STATE, "xp_bdec_step: prefill at least one token first");
+    if (b->h_pos + 1 > b->max_seq) return fail(XP_ERR_KV_FULL, "xp_bdec_step: position %u at max_seq", b->h_pos);
+    cudaSetDevice(b->device);
+    XP_CUDA_TRY(cudaGraphLaunch(b->g_step, b->st));
+    ++b->h_pos;
+    if (tokens_out) {
+        XP_CUDA_TRY(cudaMemcpyAsync(b->h_tok, b->tokens, (size_t)b->B * 4, cudaMemcpyDeviceToHost, b->st));
+        XP_CUDA_TRY(cudaStreamSynchronize(b->st));
+        std::memcpy(tokens_out, b->h_tok, (size_t)b->B * 4);
+    }
+    return XP_OK;
+}
+
+xp_status xp_bdec_generate(xp_bdec* b, uint32_t n, float* ms) {
+    if (!b) return fail(XP_ERR_INVALID, "xp_bdec_generate: null batch");
+    if (b->h_pos == 0) return fail(XP_ERR_STATE, "xp_bdec_generate: prefill at least one token first");
+    if (b->h_pos + n > b->max_seq) return fail(XP_ERR_KV_FULL, "xp_bdec_generate: %u + %u > max_seq", b->h_pos, n);
+    cudaSetDevice(b->device);
+    XP_CUDA_TRY(cudaEventRecord(b->ev_a, b->st));
+    for (uint32_t i = 0; i < n; ++i) XP_CUDA_TRY(cudaGraphLaunch(b->g_step, b->st));
+    XP_CUDA_TRY(cudaEventRecord(b->ev_b, b->st));
+    XP_CUDA_TRY(cudaEventSynchronize(b->ev_b));
+    b->h_pos += n;
+    float t = 0;
+    XP_CUDA_TRY(cudaEventElapsedTime(&t, b->ev_a, b->ev_b));
+    if (ms) *ms = t;
+    return XP_OK;
+}
+
+xp_status xp_bdec_logits(xp_bdec* b, float* out, size_t n) {
+    if (!b || !out) return fail(XP_ERR_INVALID, "xp_bdec_logits: null argument");
+    const size_t all = (size_t)b->B * b->s->cfg.vocab;
+    cudaSetDevice(b->device);
+    XP_CUDA_TRY(cudaStreamSynchronize(b->st));
+    XP_CUDA_TRY(cudaMemcpy(out, b->logits, std::min(n, all) * 4, cudaMemcpyDeviceToHost));
+    return XP_OK;
+}
+
+xp_status xp_bdec_position(xp_bdec* b, uint32_t* pos) {
+    if (!b || !pos) return fail(XP_ERR_INVALID, "xp_bdec_position: null argument");
+    *pos = b->h_pos;
     return XP_OK;
 }
 

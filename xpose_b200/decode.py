@@ -216,3 +216,55 @@ class DecodeSession:
             self.close()
         except Exception:
             pass
+
+
+class BatchDecode:
+    """nseq independent sequences decoded together over a DecodeSession's
+    weights (C ABI xp_bdec_*): tensor-core int4 matvecs for all sequences at
+    once, per-sequence attention and sampling. Sequence b samples with the
+    uniforms of seq_id = seq0 + b, as a DecodeSession with that seq_id would."""
+
+    def __init__(self, session, nseq, max_seq, sampling=None, seq0=0):
+        self.session = session  # keeps the weights alive
+        self.nseq = nseq
+        self.vocab = session.cfg.vocab
+        sp = (sampling or Sampling())._c()
+        h = C.c_void_p()
+        check(lib().xp_bdec_create(session._h, nseq, max_seq, C.byref(sp), seq0, C.byref(h)))
+        self._h = h
+
+    def prefill(self, tokens):
+        """tokens: [nseq][n] (one prompt per sequence, equal lengths)."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.uint32).T)
+        check(lib().xp_bdec_prefill(self._h, t.ctypes.data, t.shape[0]))
+
+    def step(self):
+        out = np.zeros(self.nseq, np.uint32)
+        check(lib().xp_bdec_step(self._h, out.ctypes.data))
+        return out
+
+    def generate(self, n):
+        ms = C.c_float()
+        check(lib().xp_bdec_generate(self._h, n, C.byref(ms)))
+        return ms.value
+
+    def logits(self):
+        out = np.empty((self.nseq, self.vocab), np.float32)
+        check(lib().xp_bdec_logits(self._h, out.ctypes.data, out.size))
+        return out
+
+    def position(self):
+        p = C.c_uint32()
+        check(lib().xp_bdec_position(self._h, C.byref(p)))
+        return p.value
+
+    def close(self):
+        if self._h:
+            lib().xp_bdec_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
