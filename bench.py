@@ -21,6 +21,12 @@ roofline : the persistent token kernel (the only kernel of a decode step):
         average device duration.
 cpu_baseline : the CPU restatement of the same decode (oracle/, "port"),
         timed on this host's cores over a bounded sample.
+batched : BASELINE config 4's batched decode: 64 independent sequences per
+        GPU (prompts of 128 uniform-random ids, then 256 sampled tokens with
+        top-k 64 / top-p 0.95 / T 1.0), every int4 matvec one tensor-core
+        launch for all sequences (xp_bdec_*); tokens/s over the 256 decode
+        steps (device time), all ranks' sequences / the slowest rank under
+        torchrun (data-parallel replicas, no collective).
 matvec : BASELINE configs 1 and 2 on the streaming int4 matvec
         (xp_mv_plan_*: many matvecs in one persistent launch), timed with CUDA
         events over whole plan runs (limb prep included): config 1 = W
@@ -59,6 +65,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
@@ -98,6 +105,28 @@ def config1_plan(copies=64, rows=1152, cols=6912):
     plan = C.c_void_p()
     check(lib().xp_mv_plan_create(C.cast(arr, C.c_void_p), len(jobs), C.byref(plan)))
     return plan, keep
+
+
+def batched_bench(sess, cfg, rank, world, max_over_ranks, barrier, nseq=64, prompt=128, new=256):
+    """BASELINE config 4 (batched part) on this rank's GPU."""
+    from xpose_b200.decode import BatchDecode, Sampling
+    bd = BatchDecode(sess, nseq, prompt + new + 1,
+                     Sampling(greedy=False, temperature=1.0, top_k=64, top_p=0.95, seed=4242), seq0=rank * nseq)
+    try:
+        prompts = np.random.default_rng(500 + rank).integers(0, cfg.vocab, (nseq, prompt), dtype=np.uint32)
+        bd.prefill(prompts)
+        toks = bd.step()  # the first decode step (untimed warm-up)
+        barrier()
+        ms = bd.generate(new - 1)
+        ms = max_over_ranks(ms)
+        return {"workload": f"{nseq} sequences per GPU, prompt {prompt}, {new} new tokens, top-k 64 / top-p 0.95 / "
+                            "T 1.0 (BASELINE config 4, batched part)",
+                "value": round(world * nseq * (new - 1) / (ms / 1000.0), 1), "unit": "tok/s",
+                "ms_per_step": round(ms / (new - 1), 3), "sequences": world * nseq,
+                "kernel": "bmm_kernel (tcgen05.mma kind::f16, TMEM accumulators) for every int4 matvec",
+                "first_tokens": [int(t) for t in toks[:4]]}
+    finally:
+        bd.close()
 
 
 def matvec_bench(sess, peak):
@@ -439,6 +468,13 @@ def main():
         except Exception as e:  # the checker arm must not hide the GPU result
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
 
+    bat = None
+    if not args.no_batched:
+        try:
+            bat = batched_bench(sess, cfg, rank, world, max_over_ranks, barrier)
+        except Exception as e:  # a failure here must not hide the decode result
+            bat = {"error": str(e)}
+
     mv = None
     if rank == 0 and not args.no_matvec:
         try:
@@ -468,6 +504,7 @@ def main():
             "clocks": clock_info,
             "cpu_baseline": cpu,
             "matvec": mv,
+            "batched": bat,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
