@@ -66,11 +66,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
     ap.add_argument("--no-batched", action="store_true")
-    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec"], default=None,
+    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
                          "five-kernel graph path on the bench model, 'matvec' = three runs of the config-1 "
-                         "matvec plan")
+                         "matvec plan, 'bmm' = three tensor-core batched matvecs of the LM head for 64 sequences")
     return ap.parse_args()
 
 
@@ -166,6 +166,26 @@ def matvec_bench(sess, peak):
 
 def ncu_case(which):
     """A short, untimed run used as the target of the ncu captures in profiles/."""
+    if which == "bmm":
+        import torch
+        from xpose_b200._lib import check, lib
+        rows, cols, n = 1152, 262144, 64
+        w = torch.empty(rows * cols, dtype=torch.float32, device="cuda")
+        check(lib().xp_gen_normal(None, w.data_ptr(), rows * cols, 0, 0, 1, 0.02))
+        wq = torch.empty(rows * cols // 8, dtype=torch.int32, device="cuda")
+        sc = torch.empty(rows * cols // 64, dtype=torch.int32, device="cuda")
+        check(lib().xp_pack_km4bf16(None, w.data_ptr(), rows, cols, wq.data_ptr(), sc.data_ptr()))
+        del w
+        x = torch.randn(n * rows, device="cuda")
+        out = torch.empty(n * cols, device="cuda")
+        nb = lib().xp_mv_km4_bs_batch_scratch_bytes(rows, cols, n)
+        scr = torch.empty(nb // 4 + 64, dtype=torch.int32, device="cuda")
+        for _ in range(3):
+            check(lib().xp_mv_km4_bs_batch(None, out.data_ptr(), x.data_ptr(), wq.data_ptr(), sc.data_ptr(), rows, cols,
+                                           n, scr.data_ptr()))
+        torch.cuda.synchronize()
+        print("ncu case bmm: 3 batched LM-head matvecs, 64 sequences")
+        return 0
     if which == "matvec":
         import torch
         from xpose_b200._lib import check, lib
