@@ -316,6 +316,20 @@ xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per
  * arrive / leave ns (CTA 0, %globaltimer); out[2*barriers+2] = end ns. */
 xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n);
 
+/* ---- tensor-parallel LM head ------------------------------------------------
+ * `world` processes (one GPU each, same weights, same tokens) split the LM
+ * head's 262,144 rows evenly; each token kernel computes its rank's logits and
+ * argmax, then writes its (value, index) into every rank's exchange buffer over
+ * NVLink (CUDA IPC mappings) and takes the lowest-index maximum (the reference's
+ * argmax rule, kernels/llm_sampling.cl:57-123) once all ranks' entries arrived
+ * (bounded wait; error bit 32 on timeout). Greedy sampling only. Collective:
+ * every rank calls xp_session_tp_handle, the handles (64 bytes each, rank
+ * order) are exchanged on the host, then every rank calls
+ * xp_session_tp_attach before its next decode. No counterpart in the
+ * reference, which runs on one device. */
+xp_status xp_session_tp_handle(xp_session* s, void* handle64);
+xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, const void* handles);
+
 /* ---- batched decode ---------------------------------------------------------
  * nseq (<= 64) independent sequences advance one position together over the
  * weights of session `s` (which must outlive the batch): per step every int4

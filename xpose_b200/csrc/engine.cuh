@@ -78,6 +78,8 @@ struct xp_session {
     uint32_t* h_in = nullptr;
     uint32_t* h_out = nullptr;
     cudaGraphExec_t g_dev = nullptr, g_io = nullptr, g_prefill = nullptr;
+    uint32_t* tp_buf = nullptr;              // this rank's LM-head exchange slots (IPC-exported)
+    std::vector<void*> tp_peers;             // opened peer mappings
     cudaEvent_t ev_done = nullptr, ev_a = nullptr, ev_b = nullptr;
     uint32_t host_pos = 0;
     bool have_logits = false;
@@ -106,6 +108,7 @@ struct xp_session {
         for (cudaGraphExec_t g : {g_dev, g_io, g_prefill, g_mv})
             if (g) cudaGraphExecDestroy(g);
         if (mv_plan) xp_mv_plan_destroy(mv_plan);
+        for (void* p : tp_peers) cudaIpcCloseMemHandle(p);
         for (cudaEvent_t e : {ev_done, ev_a, ev_b})
             if (e) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
@@ -483,6 +486,14 @@ struct xp_session {
         tk.bar = tk_bar; tk.epoch = tk_bar + 1;
         tk.err = static_cast<uint32_t*>(attn_scratch) + 1;
         tk.greedy = sp.greedy;
+        // LM head unsharded until xp_session_tp_attach
+        tk.head_u0 = 0;
+        tk.head_u1 = tk.head.units;
+        tk.tp_rank = 0;
+        tk.tp_world = 1;
+        if ((e = alloc(&tp_buf, TK_TP_MAX * sizeof(TkTpSlot) / 4)) != XP_OK) return e;
+        if ((e = alloc(&tk.tp_count, 4)) != XP_OK) return e;
+        tk.tp_slots[0] = reinterpret_cast<TkTpSlot*>(tp_buf);
         XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
         XP_CUDA_TRY(cudaStreamSynchronize(st));
         return XP_OK;
@@ -1156,6 +1167,57 @@ xp_status xp_bdec_position(xp_bdec* b, uint32_t* pos) {
     if (!b || !pos) return fail(XP_ERR_INVALID, "xp_bdec_position: null argument");
     *pos = b->h_pos;
     return XP_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+xp_status xp_session_tp_handle(xp_session* s, void* handle) {
+    if (!s || !handle) return fail(XP_ERR_INVALID, "xp_session_tp_handle: null argument");
+    if (!s->use_tk) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_handle: needs the persistent token kernel path");
+    cudaSetDevice(s->device);
+    cudaIpcMemHandle_t h;
+    XP_CUDA_TRY(cudaIpcGetMemHandle(&h, s->tp_buf));
+    std::memcpy(handle, &h, sizeof(h));
+    return XP_OK;
+}
+
+xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, const void* handles) {
+    if (!s || !handles) return fail(XP_ERR_INVALID, "xp_session_tp_attach: null argument");
+    if (!s->use_tk) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: needs the persistent token kernel path");
+    if (!s->sp.greedy) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: the sharded LM head exchanges argmax only (greedy)");
+    if (world == 0 || world > TK_TP_MAX || rank >= world)
+        return fail(XP_ERR_INVALID, "xp_session_tp_attach: rank %u of %u (world 1..%u)", rank, world, TK_TP_MAX);
+    cudaSetDevice(s->device);
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    for (void* p : s->tp_peers) cudaIpcCloseMemHandle(p);
+    s->tp_peers.clear();
+    const unsigned char* hb = static_cast<const unsigned char*>(handles);
+    for (uint32_t r = 0; r < world; ++r) {
+        if (r == rank) {
+            s->tk.tp_slots[r] = reinterpret_cast<TkTpSlot*>(s->tp_buf);
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)r * sizeof(h), sizeof(h));
+        void* p = nullptr;
+        XP_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        s->tp_peers.push_back(p);
+        s->tk.tp_slots[r] = static_cast<TkTpSlot*>(p);
+    }
+    // units of 64 vocabulary rows split evenly; every rank runs the same launches
+    const uint32_t U = s->tk.head.units;
+    s->tk.head_u0 = (uint32_t)((uint64_t)U * rank / world);
+    s->tk.head_u1 = (uint32_t)((uint64_t)U * (rank + 1) / world);
+    s->tk.tp_rank = rank;
+    s->tk.tp_world = world;
+    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, TK_TP_MAX * sizeof(TkTpSlot)));
+    XP_CUDA_TRY(cudaMemset(s->tk.tp_count, 0, 4));
+    for (cudaGraphExec_t* g : {&s->g_dev, &s->g_io, &s->g_prefill})
+        if (*g) { cudaGraphExecDestroy(*g); *g = nullptr; }
+    return s->build_graphs();
 }
 
 }  // extern "C"

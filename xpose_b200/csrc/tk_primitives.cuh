@@ -12,6 +12,7 @@ constexpr uint32_t TK_ERR_GRID_BAR = 2u;     // grid barrier wait ran out
 constexpr uint32_t TK_ERR_MBAR = 4u;         // bulk-copy wait ran out
 constexpr uint32_t TK_ERR_PLAN = 8u;         // a unit did not fit its slot
 constexpr uint32_t TK_ERR_RANGE = 16u;       // a K-split sum outside the fixed-point range
+constexpr uint32_t TK_ERR_TP_WAIT = 32u;     // a tensor-parallel peer's entry never arrived
 
 // A wait of ~1 s on these loops is far beyond any phase (a token is < 1 ms).
 constexpr uint32_t TK_SPIN_LIMIT = 1u << 22;

@@ -95,6 +95,16 @@ struct TkLayer {
     uint32_t global;      // RoPE table: 1 = global theta, 0 = local
 };
 
+// Tensor-parallel LM head: every rank's best (value, index) lands in one slot
+// of every rank's exchange buffer; flag = the launch counter + 1.
+struct TkTpSlot {
+    float val;
+    uint32_t idx;
+    uint32_t flag;
+    uint32_t pad;
+};
+constexpr uint32_t TK_TP_MAX = 8;
+
 struct TkArgs {
     const TkLayer* layers;
     uint32_t n_layers, H, F, QD, KVD, V;
@@ -129,6 +139,10 @@ struct TkArgs {
     uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
     uint32_t off_xn, off_xq, off_q, off_sc, off_red, off_misc;
     uint32_t head_ring;   // LM-head ring buffers laid from off_qkv on
+    uint32_t head_u0, head_u1;          // this rank's LM-head units [u0, u1)
+    uint32_t tp_rank, tp_world;         // tensor-parallel group of the LM head (world 1 = none)
+    TkTpSlot* tp_slots[TK_TP_MAX];      // every rank's exchange buffer (peer mappings), TK_TP_MAX slots each
+    uint32_t* tp_count;                 // launches so far (this rank), the exchange flag
 };
 
 // ---- helpers -------------------------------------------------------------------
@@ -337,7 +351,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         fill(tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
         wait_empty(TK_ME_DOWN);
         uint32_t i = 0;
-        for (uint32_t t = c; t < a.head.units; t += G, ++i) {
+        for (uint32_t t = a.head_u0 + c; t < a.head_u1; t += G, ++i) {
             const uint32_t r = i % a.head_ring;
             if (i >= a.head_ring) wait_empty(TK_ME_HEAD + r);
             fence_proxy_async();
@@ -723,7 +737,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 }
             } else {
                 // ---------------- 64-column tiles: QKV, O, DOWN (one), HEAD (ring) ----------------
-                const uint32_t ntile = k == TK_S_HEAD ? (P.units > c ? (P.units - c + G - 1) / G : 0) : (has ? 1 : 0);
+                const uint32_t hu = a.head_u1 - a.head_u0;
+                const uint32_t ntile = k == TK_S_HEAD ? (hu > c ? (hu - c + G - 1) / G : 0) : (has ? 1 : 0);
                 const int full = k == TK_S_QKV ? TK_MB_QKV : (k == TK_S_O ? TK_MB_O : TK_MB_DOWN);
                 long long* acc = k == TK_S_QKV ? a.acc_qkv : (k == TK_S_O ? a.acc_o : a.acc_dn);
                 const uint32_t accw = k == TK_S_QKV ? QKVW : H;
@@ -744,7 +759,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     if (k == TK_S_HEAD) {
                         if (tid == 0) mbar_arrive(&mb[TK_ME_HEAD + r]);  // the producer refills it
                         if (warp == 0) {
-                            const uint32_t t = c + i * G;
+                            const uint32_t t = a.head_u0 + c + i * G;
                             float v0 = red[lane], v1 = red[lane + 32];
                             a.logits[(size_t)t * 64 + lane] = v0;
                             a.logits[(size_t)t * 64 + lane + 32] = v1;
@@ -822,6 +837,39 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 const float ov = __shfl_xor_sync(0xffffffffu, v, o);
                 const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
                 if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+            }
+            if (a.tp_world > 1) {
+                // lane r publishes this rank's best into rank r's slot
+                // [tp_rank] over NVLink, then waits for rank r's entry in our
+                // own buffer (bounded) and the warp keeps the lowest-index max
+                const uint32_t flag = *a.tp_count + 1;
+                if ((uint32_t)lane < a.tp_world) {
+                    TkTpSlot* dst = a.tp_slots[lane] + a.tp_rank;
+                    dst->val = v;
+                    dst->idx = ix;
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(&dst->flag), "r"(flag) : "memory");
+                }
+                float rv = -INFINITY;
+                uint32_t ri = 0xFFFFFFFFu;
+                if ((uint32_t)lane < a.tp_world) {
+                    const TkTpSlot* src = a.tp_slots[a.tp_rank] + lane;
+                    uint32_t f = 0, it = 0;
+                    do {
+                        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&src->flag) : "memory");
+                        if (++it > TK_SPIN_LIMIT) { atomicOr(a.err, TK_ERR_TP_WAIT); break; }
+                    } while (f != flag);
+                    rv = *reinterpret_cast<const volatile float*>(&src->val);
+                    ri = *reinterpret_cast<const volatile uint32_t*>(&src->idx);
+                }
+                v = rv;
+                ix = ri;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                    const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
+                    if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+                }
+                if (lane == 0) *a.tp_count = flag;
             }
             if (lane == 0) {
                 if (ix == 0xFFFFFFFFu) ix = 0;

@@ -201,6 +201,18 @@ class DecodeSession:
         per = per[per[:, 0, 0] != 0]
         return per - t0
 
+    def tp_handle(self):
+        """64-byte IPC handle of this session's LM-head exchange buffer."""
+        buf = (C.c_ubyte * 64)()
+        check(lib().xp_session_tp_handle(self._h, buf))
+        return bytes(buf)
+
+    def tp_attach(self, rank, world, handles):
+        """Shard the LM head over `world` ranks (handles in rank order)."""
+        blob = b"".join(handles)
+        assert len(blob) == 64 * world
+        check(lib().xp_session_tp_attach(self._h, rank, world, blob))
+
     def error_word(self):
         w = C.c_uint32()
         check(lib().xp_session_error_word(self._h, C.byref(w)))
