@@ -36,7 +36,10 @@ matvec : BASELINE configs 1 and 2 on the streaming int4 matvec
 
 Under torchrun (N > 1) each rank decodes its own independent sequence on its
 own GPU (data-parallel replicas, weak scaling); value = all ranks' tokens /
-the slowest rank's device time.
+the slowest rank's device time. The `tp` object then reports one sequence
+decoded by all N GPUs together with the LM head's rows split over them (the
+argmax exchanged over NVLink inside the token kernel): tokens/s of that one
+sequence, the slowest rank's device time.
 """
 import argparse
 import json
@@ -66,6 +69,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
     ap.add_argument("--no-batched", action="store_true")
+    ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
@@ -488,6 +492,26 @@ def main():
         except Exception as e:  # the checker arm must not hide the GPU result
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
 
+    tp = None
+    if world > 1 and not args.no_tp:
+        try:
+            from xpose_b200.tp import shard_lm_head
+            shard_lm_head(sess)
+            sess.reset()
+            tprompt = np.random.default_rng(77).integers(0, cfg.vocab, PROMPT, dtype=np.uint32)
+            sess.prefill(tprompt)
+            sess.generate(W, want_tokens=False)
+            kt = min(K, 1000)
+            barrier()
+            _, tms = sess.generate(kt, want_tokens=False)
+            tms = max_over_ranks(tms)
+            assert sess.error_word() == 0
+            tp = {"workload": f"one sequence, LM head rows split over {world} GPUs (NVLink argmax exchange)",
+                  "value": round(kt / (tms / 1000.0), 2), "unit": "tok/s", "ms_per_step": round(tms / kt, 4),
+                  "steps": kt, "scaling": "strong"}
+        except Exception as e:
+            tp = {"error": str(e)}
+
     bat = None
     if not args.no_batched:
         try:
@@ -525,6 +549,7 @@ def main():
             "cpu_baseline": cpu,
             "matvec": mv,
             "batched": bat,
+            "tp": tp,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
