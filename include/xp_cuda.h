@@ -316,6 +316,13 @@ xp_status xp_session_profile_matvec(xp_session* s, uint32_t iters, float* ms_per
  * arrive / leave ns (CTA 0, %globaltimer); out[2*barriers+2] = end ns. */
 xp_status xp_session_trace(xp_session* s, uint64_t* out, uint32_t n);
 
+/* Failure path self-test: launches one thread whose mbarrier wait and
+ * grid-barrier wait nothing satisfies, each bounded by `spin_limit` polls (the
+ * kernels' own bound is 1 << 22), and returns the error bits they recorded in
+ * *err_word (4 = mbarrier wait, 2 = grid barrier) with the context still
+ * usable. No counterpart in the reference. */
+xp_status xp_selftest_wait_timeout(uint32_t spin_limit, uint32_t* err_word);
+
 /* ---- tensor-parallel LM head ------------------------------------------------
  * `world` processes (one GPU each, same weights, same tokens) split the LM
  * head's 262,144 rows evenly; each token kernel computes its rank's logits and

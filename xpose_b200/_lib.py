@@ -89,6 +89,7 @@ _SIGS = {
     "xp_mv_reduce": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     "xp_mv_km4_bs_batch_scratch_bytes": (C.c_size_t, [C.c_uint32, C.c_uint32, C.c_uint32]),
     "xp_mv_km4_bs_batch": (C.c_int, [C.c_void_p] * 5 + [C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "xp_selftest_wait_timeout": (C.c_int, [C.c_uint32, C.POINTER(C.c_uint32)]),
     "xp_session_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "xp_session_tp_attach": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
     "xp_bdec_create": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(Sampling), C.c_uint64,

@@ -964,6 +964,21 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
     a.att_xq = nullptr;
     return cuda_status(launch_attn(a, scratch, nsplit, max_seq, (cudaStream_t)stream, false), "attention_decode");
 }
+xp_status xp_selftest_wait_timeout(uint32_t spin_limit, uint32_t* err_word) {
+    CHECK_PTR(err_word);
+    if (spin_limit == 0 || spin_limit > TK_SPIN_LIMIT)
+        return fail(XP_ERR_INVALID, "selftest_wait_timeout: spin_limit 1..%u", TK_SPIN_LIMIT);
+    uint32_t* d = nullptr;
+    XP_CUDA_TRY(cudaMalloc(&d, 64));
+    cudaError_t e = cudaMemset(d, 0, 64);
+    if (e == cudaSuccess) {
+        selftest_wait_kernel<<<1, 32>>>(reinterpret_cast<uint64_t*>(d + 8), d, spin_limit);
+        e = cudaDeviceSynchronize();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(err_word, d, 4, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    return cuda_status(e, "selftest_wait_timeout");
+}
 size_t xp_sample_scratch_bytes(uint32_t n) { return sample_scratch_bytes(n); }
 xp_status xp_sample_topk(void* stream, uint32_t* token_dev, float* out_vals, uint32_t* out_idx, const float* logits,
                          uint32_t n, uint32_t top_k, float temperature, float top_p, uint64_t seed, uint64_t seq_id,

@@ -102,4 +102,29 @@ XP_DEV void grid_barrier(uint64_t* counter, uint64_t target, uint32_t* err) {
     __syncthreads();
 }
 
+// Failure-path self-test: one thread waits on an mbarrier nothing arrives on
+// and on a grid-barrier counter nothing increments, each with `limit` polls;
+// both waits give up, record their bits in *err and return, leaving the
+// context usable.
+__global__ void selftest_wait_kernel(uint64_t* counter, uint32_t* err, uint32_t limit) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    uint32_t it = 0;
+    while (!mbar_try_wait(&bar, 0)) {
+        if (++it > limit) {
+            atomicOr(err, TK_ERR_MBAR);
+            break;
+        }
+    }
+    it = 0;
+    while (ld_acquire_u64(counter) < 1ull) {
+        if (++it > limit) {
+            atomicOr(err, TK_ERR_GRID_BAR);
+            break;
+        }
+    }
+}
+
 }  // namespace xp
