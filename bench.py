@@ -27,6 +27,12 @@ batched : BASELINE config 4's batched decode: 64 independent sequences per
         launch for all sequences (xp_bdec_*); tokens/s over the 256 decode
         steps (device time), all ranks' sequences / the slowest rank under
         torchrun (data-parallel replicas, no collective).
+long_context : BASELINE config 5: single-query GQA attention (4 q / 1 kv x 256)
+        over fp16 K/V caches of 8192 positions ~N(0, 1), 26 layers in the
+        5 local (window 512) : 1 global pattern, 26 distinct caches (208 MB >
+        L2), RoPE at position 8191, then top-k 64 / top-p 0.95 / T 1.0
+        sampling on 262,144 logits ~N(0, 3); device time per step and the K/V
+        bytes it reads.
 matvec : BASELINE configs 1 and 2 on the streaming int4 matvec
         (xp_mv_plan_*: many matvecs in one persistent launch), timed with CUDA
         events over whole plan runs (limb prep included): config 1 = W
@@ -70,6 +76,7 @@ def parse():
     ap.add_argument("--no-matvec", action="store_true")
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
+    ap.add_argument("--no-long", action="store_true")
     ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
@@ -131,6 +138,65 @@ def batched_bench(sess, cfg, rank, world, max_over_ranks, barrier, nseq=64, prom
                 "first_tokens": [int(t) for t in toks[:4]]}
     finally:
         bd.close()
+
+
+def long_context_bench(peak, iters=20):
+    """BASELINE config 5 through the C ABI (xp_attention_decode, xp_sample_topk)."""
+    import torch
+    from xpose_b200._lib import check, lib
+    L, S, pos, vocab = 26, 8192, 8191, 262144
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kc = [torch.randn(S * 256, generator=g, device="cuda").half() for _ in range(L)]
+    vc = [torch.randn(S * 256, generator=g, device="cuda").half() for _ in range(L)]
+    q = torch.randn(1024, generator=g, device="cuda")
+    k = torch.randn(256, generator=g, device="cuda")
+    v = torch.randn(256, generator=g, device="cuda")
+    qn = torch.randn(256, generator=g, device="cuda") * 0.02
+    kn = torch.randn(256, generator=g, device="cuda") * 0.02
+    logits = torch.randn(vocab, generator=g, device="cuda") * 3.0
+    out = torch.empty(1024, device="cuda")
+    posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    ns_g, ns_l = 64, 16
+    scr = torch.zeros(lib().xp_attention_scratch_bytes(ns_g) // 4 + 64, dtype=torch.int32, device="cuda")
+    sscr = torch.zeros(lib().xp_sample_scratch_bytes(vocab) // 4 + 64, dtype=torch.int32, device="cuda")
+    layers = [(l, (l + 1) % 6 == 0) for l in range(L)]
+    stream = torch.cuda.Stream()
+
+    def step():
+        st = stream.cuda_stream
+        for l, glob in layers:
+            check(lib().xp_attention_decode(st, out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                            qn.data_ptr(), kn.data_ptr(), kc[l].data_ptr(), vc[l].data_ptr(),
+                                            posd.data_ptr(), 0 if glob else 512, 1e6 if glob else 1e4, 1e-6,
+                                            1.0 / 16, ns_g if glob else ns_l, S, scr.data_ptr()))
+        check(lib().xp_sample_topk(st, tok.data_ptr(), None, None, logits.data_ptr(), vocab, 64, 1.0, 0.95, 7, 0,
+                                   posd.data_ptr(), sscr.data_ptr()))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize()
+    # one step as a CUDA graph: the device time, not Python's submission rate
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    nglob = sum(1 for _, gl in layers if gl)
+    kv_bytes = (nglob * S + (L - nglob) * 512) * 256 * 2 * 2
+    return {"workload": "26 x single-query GQA attention over 8192-position fp16 caches (5 local w512 : 1 global) + "
+                        "top-k 64 / top-p 0.95 sampling on 262144 logits",
+            "us_per_step": round(ms * 1000.0, 1), "kv_bytes": kv_bytes,
+            "kv_GB/s": round(kv_bytes / ms / 1e6, 1), "frac": round(kv_bytes / ms / 1e6 / peak, 4),
+            "launches_per_step": 2 * L + 2}
 
 
 def matvec_bench(sess, peak):
@@ -519,6 +585,13 @@ def main():
         except Exception as e:  # a failure here must not hide the decode result
             bat = {"error": str(e)}
 
+    lc = None
+    if rank == 0 and not args.no_long:
+        try:
+            lc = long_context_bench(peak)
+        except Exception as e:
+            lc = {"error": str(e)}
+
     mv = None
     if rank == 0 and not args.no_matvec:
         try:
@@ -550,6 +623,7 @@ def main():
             "matvec": mv,
             "batched": bat,
             "tp": tp,
+            "long_context": lc,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
