@@ -211,7 +211,7 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
  * array: calls that overlap on the GPU race. Allocates nothing. No counterpart
  * in the reference. */
 #define XP_ATTN_STATIC_MAX_NSPLIT 64u
-#define XP_ATTN_STATIC_SCRATCH_BYTES (64u + 64u * 4u * 256u * 4u + 64u * 8u * 4u)
+#define XP_ATTN_STATIC_SCRATCH_BYTES (512u + 64u * (4u * 256u * 4u + 8u * 4u))
 xp_status xp_attention_decode_static(void* stream, float* out, const float* q_raw, const float* k_raw,
                                      const float* v_raw, const float* q_norm, const float* k_norm,
                                      uint16_t* kcache_f16, uint16_t* vcache_f16, const uint32_t* pos_dev,

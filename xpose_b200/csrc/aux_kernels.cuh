@@ -190,113 +190,322 @@ __global__ void advance_kernel(uint32_t* pos) {
 // reference's top-k with ties to the lower index (llm_sampling.cl:249-286).
 XP_DEV uint64_t topk_key(float v, uint32_t i) { return ((uint64_t)float_key(v) << 32) | (uint64_t)(~i); }
 
-// In-place bitonic sort of n (power of two) keys in shared memory, descending.
-XP_DEV void bitonic_desc(uint64_t* k, uint32_t n) {
-    for (uint32_t size = 2; size <= n; size <<= 1)
-        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            __syncthreads();
-            for (uint32_t i = threadIdx.x; i < n / 2; i += blockDim.x) {
-                const uint32_t lo = 2 * stride * (i / stride) + (i % stride);
-                const uint32_t hi = lo + stride;
-                const bool desc = ((lo & size) == 0);
-                const uint64_t a = k[lo], b = k[hi];
-                if ((a < b) == desc) { k[lo] = b; k[hi] = a; }
+constexpr int TOPK_THREADS = 512;
+
+struct SelShared {
+    uint32_t hist[256];
+    uint32_t digit, remaining, done, count;
+};
+
+// Block-wide radix select over keys[0, n) in shared memory (n >= k, blockDim a
+// multiple of 32): eight-bit
+// digits from the top, one histogram per digit over the keys that still share
+// the selected prefix, until the bin holding the k-th largest key is taken
+// whole. Afterwards key is among the k largest iff (key & mask) >= prefix.
+XP_DEV void block_select(const uint64_t* keys, uint32_t n, uint32_t k, SelShared& s, uint64_t& prefix,
+                         uint64_t& mask) {
+    const uint32_t tid = threadIdx.x, lane = tid & 31;
+    prefix = 0;
+    mask = 0;
+    uint32_t rem = k;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (uint32_t i = tid; i < 256; i += blockDim.x) s.hist[i] = 0;
+        __syncthreads();
+        // logits crowd a few bins: one atomic per distinct bin per warp
+        for (uint32_t i0 = 0; i0 < n; i0 += blockDim.x) {
+            const uint32_t i = i0 + tid;
+            uint32_t bin = 256;
+            if (i < n) {
+                const uint64_t key = keys[i];
+                if ((key & mask) == prefix) bin = (uint32_t)(key >> shift) & 255u;
+            }
+            const uint32_t peers = __match_any_sync(0xffffffffu, bin);
+            if (bin < 256 && lane == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&s.hist[bin], (uint32_t)__popc(peers));
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane L owns bins 255 - 8L down to 248 - 8L
+            uint32_t c[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = s.hist[255 - 8 * lane - j];
+                tot += c[j];
+            }
+            uint32_t incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= (uint32_t)o) incl += t;
+            }
+            uint32_t acc = incl - tot;
+            if (acc < rem && rem <= incl) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (acc + c[j] >= rem) {
+                        s.digit = 255 - 8 * lane - j;
+                        s.remaining = rem - acc;
+                        s.done = c[j] == rem - acc;
+                        break;
+                    }
+                    acc += c[j];
+                }
             }
         }
+        __syncthreads();
+        prefix |= (uint64_t)s.digit << shift;
+        mask |= 255ull << shift;
+        rem = s.remaining;
+        const bool done = s.done;
+        __syncthreads();
+        if (done) break;
+    }
+}
+
+// Writes the k selected keys (any order) to out[0, k).
+XP_DEV void block_collect(const uint64_t* keys, uint32_t n, uint32_t k, uint64_t prefix, uint64_t mask, SelShared& s,
+                          uint64_t* out) {
+    if (threadIdx.x == 0) s.count = 0;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint64_t key = keys[i];
+        if ((key & mask) >= prefix) {
+            const uint32_t slot = atomicAdd(&s.count, 1u);
+            if (slot < k) out[slot] = key;
+        }
+    }
     __syncthreads();
 }
 
-// Phase 1: CTA b sorts its slice of `slice` logits (power of two) and emits
-// its best TK keys. Any global top-TK element is in its slice's top-TK.
-XP_DEV void topk_slice_body(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand,
-                            uint64_t* keys) {
-    const uint32_t base = blockIdx.x * slice;
-    for (uint32_t i = threadIdx.x; i < slice; i += blockDim.x) {
-        const uint32_t g = base + i;
-        keys[i] = g < n ? topk_key(logits[g], g) : 0ull;
+// ---- fast path: an exact lower bound on the k-th largest key, then ranks ------------
+// Candidates ranked by all-pairs counting; more than this takes the radix path.
+constexpr uint32_t TOPK_FAST_MAX = 512;
+
+XP_DEV uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t t = __shfl_xor_sync(0xffffffffu, v, o);
+        v = t > v ? t : v;
     }
-    bitonic_desc(keys, slice);
-    for (uint32_t i = threadIdx.x; i < tk; i += blockDim.x) cand[(size_t)blockIdx.x * tk + i] = keys[i];
-}
-__global__ void topk_slice_kernel(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand) {
-    extern __shared__ uint64_t keys[];
-    pdl_wait();
-    topk_slice_body(logits, n, slice, tk, cand, keys);
-}
-// Batched decode: sequence blockIdx.y, logits [seq][n], candidates [seq][gridDim.x * tk].
-__global__ void topk_slice_batch_kernel(const float* logits, uint32_t n, uint32_t slice, uint32_t tk, uint64_t* cand) {
-    extern __shared__ uint64_t keys[];
-    topk_slice_body(logits + (size_t)blockIdx.y * n, n, slice, tk, cand + (size_t)blockIdx.y * gridDim.x * tk, keys);
+    return v;
 }
 
-// Phase 2 (one CTA): exact top-k of the candidates, then decode.cpp:1873-1917's
-// draw(): weights exp((l - max)/T) in fp32, sums in double, top-p keeps the
-// crossing token, multinomial walk with r = u * sum, u from the seeded
-// counter generator keyed (seed, sequence, position).
-XP_DEV void topk_sample_body(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
-                             float temperature, float top_p, uint64_t seed, uint64_t seq_id, uint32_t* token,
-                             float* sample_out, uint32_t* pos, float* out_vals, uint32_t* out_idx,
-                             const uint32_t* pos_read, uint32_t* hist, uint64_t* keys, float* w) {
-    for (uint32_t i = threadIdx.x; i < ncand_pow2; i += blockDim.x) keys[i] = i < ncand ? cand[i] : 0ull;
-    bitonic_desc(keys, ncand_pow2);
-    uint32_t k = top_k ? min(top_k, ncand) : ncand;
-    if (k > 256) k = 256;
-    if (threadIdx.x == 0) {
-        const float t = temperature > 0.0f ? temperature : 1.0f;
-        const float maxl = key_float((uint32_t)(keys[0] >> 32));
-        double sum = 0.0;
-        for (uint32_t i = 0; i < k; ++i) {
-            const float l = key_float((uint32_t)(keys[i] >> 32));
-            w[i] = expf(__fdiv_rn(__fsub_rn(l, maxl), t));
-            sum += (double)w[i];
-            if (out_vals) { out_vals[i] = l; out_idx[i] = ~(uint32_t)keys[i]; }
+// out[rank] = key for the keys of c[0, m) whose rank (descending, ties by
+// position) is below k. G consecutive lanes share one key's count (G the
+// largest power of two <= 32 with m * G <= blockDim.x).
+template <class T>
+XP_DEV void rank_place(const T* c, uint32_t m, uint32_t k, T* out) {
+    uint32_t G = 1;
+    while (G < 32 && m * G * 2 <= blockDim.x) G <<= 1;
+    const uint32_t part = threadIdx.x & (G - 1);
+    for (uint32_t t0 = 0; t0 < m * G; t0 += blockDim.x) {
+        const uint32_t i = (t0 + threadIdx.x) / G;
+        uint32_t r = 0;
+        T me = 0;
+        if (i < m) {
+            me = c[i];
+            for (uint32_t j = part; j < m; j += G) r += (c[j] > me) || (c[j] == me && j < i);
         }
-        if (top_p > 0.0f && top_p < 1.0f && sum > 0.0) {
-            double acc = 0.0;
-            const double cut = (double)top_p * sum;
-            uint32_t keep = 0;
-            for (; keep < k; ++keep) { acc += (double)w[keep]; if (acc >= cut) break; }
-            k = keep + 1 < k ? keep + 1 : k;
-            sum = 0.0;
-            for (uint32_t i = 0; i < k; ++i) sum += (double)w[i];
-        }
-        const uint32_t p = pos ? *pos : (pos_read ? *pos_read : 0u);
-        const float u = uniform01(seed, seq_id, p);
-        double r = (double)u * sum;
-        uint32_t chosen = ~(uint32_t)keys[k - 1];
-        for (uint32_t i = 0; i < k; ++i) {
-            r -= (double)w[i];
-            if (r <= 0.0) { chosen = ~(uint32_t)keys[i]; break; }
-        }
-        *token = chosen;
-        if (sample_out) { sample_out[0] = (float)chosen; sample_out[1] = 0.0f; }
-        if (pos) {
-            *pos = p + 1;
-            if (hist) hist[p + 1] = chosen;
-        }
+        for (uint32_t o = 1; o < G; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+        if (i < m && part == 0 && r < k) out[r] = me;
     }
 }
-__global__ void topk_sample_kernel(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
-                                   float temperature, float top_p, uint64_t seed, uint64_t seq_id,
-                                   uint32_t* token, float* sample_out, uint32_t* pos, float* out_vals,
-                                   uint32_t* out_idx, const uint32_t* pos_read, uint32_t* hist) {
-    extern __shared__ uint64_t keys[];
-    __shared__ float w[256];
-    pdl_wait();
-    topk_sample_body(cand, ncand_pow2, ncand, top_k, temperature, top_p, seed, seq_id, token, sample_out, pos,
-                     out_vals, out_idx, pos_read, hist, keys, w);
+
+// Warp-aggregated append of `key` (when take) to list[*count] (capacity cap;
+// *count keeps counting past it).
+XP_DEV void append_key(bool take, uint64_t key, uint64_t* list, uint32_t* count, uint32_t cap) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t bal = __ballot_sync(0xffffffffu, take);
+    if (!bal) return;
+    const uint32_t leader = __ffs(bal) - 1;
+    uint32_t off = 0;
+    if (lane == leader) off = atomicAdd(count, (uint32_t)__popc(bal));
+    off = __shfl_sync(0xffffffffu, off, leader);
+    if (take) {
+        const uint32_t idx = off + __popc(bal & ((1u << lane) - 1u));
+        if (idx < cap) list[idx] = key;
+    }
 }
-// Batched decode: sequence blockIdx.x draws from its candidates with the
-// uniform keyed (seed, seq0 + sequence, pos[sequence]); positions are read,
-// not advanced.
-__global__ void topk_sample_batch_kernel(const uint64_t* cand, uint32_t ncand_pow2, uint32_t ncand, uint32_t top_k,
-                                         float temperature, float top_p, uint64_t seed, uint64_t seq0, uint32_t* tokens,
-                                         const uint32_t* pos) {
-    extern __shared__ uint64_t keys[];
-    __shared__ float w[256];
-    const uint32_t b = blockIdx.x;
-    topk_sample_body(cand + (size_t)b * ncand, ncand_pow2, ncand, top_k, temperature, top_p, seed, seq0 + b,
-                     tokens + b, nullptr, nullptr, nullptr, nullptr, pos + b, nullptr, keys, w);
+
+// Phase 1: CTA (slice, sequence) writes the TOPK_TK largest keys of its slice
+// of TOPK_THREADS * 8 logits, in descending order. Any global top-k element
+// (k <= TOPK_TK) survives in its slice's list. Only keys >= a lower bound L on
+// the slice's 64th largest key are ranked (L from a sample of warp maxima).
+// cand: [sequence][slices][TOPK_TK].
+__global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* logits, uint32_t n, uint64_t* cand) {
+    constexpr uint32_t SL = TOPK_THREADS * 8, TK = 64, NW = TOPK_THREADS / 32;
+    static_assert(NW * 8 >= TK, "the sample holds at least 64 keys");
+    __shared__ uint64_t keys[SL];  // radix fallback only
+    __shared__ uint64_t fc[TOPK_FAST_MAX];
+    __shared__ uint32_t samp[NW * 8], sel[TK];
+    __shared__ uint32_t fcount;
+    __shared__ SelShared s;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_launch_dependents();
+    pdl_wait();
+    const float* lg = logits + (size_t)blockIdx.y * n;
+    const uint32_t base = blockIdx.x * SL;
+    uint64_t k[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t g = base + j * TOPK_THREADS + tid;
+        k[j] = g < n ? topk_key(lg[g], g) : 0ull;
+    }
+    // each warp's 8 largest values (8 rounds of a one-instruction warp max
+    // over the 32-bit value keys) sample the slice; every sample stands for a
+    // distinct key at or above it, so the 64th largest of the 128 samples
+    // bounds the slice's 64th largest value from below
+    uint32_t hv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hv[j] = (uint32_t)(k[j] >> 32);
+#pragma unroll 1
+    for (int r = 0; r < 8; ++r) {
+        uint32_t lb = hv[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) lb = max(lb, hv[j]);
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, lb);
+        if (lane == 0) samp[warp * 8 + r] = wm;
+        if (lb == wm) {
+            bool gone = false;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (!gone && hv[j] == wm) { hv[j] = 0; gone = true; }
+        }
+    }
+    if (tid == 0) fcount = 0;
+    __syncthreads();
+    rank_place(samp, NW * 8, TK, sel);
+    __syncthreads();
+    const uint64_t L = (uint64_t)sel[TK - 1] << 32;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) append_key(k[j] >= L, k[j], fc, &fcount, TOPK_FAST_MAX);
+    __syncthreads();
+    const uint32_t m = fcount;
+    uint64_t* out = cand + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * TK;
+    if (m <= TOPK_FAST_MAX) {
+        rank_place(fc, m, TK, out);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) keys[j * TOPK_THREADS + tid] = k[j];
+    __syncthreads();
+    uint64_t prefix, mask;
+    block_select(keys, SL, TK, s, prefix, mask);
+    block_collect(keys, SL, TK, prefix, mask, s, fc);
+    rank_place(fc, TK, TK, out);
+}
+
+// Phase 2 (one CTA per sequence): exact top-k of the candidates, then
+// decode.cpp:1873-1917's draw(): weights exp((l - max)/T) in fp32, sums in
+// double in rank order, top-p keeps the crossing token, multinomial walk with
+// r = u * sum, u from the seeded counter generator keyed (seed, sequence,
+// position). The slice lists are sorted: the k-th largest of their leading keys
+// bounds the global k-th largest from below; only candidates >= it are ranked.
+struct TopkDrawArgs {
+    const uint64_t* cand;  // [sequence][ncand], TOPK_TK-key lists sorted descending
+    uint32_t ncand, top_k;
+    float temperature, top_p;
+    uint64_t seed, seq0;        // sequence b draws with stream seq0 + b
+    uint32_t* token;            // [sequence]
+    float* sample_out;          // optional (id, 0) of sequence 0
+    uint32_t* pos_adv;          // single sequence: read and advanced (hist[p + 1] = token)
+    const uint32_t* pos_read;   // [sequence], read only
+    float* out_vals;            // optional [k] survivors of sequence 0
+    uint32_t* out_idx;
+    uint32_t* hist;
+};
+__global__ void __launch_bounds__(TOPK_THREADS) topk_draw_kernel(const TopkDrawArgs a) {
+    extern __shared__ uint64_t ckeys[];  // radix fallback only
+    __shared__ SelShared s;
+    __shared__ uint64_t fc[TOPK_FAST_MAX];
+    __shared__ uint64_t sorted[64];
+    __shared__ float w[64];
+    __shared__ double cum[64];
+    __shared__ uint32_t fcount, s_keep;
+    pdl_wait();
+    const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t* cand = a.cand + (size_t)b * a.ncand;
+    const uint32_t k = a.top_k, nsl = a.ncand / 64;
+    // lower bound T0 on the global k-th largest key: the k-th largest of the J
+    // leading keys of every (sorted) slice list
+    const uint32_t J = min(64u, max(1u, 128u / nsl)), S = nsl * J;
+    for (uint32_t i = tid; i < S; i += TOPK_THREADS) fc[i] = cand[(i / J) * 64 + i % J];
+    if (tid == 0) fcount = 0;
+    __syncthreads();
+    rank_place(fc, S, k, sorted);
+    __syncthreads();
+    const uint64_t T0 = sorted[k - 1];
+    __syncthreads();
+    for (uint32_t i0 = 0; i0 < a.ncand; i0 += TOPK_THREADS) {
+        const uint32_t i = i0 + tid;
+        const uint64_t key = i < a.ncand ? cand[i] : 0ull;
+        append_key(i < a.ncand && key >= T0, key, fc, &fcount, TOPK_FAST_MAX);
+    }
+    __syncthreads();
+    const uint32_t m = fcount;
+    if (m <= TOPK_FAST_MAX) {
+        rank_place(fc, m, k, sorted);
+    } else {
+        for (uint32_t i = tid; i < a.ncand; i += TOPK_THREADS) ckeys[i] = cand[i];
+        __syncthreads();
+        uint64_t prefix, mask;
+        block_select(ckeys, a.ncand, k, s, prefix, mask);
+        block_collect(ckeys, a.ncand, k, prefix, mask, s, fc);
+        rank_place(fc, k, k, sorted);
+    }
+    __syncthreads();
+    const float tt = a.temperature > 0.0f ? a.temperature : 1.0f;
+    const float maxl = key_float((uint32_t)(sorted[0] >> 32));
+    if (tid < 64) {
+        float wv = 0.0f;
+        if (tid < k) {
+            const float l = key_float((uint32_t)(sorted[tid] >> 32));
+            wv = expf(__fdiv_rn(__fsub_rn(l, maxl), tt));
+            if (a.out_vals && b == 0) { a.out_vals[tid] = l; a.out_idx[tid] = ~(uint32_t)sorted[tid]; }
+        }
+        w[tid] = wv;  // zero past k: adding +0.0 leaves a double sum unchanged
+    }
+    __syncthreads();
+    if (tid == 0) {
+        // running sums in rank order (the reference's sequential double sum)
+        double acc = 0.0;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            acc += (double)w[i];
+            cum[i] = acc;
+        }
+    }
+    __syncthreads();
+    bool use_p = a.top_p > 0.0f && a.top_p < 1.0f && cum[63] > 0.0;
+    if (use_p && warp == 0) {
+        // first rank whose running sum reaches top_p * sum
+        const double cut = (double)a.top_p * cum[63];
+        const bool h0 = lane < k && cum[lane] >= cut, h1 = lane + 32 < k && cum[lane + 32] >= cut;
+        const uint32_t b0 = __ballot_sync(0xffffffffu, h0), b1 = __ballot_sync(0xffffffffu, h1);
+        if (lane == 0) s_keep = b0 ? __ffs(b0) - 1 : (b1 ? 32 + __ffs(b1) - 1 : 64);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t kk = k;
+        if (use_p && s_keep + 1 < kk) kk = s_keep + 1;
+        const double sum = cum[kk - 1];
+        const uint32_t p = a.pos_adv ? *a.pos_adv : (a.pos_read ? a.pos_read[b] : 0u);
+        const float u = uniform01(a.seed, a.seq0 + b, p);
+        double r = (double)u * sum;
+        uint32_t chosen = kk - 1;
+        bool found = false;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            r -= (double)((uint32_t)i < kk ? w[i] : 0.0f);
+            if (!found && r <= 0.0 && (uint32_t)i < kk) { chosen = i; found = true; }
+        }
+        const uint32_t id = ~(uint32_t)sorted[chosen];
+        a.token[b] = id;
+        if (a.sample_out && b == 0) { a.sample_out[0] = (float)id; a.sample_out[1] = 0.0f; }
+        if (a.pos_adv) {
+            *a.pos_adv = p + 1;
+            if (a.hist) a.hist[p + 1] = id;
+        }
+    }
 }
 
 }  // namespace xp

@@ -92,8 +92,9 @@ struct BkAttnArgs {
     float* att;            // [B][1024]
     uint32_t max_seq, window;
     float theta, eps, scale;
+    float inv_freq[128];   // RoPE theta^(-2d/256), from rope_table_host
 };
-__global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const BkAttnArgs a) {
+__global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_constant__ BkAttnArgs a) {
     extern __shared__ __align__(16) float bsm_f[];
     __shared__ float qs[4 * 256];
     __shared__ float red[4 * 4 * 256];  // P.V partials [4 groups][4 heads][256]
@@ -107,9 +108,8 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const BkAttnArgs a)
     float* sc = bsm_f;  // [4][max_span]
     const uint32_t ms = a.window ? min(a.window, a.max_seq) : a.max_seq;
     if (tid < 128) {
-        const float inv = rope_inv_freq(tid, 256, a.theta);
         float s, c;
-        sincosf((float)pos * inv, &s, &c);
+        rope_sincos((float)pos * a.inv_freq[tid], &s, &c);
         cs[tid] = c;
         cs[128 + tid] = s;
     }

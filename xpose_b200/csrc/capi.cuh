@@ -954,6 +954,8 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
     if (nsplit == 0 || nsplit > 1024) return fail(XP_ERR_INVALID, "attention_decode: nsplit must be 1..1024");
     if (attn_smem(attn_chunk_max(nsplit, max_seq)) > 200 * 1024)
         return fail(XP_ERR_INVALID, "attention_decode: max_seq/nsplit too large for shared memory");
+    if (((uintptr_t)out | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)scratch) & 15)
+        return fail(XP_ERR_INVALID, "attention_decode: out, the caches and scratch must be 16-byte aligned");
     AttnArgs a{};
     a.q_raw = q_raw; a.k_raw = k_raw; a.v_raw = v_raw; a.q_norm = q_norm; a.k_norm = k_norm;
     a.kcache = reinterpret_cast<__half*>(kc);
@@ -962,7 +964,9 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
     a.window = window; a.theta = theta; a.eps = eps; a.scale = scale;
     a.att = out;
     a.att_xq = nullptr;
-    return cuda_status(launch_attn(a, scratch, nsplit, max_seq, (cudaStream_t)stream, false), "attention_decode");
+    // programmatic dependent launch: the kernel reads nothing before
+    // griddepcontrol.wait, so its launch may overlap any predecessor's tail
+    return cuda_status(launch_attn(a, scratch, nsplit, max_seq, (cudaStream_t)stream, true), "attention_decode");
 }
 xp_status xp_selftest_wait_timeout(uint32_t spin_limit, uint32_t* err_word) {
     CHECK_PTR(err_word);
@@ -985,10 +989,12 @@ xp_status xp_sample_topk(void* stream, uint32_t* token_dev, float* out_vals, uin
                          const uint32_t* pos_dev, void* scratch) {
     CHECK_PTR(token_dev); CHECK_PTR(logits); CHECK_PTR(pos_dev); CHECK_PTR(scratch);
     if (n < TOPK_TK) return fail(XP_ERR_INVALID, "sample_topk: n must be >= %u", TOPK_TK);
+    if ((n + TOPK_SLICE - 1) / TOPK_SLICE * TOPK_TK > TOPK_MAX_CAND)
+        return fail(XP_ERR_INVALID, "sample_topk: n must be <= %u", TOPK_MAX_CAND / TOPK_TK * TOPK_SLICE);
     if (top_k > TOPK_TK) return fail(XP_ERR_INVALID, "sample_topk: top_k must be <= %u", TOPK_TK);
     return cuda_status(launch_sample_topk(token_dev, nullptr, const_cast<uint32_t*>(pos_dev), out_vals, out_idx,
                                           logits, n, top_k, temperature, top_p, seed, seq_id, scratch,
-                                          (cudaStream_t)stream, false, false),
+                                          (cudaStream_t)stream, true, false),
                        "sample_topk");
 }
 xp_status xp_pack_km4bf16(void* stream, const float* w, uint32_t rows, uint32_t cols, uint32_t* words,

@@ -530,7 +530,7 @@ struct xp_session {
                         c.n_heads, c.n_kv_heads, c.head_dim);
         if (c.hidden % 128 || c.ffn % 128 || c.vocab % 64)
             return fail(XP_ERR_INVALID, "decode: hidden and ffn must be multiples of 128, vocab of 64");
-        if (!sp.greedy && (sp.top_k > 64 || c.vocab < 64))
+        if (!sp.greedy && (sp.top_k > 64 || c.vocab < 64 || c.vocab > TOPK_MAX_CAND / TOPK_TK * TOPK_SLICE))
             return fail(XP_ERR_UNSUPPORTED, "decode: the device sampler supports top_k <= 64");
         return XP_OK;
     }
@@ -948,7 +948,7 @@ struct xp_bdec {
     uint32_t *tokens = nullptr, *pos = nullptr, *h_tok = nullptr;
     unsigned char* bscratch = nullptr;
     uint64_t* cand = nullptr;
-    uint32_t ns = 0, nc = 0, p2 = 0;
+    uint32_t ns = 0, nc = 0;
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     uint32_t h_pos = 0;  // every sequence is at the same position
@@ -1000,6 +1000,7 @@ struct xp_bdec {
             const bool glob = s->is_global(l);
             aa.window = glob ? 0 : c.sliding_window;
             aa.theta = glob ? c.rope_theta_global : c.rope_theta_local;
+            rope_table_host(aa.theta, aa.inv_freq);
             aa.eps = c.rms_eps;
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
@@ -1020,10 +1021,16 @@ struct xp_bdec {
     // tokens[b] = sample(logits[b]) with the uniform of (seed, seq0 + b, pos[b])
     cudaError_t sample() {
         const uint32_t V = s->cfg.vocab;
-        topk_slice_batch_kernel<<<dim3(ns, B), 256, TOPK_SLICE * 8, st>>>(logits, V, TOPK_SLICE, TOPK_TK, cand);
-        const uint32_t topk = sp.greedy ? 1u : (sp.top_k == 0 || sp.top_k > TOPK_TK ? TOPK_TK : sp.top_k);
-        topk_sample_batch_kernel<<<B, 1024, (size_t)p2 * 8, st>>>(cand, p2, nc, topk, sp.temperature, sp.top_p,
-                                                                sp.seed, seq0, tokens, pos);
+        TopkDrawArgs da{};
+        da.top_k = sp.greedy ? 1u : sp.top_k;
+        da.temperature = sp.temperature;
+        da.top_p = sp.top_p;
+        da.seed = sp.seed;
+        da.seq0 = seq0;
+        da.token = tokens;
+        da.pos_read = pos;
+        cudaError_t e = launch_topk(logits, V, B, cand, da, st, false);
+        if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
     xp_status capture(cudaGraphExec_t* out, bool with_sample) {
@@ -1091,12 +1098,10 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     if ((e = b->alloc(&b->bscratch, sb)) != XP_OK) return bail(e);
     b->ns = (uint32_t)((V + TOPK_SLICE - 1) / TOPK_SLICE);
     b->nc = b->ns * TOPK_TK;
-    b->p2 = pow2_ceil(b->nc);
     if ((e = b->alloc(&b->cand, (size_t)nseq * b->nc)) != XP_OK) return bail(e);
     if (cudaHostAlloc(&b->h_tok, (size_t)nseq * 4, cudaHostAllocDefault) != cudaSuccess)
         return bail(fail(XP_ERR_OOM, "xp_bdec_create: pinned buffer"));
     XP_CUDA_TRY(cudaFuncSetAttribute(bk_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    XP_CUDA_TRY(cudaFuncSetAttribute(topk_sample_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     // warm every kernel once outside capture (attributes, lazy loading)
     if (b->forward() != cudaSuccess) return bail(fail(XP_ERR_CUDA, "xp_bdec_create: warm-up forward failed"));
     XP_CUDA_TRY(cudaMemsetAsync(b->pos, 0, (size_t)nseq * 4, b->st));

@@ -3,7 +3,9 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdarg>
+#include <cstring>
 #include <cstdio>
 #include <string>
 
@@ -102,15 +104,41 @@ inline cudaError_t launch_mv(const MvArgs& a, cudaStream_t st, bool pdl, uint32_
 }
 
 // ---- attention -------------------------------------------------------------------------
-inline size_t attn_scratch_bytes(uint32_t nsplit) {
-    return (size_t)nsplit * 4 * 256 * 4 + (size_t)nsplit * 8 * 4 + 64;
+// CTAs per split launch: nsplit, rounded up to a multiple of 8 above 64 so
+// that large grids form clusters of 8 (else 4, 2 or 1 CTAs).
+constexpr uint32_t attn_grid(uint32_t nsplit) { return nsplit <= 64 ? nsplit : (nsplit + 7) & ~7u; }
+constexpr uint32_t attn_cluster(uint32_t grid) { return grid % 8 == 0 ? 8 : grid % 4 == 0 ? 4 : grid % 2 == 0 ? 2 : 1; }
+// scratch: [ticket u32 | error word u32 | pad to 512][cluster partials | cluster stats]
+constexpr size_t ATT_SCRATCH_HDR = 512;
+constexpr size_t attn_scratch_bytes(uint32_t nsplit) {
+    return ATT_SCRATCH_HDR + (size_t)attn_grid(nsplit) * (4 * 256 * 4 + 8 * 4);
 }
 inline uint32_t attn_chunk_max(uint32_t nsplit, uint32_t max_seq) {
     uint32_t c = (max_seq + nsplit - 1) / nsplit;
     return (c + 7) & ~7u;
 }
-inline size_t attn_smem(uint32_t chunk_max) {
-    return 4 * 256 * 4 + 2 * 256 * 2 + 4 * (size_t)chunk_max * 4 + 2 * 4 * 256 * 4 + 8 * 4;
+inline size_t attn_smem(uint32_t chunk_max) { return AttnSmem::bytes(chunk_max); }
+// RoPE inverse frequencies theta^(-2d/256), d < 128, with log2 and exp2 each
+// rounded once from double (the oracle's formula, computed on the host so the
+// device table matches it bit for bit). Small per-thread cache: decode
+// alternates between two thetas.
+inline void rope_table_host(float theta, float* out) {
+    thread_local float cache_theta[4] = {-1.0f, -1.0f, -1.0f, -1.0f};
+    thread_local float cache[4][128];
+    thread_local int next = 0;
+    for (int c = 0; c < 4; ++c)
+        if (cache_theta[c] == theta) {
+            std::memcpy(out, cache[c], 128 * sizeof(float));
+            return;
+        }
+    const float l2 = (float)std::log2((double)theta);
+    for (uint32_t d = 0; d < 128; ++d) {
+        const float frac = (float)(2u * d) / 256.0f;
+        out[d] = (float)std::exp2((double)(-l2 * frac));
+    }
+    cache_theta[next] = theta;
+    std::memcpy(cache[next], out, 128 * sizeof(float));
+    next = (next + 1) & 3;
 }
 inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint32_t max_seq, cudaStream_t st,
                                bool pdl) {
@@ -119,52 +147,63 @@ inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint3
         cudaFuncSetAttribute(attn_decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         attr_set = true;
     }
-    // scratch: [ticket u32 | error word u32 | pad to 64 B | partials | stats]
     char* s = static_cast<char*>(scratch);
+    const uint32_t grid = attn_grid(nsplit), cl = attn_cluster(grid);
     a.ticket = reinterpret_cast<uint32_t*>(s);
     a.err = a.ticket + 1;
-    a.part = reinterpret_cast<float*>(s + 64);
-    a.pstat = reinterpret_cast<float*>(s + 64 + (size_t)nsplit * 4 * 256 * 4);
-    a.chunk_max = attn_chunk_max(nsplit, max_seq);
-    return launch_ex(attn_decode_kernel<4>, dim3(nsplit), dim3(ATT_THREADS), attn_smem(a.chunk_max), st, 1, pdl,
-                     a);
+    a.part = reinterpret_cast<float*>(s + ATT_SCRATCH_HDR);
+    a.pstat = a.part + (size_t)(grid / cl) * 4 * 256;
+    a.chunk_max = attn_chunk_max(grid, max_seq);
+    rope_table_host(a.theta, a.inv_freq);
+    return launch_ex(attn_decode_kernel<4>, dim3(grid), dim3(ATT_THREADS), attn_smem(a.chunk_max), st, cl, pdl, a);
 }
 
 // ---- sampling ----------------------------------------------------------------------------
-constexpr uint32_t TOPK_SLICE = 2048;
+constexpr uint32_t TOPK_SLICE = TOPK_THREADS * 8;
 constexpr uint32_t TOPK_TK = 64;
-inline uint32_t pow2_ceil(uint32_t v) {
-    uint32_t p = 1;
-    while (p < v) p <<= 1;
-    return p;
-}
+constexpr uint32_t TOPK_MAX_CAND = 200 * 1024 / 8;  // phase-2 candidates held in shared memory
 inline size_t sample_scratch_bytes(uint32_t n) {
     const uint32_t ns = (n + TOPK_SLICE - 1) / TOPK_SLICE;
     return (size_t)ns * TOPK_TK * 8 + 64;
+}
+// Two launches over nseq sequences of n logits each: slice candidates, then
+// one drawing CTA per sequence. `cand` holds nseq * slices * TOPK_TK keys.
+inline cudaError_t launch_topk(const float* logits, uint32_t n, uint32_t nseq, uint64_t* cand,
+                               const TopkDrawArgs& da_in, cudaStream_t st, bool pdl) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(topk_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr_set = true;
+    }
+    const uint32_t ns = (n + TOPK_SLICE - 1) / TOPK_SLICE;
+    cudaError_t e = launch_ex(topk_cand_kernel, dim3(ns, nseq), dim3(TOPK_THREADS), 0, st, 1, pdl, logits, n, cand);
+    if (e != cudaSuccess) return e;
+    TopkDrawArgs da = da_in;
+    da.cand = cand;
+    da.ncand = ns * TOPK_TK;
+    if (da.top_k == 0 || da.top_k > TOPK_TK) da.top_k = TOPK_TK;
+    return launch_ex(topk_draw_kernel, dim3(nseq), dim3(TOPK_THREADS), (size_t)da.ncand * 8, st, 1, true, da);
 }
 inline cudaError_t launch_sample_topk(uint32_t* token, float* sample_out, uint32_t* pos_dev, float* out_vals,
                                       uint32_t* out_idx, const float* logits, uint32_t n, uint32_t top_k,
                                       float temperature, float top_p, uint64_t seed, uint64_t seq_id, void* scratch,
                                       cudaStream_t st, bool pdl, bool advance, uint32_t* hist = nullptr) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(topk_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
-    const uint32_t ns = (n + TOPK_SLICE - 1) / TOPK_SLICE;
-    uint64_t* cand = static_cast<uint64_t*>(scratch);
-    cudaError_t e = launch_ex(topk_slice_kernel, dim3(ns), dim3(256), TOPK_SLICE * 8, st, 1, pdl, logits, n,
-                              TOPK_SLICE, TOPK_TK, cand);
-    if (e != cudaSuccess) return e;
-    const uint32_t nc = ns * TOPK_TK;
-    const uint32_t p2 = pow2_ceil(nc);
-    if (top_k == 0 || top_k > TOPK_TK) top_k = TOPK_TK;
+    TopkDrawArgs da{};
+    da.top_k = top_k;
+    da.temperature = temperature;
+    da.top_p = top_p;
+    da.seed = seed;
+    da.seq0 = seq_id;
+    da.token = token;
+    da.sample_out = sample_out;
     // the sampler reads *pos for the uniform's index; it advances it only in
     // the engine (advance == true)
-    return launch_ex(topk_sample_kernel, dim3(1), dim3(1024), (size_t)p2 * 8, st, 1, pdl, (const uint64_t*)cand,
-                     p2, nc, top_k, temperature, top_p, seed, seq_id, token, sample_out,
-                     advance ? pos_dev : (uint32_t*)nullptr, out_vals, out_idx,
-                     advance ? (const uint32_t*)nullptr : (const uint32_t*)pos_dev, hist);
+    da.pos_adv = advance ? pos_dev : nullptr;
+    da.pos_read = advance ? nullptr : pos_dev;
+    da.out_vals = out_vals;
+    da.out_idx = out_idx;
+    da.hist = hist;
+    return launch_topk(logits, n, 1, static_cast<uint64_t*>(scratch), da, st, pdl);
 }
 
 }  // namespace xp

@@ -369,12 +369,12 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     };
 
     // RoPE table for this position: theta^(-2d/256) rounded once from double,
-    // angle pos * inv in fp32, full-precision sincos (llm_transformer.cl:158-179)
+    // angle pos * inv in fp32, sin/cos after an exact reduction (llm_transformer.cl:158-179)
     if (tid < 256) {
         const uint32_t t = tid >> 7, d = tid & 127;
         const float inv = rope_inv_freq(d, 256, t ? a.theta_global : a.theta_local);
         float s, co;
-        sincosf((float)pos * inv, &s, &co);
+        rope_sincos((float)pos * inv, &s, &co);
         rope[t * 256 + d] = co;
         rope[t * 256 + 128 + d] = s;
     }

@@ -29,8 +29,7 @@ extern "C" xp_status xp_attention_decode_static(void* stream, float* out, const 
     if (nsplit == 0 || nsplit > XP_ATTN_STATIC_MAX_NSPLIT)
         return fail(XP_ERR_INVALID, "xp_attention_decode_static: nsplit %u is outside 1..%u (the fixed scratch)",
                     nsplit, (unsigned)XP_ATTN_STATIC_MAX_NSPLIT);
-    static_assert(XP_ATTN_STATIC_SCRATCH_BYTES >= 64 + (size_t)XP_ATTN_STATIC_MAX_NSPLIT * 4 * 256 * 4 +
-                                                        (size_t)XP_ATTN_STATIC_MAX_NSPLIT * 8 * 4,
+    static_assert(XP_ATTN_STATIC_SCRATCH_BYTES >= attn_scratch_bytes(XP_ATTN_STATIC_MAX_NSPLIT),
                   "static scratch smaller than the largest split count needs");
     int dev = 0;
     XP_CUDA_TRY(cudaGetDevice(&dev));
@@ -45,8 +44,8 @@ extern "C" xp_status xp_attention_decode_static(void* stream, float* out, const 
         g_attn_static_ptr[dev] = p;
     }
     void* scratch = g_attn_static_ptr[dev];
-    // the combine ticket and the error word start at zero for every call
-    XP_CUDA_TRY(cudaMemsetAsync(scratch, 0, 64, (cudaStream_t)stream));
+    // the combine tickets and the error word start at zero for every call
+    XP_CUDA_TRY(cudaMemsetAsync(scratch, 0, ATT_SCRATCH_HDR, (cudaStream_t)stream));
     return xp_attention_decode(stream, out, q_raw, k_raw, v_raw, q_norm, k_norm, kcache_f16, vcache_f16, pos_dev,
                                window, theta, eps, scale, nsplit, max_seq, scratch);
 }
