@@ -338,7 +338,7 @@ struct xp_session {
         if (env_int("XP_ENGINE_MULTI", 0)) return false;
         const uint32_t G = (uint32_t)sm_count();
         const uint32_t H = cfg.hidden, F = cfg.ffn, QD = q_dim(), KVD = kv_dim();
-        const uint32_t nbH = H / 32, nbQ = QD / 32, nbF = F / 32;
+        const uint32_t nbH = H / 32, nbQ = QD / 32;
         if (H > 512 * TK_MAXJ || (H / 64) > G || QD + 2 * KVD > 512 * TK_MAXJ) return false;
         if (cfg.vocab % 64) return false;
         const uint32_t tq = (QD + 2 * KVD) / 64;
@@ -346,14 +346,20 @@ struct xp_session {
         const uint32_t ksq = largest_divisor_upto(nbH, std::min<uint32_t>(kmax, G / tq));
         const uint32_t kso = nbQ / 4;  // 128-dim K ranges (inside one 256-dim head)
         const uint32_t to = H / 64;
-        const uint32_t ksd = largest_divisor_upto(nbF, std::min<uint32_t>(kmax, G / to));
-        if (tq * ksq > G || to * kso > G || to * ksd > G || tq == 0 || QD % 128) return false;
+        if (tq * ksq > G || to * kso > G || tq == 0 || QD % 128 || F % 16) return false;
         tk.qkv = mk_phase(tq * ksq, nbH / ksq, 64, 1, ksq, G);
         tk.o = mk_phase(to * kso, 4, 64, 1, kso, G);
         tk.gu = mk_phase(F / 16, nbH, 16, 2, 1, G);
-        tk.down = mk_phase(to * ksd, nbF / ksd, 64, 1, ksd, G);
+        // down-proj rows of every gate|up unit (fused into the GU step)
+        tk.down = TkPhase{};
+        tk.down.units = tk.gu.units;
+        tk.down.cw = H;
+        tk.down.nmat = 1;
+        tk.down.ks = 1;
+        tk.down.img_bytes = H * 10;
+        tk.down.per_cta = tk.gu.per_cta;
         tk.head = mk_phase(cfg.vocab / 64, nbH, 64, 1, 1, G);
-        if (tk.gu.per_cta > 3 || tk.down.nb * 32 > std::max<uint32_t>(H, 128)) return false;
+        if (tk.gu.per_cta > 3 || tk.gu.per_cta * 16 > std::max<uint32_t>(H, 128)) return false;
         // attention: at most TK_SPLIT_CAP splits of at least chunk_min rows
         tk.chunk_min = (uint32_t)std::max(8, env_int("XP_TK_CHUNK_MIN", 16));
         tk.chunk_max = (std::max<uint32_t>(tk.chunk_min, (cfg.max_seq + TK_SPLIT_CAP - 1) / TK_SPLIT_CAP) + 7) & ~7u;
@@ -361,7 +367,7 @@ struct xp_session {
         tk.off_qkv = off; off += al128(tk.qkv.img_bytes);
         tk.off_o = off; off += al128(tk.o.img_bytes);
         tk.off_gu = off; off += al128(tk.gu.per_cta * tk.gu.img_bytes);
-        tk.off_down = off; off += al128(tk.down.img_bytes);
+        tk.off_down = off; off += al128(tk.down.per_cta * tk.down.img_bytes);
         // KV rows of ATTN, then the flash-partial stage of O (512 B per split)
         tk.off_kv = off; off += al128(std::max<uint32_t>(2 * tk.chunk_max * KVD * 2, TK_SPLIT_CAP * 512));
         const uint32_t ring_bytes = off - tk.off_qkv;
@@ -372,7 +378,7 @@ struct xp_session {
         tk.off_cgu = off; off += al128(2 * H * 4);
         tk.off_rope = off; off += al128(512 * 4);
         tk.off_xn = off; off += al128(std::max<uint32_t>(H, 128) * 4);
-        const uint32_t maxnb = std::max(std::max(std::max(tk.qkv.nb, tk.o.nb), std::max(tk.gu.nb, tk.down.nb)), tk.head.nb);
+        const uint32_t maxnb = std::max(std::max(std::max(tk.qkv.nb, tk.o.nb), std::max(tk.gu.nb, tk.gu.per_cta)), tk.head.nb);
         tk.off_xq = off; off += al128(maxnb * (uint32_t)sizeof(XBlk));
         tk.off_q = off; off += al128(4 * 256 * 4 + 2 * 256 * 2);
         tk.off_sc = off; off += al128(4 * tk.chunk_max * 4);
@@ -425,7 +431,9 @@ struct xp_session {
             if ((e = repack(w.m[3], io, tk.o, 0, 0)) != XP_OK) return e;
             if ((e = repack(w.m[4], ig, tk.gu, 0, 0)) != XP_OK) return e;
             if ((e = repack(w.m[5], ig, tk.gu, 1, 0)) != XP_OK) return e;
-            if ((e = repack(w.m[6], id, tk.down, 0, 0)) != XP_OK) return e;
+            repack_half_kernel<<<sm_count() * 8, 256, 0, st>>>(w.m[6].wq, reinterpret_cast<const uint32_t*>(w.m[6].sc),
+                                                              w.m[6].rows, w.m[6].cols, id);
+            XP_CUDA_TRY(cudaGetLastError());
             t.qkv = iq; t.o = io; t.gu = ig; t.down = id;
             // per-phase constant vectors, contiguous for one bulk copy each
             float *cq, *ca, *cgu;
@@ -480,7 +488,7 @@ struct xp_session {
         tk.embed = embed;
         tk.x0 = xa; tk.x1 = xb;
         tk.acc_qkv = aq; tk.acc_o = ao; tk.acc_dn = ad;
-        tk.att_part = attp; tk.att_stat = atts; tk.hb = hb;
+        tk.att_part = attp; tk.att_stat = atts;
         tk.logits = logits; tk.am_val = amv2; tk.am_idx = ami2;
         tk.token = token; tk.pos = pos; tk.hist = hist; tk.sample_out = sample_out;
         tk.bar = tk_bar; tk.epoch = tk_bar + 1;

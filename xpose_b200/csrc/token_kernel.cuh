@@ -2,7 +2,7 @@
 //
 // Grid = one CTA per SM, all co-resident; each CTA is 16 compute warps plus
 // one producer warp. The reference's per-token op order
-// (examples/llm/decode.cpp:1634-1780) runs as five steps per layer separated
+// (examples/llm/decode.cpp:1634-1780) runs as four steps per layer separated
 // by grid barriers, then one LM-head step:
 //
 //   QKV  : residual + post-FFN norm of layer l-1 (or the embedding), attention
@@ -12,8 +12,10 @@
 //   O    : combine the flash partials of this CTA's 128-dim K range, o-proj
 //          unit -> sums
 //   GU   : residual + post-attention norm, FFN norm, gate|up units of 16
-//          columns over all K -> GeGLU -> hb
-//   DOWN : hb slice for this CTA's K range, down-proj unit -> sums
+//          columns over all K -> GeGLU -> hb rows of this CTA, then the
+//          down-proj of exactly those rows for every output column -> sums
+//          (the CTA that makes an hb row is the one that consumes it, so the
+//          down-proj needs no grid barrier of its own)
 //   HEAD : residual + post-FFN + final norm, LM-head tiles, per-CTA argmax;
 //          then CTA 0 picks the lowest-index maximum (greedy).
 //
@@ -22,7 +24,10 @@
 //     than the SM's instruction cache refetches all of it every layer (a cold
 //     ~150-instruction loop cost ~1 us). The layer loop is therefore ONE
 //     phase machine: the norm prologue, the limb prep and the 64-column tile
-//     loop each exist once and serve QKV, O, DOWN and HEAD.
+//     loop each exist once and serve QKV, O and HEAD.
+//   * Grid barriers (~1 us each from the last arrival to the release) are
+//     the dearest thing in a layer, so there are four per layer, the fewest
+//     the data dependences allow.
 //   * K-split sums go through int64 fixed-point accumulators (2^-32 units,
 //     red.add): integer addition is order-independent, so the result is
 //     deterministic, and a consumer loads one vector instead of every partial.
@@ -62,7 +67,8 @@ static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "
 constexpr int TK_SPLIT_CAP = 128;  // attention splits per layer (the O stage holds 512 B each)
 
 // steps of the phase machine
-constexpr uint32_t TK_S_QKV = 0, TK_S_ATTN = 1, TK_S_O = 2, TK_S_GU = 3, TK_S_DOWN = 4, TK_S_HEAD = 5;
+constexpr uint32_t TK_S_QKV = 0, TK_S_ATTN = 1, TK_S_O = 2, TK_S_GU = 3, TK_S_HEAD = 5;
+constexpr uint32_t TK_STEPS = 4;  // steps per layer
 
 // Trace layout (u64 words, %globaltimer ns): [0] barriers, [1] start,
 // [2k, 2k+1] CTA 0 arrive/leave of barrier k, [512 + 8k + i] CTA 0 marks in
@@ -109,7 +115,8 @@ struct TkArgs {
     const TkLayer* layers;
     uint32_t n_layers, H, F, QD, KVD, V;
     float eps, embed_scale, attn_scale, theta_global, theta_local;
-    TkPhase qkv, o, gu, down, head;
+    TkPhase qkv, o, gu, head;
+    TkPhase down;         // down-proj rows of each gate|up unit: units = gu.units, img = H x (uint2 + bf16)
     const unsigned char* head_img;
     const float* c_head;  // [post_ffn of the last layer | final_norm]  2H floats
     const float* embed;
@@ -120,7 +127,6 @@ struct TkArgs {
     long long* acc_dn;    // [H] fixed-point down-proj sums
     float* att_part;      // [QD / 128][grid][128] flash partials, one 128-dim slice per O unit
     float* att_stat;      // [grid][4][2] (max, sum) per split and head
-    float* hb;            // [F]
     float* logits;        // [V]
     float* am_val;        // [grid]
     uint32_t* am_idx;     // [grid]
@@ -183,6 +189,28 @@ XP_DEV void red_add_s64(long long* p, long long v) {
 
 XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
     const int d = xq_dot(w, reinterpret_cast<const int4*>(X.w), X.bias);
+    return (float)d * (X.f * __uint_as_float((uint32_t)s << 16));
+}
+
+// Down-proj of one gate|up unit: its 16 rows are one half of a KM4 block
+// (words 0-1 of the uint4 hold rows 0-15, words 2-3 rows 16-31, and the half
+// image keeps the right pair), dotted against limbs whose block carries the
+// 16 values in rows 0-15 and zeros in rows 16-31.
+XP_DEV float tk_dot_half(const uint2 w, uint16_t s, const XBlk& X) {
+    int a0 = 0, a1 = 0, a2 = 0;
+    const uint32_t ws[2] = {w.x, w.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int lo = (int)(ws[i] & 0x0F0F0F0Fu);
+        const int hi = (int)((ws[i] >> 4) & 0x0F0F0F0Fu);
+        a0 = __dp4a(lo, X.w[0][i], a0);
+        a0 = __dp4a(hi, X.w[0][4 + i], a0);
+        a1 = __dp4a(lo, X.w[1][i], a1);
+        a1 = __dp4a(hi, X.w[1][4 + i], a1);
+        a2 = __dp4a(lo, X.w[2][i], a2);
+        a2 = __dp4a(hi, X.w[2][4 + i], a2);
+    }
+    const int d = (a0 * 128 + a1) * 128 + a2 + X.bias;
     return (float)d * (X.f * __uint_as_float((uint32_t)s << 16));
 }
 
@@ -384,13 +412,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 #define TK_MARK(k) \
     if (a.trace && c == 0 && tid == 0) a.trace[512 + nbar * 8 + (k)] = globaltimer_ns();
 
-    const uint32_t nstep = 5 * L + (a.want_logits ? 1u : 0u);
+    const uint32_t nstep = TK_STEPS * L + (a.want_logits ? 1u : 0u);
     float bv = -INFINITY;  // HEAD: this thread's best logit and its index (warp 0)
     uint32_t bi = 0xFFFFFFFFu;
 #pragma unroll 1
     for (uint32_t step = 0; step < nstep; ++step) {
-        const uint32_t l = step / 5;
-        const uint32_t k = l == L ? TK_S_HEAD : step - 5 * l;
+        const uint32_t l = step / TK_STEPS;
+        const uint32_t k = l == L ? TK_S_HEAD : step - TK_STEPS * l;
         const TkLayer& Ly = a.layers[l < L ? l : L - 1];
 
         // ---------------- input of the step -> xn ----------------
@@ -503,12 +531,6 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 128 + tid];
                     xn[tid] = t / Ls;
                 }
-            }
-        } else if (k == TK_S_DOWN) {
-            if (c < a.down.units) {
-                const uint32_t kc = c % a.down.ks, n = a.down.nb * 32;
-#pragma unroll 1
-                for (uint32_t i = tid; i < n; i += TK_THREADS) xn[i] = a.hb[(size_t)kc * n + i];
             }
         } else {
             // ================= ATTN =================
@@ -670,21 +692,22 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             } else {
                 wait_slot(TK_MB_KV);
             }
-            // the down-proj sums were consumed by this layer's QKV step
+            // the down-proj sums were consumed by this layer's QKV step, the
+            // o-proj sums by the previous layer's GU step
             if (c == G - 1) {
 #pragma unroll 1
-                for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_dn[i] = 0;
+                for (uint32_t i = tid; i < H; i += TK_THREADS) {
+                    a.acc_dn[i] = 0;
+                    a.acc_o[i] = 0;
+                }
             }
         }
 
         if (k != TK_S_ATTN) {
             // ---------------- limbs of xn: one shared prep ----------------
-            const TkPhase& P = k == TK_S_QKV ? a.qkv
-                             : k == TK_S_O   ? a.o
-                             : k == TK_S_GU  ? a.gu
-                             : k == TK_S_DOWN ? a.down : a.head;
+            const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
             const bool has = c < P.units;
-            if (k == TK_S_O || k == TK_S_DOWN) {
+            if (k == TK_S_O) {
                 tk_sync();  // xn complete
                 if (has) {
                     for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[b * 32 + lane], &xq[b]);
@@ -694,7 +717,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             TK_MARK(0)
 
             if (k == TK_S_GU) {
-                // ---------------- gate|up units -> GeGLU -> hb ----------------
+                // ---------------- gate|up units -> GeGLU -> hb -> down-proj ----------------
                 wait_slot(TK_MB_GU);
                 TK_MARK(1)
                 if (has) {
@@ -727,7 +750,30 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                             gs += wp[((2 * ui) * wpp + q) * 16 + cc];
                             up += wp[((2 * ui + 1) * wpp + q) * 16 + cc];
                         }
-                        a.hb[(size_t)(c + ui * G) * 16 + cc] = gelu_tanh_ref(gs) * up;
+                        xn[tid] = gelu_tanh_ref(gs) * up;  // hb row (c + ui G) * 16 + cc
+                    }
+                    tk_sync();
+                    // limbs of each unit's 16 hb values (rows 0-15 of a block)
+                    if ((uint32_t)warp < nu) xq_prep_block(lane < 16 ? xn[warp * 16 + lane] : 0.0f, &xq[warp]);
+                    tk_sync();
+                }
+                // down-proj of this CTA's hb rows for every output column
+                wait_slot(TK_MB_DOWN);
+                TK_MARK(3)
+                if (has) {
+                    uint32_t nu = 0;
+                    for (uint32_t u = c; u < P.units; u += G) ++nu;
+                    const uint32_t ib = a.down.img_bytes;
+#pragma unroll 1
+                    for (uint32_t j = tid; j < H; j += TK_THREADS) {
+                        float s = 0.0f;
+#pragma unroll 1
+                        for (uint32_t ui = 0; ui < nu; ++ui) {
+                            const unsigned char* img = s_down + (size_t)ui * ib;
+                            s += tk_dot_half(reinterpret_cast<const uint2*>(img)[j],
+                                             reinterpret_cast<const uint16_t*>(img + (size_t)H * 8)[j], xq[ui]);
+                        }
+                        red_add_s64(&a.acc_dn[j], tk_fix(s, a.err));
                     }
                 }
                 // the q|k|v sums were consumed by this layer's ATTN step
@@ -736,13 +782,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     for (uint32_t i = tid; i < QKVW; i += TK_THREADS) a.acc_qkv[i] = 0;
                 }
             } else {
-                // ---------------- 64-column tiles: QKV, O, DOWN (one), HEAD (ring) ----------------
+                // ---------------- 64-column tiles: QKV, O (one), HEAD (ring) ----------------
                 const uint32_t hu = a.head_u1 - a.head_u0;
                 const uint32_t ntile = k == TK_S_HEAD ? (hu > c ? (hu - c + G - 1) / G : 0) : (has ? 1 : 0);
-                const int full = k == TK_S_QKV ? TK_MB_QKV : (k == TK_S_O ? TK_MB_O : TK_MB_DOWN);
-                long long* acc = k == TK_S_QKV ? a.acc_qkv : (k == TK_S_O ? a.acc_o : a.acc_dn);
+                const int full = k == TK_S_QKV ? TK_MB_QKV : TK_MB_O;
+                long long* acc = k == TK_S_QKV ? a.acc_qkv : a.acc_o;
                 const uint32_t accw = k == TK_S_QKV ? QKVW : H;
-                const unsigned char* slot = k == TK_S_QKV ? s_qkv : (k == TK_S_O ? s_o : s_down);
+                const unsigned char* slot = k == TK_S_QKV ? s_qkv : s_o;
                 if (ntile == 0 && k != TK_S_HEAD) wait_slot(full);
 #pragma unroll 1
                 for (uint32_t i = 0; i < ntile; ++i) {
@@ -782,11 +828,6 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     }
                     if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
                 }
-                // the o-proj sums were consumed by this layer's GU step
-                if (k == TK_S_DOWN && c == G - 1) {
-#pragma unroll 1
-                    for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_o[i] = 0;
-                }
             }
         }
 
@@ -802,6 +843,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             }
             red_release_add_u64(a.bar, 1ull);
             if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
+            if (k == TK_S_GU) mbar_arrive(&mb[TK_ME_DOWN]);
             const uint64_t target = base + (uint64_t)nbar * G;
             uint32_t it = 0;
             // acquire load + the closing bar.sync order every thread's later
@@ -915,6 +957,25 @@ __global__ void repack_units_kernel(const RepackArgs r) {
         const size_t e = ((size_t)r.mat * r.nb + bl) * r.cw + cl;
         reinterpret_cast<uint4*>(img)[e] = w;
         reinterpret_cast<uint16_t*>(img + (size_t)r.nmat * r.nb * r.cw * 16)[e] = s;
+    }
+}
+
+// Down-proj images for the fused GU step: gate|up unit U (rows 16U..16U+15
+// of the [rows = F][cols = H] down matrix, one half of KM4 block U / 2) gets
+// [cols] uint2 (the half's two nibble words) then [cols] bf16 (the block's
+// scale). The nibbles and scales are the reference's, unchanged.
+__global__ void repack_half_kernel(const uint4* words, const uint32_t* sc, uint32_t rows, uint32_t cols,
+                                   unsigned char* dst) {
+    const uint32_t nblk = rows / 32;
+    const uint64_t total = (uint64_t)(rows / 16) * cols;
+    for (uint64_t id = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; id < total;
+         id += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t j = (uint32_t)(id % cols), U = (uint32_t)(id / cols), b = U / 2;
+        const uint4 w = words[((size_t)(j / 64) * nblk + b) * 64 + (j % 64)];
+        const uint32_t sw = sc[((size_t)(b / 4) * cols + j) * 2 + ((b % 4) >> 1)];
+        unsigned char* img = dst + (size_t)U * cols * 10;
+        reinterpret_cast<uint2*>(img)[j] = (U & 1) ? make_uint2(w.z, w.w) : make_uint2(w.x, w.y);
+        reinterpret_cast<uint16_t*>(img + (size_t)cols * 8)[j] = (uint16_t)((b & 1) ? (sw >> 16) : (sw & 0xFFFFu));
     }
 }
 
