@@ -14,6 +14,15 @@ namespace xp {
 
 constexpr int BK_THREADS = 512;
 
+// Matvec results arrive as int64 fixed-point sums (2^-32 units) that the
+// tensor-core kernel adds into; each is read once, here, and left zero for
+// the next step.
+XP_DEV float bk_take(long long* p) {
+    const float v = __ll2float_rn(*p) * 2.3283064365386963e-10f;
+    *p = 0;
+    return v;
+}
+
 // x[b] = embed[token[b]] * scale
 __global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, float scale, float* x, uint32_t H) {
     const uint32_t b = blockIdx.x;
@@ -22,14 +31,14 @@ __global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, floa
 }
 
 // mode 0: xn = rmsnorm_gemma(x, w_pre)
-// mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)
-__global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, const float* y, const float* w_post,
+// mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)  (y: fixed-point sums)
+__global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, long long* y, const float* w_post,
                                                                  const float* w_pre, float* xn, uint32_t H, float eps,
                                                                  int mode) {
     __shared__ float red[32];
     const uint32_t b = blockIdx.x;
     float* xb = x + (size_t)b * H;
-    const float* yb = y + (size_t)b * H;
+    long long* yb = y + (size_t)b * H;
     constexpr int J = 4;  // H <= 2048
     float r[J];
     if (mode == 1) {
@@ -37,7 +46,7 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, con
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const uint32_t i = threadIdx.x + j * BK_THREADS;
-            yv[j] = i < H ? yb[i] : 0.0f;
+            yv[j] = i < H ? bk_take(yb + i) : 0.0f;
             ss += yv[j] * yv[j];
         }
         ss = block_sum(ss, red);
@@ -72,18 +81,18 @@ __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
     if (threadIdx.x < B) pos[threadIdx.x] += 1;
 }
 
-__global__ void bk_geglu_kernel(const float* g, const float* u, float* hb, size_t n) {
+__global__ void bk_geglu_kernel(long long* g, long long* u, float* hb, size_t n) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) hb[i] = gelu_tanh_ref(g[i]) * u[i];
+    if (i < n) hb[i] = gelu_tanh_ref(bk_take(g + i)) * bk_take(u + i);
 }
 
 // One CTA per sequence: QK-norm + RoPE of the raw q (4 heads) and k, fp16 KV
 // append at pos[b], then 4-head attention over [kv_start, pos] of this
 // sequence's cache (window 0 = global). Dynamic smem: 4 * span_max floats.
 struct BkAttnArgs {
-    const float* q;        // [B][1024] raw
-    const float* k;        // [B][256]
-    const float* v;        // [B][256]
+    long long* q;          // [B][1024] raw, fixed-point sums
+    long long* k;          // [B][256]
+    long long* v;          // [B][256]
     const float* qn;       // [256] q_norm weights
     const float* kn;       // [256] k_norm weights
     __half* kc;            // [B][max_seq][256]
@@ -118,10 +127,10 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
     __half* vcb = a.vc + (size_t)b * a.max_seq * 256;
     if (warp < 6) {
         // warps 0-3: q heads, 4: k, 5: v; lane holds dims 4 lane..+3 and 128 + 4 lane..+3
-        const float* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
+        long long* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
         float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
+        for (int i = 0; i < 8; ++i) v[i] = bk_take(src + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)));
         if (warp < 5) {
             const float* w = warp < 4 ? a.qn : a.kn;
             float ss = 0.0f;

@@ -50,11 +50,12 @@ struct BmmArgs {
     const unsigned char* xb;  // prepared activations: [nblk][hi, lo][chunk 4][N][16 B]
     const float* xs;          // [N] per-sequence power-of-two scale 2^e
     float* out;               // [N][cols] (ksplit == 1)
-    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1), zero at launch
+    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1 or raw), zero at launch
     uint32_t nblk, cols, N;   // N = padded sequence count (32 or 64)
     uint32_t nreal;           // sequences actually present (rows of out)
     uint32_t ksplit, cb;      // K ranges per tile, blocks per range
     uint32_t nitems;          // (cols / 128) * ksplit
+    uint32_t raw;             // 1: leave the result in acc as fixed-point sums (the consumer converts)
     uint32_t* err;
 };
 
@@ -146,41 +147,72 @@ XP_DEV uint4 bmm_unpack8(uint32_t w) {
 
 // Activation prep, pass 1: per sequence the power-of-two 2^e >= max |x| (one
 // warp per sequence); also zeroes the fixed-point sums of this call.
-__global__ void bmm_scale_kernel(const float* x, uint32_t rows, uint32_t N, uint32_t Npad, float* xs, long long* acc,
-                                 size_t acc_n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; acc && i < acc_n; i += (size_t)gridDim.x * blockDim.x)
-        acc[i] = 0;
-    const uint32_t n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (n >= Npad) return;
-    float am = 0.0f;
-    if (n < N)
-        for (uint32_t i = lane; i < rows; i += 32) am = fmaxf(am, fabsf(x[(size_t)n * rows + i]));
-    am = warp_max(am);
-    // am = m 2^(eb-127), m in [1,2): 2^(eb-126) > am
-    const int eb = (int)((__float_as_uint(am) >> 23) & 0xFFu);
-    if (lane == 0) xs[n] = eb > 0 && eb < 253 ? __uint_as_float((uint32_t)(eb + 1) << 23) : 1.0f;
-}
-// Pass 2: x / 2^e = hi + lo in fp16, written in the kernel's operand layout
-// and K order. One warp per (block, sequence).
-__global__ void bmm_prep_kernel(const float* x, uint32_t rows, uint32_t N, uint32_t Npad, const float* xs,
-                                unsigned char* xb) {
-    const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const uint32_t nblk = rows / 32;
-    if (gw >= nblk * Npad) return;
-    const uint32_t b = gw / Npad, n = gw % Npad;
-    const float y = n < N ? x[(size_t)n * rows + b * 32 + lane] / xs[n] : 0.0f;  // exact: power of two
+// Activations of one call, one CTA per (padded) sequence: the power-of-two
+// scale 2^e > max |x| of the sequence, then x / 2^e as hi + lo fp16 in the
+// B-operand layout [nblk][hi, lo][chunk 4][N][8 halves]. Padded sequences get
+// zeros. CTA 0 also clears the call's error word. Rows up to 8 x 1024 are
+// loaded once into registers (every load in flight together).
+constexpr int BMM_XP_THREADS = 1024, BMM_XP_PER = 8;
+XP_DEV void bmm_xput(unsigned char* xb, uint32_t Npad, uint32_t n, uint32_t i, float y) {
+    // element k = i % 32 of block b = i / 32: chunk c = k / 8, position of k in
+    // the extraction order k0 k4 k1 k5 k2 k6 k3 k7
+    const uint32_t b = i >> 5, k = i & 31, c = k >> 3, e = k & 7, pos = (e & 3) * 2 + (e >> 2);
     const __half hi = __float2half_rn(y);
     const __half lo = __float2half_rn(y - __half2float(hi));
-    // element k = lane of the block: chunk c = k / 8, position of k in the
-    // extraction order k0 k4 k1 k5 k2 k6 k3 k7
-    const uint32_t c = lane >> 3, e = lane & 7, pos = (e & 3) * 2 + (e >> 2);
     __half* base = reinterpret_cast<__half*>(xb + (size_t)b * 2 * 4 * Npad * 16);
     base[((0 * 4 + c) * Npad + n) * 8 + pos] = hi;
     base[((1 * 4 + c) * Npad + n) * 8 + pos] = lo;
 }
+__global__ void __launch_bounds__(BMM_XP_THREADS) bmm_xprep_kernel(const float* x, uint32_t rows, uint32_t N,
+                                                                  uint32_t Npad, float* xs, unsigned char* xb,
+                                                                  uint32_t* err) {
+    __shared__ float red[BMM_XP_THREADS / 32];
+    const uint32_t n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (n == 0 && tid == 0) *err = 0;
+    const float* xr = x + (size_t)n * rows;
+    const bool inreg = rows <= BMM_XP_THREADS * BMM_XP_PER;
+    float v[BMM_XP_PER];
+    float am = 0.0f;
+    if (inreg) {
+#pragma unroll
+        for (int r = 0; r < BMM_XP_PER; ++r) {
+            const uint32_t i = tid + r * BMM_XP_THREADS;
+            v[r] = (n < N && i < rows) ? xr[i] : 0.0f;
+            am = fmaxf(am, fabsf(v[r]));
+        }
+    } else if (n < N) {
+        for (uint32_t i = tid; i < rows; i += BMM_XP_THREADS) am = fmaxf(am, fabsf(xr[i]));
+    }
+    am = warp_max(am);
+    if (lane == 0) red[warp] = am;
+    __syncthreads();
+    am = warp_max(red[lane]);
+    // am = m 2^(eb-127), m in [1,2): 2^(eb-126) > am
+    const int eb = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+    const float sc = eb > 0 && eb < 253 ? __uint_as_float((uint32_t)(eb + 1) << 23) : 1.0f;
+    if (tid == 0) xs[n] = sc;
+    if (inreg) {
+#pragma unroll
+        for (int r = 0; r < BMM_XP_PER; ++r) {
+            const uint32_t i = tid + r * BMM_XP_THREADS;
+            if (i < rows) bmm_xput(xb, Npad, n, i, v[r] / sc);  // exact: power of two
+        }
+    } else {
+        for (uint32_t i = tid; i < rows; i += BMM_XP_THREADS) bmm_xput(xb, Npad, n, i, n < N ? xr[i] / sc : 0.0f);
+    }
+}
 
 XP_DEV void bmm_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// fixed-point sums -> fp32, leaving the sums zero for the next call
+__global__ void bmm_finish_kernel(long long* acc, float* out, size_t n) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        out[i] = __ll2float_rn(acc[i]) * 2.3283064365386963e-10f;
+        acc[i] = 0;
+    }
 }
 
 __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
@@ -351,7 +383,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
                 const uint32_t n = half * nh + i;
                 if ((uint32_t)i < nh && n < a.nreal) {
                     const float v = sum[i] * a.xs[n];
-                    if (a.ksplit == 1) {
+                    if (a.ksplit == 1 && !a.raw) {
                         a.out[(size_t)n * a.cols + col] = v;
                     } else {
                         const float f = v * 4294967296.0f;
@@ -374,10 +406,5 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
     }
 }
 
-// fixed-point sums -> fp32
-__global__ void bmm_finish_kernel(const long long* acc, float* out, size_t n) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = __ll2float_rn(acc[i]) * 2.3283064365386963e-10f;
-}
 
 }  // namespace xp

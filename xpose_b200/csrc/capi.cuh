@@ -679,28 +679,35 @@ size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n
     if (rows == 0 || rows % 128 || cols == 0 || cols % 128 || n == 0 || n > BMM_MAXN) return 0;
     return bmm_plan(rows, cols, n).bytes;
 }
-xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
-                             uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {
-    CHECK_PTR(out); CHECK_PTR(in); CHECK_PTR(wq); CHECK_PTR(sc); CHECK_PTR(scratch);
-    if (rows == 0 || rows % 128 || cols == 0 || cols % 128)
-        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: rows must be a multiple of 128 and cols of 128 (got %u x %u)",
-                    rows, cols);
-    if (n == 0 || n > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: 1..%d sequences (got %u)", BMM_MAXN, n);
-    if (reinterpret_cast<uintptr_t>(scratch) % 256)
-        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: scratch must be 256-byte aligned");
+// One batched matvec: activation prep + the tensor-core kernel. raw != null
+// leaves the result as fixed-point sums in raw (zero at entry; the consumer
+// converts and re-zeroes them); otherwise out gets fp32 (K-split sums go
+// through the scratch and a finish launch that leaves them zero).
+static xp_status bmm_run(cudaStream_t st, float* out, long long* raw, const float* in, const uint32_t* wq,
+                         const uint32_t* sc, uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {
     const BmmPlan p = bmm_plan(rows, cols, n);
-    const cudaStream_t st = (cudaStream_t)stream;
     unsigned char* base = static_cast<unsigned char*>(scratch);
     float* xs = reinterpret_cast<float*>(base + p.off_xs);
     unsigned char* xb = base + p.off_xb;
-    long long* acc = p.ksplit > 1 ? reinterpret_cast<long long*>(base + p.off_acc) : nullptr;
-    const size_t acc_n = acc ? (size_t)p.npad * cols : 0;
-    const uint32_t sblocks = (uint32_t)std::max<size_t>((p.npad * 32 + 255) / 256, std::min<size_t>((acc_n + 255) / 256, 1024));
+    long long* acc = raw ? raw : (p.ksplit > 1 ? reinterpret_cast<long long*>(base + p.off_acc) : nullptr);
     uint32_t* err = reinterpret_cast<uint32_t*>(base + p.off_err);
-    XP_CUDA_TRY(cudaMemsetAsync(err, 0, 4, st));
-    bmm_scale_kernel<<<sblocks, 256, 0, st>>>(in, rows, n, p.npad, xs, acc, acc_n);
-    XP_CUDA_TRY(cudaGetLastError());
-    bmm_prep_kernel<<<(p.nblk * p.npad * 32 + 255) / 256, 256, 0, st>>>(in, rows, n, p.npad, xs, xb);
+    if (!raw && acc) {
+        // The fixed-point sums are zero between calls of one shape (the
+        // finish launch clears them). A scratch last used by another shape
+        // may hold that call's activations there.
+        static std::mutex mu;
+        static std::unordered_map<const void*, uint64_t> last_shape;
+        const uint64_t sig = ((uint64_t)rows << 40) ^ ((uint64_t)cols << 8) ^ p.npad;
+        bool clear = false;
+        {
+            std::lock_guard<std::mutex> g(mu);
+            auto it = last_shape.find(scratch);
+            clear = it != last_shape.end() && it->second != sig;
+            last_shape[scratch] = sig;
+        }
+        if (clear) XP_CUDA_TRY(cudaMemsetAsync(base + p.off_acc, 0, p.bytes - p.off_acc, st));
+    }
+    bmm_xprep_kernel<<<p.npad, BMM_XP_THREADS, 0, st>>>(in, rows, n, p.npad, xs, xb, err);
     XP_CUDA_TRY(cudaGetLastError());
     static size_t attr_set[64] = {};
     int dev = 0;
@@ -716,6 +723,7 @@ xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const ui
     a.xs = xs;
     a.out = out;
     a.acc = acc;
+    a.raw = raw ? 1u : 0u;
     a.nblk = p.nblk;
     a.cols = cols;
     a.N = p.npad;
@@ -727,12 +735,23 @@ xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const ui
     const uint32_t grid = std::min<uint32_t>(p.nitems, 2 * (uint32_t)sm_count());
     bmm_kernel<<<grid, BMM_THREADS, p.smem, st>>>(a);
     XP_CUDA_TRY(cudaGetLastError());
-    if (acc) {
+    if (!raw && acc) {
         // rows n >= the real sequence count are padding: convert only [n][cols]
         bmm_finish_kernel<<<(uint32_t)(((size_t)n * cols + 255) / 256), 256, 0, st>>>(acc, out, (size_t)n * cols);
         XP_CUDA_TRY(cudaGetLastError());
     }
     return XP_OK;
+}
+xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
+                             uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {
+    CHECK_PTR(out); CHECK_PTR(in); CHECK_PTR(wq); CHECK_PTR(sc); CHECK_PTR(scratch);
+    if (rows == 0 || rows % 128 || cols == 0 || cols % 128)
+        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: rows must be a multiple of 128 and cols of 128 (got %u x %u)",
+                    rows, cols);
+    if (n == 0 || n > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: 1..%d sequences (got %u)", BMM_MAXN, n);
+    if (reinterpret_cast<uintptr_t>(scratch) % 256)
+        return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: scratch must be 256-byte aligned");
+    return bmm_run((cudaStream_t)stream, out, nullptr, in, wq, sc, rows, cols, n, scratch);
 }
 
 struct xp_mv_plan {

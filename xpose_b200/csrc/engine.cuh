@@ -950,11 +950,15 @@ struct xp_bdec {
     xp_sampling sp{};
     uint64_t seq0 = 0;
     std::vector<void*> allocs;
-    float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *o = nullptr;
-    float *g = nullptr, *u = nullptr, *hb = nullptr, *dn = nullptr, *logits = nullptr;
+    float *x = nullptr, *xn = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
+    // matvec results as int64 fixed-point sums (2^-32): the tensor-core kernel
+    // adds into them, the consuming kernel converts and re-zeroes them
+    long long *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *g = nullptr, *u = nullptr, *dn = nullptr;
     std::vector<__half*> kc, vc;
     uint32_t *tokens = nullptr, *pos = nullptr, *h_tok = nullptr;
-    unsigned char* bscratch = nullptr;
+    // one tensor-core scratch per matrix shape: a call leaves its fixed-point
+    // sums zero only where its own shape keeps them
+    std::vector<std::pair<uint64_t, unsigned char*>> bscratch;
     uint64_t* cand = nullptr;
     uint32_t ns = 0, nc = 0;
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
@@ -982,9 +986,15 @@ struct xp_bdec {
         *p = static_cast<T*>(d);
         return XP_OK;
     }
-    cudaError_t mm(float* out, const float* in, const QW& w) {
-        const xp_status e = xp_mv_km4_bs_batch(st, out, in, reinterpret_cast<const uint32_t*>(w.wq),
-                                               reinterpret_cast<const uint32_t*>(w.sc), w.rows, w.cols, B, bscratch);
+    // out (fp32) or raw (fixed-point sums, zero on entry) = in x W for every sequence
+    cudaError_t mm(float* out, long long* raw, const float* in, const QW& w) {
+        unsigned char* scr = nullptr;
+        const uint64_t key = ((uint64_t)w.rows << 32) | w.cols;
+        for (auto& kv : bscratch)
+            if (kv.first == key) scr = kv.second;
+        if (!scr) return cudaErrorInvalidValue;
+        const xp_status e = bmm_run(st, out, raw, in, reinterpret_cast<const uint32_t*>(w.wq),
+                                    reinterpret_cast<const uint32_t*>(w.sc), w.rows, w.cols, B, scr);
         return e == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
@@ -999,9 +1009,9 @@ struct xp_bdec {
             const LayerDev& W = s->L[l];
             if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], xn, H, c.rms_eps, 0);
             else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], xn, H, c.rms_eps, 1);
-            if ((e = mm(q, xn, W.m[0])) != cudaSuccess) return e;
-            if ((e = mm(k, xn, W.m[1])) != cudaSuccess) return e;
-            if ((e = mm(v, xn, W.m[2])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, q, xn, W.m[0])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, k, xn, W.m[1])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, v, xn, W.m[2])) != cudaSuccess) return e;
             BkAttnArgs aa{};
             aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
             aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = att; aa.max_seq = max_seq;
@@ -1013,16 +1023,16 @@ struct xp_bdec {
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
             bk_attn_kernel<<<B, BK_THREADS, (size_t)4 * ms * 4, st>>>(aa);
-            if ((e = mm(o, att, W.m[3])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, o, att, W.m[3])) != cudaSuccess) return e;
             bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], xn, H, c.rms_eps, 1);
-            if ((e = mm(g, xn, W.m[4])) != cudaSuccess) return e;
-            if ((e = mm(u, xn, W.m[5])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, g, xn, W.m[4])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, u, xn, W.m[5])) != cudaSuccess) return e;
             const size_t nf = (size_t)B * F;
             bk_geglu_kernel<<<(uint32_t)((nf + 255) / 256), 256, 0, st>>>(g, u, hb, nf);
-            if ((e = mm(dn, hb, W.m[6])) != cudaSuccess) return e;
+            if ((e = mm(nullptr, dn, hb, W.m[6])) != cudaSuccess) return e;
         }
         bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, xn, H, c.rms_eps, 1);
-        if ((e = mm(logits, xn, s->lm)) != cudaSuccess) return e;
+        if ((e = mm(logits, nullptr, xn, s->lm)) != cudaSuccess) return e;
         bk_pos_inc_kernel<<<1, 64, 0, st>>>(pos, B);
         return cudaGetLastError();
     }
@@ -1097,13 +1107,19 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
         if ((e = b->alloc(&b->kc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
         if ((e = b->alloc(&b->vc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
     }
-    size_t sb = 0;
-    const uint32_t shapes[5][2] = {{(uint32_t)H, (uint32_t)QD}, {(uint32_t)H, (uint32_t)KVD}, {(uint32_t)QD, (uint32_t)H},
-                                   {(uint32_t)H, (uint32_t)F}, {(uint32_t)F, (uint32_t)H}};
-    for (auto& sh : shapes) sb = std::max(sb, xp_mv_km4_bs_batch_scratch_bytes(sh[0], sh[1], nseq));
-    sb = std::max(sb, xp_mv_km4_bs_batch_scratch_bytes((uint32_t)H, (uint32_t)V, nseq));
-    if (sb == 0) return bail(fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: a matrix shape is not supported by the batched matvec"));
-    if ((e = b->alloc(&b->bscratch, sb)) != XP_OK) return bail(e);
+    const uint32_t shapes[6][2] = {{(uint32_t)H, (uint32_t)QD}, {(uint32_t)H, (uint32_t)KVD}, {(uint32_t)QD, (uint32_t)H},
+                                   {(uint32_t)H, (uint32_t)F},  {(uint32_t)F, (uint32_t)H},  {(uint32_t)H, (uint32_t)V}};
+    for (auto& sh : shapes) {
+        const uint64_t key = ((uint64_t)sh[0] << 32) | sh[1];
+        bool have = false;
+        for (auto& kv : b->bscratch) have = have || kv.first == key;
+        if (have) continue;
+        const size_t sb = xp_mv_km4_bs_batch_scratch_bytes(sh[0], sh[1], nseq);
+        if (sb == 0) return bail(fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: a matrix shape is not supported by the batched matvec"));
+        unsigned char* scr = nullptr;
+        if ((e = b->alloc(&scr, sb)) != XP_OK) return bail(e);
+        b->bscratch.push_back({key, scr});
+    }
     b->ns = (uint32_t)((V + TOPK_SLICE - 1) / TOPK_SLICE);
     b->nc = b->ns * TOPK_TK;
     if ((e = b->alloc(&b->cand, (size_t)nseq * b->nc)) != XP_OK) return bail(e);
