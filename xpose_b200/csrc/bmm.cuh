@@ -44,20 +44,36 @@ constexpr int BMM_ND = 4;            // TMEM accumulator slots in flight
 constexpr int BMM_MAXN = 64;         // sequences per launch (N is 32 or 64)
 constexpr uint32_t BMM_ERR_WAIT = 64u;
 
-struct BmmArgs {
+// One weight matrix of a launch; a launch covers up to BMM_MAXPARTS matrices
+// with the same rows (K), their 128-column tiles numbered consecutively.
+struct BmmPart {
     const uint4* wq;          // nibble plane of the matrix (reference layout)
     const uint2* sc;          // bf16 scale plane
+    float* out;               // [N][cols] (ksplit == 1 and not raw)
+    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1 or raw), zero at launch
+    uint32_t cols;            // columns of this matrix
+    uint32_t tile0;           // first tile of this matrix in the launch
+};
+constexpr int BMM_MAXPARTS = 3;
+struct BmmArgs {
+    BmmPart part[BMM_MAXPARTS];
+    uint32_t nparts;
     const unsigned char* xb;  // prepared activations: [nblk][hi, lo][chunk 4][N][16 B]
     const float* xs;          // [N] per-sequence power-of-two scale 2^e
-    float* out;               // [N][cols] (ksplit == 1)
-    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1 or raw), zero at launch
-    uint32_t nblk, cols, N;   // N = padded sequence count (32 or 64)
+    uint32_t nblk, N;         // N = padded sequence count (32 or 64)
     uint32_t nreal;           // sequences actually present (rows of out)
     uint32_t ksplit, cb;      // K ranges per tile, blocks per range
-    uint32_t nitems;          // (cols / 128) * ksplit
+    uint32_t nitems;          // tiles * ksplit
     uint32_t raw;             // 1: leave the result in acc as fixed-point sums (the consumer converts)
     uint32_t* err;
 };
+// The matrix holding launch tile `tile`, and the tile's index within it.
+XP_DEV const BmmPart& bmm_part(const BmmArgs& a, uint32_t tile, uint32_t& lt) {
+    const uint32_t p = (a.nparts > 2 && tile >= a.part[2].tile0) ? 2u : (a.nparts > 1 && tile >= a.part[1].tile0) ? 1u : 0u;
+    lt = tile - a.part[p].tile0;
+    return a.part[p];
+}
+
 
 // ---- tcgen05 helpers (PTX of the sm_100a tensor-core and TMEM instructions) ----
 XP_DEV uint64_t bmm_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -215,7 +231,7 @@ __global__ void bmm_finish_kernel(long long* acc, float* out, size_t n) {
     }
 }
 
-__global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
+__global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_constant__ BmmArgs a) {
     extern __shared__ __align__(1024) unsigned char bsm[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t N = a.N;
@@ -267,6 +283,8 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
             for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
                 const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
                 const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                uint32_t lt;
+                const uint4* wq = bmm_part(a, tile, lt).wq;
                 for (uint32_t b = b0; b < b1; ++b, ++t) {
                     const uint32_t s = t % BMM_STAGES;
                     if (t >= BMM_STAGES) bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);
@@ -274,8 +292,8 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
                     fence_proxy_async();
                     mbar_expect_tx(&full[s], 2048 + xbytes);
                     // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups
-                    bulk_g2s(st, a.wq + ((size_t)(2 * tile) * a.nblk + b) * 64, 1024, &full[s]);
-                    bulk_g2s(st + 1024, a.wq + ((size_t)(2 * tile + 1) * a.nblk + b) * 64, 1024, &full[s]);
+                    bulk_g2s(st, wq + ((size_t)(2 * lt) * a.nblk + b) * 64, 1024, &full[s]);
+                    bulk_g2s(st + 1024, wq + ((size_t)(2 * lt + 1) * a.nblk + b) * 64, 1024, &full[s]);
                     bulk_g2s(st + 2048, a.xb + (size_t)b * xbytes, xbytes, &full[s]);
                 }
             }
@@ -351,18 +369,20 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
         for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
             const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
             const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
-            const uint32_t col = tile * BMM_M + j;
+            uint32_t lt;
+            const BmmPart& P = bmm_part(a, tile, lt);
+            const uint32_t col = lt * BMM_M + j;
             float sum[BMM_MAXN / 2];
 #pragma unroll
             for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
             // scales one quad ahead: the scale plane is read from HBM
-            uint2 sw = __ldg(a.sc + (size_t)(b0 >> 2) * a.cols + col);
-            uint2 sw_next = b0 + 4 < b1 ? __ldg(a.sc + (size_t)((b0 >> 2) + 1) * a.cols + col) : sw;
+            uint2 sw = __ldg(P.sc + (size_t)(b0 >> 2) * P.cols + col);
+            uint2 sw_next = b0 + 4 < b1 ? __ldg(P.sc + (size_t)((b0 >> 2) + 1) * P.cols + col) : sw;
             for (uint32_t b = b0; b < b1; ++b, ++t) {
                 const uint32_t q = t % BMM_ND;
                 if ((b & 3) == 0 && b != b0) {
                     sw = sw_next;
-                    if (b + 4 < b1) sw_next = __ldg(a.sc + (size_t)((b >> 2) + 1) * a.cols + col);
+                    if (b + 4 < b1) sw_next = __ldg(P.sc + (size_t)((b >> 2) + 1) * P.cols + col);
                 }
                 const uint32_t word = (b & 2) ? sw.y : sw.x;
                 const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
@@ -384,13 +404,13 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const BmmArgs a) {
                 if ((uint32_t)i < nh && n < a.nreal) {
                     const float v = sum[i] * a.xs[n];
                     if (a.ksplit == 1 && !a.raw) {
-                        a.out[(size_t)n * a.cols + col] = v;
+                        P.out[(size_t)n * P.cols + col] = v;
                     } else {
                         const float f = v * 4294967296.0f;
                         long long fx = 0;
                         if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
                         else atomicOr(a.err, TK_ERR_RANGE);
-                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(a.acc + (size_t)n * a.cols + col),
+                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(P.acc + (size_t)n * P.cols + col),
                                      "l"(fx) : "memory");
                     }
                 }

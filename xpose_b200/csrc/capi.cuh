@@ -679,19 +679,32 @@ size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n
     if (rows == 0 || rows % 128 || cols == 0 || cols % 128 || n == 0 || n > BMM_MAXN) return 0;
     return bmm_plan(rows, cols, n).bytes;
 }
-// One batched matvec: activation prep + the tensor-core kernel. raw != null
-// leaves the result as fixed-point sums in raw (zero at entry; the consumer
-// converts and re-zeroes them); otherwise out gets fp32 (K-split sums go
-// through the scratch and a finish launch that leaves them zero).
-static xp_status bmm_run(cudaStream_t st, float* out, long long* raw, const float* in, const uint32_t* wq,
-                         const uint32_t* sc, uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {
+// One batched matvec launch over up to BMM_MAXPARTS matrices that share the
+// input (same rows): activation prep once, then the tensor-core kernel over
+// every matrix's column tiles. raw: each matrix's result stays as fixed-point
+// sums in its raw buffer (zero at entry; the consumer converts and re-zeroes
+// them). Otherwise (one matrix) out gets fp32, K-split sums going through the
+// scratch and a finish launch that leaves them zero.
+struct BmmMat {
+    const uint32_t* wq;
+    const uint32_t* sc;
+    uint32_t cols;
+    float* out;
+    long long* raw;
+};
+static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, bool raw, const float* in, uint32_t rows,
+                         uint32_t n, void* scratch) {
+    if (nmat == 0 || nmat > (uint32_t)BMM_MAXPARTS || (!raw && nmat != 1))
+        return fail(XP_ERR_INVALID, "bmm_run: %u matrices", nmat);
+    uint32_t cols = 0;
+    for (uint32_t m = 0; m < nmat; ++m) cols += mats[m].cols;
     const BmmPlan p = bmm_plan(rows, cols, n);
     unsigned char* base = static_cast<unsigned char*>(scratch);
     float* xs = reinterpret_cast<float*>(base + p.off_xs);
     unsigned char* xb = base + p.off_xb;
-    long long* acc = raw ? raw : (p.ksplit > 1 ? reinterpret_cast<long long*>(base + p.off_acc) : nullptr);
+    long long* acc = (!raw && p.ksplit > 1) ? reinterpret_cast<long long*>(base + p.off_acc) : nullptr;
     uint32_t* err = reinterpret_cast<uint32_t*>(base + p.off_err);
-    if (!raw && acc) {
+    if (acc) {
         // The fixed-point sums are zero between calls of one shape (the
         // finish launch clears them). A scratch last used by another shape
         // may hold that call's activations there.
@@ -717,15 +730,22 @@ static xp_status bmm_run(cudaStream_t st, float* out, long long* raw, const floa
         attr_set[dev] = p.smem;
     }
     BmmArgs a{};
-    a.wq = reinterpret_cast<const uint4*>(wq);
-    a.sc = reinterpret_cast<const uint2*>(sc);
+    uint32_t tile0 = 0;
+    for (uint32_t m = 0; m < nmat; ++m) {
+        BmmPart& P = a.part[m];
+        P.wq = reinterpret_cast<const uint4*>(mats[m].wq);
+        P.sc = reinterpret_cast<const uint2*>(mats[m].sc);
+        P.out = mats[m].out;
+        P.acc = raw ? mats[m].raw : acc;
+        P.cols = mats[m].cols;
+        P.tile0 = tile0;
+        tile0 += mats[m].cols / BMM_M;
+    }
+    a.nparts = nmat;
     a.xb = xb;
     a.xs = xs;
-    a.out = out;
-    a.acc = acc;
     a.raw = raw ? 1u : 0u;
     a.nblk = p.nblk;
-    a.cols = cols;
     a.N = p.npad;
     a.nreal = n;
     a.ksplit = p.ksplit;
@@ -735,9 +755,9 @@ static xp_status bmm_run(cudaStream_t st, float* out, long long* raw, const floa
     const uint32_t grid = std::min<uint32_t>(p.nitems, 2 * (uint32_t)sm_count());
     bmm_kernel<<<grid, BMM_THREADS, p.smem, st>>>(a);
     XP_CUDA_TRY(cudaGetLastError());
-    if (!raw && acc) {
+    if (acc) {
         // rows n >= the real sequence count are padding: convert only [n][cols]
-        bmm_finish_kernel<<<(uint32_t)(((size_t)n * cols + 255) / 256), 256, 0, st>>>(acc, out, (size_t)n * cols);
+        bmm_finish_kernel<<<(uint32_t)(((size_t)n * cols + 255) / 256), 256, 0, st>>>(acc, mats[0].out, (size_t)n * cols);
         XP_CUDA_TRY(cudaGetLastError());
     }
     return XP_OK;
@@ -751,7 +771,8 @@ xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const ui
     if (n == 0 || n > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: 1..%d sequences (got %u)", BMM_MAXN, n);
     if (reinterpret_cast<uintptr_t>(scratch) % 256)
         return fail(XP_ERR_INVALID, "xp_mv_km4_bs_batch: scratch must be 256-byte aligned");
-    return bmm_run((cudaStream_t)stream, out, nullptr, in, wq, sc, rows, cols, n, scratch);
+    const BmmMat m{wq, sc, cols, out, nullptr};
+    return bmm_run((cudaStream_t)stream, &m, 1, false, in, rows, n, scratch);
 }
 
 struct xp_mv_plan {

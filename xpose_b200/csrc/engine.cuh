@@ -14,6 +14,7 @@
 #pragma once
 #include <cmath>
 #include <cstdlib>
+#include <initializer_list>
 #include <string>
 #include <vector>
 
@@ -986,16 +987,34 @@ struct xp_bdec {
         *p = static_cast<T*>(d);
         return XP_OK;
     }
-    // out (fp32) or raw (fixed-point sums, zero on entry) = in x W for every sequence
-    cudaError_t mm(float* out, long long* raw, const float* in, const QW& w) {
-        unsigned char* scr = nullptr;
-        const uint64_t key = ((uint64_t)w.rows << 32) | w.cols;
+    unsigned char* scratch_for(uint32_t rows, uint32_t cols) {
+        const uint64_t key = ((uint64_t)rows << 32) | cols;
         for (auto& kv : bscratch)
-            if (kv.first == key) scr = kv.second;
+            if (kv.first == key) return kv.second;
+        return nullptr;
+    }
+    // out (fp32) = in x W for every sequence
+    cudaError_t mm(float* out, const float* in, const QW& w) {
+        unsigned char* scr = scratch_for(w.rows, w.cols);
         if (!scr) return cudaErrorInvalidValue;
-        const xp_status e = bmm_run(st, out, raw, in, reinterpret_cast<const uint32_t*>(w.wq),
-                                    reinterpret_cast<const uint32_t*>(w.sc), w.rows, w.cols, B, scr);
-        return e == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        const BmmMat m{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols, out, nullptr};
+        return bmm_run(st, &m, 1, false, in, w.rows, B, scr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+    }
+    // raw[i] (fixed-point sums, zero on entry) = in x W[i] for every sequence:
+    // matrices with the same rows in one launch
+    cudaError_t mm_raw(std::initializer_list<std::pair<long long*, const QW*>> parts, const float* in) {
+        BmmMat m[BMM_MAXPARTS];
+        uint32_t n = 0, cols = 0, rows = 0;
+        for (auto& pr : parts) {
+            const QW& w = *pr.second;
+            m[n++] = BmmMat{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols,
+                            nullptr, pr.first};
+            cols += w.cols;
+            rows = w.rows;
+        }
+        unsigned char* scr = scratch_for(rows, cols);
+        if (!scr) return cudaErrorInvalidValue;
+        return bmm_run(st, m, n, true, in, rows, B, scr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
     cudaError_t forward() {
@@ -1009,9 +1028,7 @@ struct xp_bdec {
             const LayerDev& W = s->L[l];
             if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], xn, H, c.rms_eps, 0);
             else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], xn, H, c.rms_eps, 1);
-            if ((e = mm(nullptr, q, xn, W.m[0])) != cudaSuccess) return e;
-            if ((e = mm(nullptr, k, xn, W.m[1])) != cudaSuccess) return e;
-            if ((e = mm(nullptr, v, xn, W.m[2])) != cudaSuccess) return e;
+            if ((e = mm_raw({{q, &W.m[0]}, {k, &W.m[1]}, {v, &W.m[2]}}, xn)) != cudaSuccess) return e;
             BkAttnArgs aa{};
             aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
             aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = att; aa.max_seq = max_seq;
@@ -1023,16 +1040,15 @@ struct xp_bdec {
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
             bk_attn_kernel<<<B, BK_THREADS, (size_t)4 * ms * 4, st>>>(aa);
-            if ((e = mm(nullptr, o, att, W.m[3])) != cudaSuccess) return e;
+            if ((e = mm_raw({{o, &W.m[3]}}, att)) != cudaSuccess) return e;
             bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], xn, H, c.rms_eps, 1);
-            if ((e = mm(nullptr, g, xn, W.m[4])) != cudaSuccess) return e;
-            if ((e = mm(nullptr, u, xn, W.m[5])) != cudaSuccess) return e;
+            if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, xn)) != cudaSuccess) return e;
             const size_t nf = (size_t)B * F;
             bk_geglu_kernel<<<(uint32_t)((nf + 255) / 256), 256, 0, st>>>(g, u, hb, nf);
-            if ((e = mm(nullptr, dn, hb, W.m[6])) != cudaSuccess) return e;
+            if ((e = mm_raw({{dn, &W.m[6]}}, hb)) != cudaSuccess) return e;
         }
         bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, xn, H, c.rms_eps, 1);
-        if ((e = mm(logits, nullptr, xn, s->lm)) != cudaSuccess) return e;
+        if ((e = mm(logits, xn, s->lm)) != cudaSuccess) return e;
         bk_pos_inc_kernel<<<1, 64, 0, st>>>(pos, B);
         return cudaGetLastError();
     }
@@ -1107,8 +1123,9 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
         if ((e = b->alloc(&b->kc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
         if ((e = b->alloc(&b->vc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
     }
-    const uint32_t shapes[6][2] = {{(uint32_t)H, (uint32_t)QD}, {(uint32_t)H, (uint32_t)KVD}, {(uint32_t)QD, (uint32_t)H},
-                                   {(uint32_t)H, (uint32_t)F},  {(uint32_t)F, (uint32_t)H},  {(uint32_t)H, (uint32_t)V}};
+    // launch shapes (rows, total columns): q|k|v, o, gate|up, down, LM head
+    const uint32_t shapes[5][2] = {{(uint32_t)H, (uint32_t)(QD + 2 * KVD)}, {(uint32_t)QD, (uint32_t)H},
+                                   {(uint32_t)H, (uint32_t)(2 * F)}, {(uint32_t)F, (uint32_t)H}, {(uint32_t)H, (uint32_t)V}};
     for (auto& sh : shapes) {
         const uint64_t key = ((uint64_t)sh[0] << 32) | sh[1];
         bool have = false;
