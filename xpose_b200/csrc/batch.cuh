@@ -8,6 +8,7 @@
 // softmax, tanh-approximate GeGLU.
 #pragma once
 #include "attention.cuh"
+#include "bmm.cuh"
 #include "common.cuh"
 
 namespace xp {
@@ -15,13 +16,10 @@ namespace xp {
 constexpr int BK_THREADS = 512;
 
 // Matvec results arrive as int64 fixed-point sums (2^-32 units) that the
-// tensor-core kernel adds into; each is read once, here, and left zero for
-// the next step.
-XP_DEV float bk_take(long long* p) {
-    const float v = __ll2float_rn(*p) * 2.3283064365386963e-10f;
-    *p = 0;
-    return v;
-}
+// tensor-core kernel adds into; each is read once by the consuming kernel and
+// left zero for the next step. Kernels load all of theirs before clearing any,
+// so the loads are in flight together.
+XP_DEV float bk_unfix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
 
 // x[b] = embed[token[b]] * scale
 __global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, float scale, float* x, uint32_t H) {
@@ -30,10 +28,19 @@ __global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, floa
     for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)b * H + i] = row[i] * scale;
 }
 
+// Where a kernel leaves a matvec input: the tensor-core operand of its
+// sequence (bmm_put_seq), padded to Npad sequences.
+struct BkOperand {
+    float* xs;
+    unsigned char* xb;
+    uint32_t Npad;
+};
+
 // mode 0: xn = rmsnorm_gemma(x, w_pre)
 // mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)  (y: fixed-point sums)
+// xn goes out as the next matvec's operand.
 __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, long long* y, const float* w_post,
-                                                                 const float* w_pre, float* xn, uint32_t H, float eps,
+                                                                 const float* w_pre, BkOperand xn, uint32_t H, float eps,
                                                                  int mode) {
     __shared__ float red[32];
     const uint32_t b = blockIdx.x;
@@ -43,10 +50,17 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, lon
     float r[J];
     if (mode == 1) {
         float yv[J], ss = 0.0f;
+        long long yr[J];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const uint32_t i = threadIdx.x + j * BK_THREADS;
-            yv[j] = i < H ? bk_take(yb + i) : 0.0f;
+            yr[j] = i < H ? yb[i] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const uint32_t i = threadIdx.x + j * BK_THREADS;
+            if (i < H) yb[i] = 0;
+            yv[j] = bk_unfix(yr[j]);
             ss += yv[j] * yv[j];
         }
         ss = block_sum(ss, red);
@@ -70,20 +84,41 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, lon
     for (int j = 0; j < J; ++j) ss2 += r[j] * r[j];
     ss2 = block_sum(ss2, red);
     const float sc2 = rsqrtf(ss2 / (float)H + eps);
+    float o[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const uint32_t i = threadIdx.x + j * BK_THREADS;
-        if (i < H) xn[(size_t)b * H + i] = r[j] * sc2 * (1.0f + w_pre[i]);
+        o[j] = i < H ? r[j] * sc2 * (1.0f + w_pre[i]) : 0.0f;
     }
+    bmm_put_seq(o, H, b, xn.Npad, xn.xs, xn.xb);
 }
 
 __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
     if (threadIdx.x < B) pos[threadIdx.x] += 1;
 }
 
-__global__ void bk_geglu_kernel(long long* g, long long* u, float* hb, size_t n) {
-    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) hb[i] = gelu_tanh_ref(bk_take(g + i)) * bk_take(u + i);
+// hb = gelu(g) * u for one sequence per CTA (F <= BK_THREADS * BK_GJ), left
+// as the down-proj operand
+constexpr int BK_GJ = 16;
+__global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(long long* g, long long* u, BkOperand hb, uint32_t F) {
+    const uint32_t b = blockIdx.x;
+    long long* gb = g + (size_t)b * F;
+    long long* ub = u + (size_t)b * F;
+    long long gr[BK_GJ], ur[BK_GJ];
+#pragma unroll
+    for (int j = 0; j < BK_GJ; ++j) {
+        const uint32_t i = threadIdx.x + j * BK_THREADS;
+        gr[j] = i < F ? gb[i] : 0;
+        ur[j] = i < F ? ub[i] : 0;
+    }
+    float h[BK_GJ];
+#pragma unroll
+    for (int j = 0; j < BK_GJ; ++j) {
+        const uint32_t i = threadIdx.x + j * BK_THREADS;
+        if (i < F) { gb[i] = 0; ub[i] = 0; }
+        h[j] = i < F ? gelu_tanh_ref(bk_unfix(gr[j])) * bk_unfix(ur[j]) : 0.0f;
+    }
+    bmm_put_seq(h, F, b, hb.Npad, hb.xs, hb.xb);
 }
 
 // One CTA per sequence: QK-norm + RoPE of the raw q (4 heads) and k, fp16 KV
@@ -98,7 +133,7 @@ struct BkAttnArgs {
     __half* kc;            // [B][max_seq][256]
     __half* vc;
     const uint32_t* pos;   // [B]
-    float* att;            // [B][1024]
+    BkOperand att;         // [B][1024] as the o-proj operand
     uint32_t max_seq, window;
     float theta, eps, scale;
     float inv_freq[128];   // RoPE theta^(-2d/256), from rope_table_host
@@ -129,8 +164,14 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         // warps 0-3: q heads, 4: k, 5: v; lane holds dims 4 lane..+3 and 128 + 4 lane..+3
         long long* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
         float v[8];
+        long long vr[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = bk_take(src + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)));
+        for (int i = 0; i < 8; ++i) vr[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)] = 0;
+            v[i] = bk_unfix(vr[i]);
+        }
         if (warp < 5) {
             const float* w = warp < 4 ? a.qn : a.kn;
             float ss = 0.0f;
@@ -229,10 +270,14 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         }
     }
     __syncthreads();
-    for (uint32_t i = tid; i < 1024; i += BK_THREADS) {
+    float o[1024 / BK_THREADS];
+#pragma unroll
+    for (int j = 0; j < 1024 / BK_THREADS; ++j) {
+        const uint32_t i = tid + j * BK_THREADS;
         const float t = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
-        a.att[(size_t)b * 1024 + i] = t / sums[i >> 8];
+        o[j] = t / sums[i >> 8];
     }
+    bmm_put_seq(o, 1024, b, a.att.Npad, a.att.xs, a.att.xb);
 }
 
 }  // namespace xp

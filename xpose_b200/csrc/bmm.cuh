@@ -41,7 +41,11 @@ constexpr int BMM_M = 128;           // output columns per tile
 constexpr int BMM_STAGES = 4;        // copy ring depth (blocks)
 constexpr int BMM_NA = 4;            // A tiles (dequantised blocks) in flight
 constexpr int BMM_ND = 4;            // TMEM accumulator slots in flight
-constexpr int BMM_MAXN = 64;         // sequences per launch (N is 32 or 64)
+constexpr int BMM_MAXN = 64;
+// sequences padded to the MMA's N (32 or 64)
+inline uint32_t bmm_npad(uint32_t n) { return n <= 32 ? 32u : 64u; }
+// bytes of a prepared activation operand of `rows` for n sequences
+inline size_t bmm_xb_bytes(uint32_t rows, uint32_t n) { return (size_t)(rows / 32) * 2 * 4 * bmm_npad(n) * 16; }         // sequences per launch (N is 32 or 64)
 constexpr uint32_t BMM_ERR_WAIT = 64u;
 
 // One weight matrix of a launch; a launch covers up to BMM_MAXPARTS matrices
@@ -179,6 +183,32 @@ XP_DEV void bmm_xput(unsigned char* xb, uint32_t Npad, uint32_t n, uint32_t i, f
     base[((0 * 4 + c) * Npad + n) * 8 + pos] = hi;
     base[((1 * 4 + c) * Npad + n) * 8 + pos] = lo;
 }
+// The same operand written by the kernel that produces the activations: the
+// calling CTA holds sequence n, element i = threadIdx.x + j * blockDim.x in
+// v[j] (rows <= J * blockDim.x, blockDim.x a multiple of 32). Every thread of
+// the CTA must call it.
+template <int J>
+XP_DEV void bmm_put_seq(const float (&v)[J], uint32_t rows, uint32_t n, uint32_t Npad, float* xs, unsigned char* xb) {
+    __shared__ float bmm_red[32];
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    float am = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) am = fmaxf(am, fabsf(v[j]));
+    am = warp_max(am);
+    __syncthreads();  // bmm_red free
+    if (lane == 0) bmm_red[warp] = am;
+    __syncthreads();
+    am = warp_max(lane < nw ? bmm_red[lane] : 0.0f);
+    const int eb = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+    const float sc = eb > 0 && eb < 253 ? __uint_as_float((uint32_t)(eb + 1) << 23) : 1.0f;
+    if (tid == 0) xs[n] = sc;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const uint32_t i = tid + j * blockDim.x;
+        if (i < rows) bmm_xput(xb, Npad, n, i, v[j] / sc);  // exact: power of two
+    }
+}
+
 __global__ void __launch_bounds__(BMM_XP_THREADS) bmm_xprep_kernel(const float* x, uint32_t rows, uint32_t N,
                                                                   uint32_t Npad, float* xs, unsigned char* xb,
                                                                   uint32_t* err) {

@@ -652,7 +652,7 @@ struct BmmPlan {
 };
 BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     BmmPlan p{};
-    p.npad = n <= 32 ? 32 : 64;
+    p.npad = bmm_npad(n);
     p.nblk = rows / 32;
     p.tiles = cols / BMM_M;
     const uint32_t G = (uint32_t)sm_count();
@@ -692,8 +692,14 @@ struct BmmMat {
     float* out;
     long long* raw;
 };
+// prep: the activation operand already written by its producer (xs, xb of
+// bmm_put_seq); then `in` is unused and no prep launch runs.
+struct BmmPrep {
+    const float* xs;
+    const unsigned char* xb;
+};
 static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, bool raw, const float* in, uint32_t rows,
-                         uint32_t n, void* scratch) {
+                         uint32_t n, void* scratch, const BmmPrep* prep = nullptr) {
     if (nmat == 0 || nmat > (uint32_t)BMM_MAXPARTS || (!raw && nmat != 1))
         return fail(XP_ERR_INVALID, "bmm_run: %u matrices", nmat);
     uint32_t cols = 0;
@@ -720,8 +726,10 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
         }
         if (clear) XP_CUDA_TRY(cudaMemsetAsync(base + p.off_acc, 0, p.bytes - p.off_acc, st));
     }
-    bmm_xprep_kernel<<<p.npad, BMM_XP_THREADS, 0, st>>>(in, rows, n, p.npad, xs, xb, err);
-    XP_CUDA_TRY(cudaGetLastError());
+    if (!prep) {
+        bmm_xprep_kernel<<<p.npad, BMM_XP_THREADS, 0, st>>>(in, rows, n, p.npad, xs, xb, err);
+        XP_CUDA_TRY(cudaGetLastError());
+    }
     static size_t attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -742,8 +750,8 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
         tile0 += mats[m].cols / BMM_M;
     }
     a.nparts = nmat;
-    a.xb = xb;
-    a.xs = xs;
+    a.xb = prep ? prep->xb : xb;
+    a.xs = prep ? prep->xs : xs;
     a.raw = raw ? 1u : 0u;
     a.nblk = p.nblk;
     a.N = p.npad;

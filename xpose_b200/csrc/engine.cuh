@@ -951,7 +951,9 @@ struct xp_bdec {
     xp_sampling sp{};
     uint64_t seq0 = 0;
     std::vector<void*> allocs;
-    float *x = nullptr, *xn = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
+    float *x = nullptr, *logits = nullptr;
+    // matvec inputs, written as tensor-core operands by the kernels that make them
+    BkOperand op_xn{}, op_att{}, op_hb{};
     // matvec results as int64 fixed-point sums (2^-32): the tensor-core kernel
     // adds into them, the consuming kernel converts and re-zeroes them
     long long *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *g = nullptr, *u = nullptr, *dn = nullptr;
@@ -994,15 +996,16 @@ struct xp_bdec {
         return nullptr;
     }
     // out (fp32) = in x W for every sequence
-    cudaError_t mm(float* out, const float* in, const QW& w) {
+    cudaError_t mm(float* out, const BkOperand& in, const QW& w) {
         unsigned char* scr = scratch_for(w.rows, w.cols);
         if (!scr) return cudaErrorInvalidValue;
         const BmmMat m{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols, out, nullptr};
-        return bmm_run(st, &m, 1, false, in, w.rows, B, scr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        const BmmPrep pr{in.xs, in.xb};
+        return bmm_run(st, &m, 1, false, nullptr, w.rows, B, scr, &pr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // raw[i] (fixed-point sums, zero on entry) = in x W[i] for every sequence:
     // matrices with the same rows in one launch
-    cudaError_t mm_raw(std::initializer_list<std::pair<long long*, const QW*>> parts, const float* in) {
+    cudaError_t mm_raw(std::initializer_list<std::pair<long long*, const QW*>> parts, const BkOperand& in) {
         BmmMat m[BMM_MAXPARTS];
         uint32_t n = 0, cols = 0, rows = 0;
         for (auto& pr : parts) {
@@ -1014,7 +1017,8 @@ struct xp_bdec {
         }
         unsigned char* scr = scratch_for(rows, cols);
         if (!scr) return cudaErrorInvalidValue;
-        return bmm_run(st, m, n, true, in, rows, B, scr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        const BmmPrep pr{in.xs, in.xb};
+        return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
     cudaError_t forward() {
@@ -1026,12 +1030,12 @@ struct xp_bdec {
         bk_embed_kernel<<<B, 256, 0, st>>>(tokens, s->embed, escale, x, H);
         for (uint32_t l = 0; l < L; ++l) {
             const LayerDev& W = s->L[l];
-            if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], xn, H, c.rms_eps, 0);
-            else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], xn, H, c.rms_eps, 1);
-            if ((e = mm_raw({{q, &W.m[0]}, {k, &W.m[1]}, {v, &W.m[2]}}, xn)) != cudaSuccess) return e;
+            if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], op_xn, H, c.rms_eps, 0);
+            else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], op_xn, H, c.rms_eps, 1);
+            if ((e = mm_raw({{q, &W.m[0]}, {k, &W.m[1]}, {v, &W.m[2]}}, op_xn)) != cudaSuccess) return e;
             BkAttnArgs aa{};
             aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
-            aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = att; aa.max_seq = max_seq;
+            aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = op_att; aa.max_seq = max_seq;
             const bool glob = s->is_global(l);
             aa.window = glob ? 0 : c.sliding_window;
             aa.theta = glob ? c.rope_theta_global : c.rope_theta_local;
@@ -1040,15 +1044,14 @@ struct xp_bdec {
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
             bk_attn_kernel<<<B, BK_THREADS, (size_t)4 * ms * 4, st>>>(aa);
-            if ((e = mm_raw({{o, &W.m[3]}}, att)) != cudaSuccess) return e;
-            bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], xn, H, c.rms_eps, 1);
-            if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, xn)) != cudaSuccess) return e;
-            const size_t nf = (size_t)B * F;
-            bk_geglu_kernel<<<(uint32_t)((nf + 255) / 256), 256, 0, st>>>(g, u, hb, nf);
-            if ((e = mm_raw({{dn, &W.m[6]}}, hb)) != cudaSuccess) return e;
+            if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
+            bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], op_xn, H, c.rms_eps, 1);
+            if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, op_xn)) != cudaSuccess) return e;
+            bk_geglu_kernel<<<B, BK_THREADS, 0, st>>>(g, u, op_hb, F);
+            if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
         }
-        bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, xn, H, c.rms_eps, 1);
-        if ((e = mm(logits, xn, s->lm)) != cudaSuccess) return e;
+        bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, op_xn, H, c.rms_eps, 1);
+        if ((e = mm(logits, op_xn, s->lm)) != cudaSuccess) return e;
         bk_pos_inc_kernel<<<1, 64, 0, st>>>(pos, B);
         return cudaGetLastError();
     }
@@ -1093,8 +1096,9 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     if (nseq == 0 || nseq > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_bdec_create: 1..%d sequences (got %u)", BMM_MAXN, nseq);
     if (max_seq == 0 || max_seq > s->cfg.max_seq)
         return fail(XP_ERR_INVALID, "xp_bdec_create: max_seq %u (1..%u)", max_seq, s->cfg.max_seq);
-    if (s->cfg.hidden > 4 * BK_THREADS || s->cfg.hidden % 128 || s->cfg.ffn % 128 || s->cfg.vocab % 128)
-        return fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: hidden <= 2048 and hidden, ffn, vocab multiples of 128");
+    if (s->cfg.hidden > 4 * BK_THREADS || s->cfg.ffn > BK_GJ * BK_THREADS || s->cfg.hidden % 128 || s->cfg.ffn % 128 ||
+        s->cfg.vocab % 128)
+        return fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: hidden <= 2048, ffn <= 8192, and hidden, ffn, vocab multiples of 128");
     if ((size_t)4 * max_seq * 4 > 200 * 1024)
         return fail(XP_ERR_UNSUPPORTED, "xp_bdec_create: max_seq %u exceeds the attention kernel's score buffer", max_seq);
     auto* b = new xp_bdec();
@@ -1113,8 +1117,14 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     const size_t H = c.hidden, F = c.ffn, QD = s->q_dim(), KVD = s->kv_dim(), V = c.vocab;
     xp_status e;
 #define BA(p, n) if ((e = b->alloc(&b->p, (n))) != XP_OK) return bail(e)
-    BA(x, nseq * H); BA(xn, nseq * H); BA(q, nseq * QD); BA(k, nseq * KVD); BA(v, nseq * KVD); BA(att, nseq * QD);
-    BA(o, nseq * H); BA(g, nseq * F); BA(u, nseq * F); BA(hb, nseq * F); BA(dn, nseq * H); BA(logits, nseq * V);
+    BA(x, nseq * H); BA(q, nseq * QD); BA(k, nseq * KVD); BA(v, nseq * KVD);
+    BA(o, nseq * H); BA(g, nseq * F); BA(u, nseq * F); BA(dn, nseq * H); BA(logits, nseq * V);
+    for (auto pr : {std::make_pair(&b->op_xn, H), std::make_pair(&b->op_att, QD), std::make_pair(&b->op_hb, F)}) {
+        BkOperand& op = *pr.first;
+        op.Npad = bmm_npad(nseq);
+        if ((e = b->alloc(&op.xs, 64)) != XP_OK) return bail(e);
+        if ((e = b->alloc(&op.xb, bmm_xb_bytes(pr.second, nseq))) != XP_OK) return bail(e);
+    }
     BA(tokens, nseq); BA(pos, nseq);
 #undef BA
     b->kc.resize(c.n_layers);
