@@ -77,7 +77,7 @@ def parse():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-long", action="store_true")
-    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm"], default=None,
+    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm", "batched", "long"], default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
                          "five-kernel graph path on the bench model, 'matvec' = three runs of the config-1 "
@@ -249,7 +249,7 @@ def ncu_case(which):
         x = torch.randn(n * rows, device="cuda")
         out = torch.empty(n * cols, device="cuda")
         nb = lib().xp_mv_km4_bs_batch_scratch_bytes(rows, cols, n)
-        scr = torch.empty(nb // 4 + 64, dtype=torch.int32, device="cuda")
+        scr = torch.zeros(nb // 4 + 64, dtype=torch.int32, device="cuda")
         for _ in range(3):
             check(lib().xp_mv_km4_bs_batch(None, out.data_ptr(), x.data_ptr(), wq.data_ptr(), sc.data_ptr(), rows, cols,
                                            n, scr.data_ptr()))
@@ -266,7 +266,24 @@ def ncu_case(which):
         lib().xp_mv_plan_destroy(plan)
         print("ncu case matvec: 3 runs of the config-1 plan")
         return 0
+    if which == "long":
+        r = long_context_bench(1.0, iters=2)
+        print("ncu case long:", r["us_per_step"], "us per step (graph replays of 26 attention calls + sampling)")
+        return 0
     from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling
+    if which == "batched":
+        from xpose_b200.decode import BatchDecode
+        cfg = DecodeConfig(max_seq=512)
+        s = DecodeSession.random(cfg, Sampling(), seed=1)
+        bd = BatchDecode(s, 64, 512, Sampling(greedy=False, temperature=1.0, top_k=64, top_p=0.95, seed=5))
+        try:
+            bd.prefill(np.random.default_rng(0).integers(0, cfg.vocab, size=(64, 1)).astype(np.uint32))
+            bd.step()
+            bd.step()
+        finally:
+            bd.close()
+        print("ncu case batched: 64 sequences, one prompt position, two decode steps")
+        return 0
     if which == "multi":
         os.environ["XP_ENGINE_MULTI"] = "1"
     cfg = DecodeConfig(max_seq=4096) if which in ("full", "multi") else DecodeConfig(n_layers=4, vocab=32768,
