@@ -21,8 +21,15 @@ constexpr int BK_THREADS = 512;
 // so the loads are in flight together.
 XP_DEV float bk_unfix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
 
+// Every kernel of a batched step may be launched programmatically (its
+// launch overlapping the previous kernel's tail): each one lets its
+// dependents launch at once and reads nothing the previous kernels write
+// before griddepcontrol.wait.
+
 // x[b] = embed[token[b]] * scale
 __global__ void bk_embed_kernel(const uint32_t* tokens, const float* embed, float scale, float* x, uint32_t H) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t b = blockIdx.x;
     const float* row = embed + (size_t)tokens[b] * H;
     for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) x[(size_t)b * H + i] = row[i] * scale;
@@ -43,6 +50,8 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, lon
                                                                  const float* w_pre, BkOperand xn, uint32_t H, float eps,
                                                                  int mode) {
     __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t b = blockIdx.x;
     float* xb = x + (size_t)b * H;
     long long* yb = y + (size_t)b * H;
@@ -94,6 +103,8 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, lon
 }
 
 __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
+    pdl_launch_dependents();
+    pdl_wait();
     if (threadIdx.x < B) pos[threadIdx.x] += 1;
 }
 
@@ -101,6 +112,8 @@ __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
 // as the down-proj operand
 constexpr int BK_GJ = 16;
 __global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(long long* g, long long* u, BkOperand hb, uint32_t F) {
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t b = blockIdx.x;
     long long* gb = g + (size_t)b * F;
     long long* ub = u + (size_t)b * F;
@@ -144,6 +157,8 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
     __shared__ float red[4 * 4 * 256];  // P.V partials [4 groups][4 heads][256]
     __shared__ __align__(16) __half knew[256], vnew[256];
     __shared__ float cs[256];           // cos | sin for this position
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t pos = a.pos[b];
     const uint32_t seq = pos + 1;

@@ -309,7 +309,20 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
         if (lane == 0) {
+            // The weights do not depend on the kernel before this one, the
+            // activations do: the first stages' nibbles are requested before
+            // griddepcontrol.wait (under the previous kernel's tail when this
+            // launch is programmatic), their activations after it.
             uint32_t t = 0;  // global block counter of this CTA
+            uint32_t deferred[BMM_STAGES];
+            uint32_t ndef = 0;
+            bool waited = false;
+            auto release = [&]() {
+                pdl_wait();
+                waited = true;
+                for (uint32_t i = 0; i < ndef; ++i)
+                    bulk_g2s(stage0 + i * sbytes + 2048, a.xb + (size_t)deferred[i] * xbytes, xbytes, &full[i]);
+            };
             for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
                 const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
                 const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
@@ -317,16 +330,21 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 const uint4* wq = bmm_part(a, tile, lt).wq;
                 for (uint32_t b = b0; b < b1; ++b, ++t) {
                     const uint32_t s = t % BMM_STAGES;
-                    if (t >= BMM_STAGES) bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);
+                    if (t >= BMM_STAGES) {
+                        if (!waited) release();
+                        bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);
+                    }
                     unsigned char* st = stage0 + s * sbytes;
                     fence_proxy_async();
                     mbar_expect_tx(&full[s], 2048 + xbytes);
                     // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups
                     bulk_g2s(st, wq + ((size_t)(2 * lt) * a.nblk + b) * 64, 1024, &full[s]);
                     bulk_g2s(st + 1024, wq + ((size_t)(2 * lt + 1) * a.nblk + b) * 64, 1024, &full[s]);
-                    bulk_g2s(st + 2048, a.xb + (size_t)b * xbytes, xbytes, &full[s]);
+                    if (waited) bulk_g2s(st + 2048, a.xb + (size_t)b * xbytes, xbytes, &full[s]);
+                    else deferred[ndef++] = b;  // stage s == ndef while t < BMM_STAGES
                 }
             }
+            if (!waited) release();
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
@@ -390,6 +408,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         }
     } else {
         // ------------------------------ epilogue ------------------------------
+        pdl_wait();  // the sequence scales and the sums it adds into follow the previous kernel
         const uint32_t e = warp - 6;
         const uint32_t q4 = warp & 3;                // TMEM lane quadrant of this warp
         const uint32_t j = q4 * 32 + lane;           // column within the tile
@@ -447,6 +466,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             }
         }
     }
+    pdl_launch_dependents();
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -699,7 +699,7 @@ struct BmmPrep {
     const unsigned char* xb;
 };
 static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, bool raw, const float* in, uint32_t rows,
-                         uint32_t n, void* scratch, const BmmPrep* prep = nullptr) {
+                         uint32_t n, void* scratch, const BmmPrep* prep = nullptr, bool pdl = false) {
     if (nmat == 0 || nmat > (uint32_t)BMM_MAXPARTS || (!raw && nmat != 1))
         return fail(XP_ERR_INVALID, "bmm_run: %u matrices", nmat);
     uint32_t cols = 0;
@@ -761,8 +761,7 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
     a.nitems = p.nitems;
     a.err = err;
     const uint32_t grid = std::min<uint32_t>(p.nitems, 2 * (uint32_t)sm_count());
-    bmm_kernel<<<grid, BMM_THREADS, p.smem, st>>>(a);
-    XP_CUDA_TRY(cudaGetLastError());
+    XP_CUDA_TRY(launch_ex(bmm_kernel, dim3(grid), dim3(BMM_THREADS), p.smem, st, 1, pdl, a));
     if (acc) {
         // rows n >= the real sequence count are padding: convert only [n][cols]
         bmm_finish_kernel<<<(uint32_t)(((size_t)n * cols + 255) / 256), 256, 0, st>>>(acc, mats[0].out, (size_t)n * cols);

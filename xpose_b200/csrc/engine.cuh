@@ -967,6 +967,10 @@ struct xp_bdec {
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     uint32_t h_pos = 0;  // every sequence is at the same position
+    // Programmatic dependent launch (XP_BDEC_PDL bit 0: tensor-core launches,
+    // which then request their first weights under the previous kernel's tail;
+    // bit 1: the per-sequence kernels, measured slightly slower, so off)
+    bool pdl_mm = (env_int("XP_BDEC_PDL", 1) & 1) != 0, pdl_k = (env_int("XP_BDEC_PDL", 1) & 2) != 0;
 
     ~xp_bdec() {
         cudaSetDevice(device);
@@ -1001,7 +1005,7 @@ struct xp_bdec {
         if (!scr) return cudaErrorInvalidValue;
         const BmmMat m{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols, out, nullptr};
         const BmmPrep pr{in.xs, in.xb};
-        return bmm_run(st, &m, 1, false, nullptr, w.rows, B, scr, &pr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        return bmm_run(st, &m, 1, false, nullptr, w.rows, B, scr, &pr, pdl_mm) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // raw[i] (fixed-point sums, zero on entry) = in x W[i] for every sequence:
     // matrices with the same rows in one launch
@@ -1018,20 +1022,26 @@ struct xp_bdec {
         unsigned char* scr = scratch_for(rows, cols);
         if (!scr) return cudaErrorInvalidValue;
         const BmmPrep pr{in.xs, in.xb};
-        return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr, pdl_mm) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
+    cudaError_t resid_norm(long long* y, const float* w_post, const float* w_pre, int mode) {
+        return launch_ex(bk_resid_norm_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, x, y, w_post, w_pre, op_xn,
+                         s->cfg.hidden, s->cfg.rms_eps, mode);
+    }
     cudaError_t forward() {
         const xp_model_config& c = s->cfg;
         const uint32_t H = c.hidden, F = c.ffn, L = c.n_layers;
         const float escale = c.embed_scale > 0 ? c.embed_scale : std::sqrt((float)H);
         const float ascale = c.attn_scale > 0 ? c.attn_scale : 1.0f / std::sqrt((float)c.head_dim);
         cudaError_t e;
-        bk_embed_kernel<<<B, 256, 0, st>>>(tokens, s->embed, escale, x, H);
+        if ((e = launch_ex(bk_embed_kernel, dim3(B), dim3(256), 0, st, 1, pdl_k, (const uint32_t*)tokens, (const float*)s->embed,
+                           escale, x, H)) != cudaSuccess)
+            return e;
         for (uint32_t l = 0; l < L; ++l) {
             const LayerDev& W = s->L[l];
-            if (l == 0) bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, nullptr, W.norm[0], op_xn, H, c.rms_eps, 0);
-            else bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[l - 1].norm[3], W.norm[0], op_xn, H, c.rms_eps, 1);
+            if ((e = resid_norm(dn, l == 0 ? nullptr : s->L[l - 1].norm[3], W.norm[0], l == 0 ? 0 : 1)) != cudaSuccess)
+                return e;
             if ((e = mm_raw({{q, &W.m[0]}, {k, &W.m[1]}, {v, &W.m[2]}}, op_xn)) != cudaSuccess) return e;
             BkAttnArgs aa{};
             aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
@@ -1043,16 +1053,18 @@ struct xp_bdec {
             aa.eps = c.rms_eps;
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
-            bk_attn_kernel<<<B, BK_THREADS, (size_t)4 * ms * 4, st>>>(aa);
+            if ((e = launch_ex(bk_attn_kernel, dim3(B), dim3(BK_THREADS), (size_t)4 * ms * 4, st, 1, pdl_k, aa)) != cudaSuccess)
+                return e;
             if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
-            bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, o, W.norm[1], W.norm[2], op_xn, H, c.rms_eps, 1);
+            if ((e = resid_norm(o, W.norm[1], W.norm[2], 1)) != cudaSuccess) return e;
             if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, op_xn)) != cudaSuccess) return e;
-            bk_geglu_kernel<<<B, BK_THREADS, 0, st>>>(g, u, op_hb, F);
+            if ((e = launch_ex(bk_geglu_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, g, u, op_hb, F)) != cudaSuccess)
+                return e;
             if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
         }
-        bk_resid_norm_kernel<<<B, BK_THREADS, 0, st>>>(x, dn, s->L[L - 1].norm[3], s->final_norm, op_xn, H, c.rms_eps, 1);
+        if ((e = resid_norm(dn, s->L[L - 1].norm[3], s->final_norm, 1)) != cudaSuccess) return e;
         if ((e = mm(logits, op_xn, s->lm)) != cudaSuccess) return e;
-        bk_pos_inc_kernel<<<1, 64, 0, st>>>(pos, B);
+        if ((e = launch_ex(bk_pos_inc_kernel, dim3(1), dim3(64), 0, st, 1, pdl_k, pos, B)) != cudaSuccess) return e;
         return cudaGetLastError();
     }
     // tokens[b] = sample(logits[b]) with the uniform of (seed, seq0 + b, pos[b])
@@ -1066,7 +1078,7 @@ struct xp_bdec {
         da.seq0 = seq0;
         da.token = tokens;
         da.pos_read = pos;
-        cudaError_t e = launch_topk(logits, V, B, cand, da, st, false);
+        cudaError_t e = launch_topk(logits, V, B, cand, da, st, true);
         if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
