@@ -372,7 +372,8 @@ struct xp_session {
         // KV rows of ATTN, then the flash-partial stage of O (512 B per split)
         tk.off_kv = off; off += al128(std::max<uint32_t>(2 * tk.chunk_max * KVD * 2, TK_SPLIT_CAP * 512));
         const uint32_t ring_bytes = off - tk.off_qkv;
-        tk.head_ring = std::min<uint32_t>(TK_MAX_RING, ring_bytes / tk.head.img_bytes);
+        // a multiple of the LM-head warp groups: each group owns its ring slots
+        tk.head_ring = std::min<uint32_t>(TK_MAX_RING, ring_bytes / tk.head.img_bytes) / TK_HEAD_GROUPS * TK_HEAD_GROUPS;
         if (tk.head_ring == 0) return false;
         tk.off_cqkv = off; off += al128(2 * H * 4);
         tk.off_catt = off; off += al128(512 * 4);

@@ -64,7 +64,8 @@ constexpr int TK_MAX_RING = 8;
 constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME_DOWN = 20, TK_ME_HEAD = 21;
 constexpr int TK_MB_STAGE = 29;  // flash partials staged for the O combine
 static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "mbarrier count");
-constexpr int TK_SPLIT_CAP = 128;  // attention splits per layer (the O stage holds 512 B each)
+constexpr int TK_SPLIT_CAP = 128;
+constexpr int TK_HEAD_GROUPS = TK_WARPS / 4;  // LM-head tiles in flight per CTA (4 warps each)  // attention splits per layer (the O stage holds 512 B each)
 
 // steps of the phase machine
 constexpr uint32_t TK_S_QKV = 0, TK_S_ATTN = 1, TK_S_O = 2, TK_S_GU = 3, TK_S_HEAD = 5;
@@ -782,51 +783,83 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     for (uint32_t i = tid; i < QKVW; i += TK_THREADS) a.acc_qkv[i] = 0;
                 }
             } else {
-                // ---------------- 64-column tiles: QKV, O (one), HEAD (ring) ----------------
-                const uint32_t hu = a.head_u1 - a.head_u0;
-                const uint32_t ntile = k == TK_S_HEAD ? (hu > c ? (hu - c + G - 1) / G : 0) : (has ? 1 : 0);
-                const int full = k == TK_S_QKV ? TK_MB_QKV : TK_MB_O;
-                long long* acc = k == TK_S_QKV ? a.acc_qkv : a.acc_o;
-                const uint32_t accw = k == TK_S_QKV ? QKVW : H;
-                const unsigned char* slot = k == TK_S_QKV ? s_qkv : s_o;
-                if (ntile == 0 && k != TK_S_HEAD) wait_slot(full);
-#pragma unroll 1
-                for (uint32_t i = 0; i < ntile; ++i) {
-                    const uint32_t r = i % a.head_ring;
-                    const unsigned char* img = slot;
-                    if (k == TK_S_HEAD) {
-                        wait_slot(TK_MB_HEAD + r);
-                        img = s_qkv + (size_t)r * P.img_bytes;
-                    } else {
-                        wait_slot(full);
-                    }
+                if (k == TK_S_HEAD) {
+                    // ---------------- LM head: ring of 64-column tiles, four at a time ----------------
+                    // warp group g (4 warps) takes tiles i = g, g + 4, ... from ring
+                    // slot i % head_ring (a multiple of 4, so a group's slots are its
+                    // own), splits the blocks over its warps and reduces through a
+                    // double-buffered [4][64] partial with a 128-thread named barrier
+                    const uint32_t hu = a.head_u1 - a.head_u0;
+                    const uint32_t ntile = hu > c ? (hu - c + G - 1) / G : 0;
+                    const uint32_t grp = warp >> 2, gw = warp & 3;
                     TK_MARK(1)
-                    tk_tile64(img, P.nb, xq, red);
-                    if (k == TK_S_HEAD) {
-                        if (tid == 0) mbar_arrive(&mb[TK_ME_HEAD + r]);  // the producer refills it
-                        if (warp == 0) {
-                            const uint32_t t = a.head_u0 + c + i * G;
-                            float v0 = red[lane], v1 = red[lane + 32];
-                            a.logits[(size_t)t * 64 + lane] = v0;
-                            a.logits[(size_t)t * 64 + lane + 32] = v1;
-                            uint32_t ix = t * 64 + lane;
-                            if (v1 > v0) { v0 = v1; ix += 32; }
-                            if (v0 > bv || (v0 == bv && ix < bi)) { bv = v0; bi = ix; }
+#pragma unroll 1
+                    for (uint32_t i = grp, it = 0; i < ntile; i += TK_HEAD_GROUPS, ++it) {
+                        const uint32_t r = i % a.head_ring;
+                        wait_slot(TK_MB_HEAD + r);
+                        const unsigned char* img = s_qkv + (size_t)r * P.img_bytes;
+                        const uint4* nib = reinterpret_cast<const uint4*>(img);
+                        const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)P.nb * 64 * 16);
+                        float a0 = 0.0f, a1 = 0.0f;
+                        for (uint32_t b = gw; b < P.nb; b += 4) {
+                            const XBlk& X = xq[b];
+                            a0 += tk_dot(nib[b * 64 + lane], scl[b * 64 + lane], X);
+                            a1 += tk_dot(nib[b * 64 + lane + 32], scl[b * 64 + lane + 32], X);
                         }
-                    } else if (tid < 64) {
-                        const uint32_t col = (c / P.ks) * 64 + tid;
-                        if (col < accw) red_add_s64(&acc[col], tk_fix(red[tid], a.err));
+                        float* wr = red + grp * 512 + (it & 1) * 256;
+                        wr[gw * 64 + lane] = a0;
+                        wr[gw * 64 + lane + 32] = a1;
+                        asm volatile("bar.sync %0, 128;" ::"r"(2 + grp) : "memory");
+                        if (gw == 0 && lane == 0) mbar_arrive(&mb[TK_ME_HEAD + r]);  // the producer refills it
+                        if (gw < 2) {
+                            const uint32_t col = gw * 32 + lane;
+                            const float v = (wr[col] + wr[64 + col]) + (wr[128 + col] + wr[192 + col]);
+                            const uint32_t t = a.head_u0 + c + i * G;
+                            a.logits[(size_t)t * 64 + col] = v;
+                            const uint32_t ix = t * 64 + col;
+                            if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+                        }
                     }
-                }
-                TK_MARK(2)
-                if (k == TK_S_HEAD && warp == 0) {
+                    TK_MARK(2)
+                    // lowest-index maximum of the CTA
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
                         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                         const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
                         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
                     }
-                    if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
+                    if (lane == 0) {
+                        red32[warp] = bv;
+                        reinterpret_cast<uint32_t*>(red32)[TK_WARPS + warp] = bi;
+                    }
+                    tk_sync();
+                    if (warp == 0) {
+                        bv = lane < TK_WARPS ? red32[lane] : -INFINITY;
+                        bi = lane < TK_WARPS ? reinterpret_cast<const uint32_t*>(red32)[TK_WARPS + lane] : 0xFFFFFFFFu;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                        }
+                        if (lane == 0) { a.am_val[c] = bv; a.am_idx[c] = bi; }
+                    }
+                } else {
+                    // ---------------- one 64-column tile: QKV, O ----------------
+                    const int full = k == TK_S_QKV ? TK_MB_QKV : TK_MB_O;
+                    long long* acc = k == TK_S_QKV ? a.acc_qkv : a.acc_o;
+                    const uint32_t accw = k == TK_S_QKV ? QKVW : H;
+                    const unsigned char* slot = k == TK_S_QKV ? s_qkv : s_o;
+                    wait_slot(full);
+                    TK_MARK(1)
+                    if (has) {
+                        tk_tile64(slot, P.nb, xq, red);
+                        if (tid < 64) {
+                            const uint32_t col = (c / P.ks) * 64 + tid;
+                            if (col < accw) red_add_s64(&acc[col], tk_fix(red[tid], a.err));
+                        }
+                    }
+                    TK_MARK(2)
                 }
             }
         }
