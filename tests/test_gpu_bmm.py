@@ -54,3 +54,25 @@ def test_batch_rejects_bad_shapes():
     with pytest.raises(XpError):
         check(lib().xp_mv_km4_bs_batch(None, ptr(t), ptr(t), ptr(t), ptr(t), 1152, 1024, 65, ptr(t)))
     assert lib().xp_mv_km4_bs_batch_scratch_bytes(1152, 1024, 0) == 0
+
+
+def test_batch_scratch_shared_across_shapes():
+    """One scratch, zeroed once, used by a K-split shape, another K-split shape
+    whose activations land where the first keeps its sums, then the first
+    again: every call must still match the oracle (the library clears the
+    sums when a scratch changes shape)."""
+    shapes = [(6912, 1152, 64), (1152, 1024, 64), (6912, 1152, 64), (1152, 6912, 40)]
+    need = max(lib().xp_mv_km4_bs_batch_scratch_bytes(r, c, n) for r, c, n in shapes)
+    scratch = torch.zeros(need // 4 + 64, dtype=torch.int32, device="cuda")
+    for i, (rows, cols, n) in enumerate(shapes):
+        w = O.gen_normal(40 + i, 1, rows * cols, 0.02)
+        words, scales = O.pack(w, rows, cols)
+        xs = np.stack([O.gen_normal(40 + i, 100 + s, rows, 1.0) for s in range(n)])
+        out = torch.full((n * cols,), -1e30, device="cuda")
+        check(lib().xp_mv_km4_bs_batch(None, ptr(out), ptr(dev(xs.reshape(-1))), ptr(dev(words)), ptr(dev(scales)),
+                                       rows, cols, n, ptr(scratch)))
+        sync()
+        got = host(out).reshape(n, cols)
+        for s in (0, n - 1):
+            want = O.mv(xs[s], words, scales, rows, cols)
+            assert rel_l2(got[s], want) < 1e-5, (i, rows, cols, s, rel_l2(got[s], want))
