@@ -53,7 +53,7 @@ constexpr int TK_WARPS = TK_THREADS / 32;
 constexpr int TK_BLOCK = TK_THREADS + 32;      // + one producer warp that issues every bulk copy
 constexpr int TK_MAXJ = (1536 + TK_THREADS - 1) / TK_THREADS;  // hidden and q|k|v width <= 1536
 constexpr int TK_GROUPS = TK_THREADS / 128;  // 128-thread groups (attention P.V, O combine)
-static_assert(TK_THREADS % 128 == 0 && TK_THREADS >= 256 && TK_THREADS <= 1024, "compute threads");
+static_assert(TK_THREADS % 128 == 0 && TK_THREADS >= 256 && TK_THREADS <= 512, "compute threads");
 constexpr int TK_NMB = 32;   // mbarriers
 // "full" mbarriers: complete once per fill of a slot
 constexpr int TK_MB_QKV = 0, TK_MB_O = 1, TK_MB_GU = 2, TK_MB_DOWN = 3, TK_MB_KV = 4;
@@ -459,33 +459,37 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     sums.w += uv[j] * uv[j];
                 }
             }
-            sums.x = warp_sum(sums.x);
-            sums.y = warp_sum(sums.y);
-            sums.z = warp_sum(sums.z);
-            sums.w = warp_sum(sums.w);
-            if (lane == 0) reinterpret_cast<float4*>(red32)[warp] = sums;
+            // one reduction for the four sums: reduce4 leaves sum q in lanes
+            // with (lane >> 3) == q; then lane l adds its sum l % 4 over the
+            // warps l / 4, l / 4 + 8, ... and three shuffles finish it
+            {
+                const float q4 = reduce4(sums.x, sums.y, sums.z, sums.w);
+                if ((lane & 7) == 0) red32[warp * 4 + (lane >> 3)] = q4;
+            }
+            TK_MARK(4)
             tk_sync();
-            float4 t = lane < TK_WARPS ? reinterpret_cast<const float4*>(red32)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-            t.x = warp_sum(t.x);
-            t.y = warp_sum(t.y);
-            t.z = warp_sum(t.z);
-            t.w = warp_sum(t.w);
-            const float s1 = emb ? 0.0f : rsqrtf(t.x / (float)H + a.eps);
-            const float sc2 = rsqrtf((t.y + 2.0f * s1 * t.z + s1 * s1 * t.w) / (float)H + a.eps);
-            // limbs straight from registers: warp w holds blocks w, w + 16 and
-            // w + 32 in lane order
-            const TkPhase& P = k == TK_S_QKV ? a.qkv : (k == TK_S_GU ? a.gu : a.head);
-            const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
-            const bool has = c < P.units;
+            TK_MARK(5)
+            float t4 = 0.0f;
+#pragma unroll
+            for (int q = lane; q < 4 * TK_WARPS; q += 32) t4 += red32[q];
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 4);
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 8);
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 16);
+            const float tx = __shfl_sync(0xffffffffu, t4, 0), ty = __shfl_sync(0xffffffffu, t4, 1);
+            const float tz = __shfl_sync(0xffffffffu, t4, 2), tw = __shfl_sync(0xffffffffu, t4, 3);
+            const float s1 = emb ? 0.0f : rsqrtf(tx / (float)H + a.eps);
+            const float sc2 = rsqrtf((ty + 2.0f * s1 * tz + s1 * s1 * tw) / (float)H + a.eps);
+            // normalised input -> xn; the shared limb prep below reads it
 #pragma unroll
             for (int j = 0; j < TK_MAXJ; ++j) {
                 const uint32_t i = tid + j * TK_THREADS;
-                const float r = rv[j] + s1 * uv[j];
-                if (i < H && x_out && c == 0) x_out[i] = r;
-                const uint32_t blk = warp + TK_WARPS * j;
-                if (has && blk >= b0 && blk < b0 + P.nb)
-                    xq_prep_block(r * sc2 * (1.0f + wv[H + (i < H ? i : 0)]), &xq[blk - b0]);
+                if (i < H) {
+                    const float r = rv[j] + s1 * uv[j];
+                    if (x_out && c == 0) x_out[i] = r;
+                    xn[i] = r * sc2 * (1.0f + wv[H + i]);
+                }
             }
+            TK_MARK(6)
         } else if (k == TK_S_O) {
             // flash combine of this CTA's 128-dim slice over the splits: the
             // slice of every split arrives in one bulk copy while each warp
@@ -518,8 +522,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     if (warp == 0) wts[lane + 32 * r] = e;
                 }
                 Ls = warp_sum(Ls);
+                TK_MARK(4)
                 wait_slot(TK_MB_STAGE);
                 tk_sync();
+                TK_MARK(5)
                 const uint32_t d = tid & 127, g = tid >> 7;
                 float acc = 0.0f;
 #pragma unroll 4
@@ -532,6 +538,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 128 + tid];
                     xn[tid] = t / Ls;
                 }
+                TK_MARK(6)
             }
         } else {
             // ================= ATTN =================
@@ -708,11 +715,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // ---------------- limbs of xn: one shared prep ----------------
             const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
             const bool has = c < P.units;
-            if (k == TK_S_O) {
-                tk_sync();  // xn complete
-                if (has) {
-                    for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[b * 32 + lane], &xq[b]);
-                }
+            tk_sync();  // xn complete
+            if (has) {
+                const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
+#pragma unroll 1
+                for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
             }
             tk_sync();
             TK_MARK(0)
@@ -725,31 +732,42 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     const uint32_t nb = P.nb;
                     uint32_t nu = 0;
                     for (uint32_t u = c; u < P.units; u += G) ++nu;
-                    // half-warp workers (16 lanes = 16 columns), each fixed on one
-                    // (unit, matrix) pair and a stride of blocks, accumulating in a register
-                    const uint32_t worker = tid >> 4, col = tid & 15, nwk = TK_THREADS / 16;
-                    const uint32_t npair = nu * 2, wpp = nwk / npair;
-                    const uint32_t p = worker / wpp, r = worker % wpp;
-                    float acc = 0.0f;
-                    if (p < npair) {
-                        const uint32_t ui = p >> 1, m = p & 1;
-                        const unsigned char* img = s_gu + (size_t)ui * P.img_bytes;
-                        const uint4* nib = reinterpret_cast<const uint4*>(img);
-                        const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)2 * nb * 16 * 16);
-                        for (uint32_t b = r; b < nb; b += wpp)
-                            acc += tk_dot(nib[(m * nb + b) * 16 + col], scl[(m * nb + b) * 16 + col], xq[b]);
+                    // warp w takes blocks w, w + 16, ... and holds that block's limbs
+                    // in registers for every unit; lane = (matrix lane / 16,
+                    // column lane % 16), so the limb loads are warp-wide broadcasts
+                    // and a quarter-warp's nibble load is one contiguous 128 B
+                    const uint32_t m = lane >> 4, col = lane & 15;
+                    float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f;
+#pragma unroll 1
+                    for (uint32_t b = warp; b < nb; b += TK_WARPS) {
+                        const XBlk X = xq[b];
+#pragma unroll
+                        for (uint32_t ui = 0; ui < 3; ++ui) {
+                            if (ui < nu) {
+                                const unsigned char* img = s_gu + (size_t)ui * P.img_bytes;
+                                const uint32_t e = (m * nb + b) * 16 + col;
+                                const float d = tk_dot(reinterpret_cast<const uint4*>(img)[e],
+                                                       reinterpret_cast<const uint16_t*>(img + (size_t)2 * nb * 16 * 16)[e], X);
+                                if (ui == 0) acc0 += d;
+                                else if (ui == 1) acc1 += d;
+                                else acc2 += d;
+                            }
+                        }
                     }
-                    float* wp = red;  // [npair * wpp][16]
-                    if (p < npair) wp[(p * wpp + r) * 16 + col] = acc;
+                    float* wp = red;  // [warp][unit][32]
+                    wp[(warp * 3 + 0) * 32 + lane] = acc0;
+                    wp[(warp * 3 + 1) * 32 + lane] = acc1;
+                    wp[(warp * 3 + 2) * 32 + lane] = acc2;
                     tk_sync();
                     TK_MARK(2)
                     if ((uint32_t)tid < nu * 16) {
                         const uint32_t ui = tid / 16, cc = tid % 16;
+                        const uint32_t nw = nb < (uint32_t)TK_WARPS ? nb : (uint32_t)TK_WARPS;
                         float gs = 0.0f, up = 0.0f;
-#pragma unroll 1
-                        for (uint32_t q = 0; q < wpp; ++q) {
-                            gs += wp[((2 * ui) * wpp + q) * 16 + cc];
-                            up += wp[((2 * ui + 1) * wpp + q) * 16 + cc];
+#pragma unroll 4
+                        for (uint32_t q = 0; q < nw; ++q) {
+                            gs += wp[(q * 3 + ui) * 32 + cc];
+                            up += wp[(q * 3 + ui) * 32 + 16 + cc];
                         }
                         xn[tid] = gelu_tanh_ref(gs) * up;  // hb row (c + ui G) * 16 + cc
                     }
@@ -765,16 +783,26 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     uint32_t nu = 0;
                     for (uint32_t u = c; u < P.units; u += G) ++nu;
                     const uint32_t ib = a.down.img_bytes;
+                    // unit-outer: each unit's limbs are loaded once per thread
+                    float s[TK_MAXJ];
+#pragma unroll
+                    for (int jj = 0; jj < TK_MAXJ; ++jj) s[jj] = 0.0f;
 #pragma unroll 1
-                    for (uint32_t j = tid; j < H; j += TK_THREADS) {
-                        float s = 0.0f;
-#pragma unroll 1
-                        for (uint32_t ui = 0; ui < nu; ++ui) {
-                            const unsigned char* img = s_down + (size_t)ui * ib;
-                            s += tk_dot_half(reinterpret_cast<const uint2*>(img)[j],
-                                             reinterpret_cast<const uint16_t*>(img + (size_t)H * 8)[j], xq[ui]);
+                    for (uint32_t ui = 0; ui < nu; ++ui) {
+                        const XBlk& X = xq[ui];
+                        const unsigned char* img = s_down + (size_t)ui * ib;
+#pragma unroll
+                        for (int jj = 0; jj < TK_MAXJ; ++jj) {
+                            const uint32_t j = tid + jj * TK_THREADS;
+                            if (j < H)
+                                s[jj] += tk_dot_half(reinterpret_cast<const uint2*>(img)[j],
+                                                     reinterpret_cast<const uint16_t*>(img + (size_t)H * 8)[j], X);
                         }
-                        red_add_s64(&a.acc_dn[j], tk_fix(s, a.err));
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < TK_MAXJ; ++jj) {
+                        const uint32_t j = tid + jj * TK_THREADS;
+                        if (j < H) red_add_s64(&a.acc_dn[j], tk_fix(s[jj], a.err));
                     }
                 }
                 // the q|k|v sums were consumed by this layer's ATTN step

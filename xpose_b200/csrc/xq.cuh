@@ -36,8 +36,10 @@ static_assert(sizeof(XBlk) == 128, "XBlk is 128 bytes");
 // One warp converts one block: lane k holds x[k] of the block.
 XP_DEV void xq_prep_block(float v, XBlk* dst) {
     const int lane = threadIdx.x & 31;
-    const float amax = warp_max(fabsf(v));
-    const int eb = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+    // |v| as bits orders like |v|, so one integer max reduction finds the
+    // exponent of the block's largest magnitude
+    const uint32_t amax = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7FFFFFFFu);
+    const int eb = (int)((amax >> 23) & 0xFFu);
     int d0 = 0, d1 = 0, d2 = 0;
     float f = 0.0f;
     if (eb >= 8) {
