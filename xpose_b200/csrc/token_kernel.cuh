@@ -73,7 +73,8 @@ constexpr uint32_t TK_STEPS = 4;  // steps per layer
 
 // Trace layout (u64 words, %globaltimer ns): [0] barriers, [1] start,
 // [2k, 2k+1] CTA 0 arrive/leave of barrier k, [512 + 8k + i] CTA 0 marks in
-// step k, then per CTA c and barrier k < TK_TRACE_MAXBAR its arrive/leave at
+// step k ([508] the previous launch's end, [509] this launch's end, [510] its
+// entry), then per CTA c and barrier k < TK_TRACE_MAXBAR its arrive/leave at
 // TK_TRACE_CTA + (c * TK_TRACE_MAXBAR + k) * 2.
 constexpr uint32_t TK_TRACE_CTA = 512 + 8 * 1024, TK_TRACE_MAXBAR = 160, TK_TRACE_MAXCTA = 160;
 constexpr uint32_t TK_TRACE_WORDS = TK_TRACE_CTA + 2 * TK_TRACE_MAXBAR * TK_TRACE_MAXCTA;
@@ -323,6 +324,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     uint32_t nbar = 0;
     uint32_t par = 0;  // parity bit per "full" mbarrier, identical in every compute thread
 
+    if (a.trace && c == 0 && tid == 0) {
+        a.trace[508] = a.trace[509];  // the previous launch's end
+        a.trace[510] = globaltimer_ns();
+    }
     if (tid == 0) {
         for (int i = 0; i < TK_NMB; ++i) mbar_init(&mb[i], 1);
         fence_mbar_init();
@@ -585,11 +590,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                         }
                     }
                     if (warp < 4) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            qs[warp * 256 + 4 * lane + i] = v[i] * a.attn_scale;
-                            qs[warp * 256 + 128 + 4 * lane + i] = v[4 + i] * a.attn_scale;
-                        }
+                        // q in the key-lane order of the score loop: dim d sits at
+                        // [(d & 7) >> 2][d >> 3][d & 3] of the head's 256 floats, so
+                        // lane l's dims 8l..8l+7 are two conflict-free float4 loads
+                        const float sq = a.attn_scale;
+                        float* qh = qs + warp * 256 + (lane & 1) * 128 + (lane >> 1) * 4;
+                        *reinterpret_cast<float4*>(qh) = make_float4(v[0] * sq, v[1] * sq, v[2] * sq, v[3] * sq);
+                        *reinterpret_cast<float4*>(qh + 64) = make_float4(v[4] * sq, v[5] * sq, v[6] * sq, v[7] * sq);
                     } else {
                         __half* dst = warp == 4 ? kn : vn;
                         __half* cache = warp == 4 ? Ly.kc : Ly.vc;
@@ -610,37 +617,44 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 TK_MARK(1)
                 const __half* ks = reinterpret_cast<const __half*>(s_kv);
                 const __half* vs = ks + (size_t)a.chunk_max * 256;
-                // scores: one key per warp, lane holds 8 dims of every head
+                // scores: a warp per key, lane l holds dims 8l..8l+7 of every
+                // head's q in registers (loaded once per warp), so each key costs
+                // one conflict-free row load; about two keys per warp keeps the
+                // q loads few when the chunk is short
+                {
+                    const uint32_t nwk = min((uint32_t)TK_WARPS, max(1u, (n + 1) / 2));
+                    if ((uint32_t)warp < nwk) {
+                        float4 qa[4], qb[4];
+#pragma unroll
+                        for (int hh = 0; hh < 4; ++hh) {
+                            qa[hh] = *reinterpret_cast<const float4*>(qs + hh * 256 + 4 * lane);
+                            qb[hh] = *reinterpret_cast<const float4*>(qs + hh * 256 + 128 + 4 * lane);
+                        }
 #pragma unroll 1
-                for (uint32_t jj = warp; jj < n; jj += TK_WARPS) {
-                    const uint32_t j = w.j0 + jj;
-                    const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(kn + 8 * lane)
-                                               : *reinterpret_cast<const uint4*>(ks + (size_t)jj * 256 + 8 * lane);
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-                    float kf[8];
+                        for (uint32_t jj = warp; jj < n; jj += nwk) {
+                            const uint32_t j = w.j0 + jj;
+                            const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(kn + 8 * lane)
+                                                       : *reinterpret_cast<const uint4*>(ks + (size_t)jj * 256 + 8 * lane);
+                            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+                            const float2 k0 = __half22float2(h2[0]), k1 = __half22float2(h2[1]);
+                            const float2 k2 = __half22float2(h2[2]), k3 = __half22float2(h2[3]);
+                            float s4[4];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 f = __half22float2(h2[i]);
-                        kf[2 * i] = f.x;
-                        kf[2 * i + 1] = f.y;
+                            for (int hh = 0; hh < 4; ++hh) {
+                                float acc = qa[hh].x * k0.x;
+                                acc = fmaf(qa[hh].y, k0.y, acc);
+                                acc = fmaf(qa[hh].z, k1.x, acc);
+                                acc = fmaf(qa[hh].w, k1.y, acc);
+                                acc = fmaf(qb[hh].x, k2.x, acc);
+                                acc = fmaf(qb[hh].y, k2.y, acc);
+                                acc = fmaf(qb[hh].z, k3.x, acc);
+                                acc = fmaf(qb[hh].w, k3.y, acc);
+                                s4[hh] = acc;
+                            }
+                            const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
+                            if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
+                        }
                     }
-                    float s4[4];
-#pragma unroll
-                    for (int hh = 0; hh < 4; ++hh) {
-                        const float4 qa = *reinterpret_cast<const float4*>(qs + hh * 256 + 8 * lane);
-                        const float4 qb = *reinterpret_cast<const float4*>(qs + hh * 256 + 8 * lane + 4);
-                        float acc = qa.x * kf[0];
-                        acc = fmaf(qa.y, kf[1], acc);
-                        acc = fmaf(qa.z, kf[2], acc);
-                        acc = fmaf(qa.w, kf[3], acc);
-                        acc = fmaf(qb.x, kf[4], acc);
-                        acc = fmaf(qb.y, kf[5], acc);
-                        acc = fmaf(qb.z, kf[6], acc);
-                        acc = fmaf(qb.w, kf[7], acc);
-                        s4[hh] = acc;
-                    }
-                    const float tot = reduce4(s4[0], s4[1], s4[2], s4[3]);
-                    if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * a.chunk_max + jj] = tot;
                 }
                 tk_sync();
                 TK_MARK(2)
@@ -987,7 +1001,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     }
     if (c == 0 && tid == 0) {
         *a.epoch = base + (uint64_t)nbar * G;
-        if (a.trace) { a.trace[0] = nbar; a.trace[2 * nbar + 2] = globaltimer_ns(); }
+        if (a.trace) {
+            a.trace[0] = nbar;
+            a.trace[509] = a.trace[2 * nbar + 2] = globaltimer_ns();
+        }
     }
 #undef TK_MARK
 }
