@@ -555,26 +555,26 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 __half* kn = reinterpret_cast<__half*>(qs + 4 * 256);  // [256]
                 __half* vn = kn + 256;                                 // [256]
                 float* sc = reinterpret_cast<float*>(sm + a.off_sc);   // [4][chunk_max]
-                float* qkvs = red;                                     // [QKVW]
-#pragma unroll
-                for (int r = 0; r < TK_MAXJ; ++r) {
-                    const uint32_t i = tid + r * TK_THREADS;
-                    if (i < QKVW) qkvs[i] = tk_unfix(a.acc_qkv[i]);
-                }
-                tk_sync();
-                TK_MARK(0)
                 if (warp < 6) {
-                    // warps 0-3: q heads, 4: k, 5: v; a head held as 8 values
-                    // per lane (dims 4*lane..+3 and 128+4*lane..+3)
+                    // warps 0-3: q heads, 4: k, 5: v, each loading its head's
+                    // fixed-point sums itself; lane holds dims 4l..4l+3 and
+                    // 128+4l..+3 (the rotate-half pairs)
                     const uint32_t off = warp < 4 ? warp * 256 : (warp == 4 ? a.QD : a.QD + a.KVD);
-                    float v[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = qkvs[off + (i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4))];
+                    const longlong2* src = reinterpret_cast<const longlong2*>(a.acc_qkv + off + 4 * lane);
+                    const longlong2 r0 = src[0], r1 = src[1], r2 = src[64], r3 = src[65];
+                    float v[8] = {tk_unfix(r0.x), tk_unfix(r0.y), tk_unfix(r1.x), tk_unfix(r1.y),
+                                  tk_unfix(r2.x), tk_unfix(r2.y), tk_unfix(r3.x), tk_unfix(r3.y)};
+                    TK_MARK(0)
                     if (warp < 5) {
                         // QK-norm + rotate-half RoPE
-                        const float* wq = warp < 4 ? ca : ca + 256;
-                        const float* cosT = rope + (Ly.global ? 256 : 0);
-                        const float* sinT = cosT + 128;
+                        const float* wq = (warp < 4 ? ca : ca + 256) + 4 * lane;
+                        const float* cosT = rope + (Ly.global ? 256 : 0) + 4 * lane;
+                        const float4 wl = *reinterpret_cast<const float4*>(wq);
+                        const float4 wh = *reinterpret_cast<const float4*>(wq + 128);
+                        const float4 cs = *reinterpret_cast<const float4*>(cosT);
+                        const float4 sn = *reinterpret_cast<const float4*>(cosT + 128);
+                        const float wlo[4] = {wl.x, wl.y, wl.z, wl.w}, whi[4] = {wh.x, wh.y, wh.z, wh.w};
+                        const float co[4] = {cs.x, cs.y, cs.z, cs.w}, si[4] = {sn.x, sn.y, sn.z, sn.w};
                         float ss = 0.0f;
 #pragma unroll
                         for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
@@ -582,11 +582,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                         const float scl = rsqrtf(ss / 256.0f + a.eps);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            const uint32_t d = 4 * lane + i;
-                            const float lo = v[i] * scl * (1.0f + wq[d]);
-                            const float hi = v[4 + i] * scl * (1.0f + wq[128 + d]);
-                            v[i] = lo * cosT[d] - hi * sinT[d];
-                            v[4 + i] = lo * sinT[d] + hi * cosT[d];
+                            const float lo = v[i] * scl * (1.0f + wlo[i]);
+                            const float hi = v[4 + i] * scl * (1.0f + whi[i]);
+                            v[i] = lo * co[i] - hi * si[i];
+                            v[4 + i] = lo * si[i] + hi * co[i];
                         }
                     }
                     if (warp < 4) {
@@ -598,17 +597,20 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                         *reinterpret_cast<float4*>(qh) = make_float4(v[0] * sq, v[1] * sq, v[2] * sq, v[3] * sq);
                         *reinterpret_cast<float4*>(qh + 64) = make_float4(v[4] * sq, v[5] * sq, v[6] * sq, v[7] * sq);
                     } else {
+                        const __half2 l01 = __floats2half2_rn(v[0], v[1]), l23 = __floats2half2_rn(v[2], v[3]);
+                        const __half2 h01 = __floats2half2_rn(v[4], v[5]), h23 = __floats2half2_rn(v[6], v[7]);
+                        uint2 lo, hi;
+                        lo.x = *reinterpret_cast<const uint32_t*>(&l01);
+                        lo.y = *reinterpret_cast<const uint32_t*>(&l23);
+                        hi.x = *reinterpret_cast<const uint32_t*>(&h01);
+                        hi.y = *reinterpret_cast<const uint32_t*>(&h23);
                         __half* dst = warp == 4 ? kn : vn;
-                        __half* cache = warp == 4 ? Ly.kc : Ly.vc;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
-                            dst[4 * lane + i] = lo;
-                            dst[128 + 4 * lane + i] = hi;
-                            if (c == 0) {
-                                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
-                                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
-                            }
+                        reinterpret_cast<uint2*>(dst + 4 * lane)[0] = lo;
+                        reinterpret_cast<uint2*>(dst + 128 + 4 * lane)[0] = hi;
+                        if (c == 0) {
+                            __half* cache = (warp == 4 ? Ly.kc : Ly.vc) + (size_t)pos * 256;
+                            reinterpret_cast<uint2*>(cache + 4 * lane)[0] = lo;
+                            reinterpret_cast<uint2*>(cache + 128 + 4 * lane)[0] = hi;
                         }
                     }
                 }
