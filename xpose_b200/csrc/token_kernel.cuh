@@ -65,6 +65,7 @@ constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME
 constexpr int TK_MB_STAGE = 29;  // flash partials staged for the O combine
 static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "mbarrier count");
 constexpr int TK_SPLIT_CAP = 128;
+constexpr uint32_t TK_XR = 2048;  // x1 kept in red[TK_XR .. TK_XR + H) from GU to the next QKV
 constexpr int TK_HEAD_GROUPS = TK_WARPS / 4;  // LM-head tiles in flight per CTA (4 warps each)  // attention splits per layer (the O stage holds 512 B each)
 
 // steps of the phase machine
@@ -421,14 +422,91 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     const uint32_t nstep = TK_STEPS * L + (a.want_logits ? 1u : 0u);
     float bv = -INFINITY;  // HEAD: this thread's best logit and its index (warp 0)
     uint32_t bi = 0xFFFFFFFFu;
+    // split-norm QKV: dot(W, A) of the next layer's unit (warps 1..nb, made
+    // during the GU barrier wait) and sum x1^2 of the residual it starts from
+    float aq0 = 0.0f, aq1 = 0.0f, ss_x1 = 0.0f;
+    float* xr = red + TK_XR;  // x1 (residual after attention), GU -> next QKV
 #pragma unroll 1
     for (uint32_t step = 0; step < nstep; ++step) {
         const uint32_t l = step / TK_STEPS;
         const uint32_t k = l == L ? TK_S_HEAD : step - TK_STEPS * l;
         const TkLayer& Ly = a.layers[l < L ? l : L - 1];
 
-        // ---------------- input of the step -> xn ----------------
-        if (k == TK_S_QKV || k == TK_S_GU || k == TK_S_HEAD) {
+        const bool split_qkv = k == TK_S_QKV && l > 0;
+        if (split_qkv) {
+            // ---------------- QKV of layers >= 1: split norm ----------------
+            // The unit's input is x = sc2 (1 + w_attn) (x1 + s1 u) with
+            // u = y (1 + w_post) and y the down-proj sums, so its dot is
+            // sc2 [dot(W, A) + s1 dot(W, B)], A = (1 + w_attn) x1 (dotted during
+            // the previous barrier wait) and B = (1 + w_attn) u. B's limbs need
+            // only y, not the norms, so the B dot runs beside the block
+            // reduction of the norm sums instead of after it.
+            const TkPhase& P = a.qkv;
+            const bool mine = c < P.units && warp >= 1 && (uint32_t)(warp - 1) < P.nb;
+            const uint32_t bw = warp - 1, b0 = (c % P.ks) * P.nb;
+            float uv[TK_MAXJ], xb[TK_MAXJ];
+            float sy = 0.0f, sbu = 0.0f, suu = 0.0f;
+#pragma unroll
+            for (int j = 0; j < TK_MAXJ; ++j) {
+                const uint32_t i = tid + j * TK_THREADS;
+                const float y = i < H ? tk_unfix(a.acc_dn[i]) : 0.0f;
+                xb[j] = i < H ? xr[i] : 0.0f;
+                uv[j] = i < H ? y * (1.0f + cq[i]) : 0.0f;
+                sy += y * y;
+                sbu += xb[j] * uv[j];
+                suu += uv[j] * uv[j];
+            }
+            float bq0 = 0.0f, bq1 = 0.0f;
+            if (mine) {
+                const uint32_t i = (b0 + bw) * 32 + lane;
+                const float yb = tk_unfix(a.acc_dn[i]);
+                xq_prep_block(yb * (1.0f + cq[i]) * (1.0f + cq[H + i]), &xq[bw]);
+                __syncwarp();
+                const uint4* nib = reinterpret_cast<const uint4*>(s_qkv);
+                const uint16_t* scl = reinterpret_cast<const uint16_t*>(s_qkv + (size_t)P.nb * 64 * 16);
+                bq0 = tk_dot(nib[bw * 64 + lane], scl[bw * 64 + lane], xq[bw]);
+                bq1 = tk_dot(nib[bw * 64 + lane + 32], scl[bw * 64 + lane + 32], xq[bw]);
+            }
+            TK_MARK(4)
+            {
+                const float q4 = reduce4(sy, sbu, suu, 0.0f);
+                if ((lane & 7) == 0) red32[warp * 4 + (lane >> 3)] = q4;
+            }
+            tk_sync();
+            TK_MARK(5)
+            float t4 = 0.0f;
+#pragma unroll
+            for (int q = lane; q < 4 * TK_WARPS; q += 32) t4 += red32[q];
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 4);
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 8);
+            t4 += __shfl_xor_sync(0xffffffffu, t4, 16);
+            const float tx = __shfl_sync(0xffffffffu, t4, 0), ty = __shfl_sync(0xffffffffu, t4, 1);
+            const float tz = __shfl_sync(0xffffffffu, t4, 2);
+            const float s1 = rsqrtf(tx / (float)H + a.eps);
+            const float sc2 = rsqrtf((ss_x1 + 2.0f * s1 * ty + s1 * s1 * tz) / (float)H + a.eps);
+            if (c == 0) {
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) {
+                    const uint32_t i = tid + j * TK_THREADS;
+                    if (i < H) a.x0[i] = xb[j] + s1 * uv[j];
+                }
+            }
+            float* wr = red;  // [nb][64] per-block partials
+            if (mine) {
+                wr[bw * 64 + lane] = aq0 + s1 * bq0;
+                wr[bw * 64 + lane + 32] = aq1 + s1 * bq1;
+            }
+            tk_sync();
+            if (c < P.units && tid < 64) {
+                float sum = 0.0f;
+#pragma unroll 1
+                for (uint32_t w = 0; w < P.nb; ++w) sum += wr[w * 64 + tid];
+                const uint32_t col = (c / P.ks) * 64 + tid;
+                if (col < QKVW) red_add_s64(&a.acc_qkv[col], tk_fix(sum * sc2, a.err));
+            }
+            TK_MARK(2)
+        } else if (k == TK_S_QKV || k == TK_S_GU || k == TK_S_HEAD) {
+            // ---------------- input of the step -> xn ----------------
             // r = base + rmsnorm_gemma(sum, w_post) (or the scaled embedding
             // row); x_out = r (CTA 0); xn = rmsnorm_gemma(r, w_pre)
             wait_slot(k == TK_S_GU ? TK_MB_CGU : TK_MB_CQKV);
@@ -483,7 +561,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             const float tx = __shfl_sync(0xffffffffu, t4, 0), ty = __shfl_sync(0xffffffffu, t4, 1);
             const float tz = __shfl_sync(0xffffffffu, t4, 2), tw = __shfl_sync(0xffffffffu, t4, 3);
             const float s1 = emb ? 0.0f : rsqrtf(tx / (float)H + a.eps);
-            const float sc2 = rsqrtf((ty + 2.0f * s1 * tz + s1 * s1 * tw) / (float)H + a.eps);
+            const float ssr = ty + 2.0f * s1 * tz + s1 * s1 * tw;  // sum r^2
+            const float sc2 = rsqrtf(ssr / (float)H + a.eps);
+            if (k == TK_S_GU) ss_x1 = ssr;
             // normalised input -> xn; the shared limb prep below reads it
 #pragma unroll
             for (int j = 0; j < TK_MAXJ; ++j) {
@@ -491,6 +571,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 if (i < H) {
                     const float r = rv[j] + s1 * uv[j];
                     if (x_out && c == 0) x_out[i] = r;
+                    if (k == TK_S_GU) xr[i] = r;
                     xn[i] = r * sc2 * (1.0f + wv[H + i]);
                 }
             }
@@ -727,7 +808,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             }
         }
 
-        if (k != TK_S_ATTN) {
+        if (k != TK_S_ATTN && !split_qkv) {
             // ---------------- limbs of xn: one shared prep ----------------
             const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
             const bool has = c < P.units;
@@ -776,20 +857,17 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     wp[(warp * 3 + 2) * 32 + lane] = acc2;
                     tk_sync();
                     TK_MARK(2)
-                    if ((uint32_t)tid < nu * 16) {
-                        const uint32_t ui = tid / 16, cc = tid % 16;
+                    // warp ui: lanes 0-15 sum unit ui's gate partials, lanes 16-31
+                    // its up partials; hb = GeGLU in lanes 0-15 (zeros above),
+                    // whose limbs the same warp makes (rows 0-15 of a block)
+                    if ((uint32_t)warp < nu) {
                         const uint32_t nw = nb < (uint32_t)TK_WARPS ? nb : (uint32_t)TK_WARPS;
-                        float gs = 0.0f, up = 0.0f;
+                        float t = 0.0f;
 #pragma unroll 4
-                        for (uint32_t q = 0; q < nw; ++q) {
-                            gs += wp[(q * 3 + ui) * 32 + cc];
-                            up += wp[(q * 3 + ui) * 32 + 16 + cc];
-                        }
-                        xn[tid] = gelu_tanh_ref(gs) * up;  // hb row (c + ui G) * 16 + cc
+                        for (uint32_t q = 0; q < nw; ++q) t += wp[(q * 3 + warp) * 32 + lane];
+                        const float upv = __shfl_down_sync(0xffffffffu, t, 16);
+                        xq_prep_block(lane < 16 ? gelu_tanh_ref(t) * upv : 0.0f, &xq[warp]);  // hb rows (c + warp G) * 16 + lane
                     }
-                    tk_sync();
-                    // limbs of each unit's 16 hb values (rows 0-15 of a block)
-                    if ((uint32_t)warp < nu) xq_prep_block(lane < 16 ? xn[warp * 16 + lane] : 0.0f, &xq[warp]);
                     tk_sync();
                 }
                 // down-proj of this CTA's hb rows for every output column
@@ -921,6 +999,25 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             red_release_add_u64(a.bar, 1ull);
             if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
             if (k == TK_S_GU) mbar_arrive(&mb[TK_ME_DOWN]);
+        }
+        if (k == TK_S_GU && l + 1 < L) {
+            // while thread 0 waits: dot(W, A) of the next layer's QKV unit,
+            // A = (1 + w_attn) x1 for this warp's block (warps 1..nb)
+            wait_slot(TK_MB_CQKV);
+            wait_slot(TK_MB_QKV);
+            const TkPhase& P = a.qkv;
+            const uint32_t bw = warp - 1;
+            if (c < P.units && warp >= 1 && bw < P.nb) {
+                const uint32_t i = ((c % P.ks) * P.nb + bw) * 32 + lane;
+                xq_prep_block(xr[i] * (1.0f + cq[H + i]), &xq[bw]);
+                __syncwarp();
+                const uint4* nib = reinterpret_cast<const uint4*>(s_qkv);
+                const uint16_t* scl = reinterpret_cast<const uint16_t*>(s_qkv + (size_t)P.nb * 64 * 16);
+                aq0 = tk_dot(nib[bw * 64 + lane], scl[bw * 64 + lane], xq[bw]);
+                aq1 = tk_dot(nib[bw * 64 + lane + 32], scl[bw * 64 + lane + 32], xq[bw]);
+            }
+        }
+        if (tid == 0) {
             const uint64_t target = base + (uint64_t)nbar * G;
             uint32_t it = 0;
             // acquire load + the closing bar.sync order every thread's later
