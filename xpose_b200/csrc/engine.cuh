@@ -504,7 +504,8 @@ struct xp_session {
         if ((e = alloc(&tp_buf, TK_TP_MAX * sizeof(TkTpSlot) / 4)) != XP_OK) return e;
         if ((e = alloc(&tk.tp_count, 4)) != XP_OK) return e;
         tk.tp_slots[0] = reinterpret_cast<TkTpSlot*>(tp_buf);
-        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
         XP_CUDA_TRY(cudaStreamSynchronize(st));
         return XP_OK;
     }
@@ -523,7 +524,7 @@ struct xp_session {
         c.attrs = at;
         c.numAttrs = 1;
         ++launches;
-        cudaError_t e = cudaLaunchKernelEx(&c, token_kernel, a);
+        cudaError_t e = a.trace ? cudaLaunchKernelEx(&c, token_kernel<true>, a) : cudaLaunchKernelEx(&c, token_kernel<false>, a);
         if (e != cudaSuccess || !want_logits || sp.greedy) return e;
         launches += 2;
         return launch_sample_topk(token, sample_out, pos, nullptr, nullptr, logits, cfg.vocab, sp.top_k,

@@ -245,7 +245,7 @@ XP_DEV void tk_tile64(const unsigned char* img, uint32_t nb, const XBlk* xq, flo
 
 // Issue the bulk copies of this CTA's units of a phase into its slot
 // (producer lane). Returns whether anything was armed on `bar`.
-XP_DEV bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar) {
+__device__ __noinline__ bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar) {
     const uint32_t G = gridDim.x, c = blockIdx.x;
     if (c >= P.units) return false;
     uint32_t n = 0;
@@ -284,7 +284,7 @@ XP_DEV TkWin tk_window(uint32_t pos, uint32_t window, uint32_t chunk_min) {
 }
 
 // Stage the KV rows [j0, min(j1, pos)) of one layer (producer lane).
-XP_DEV bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigned char* kvs, uint64_t* bar) {
+__device__ __noinline__ bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigned char* kvs, uint64_t* bar) {
     const TkWin w = tk_window(pos, L.window, a.chunk_min);
     const uint32_t end = min(w.j1, pos);
     if (w.j1 - w.j0 > a.chunk_max) { atomicOr(a.err, TK_ERR_ATTN_CHUNK); return false; }
@@ -299,7 +299,11 @@ XP_DEV bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigne
 }
 
 // ---------------------------------------------------------------------------------
+// TRACE: record the phase timeline into a.trace (XP_TRACE); the production
+// instance carries none of that code.
+template <bool TRACE>
 __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constant__ TkArgs a) {
+    uint64_t* const trace = TRACE ? a.trace : nullptr;
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -325,9 +329,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     uint32_t nbar = 0;
     uint32_t par = 0;  // parity bit per "full" mbarrier, identical in every compute thread
 
-    if (a.trace && c == 0 && tid == 0) {
-        a.trace[508] = a.trace[509];  // the previous launch's end
-        a.trace[510] = globaltimer_ns();
+    if (trace && c == 0 && tid == 0) {
+        trace[508] = trace[509];  // the previous launch's end
+        trace[510] = globaltimer_ns();
     }
     if (tid == 0) {
         for (int i = 0; i < TK_NMB; ++i) mbar_init(&mb[i], 1);
@@ -413,11 +417,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         rope[t * 256 + d] = co;
         rope[t * 256 + 128 + d] = s;
     }
-    if (a.trace && c == 0 && tid == 0) a.trace[1] = globaltimer_ns();
+    if (trace && c == 0 && tid == 0) trace[1] = globaltimer_ns();
     tk_sync();
 
 #define TK_MARK(k) \
-    if (a.trace && c == 0 && tid == 0) a.trace[512 + nbar * 8 + (k)] = globaltimer_ns();
+    if (trace && c == 0 && tid == 0) trace[512 + nbar * 8 + (k)] = globaltimer_ns();
 
     const uint32_t nstep = TK_STEPS * L + (a.want_logits ? 1u : 0u);
     float bv = -INFINITY;  // HEAD: this thread's best logit and its index (warp 0)
@@ -990,11 +994,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         ++nbar;
         tk_sync();
         if (tid == 0) {
-            if (a.trace) {
+            if (trace) {
                 const uint64_t t = globaltimer_ns();
-                if (c == 0) a.trace[2 * nbar] = t;
+                if (c == 0) trace[2 * nbar] = t;
                 if (nbar < TK_TRACE_MAXBAR && c < TK_TRACE_MAXCTA)
-                    a.trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
+                    trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
             }
             red_release_add_u64(a.bar, 1ull);
             if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
@@ -1028,11 +1032,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     break;
                 }
             }
-            if (a.trace) {
+            if (trace) {
                 const uint64_t t = globaltimer_ns();
-                if (c == 0) a.trace[2 * nbar + 1] = t;
+                if (c == 0) trace[2 * nbar + 1] = t;
                 if (nbar < TK_TRACE_MAXBAR && c < TK_TRACE_MAXCTA)
-                    a.trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2 + 1] = t;
+                    trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2 + 1] = t;
             }
         }
         tk_sync();
@@ -1100,9 +1104,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     }
     if (c == 0 && tid == 0) {
         *a.epoch = base + (uint64_t)nbar * G;
-        if (a.trace) {
-            a.trace[0] = nbar;
-            a.trace[509] = a.trace[2 * nbar + 2] = globaltimer_ns();
+        if (trace) {
+            trace[0] = nbar;
+            trace[509] = trace[2 * nbar + 2] = globaltimer_ns();
         }
     }
 #undef TK_MARK
