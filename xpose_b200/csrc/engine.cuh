@@ -386,6 +386,8 @@ struct xp_session {
         tk.off_sc = off; off += al128(4 * tk.chunk_max * 4);
         tk.off_red = off; off += al128(std::max<uint32_t>(4096, 64 + 16 * 64) * 4);
         tk.off_misc = off; off += 512;
+        if (cfg.n_layers > TK_MAX_LAYERS) return false;
+        tk.off_lay = off; off += al128(cfg.n_layers * (uint32_t)sizeof(TkLayInfo));
         tk_smem = off;
         if (tk_smem + 1024 > 227 * 1024) return false;
         tk_grid = G;

@@ -104,6 +104,17 @@ struct TkLayer {
     uint32_t global;      // RoPE table: 1 = global theta, 0 = local
 };
 
+// What the compute warps need of a layer in every step, kept in shared
+// memory: global loads there would each cost an L2 round trip after the grid
+// barrier's acquire.
+struct TkLayInfo {
+    __half* kc;
+    __half* vc;
+    uint32_t window;
+    uint32_t global;
+};
+constexpr uint32_t TK_MAX_LAYERS = 64;
+
 // Tensor-parallel LM head: every rank's best (value, index) lands in one slot
 // of every rank's exchange buffer; flag = the launch counter + 1.
 struct TkTpSlot {
@@ -147,6 +158,7 @@ struct TkArgs {
     uint32_t chunk_min;   // fewest KV rows per split
     uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
     uint32_t off_xn, off_xq, off_q, off_sc, off_red, off_misc;
+    uint32_t off_lay;     // TkLayInfo per layer, copied to shared memory at launch
     uint32_t head_ring;   // LM-head ring buffers laid from off_qkv on
     uint32_t head_u0, head_u1;          // this rank's LM-head units [u0, u1)
     uint32_t tp_rank, tp_world;         // tensor-parallel group of the LM head (world 1 = none)
@@ -321,6 +333,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     const float* ca = reinterpret_cast<const float*>(sm + a.off_catt);
     const float* cg = reinterpret_cast<const float*>(sm + a.off_cgu);
     float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128]
+    TkLayInfo* lay = reinterpret_cast<TkLayInfo*>(sm + a.off_lay);
 
     const uint32_t pos = *a.pos;
     const uint64_t base = *a.epoch;
@@ -417,6 +430,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         rope[t * 256 + d] = co;
         rope[t * 256 + 128 + d] = s;
     }
+    if ((uint32_t)tid < a.n_layers) {
+        const TkLayer& Li = a.layers[tid];
+        lay[tid] = TkLayInfo{Li.kc, Li.vc, Li.window, Li.global};
+    }
     if (trace && c == 0 && tid == 0) trace[1] = globaltimer_ns();
     tk_sync();
 
@@ -434,7 +451,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     for (uint32_t step = 0; step < nstep; ++step) {
         const uint32_t l = step / TK_STEPS;
         const uint32_t k = l == L ? TK_S_HEAD : step - TK_STEPS * l;
-        const TkLayer& Ly = a.layers[l < L ? l : L - 1];
+        const TkLayInfo& Ly = lay[l < L ? l : L - 1];
 
         const bool split_qkv = k == TK_S_QKV && l > 0;
         if (split_qkv) {
