@@ -474,6 +474,8 @@ struct xp_session {
         if ((e = alloc(&ad, (size_t)H)) != XP_OK) return e;
         if ((e = alloc(&attp, (size_t)G * QD)) != XP_OK) return e;
         if ((e = alloc(&atts, (size_t)G * 8)) != XP_OK) return e;
+        if ((e = alloc(&tk.att_ll, (size_t)(QD / 128) * TK_LL_SPLITS * 128)) != XP_OK) return e;
+        if ((e = alloc(&tk.att_ll_st, (size_t)TK_LL_SPLITS * 8)) != XP_OK) return e;
         if ((e = alloc(&amv2, G)) != XP_OK) return e;
         if ((e = alloc(&ami2, G)) != XP_OK) return e;
         if ((e = alloc(&tk_bar, 4)) != XP_OK) return e;
@@ -741,6 +743,12 @@ xp_status xp_session_reset(xp_session* s) {
     XP_CUDA_TRY(cudaStreamSynchronize(s->st));
     XP_CUDA_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
     if (s->tk_bar) XP_CUDA_TRY(cudaMemsetAsync(s->tk_bar, 0, 16, s->st));
+    // the flagged attention words carry flags derived from the barrier count
+    // just reset: clear them so no stale word can match a new flag
+    if (s->tk.att_ll) {
+        XP_CUDA_TRY(cudaMemsetAsync(s->tk.att_ll, 0, (size_t)(s->q_dim() / 128) * TK_LL_SPLITS * 128 * 8, s->st));
+        XP_CUDA_TRY(cudaMemsetAsync(s->tk.att_ll_st, 0, (size_t)TK_LL_SPLITS * 8 * 8, s->st));
+    }
     XP_CUDA_TRY(cudaStreamSynchronize(s->st));
     s->host_pos = 0;
     s->have_logits = false;

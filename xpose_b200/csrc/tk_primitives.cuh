@@ -13,6 +13,7 @@ constexpr uint32_t TK_ERR_MBAR = 4u;         // bulk-copy wait ran out
 constexpr uint32_t TK_ERR_PLAN = 8u;         // a unit did not fit its slot
 constexpr uint32_t TK_ERR_RANGE = 16u;       // a K-split sum outside the fixed-point range
 constexpr uint32_t TK_ERR_TP_WAIT = 32u;     // a tensor-parallel peer's entry never arrived
+constexpr uint32_t TK_ERR_LL_WAIT = 64u;     // a flagged attention partial never arrived
 
 // A wait of ~1 s on these loops is far beyond any phase (a token is < 1 ms).
 constexpr uint32_t TK_SPIN_LIMIT = 1u << 22;
@@ -61,6 +62,26 @@ XP_DEV void mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
         }
     }
 }
+
+// Flagged 8-byte words: value in the low half, the writer's flag in the high
+// half, stored and loaded as one 64-bit access (single-copy atomic), so a
+// reader that sees the expected flag has the value that came with it.
+XP_DEV void st_flagged(unsigned long long* p, float v, uint32_t flag) {
+    const unsigned long long w = ((unsigned long long)flag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+XP_DEV ulonglong2 ld_flagged2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+XP_DEV unsigned long long ld_flagged(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+XP_DEV bool flag_is(unsigned long long w, uint32_t flag) { return (uint32_t)(w >> 32) == flag; }
+XP_DEV float flag_val(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
 XP_DEV uint64_t globaltimer_ns() {
     uint64_t t;

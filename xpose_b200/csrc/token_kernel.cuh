@@ -65,6 +65,9 @@ constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME
 constexpr int TK_MB_STAGE = 29;  // flash partials staged for the O combine
 static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "mbarrier count");
 constexpr int TK_SPLIT_CAP = 128;
+// Layers attended in at most TK_LL_SPLITS splits hand the flash partials to
+// the O step as flagged words (no grid barrier between ATTN and O)
+constexpr uint32_t TK_LL_SPLITS = 32;
 constexpr uint32_t TK_XR = 2048;  // x1 kept in red[TK_XR .. TK_XR + H) from GU to the next QKV
 constexpr int TK_HEAD_GROUPS = TK_WARPS / 4;  // LM-head tiles in flight per CTA (4 warps each)  // attention splits per layer (the O stage holds 512 B each)
 
@@ -141,6 +144,8 @@ struct TkArgs {
     long long* acc_dn;    // [H] fixed-point down-proj sums
     float* att_part;      // [QD / 128][grid][128] flash partials, one 128-dim slice per O unit
     float* att_stat;      // [grid][4][2] (max, sum) per split and head
+    unsigned long long* att_ll;     // [QD / 128][TK_LL_SPLITS][128] flagged partials
+    unsigned long long* att_ll_st;  // [TK_LL_SPLITS][4][2] flagged (max, sum)
     float* logits;        // [V]
     float* am_val;        // [grid]
     uint32_t* am_idx;     // [grid]
@@ -454,6 +459,14 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         const TkLayInfo& Ly = lay[l < L ? l : L - 1];
 
         const bool split_qkv = k == TK_S_QKV && l > 0;
+        // flag of this layer's flagged words: unique per launch and layer
+        const uint32_t llf = (uint32_t)(base / G) + l + 1;
+        if (k == TK_S_QKV && c == G - 1) {
+            // the o-proj sums were consumed by the previous layer's GU step;
+            // the QKV -> ATTN barrier orders this before this layer's O red.adds
+#pragma unroll 1
+            for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_o[i] = 0;
+        }
         if (split_qkv) {
             // ---------------- QKV of layers >= 1: split norm ----------------
             // The unit's input is x = sc2 (1 + w_attn) (x1 + s1 u) with
@@ -602,21 +615,73 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // slice of every split arrives in one bulk copy while each warp
             // reduces the splits' statistics itself
             const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            const bool ll = w.nsplit <= TK_LL_SPLITS;
             if (c < a.o.units) {
                 const uint32_t kc = c % a.o.ks, h = kc * 128 / 256;
-                const float* stage = reinterpret_cast<const float*>(s_kv);
-                if (tid == 0) {
-                    fence_proxy_async_all();
-                    mbar_expect_tx(&mb[TK_MB_STAGE], w.nsplit * 512);
-                    bulk_g2s(s_kv, a.att_part + (size_t)kc * G * 128, w.nsplit * 512, &mb[TK_MB_STAGE]);
+                float* stage = reinterpret_cast<float*>(s_kv);  // [nsplit][128]
+                float* mst = red + 1024 + TK_SPLIT_CAP;        // [nsplit][2] (max, sum) of head h
+                if (ll) {
+                    // no grid barrier: polling the flagged partials is the wait;
+                    // warp w takes splits w and w + 16, loads in flight together
+                    const uint32_t s0 = warp, s1 = warp + TK_WARPS;
+                    const bool h0 = s0 < w.nsplit, h1 = s1 < w.nsplit;
+                    const unsigned long long* p0 = a.att_ll + (kc * TK_LL_SPLITS + s0) * 128 + 4 * lane;
+                    const unsigned long long* p1 = a.att_ll + (kc * TK_LL_SPLITS + s1) * 128 + 4 * lane;
+                    const unsigned long long* q0 = a.att_ll_st + (s0 * 4 + h) * 2 + (lane & 1);
+                    const unsigned long long* q1 = a.att_ll_st + (s1 * 4 + h) * 2 + (lane & 1);
+                    ulonglong2 a0 = {}, a1 = {}, b0 = {}, b1 = {};
+                    unsigned long long t0 = 0, t1 = 0;
+                    uint32_t it = 0;
+                    for (;;) {
+                        bool ok = true;
+                        if (h0) {
+                            a0 = ld_flagged2(p0);
+                            a1 = ld_flagged2(p0 + 2);
+                            t0 = ld_flagged(q0);
+                        }
+                        if (h1) {
+                            b0 = ld_flagged2(p1);
+                            b1 = ld_flagged2(p1 + 2);
+                            t1 = ld_flagged(q1);
+                        }
+                        if (h0) ok = flag_is(a0.x, llf) && flag_is(a0.y, llf) && flag_is(a1.x, llf) && flag_is(a1.y, llf) && flag_is(t0, llf);
+                        if (h1) ok = ok && flag_is(b0.x, llf) && flag_is(b0.y, llf) && flag_is(b1.x, llf) && flag_is(b1.y, llf) && flag_is(t1, llf);
+                        if (__all_sync(0xffffffffu, ok)) break;
+                        if (++it > TK_SPIN_LIMIT) {
+                            if (lane == 0) atomicOr(a.err, TK_ERR_LL_WAIT);
+                            break;
+                        }
+                    }
+                    if (h0) {
+                        *reinterpret_cast<float4*>(stage + s0 * 128 + 4 * lane) =
+                            make_float4(flag_val(a0.x), flag_val(a0.y), flag_val(a1.x), flag_val(a1.y));
+                        if (lane < 2) mst[s0 * 2 + lane] = flag_val(t0);
+                    }
+                    if (h1) {
+                        *reinterpret_cast<float4*>(stage + s1 * 128 + 4 * lane) =
+                            make_float4(flag_val(b0.x), flag_val(b0.y), flag_val(b1.x), flag_val(b1.y));
+                        if (lane < 2) mst[s1 * 2 + lane] = flag_val(t1);
+                    }
+                } else {
+                    // after the grid barrier: one bulk copy of every split's slice,
+                    // the statistics by plain loads
+                    if (tid == 0) {
+                        fence_proxy_async_all();
+                        mbar_expect_tx(&mb[TK_MB_STAGE], w.nsplit * 512);
+                        bulk_g2s(s_kv, a.att_part + (size_t)kc * G * 128, w.nsplit * 512, &mb[TK_MB_STAGE]);
+                    }
+                    if ((uint32_t)tid < 2 * w.nsplit) mst[tid] = a.att_stat[((size_t)(tid >> 1) * 4 + h) * 2 + (tid & 1)];
+                    wait_slot(TK_MB_STAGE);
                 }
+                tk_sync();
+                TK_MARK(5)
                 float mv[TK_SPLIT_CAP / 32], lv[TK_SPLIT_CAP / 32];
                 float M = -INFINITY;
 #pragma unroll
                 for (int r = 0; r < TK_SPLIT_CAP / 32; ++r) {
                     const uint32_t s_ = lane + 32 * r;
-                    mv[r] = s_ < w.nsplit ? a.att_stat[((size_t)s_ * 4 + h) * 2] : -INFINITY;
-                    lv[r] = s_ < w.nsplit ? a.att_stat[((size_t)s_ * 4 + h) * 2 + 1] : 0.0f;
+                    mv[r] = s_ < w.nsplit ? mst[s_ * 2] : -INFINITY;
+                    lv[r] = s_ < w.nsplit ? mst[s_ * 2 + 1] : 0.0f;
                     M = fmaxf(M, mv[r]);
                 }
                 M = warp_max(M);
@@ -629,10 +694,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     if (warp == 0) wts[lane + 32 * r] = e;
                 }
                 Ls = warp_sum(Ls);
-                TK_MARK(4)
-                wait_slot(TK_MB_STAGE);
                 tk_sync();
-                TK_MARK(5)
+                TK_MARK(4)
                 const uint32_t d = tid & 127, g = tid >> 7;
                 float acc = 0.0f;
 #pragma unroll 4
@@ -650,6 +713,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         } else {
             // ================= ATTN =================
             const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            const bool ll = w.nsplit <= TK_LL_SPLITS;
             wait_slot(TK_MB_CATT);
             if (c < w.nsplit) {
                 const uint32_t n = w.j1 - w.j0;
@@ -776,8 +840,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     }
                     sum = warp_sum(sum);
                     if (lane == 0) {
-                        a.att_stat[((size_t)c * 4 + warp) * 2] = m;
-                        a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
+                        if (ll) {
+                            st_flagged(a.att_ll_st + (c * 4 + warp) * 2, m, llf);
+                            st_flagged(a.att_ll_st + (c * 4 + warp) * 2 + 1, sum, llf);
+                        } else {
+                            a.att_stat[((size_t)c * 4 + warp) * 2] = m;
+                            a.att_stat[((size_t)c * 4 + warp) * 2 + 1] = sum;
+                        }
                     }
                 }
                 tk_sync();
@@ -812,20 +881,20 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     float t = 0.0f;
 #pragma unroll
                     for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 1024 + i];
-                    a.att_part[((size_t)(i >> 7) * G + c) * 128 + (i & 127)] = t;
+                    if (ll)
+                        st_flagged(a.att_ll + ((i >> 7) * TK_LL_SPLITS + c) * 128 + (i & 127), t, llf);
+                    else
+                        a.att_part[((size_t)(i >> 7) * G + c) * 128 + (i & 127)] = t;
                 }
                 TK_MARK(3)
             } else {
                 wait_slot(TK_MB_KV);
             }
-            // the down-proj sums were consumed by this layer's QKV step, the
-            // o-proj sums by the previous layer's GU step
+            // the down-proj sums were consumed by this layer's QKV step (and
+            // the O -> GU barrier orders this before GU's red.adds)
             if (c == G - 1) {
 #pragma unroll 1
-                for (uint32_t i = tid; i < H; i += TK_THREADS) {
-                    a.acc_dn[i] = 0;
-                    a.acc_o[i] = 0;
-                }
+                for (uint32_t i = tid; i < H; i += TK_THREADS) a.acc_dn[i] = 0;
             }
         }
 
@@ -1008,16 +1077,18 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         }
 
         // ---------------- grid barrier; the step's slots go back to the producer ----------------
-        ++nbar;
+        // (none after ATTN when its partials travel as flagged words)
+        const bool gbar = k != TK_S_ATTN || tk_window(pos, Ly.window, a.chunk_min).nsplit > TK_LL_SPLITS;
+        if (gbar) ++nbar;
         tk_sync();
         if (tid == 0) {
-            if (trace) {
+            if (trace && gbar) {
                 const uint64_t t = globaltimer_ns();
                 if (c == 0) trace[2 * nbar] = t;
                 if (nbar < TK_TRACE_MAXBAR && c < TK_TRACE_MAXCTA)
                     trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
             }
-            red_release_add_u64(a.bar, 1ull);
+            if (gbar) red_release_add_u64(a.bar, 1ull);
             if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
             if (k == TK_S_GU) mbar_arrive(&mb[TK_ME_DOWN]);
         }
@@ -1038,7 +1109,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 aq1 = tk_dot(nib[bw * 64 + lane + 32], scl[bw * 64 + lane + 32], xq[bw]);
             }
         }
-        if (tid == 0) {
+        if (tid == 0 && gbar) {
             const uint64_t target = base + (uint64_t)nbar * G;
             uint32_t it = 0;
             // acquire load + the closing bar.sync order every thread's later
