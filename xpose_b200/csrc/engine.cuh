@@ -514,9 +514,10 @@ struct xp_session {
         return XP_OK;
     }
 
-    cudaError_t record_token_kernel(bool want_logits) {
+    cudaError_t record_token_kernel(bool want_logits, uint32_t ntok = 1) {
         TkArgs a = tk;
         a.want_logits = want_logits ? 1 : 0;
+        a.ntok = ntok;
         cudaLaunchConfig_t c = {};
         c.gridDim = dim3(tk_grid);
         c.blockDim = dim3(TK_BLOCK);
@@ -806,7 +807,17 @@ xp_status xp_session_generate(xp_session* s, uint32_t n, uint32_t* tokens, float
     if (st != XP_OK) return st;
     const uint32_t p0 = s->host_pos;
     XP_CUDA_TRY(cudaEventRecord(s->ev_a, s->st));
-    for (uint32_t i = 0; i < n; ++i) XP_CUDA_TRY(cudaGraphLaunch(s->g_dev, s->st));
+    if (s->use_tk && !s->mv_only && s->sp.greedy && s->tk.tp_world == 1 && !s->tk.trace) {
+        // greedy on one GPU: the token kernel decodes up to 512 positions per
+        // launch, each position's input token picked on the device
+        for (uint32_t i = 0; i < n;) {
+            const uint32_t m = std::min<uint32_t>(n - i, 512);
+            XP_CUDA_TRY(s->record_token_kernel(true, m));
+            i += m;
+        }
+    } else {
+        for (uint32_t i = 0; i < n; ++i) XP_CUDA_TRY(cudaGraphLaunch(s->g_dev, s->st));
+    }
     XP_CUDA_TRY(cudaEventRecord(s->ev_b, s->st));
     XP_CUDA_TRY(cudaMemcpyAsync(s->h_out, s->token, 4, cudaMemcpyDeviceToHost, s->st));
     XP_CUDA_TRY(cudaEventRecord(s->ev_done, s->st));

@@ -159,6 +159,7 @@ struct TkArgs {
     uint64_t* trace;      // optional timeline (XP_TRACE)
     int want_logits;
     int greedy;
+    uint32_t ntok;        // tokens this launch decodes back to back (> 1: greedy, one rank)
     uint32_t chunk_max;   // most KV rows one CTA attends to
     uint32_t chunk_min;   // fewest KV rows per split
     uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128]
     TkLayInfo* lay = reinterpret_cast<TkLayInfo*>(sm + a.off_lay);
 
-    const uint32_t pos = *a.pos;
+    const uint32_t pos0 = *a.pos;
     const uint64_t base = *a.epoch;
     const uint32_t L = a.n_layers, H = a.H;
     const uint32_t QKVW = a.QD + 2 * a.KVD;
@@ -374,6 +375,18 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             mbar_wait(&mb[i], (epar >> i) & 1u, a.err);
             epar ^= 1u << i;
         };
+        const uint32_t ring_used = min(a.head_ring, (a.head_u1 - a.head_u0 + G - 1 - c) / G);
+        for (uint32_t tk = 0; tk < a.ntok; ++tk) {
+        const uint32_t pos = pos0 + tk;
+        if (tk > 0) {
+            // the previous token's last uses of every slot: its last layer's
+            // ATTN, O and GU steps, the HEAD constants and the LM-head ring
+            wait_empty(TK_ME_ATT);
+            wait_empty(TK_ME_O);
+            wait_empty(TK_ME_GU);
+            wait_empty(TK_ME_QKV);
+            for (uint32_t r = 0; r < ring_used; ++r) wait_empty(TK_ME_HEAD + r);
+        }
         {
             const TkLayer& L0 = a.layers[0];
             fill(tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
@@ -416,6 +429,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             bulk_g2s(s_qkv + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
                      a.head.img_bytes, &mb[TK_MB_HEAD + r]);
         }
+        }  // token
         return;
     }
 
@@ -425,6 +439,15 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         par ^= 1u << i;
     };
 
+    __shared__ uint32_t s_tok;  // the input token of the next position (multi-token launches)
+    if ((uint32_t)tid < a.n_layers) {
+        const TkLayer& Li = a.layers[tid];
+        lay[tid] = TkLayInfo{Li.kc, Li.vc, Li.window, Li.global};
+    }
+    if (tid == 0) s_tok = *a.token;
+#pragma unroll 1
+    for (uint32_t tk = 0; tk < a.ntok; ++tk) {
+    const uint32_t pos = pos0 + tk;
     // RoPE table for this position: theta^(-2d/256) rounded once from double,
     // angle pos * inv in fp32, sin/cos after an exact reduction (llm_transformer.cl:158-179)
     if (tid < 256) {
@@ -434,10 +457,6 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         rope_sincos((float)pos * inv, &s, &co);
         rope[t * 256 + d] = co;
         rope[t * 256 + 128 + d] = s;
-    }
-    if ((uint32_t)tid < a.n_layers) {
-        const TkLayer& Li = a.layers[tid];
-        lay[tid] = TkLayInfo{Li.kc, Li.vc, Li.window, Li.global};
     }
     if (trace && c == 0 && tid == 0) trace[1] = globaltimer_ns();
     tk_sync();
@@ -460,7 +479,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 
         const bool split_qkv = k == TK_S_QKV && l > 0;
         // flag of this layer's flagged words: unique per launch and layer
-        const uint32_t llf = (uint32_t)(base / G) + l + 1;
+        const uint32_t llf = (uint32_t)(base / G) + nbar + 1;
         if (k == TK_S_QKV && c == G - 1) {
             // the o-proj sums were consumed by the previous layer's GU step;
             // the QKV -> ATTN barrier orders this before this layer's O red.adds
@@ -555,7 +574,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             float4 sums = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // y^2, b^2, b u, u^2
             const bool emb = k == TK_S_QKV && l == 0;
             if (emb) {
-                const float* row = a.embed + (size_t)(*a.token) * H;
+                const float* row = a.embed + (size_t)s_tok * H;
 #pragma unroll
                 for (int j = 0; j < TK_MAXJ; ++j) {
                     const uint32_t i = tid + j * TK_THREADS;
@@ -1089,7 +1108,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     trace[TK_TRACE_CTA + ((size_t)c * TK_TRACE_MAXBAR + nbar) * 2] = t;
             }
             if (gbar) red_release_add_u64(a.bar, 1ull);
-            if (k != TK_S_HEAD) mbar_arrive(&mb[TK_ME_QKV + k]);
+            mbar_arrive(&mb[TK_ME_QKV + (k == TK_S_HEAD ? 0u : k)]);  // HEAD: its constants were in the QKV slot
             if (k == TK_S_GU) mbar_arrive(&mb[TK_ME_DOWN]);
         }
         if (k == TK_S_GU && l + 1 < L) {
@@ -1132,7 +1151,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 
     // ---------------- sample (greedy): lowest-index maximum over the CTAs ----------------
     if (a.want_logits) {
-        if (a.greedy && c == 0 && warp == 0) {
+        // one CTA publishes the token; with more tokens to go every CTA picks
+        // it too (the same lowest-index maximum) for the next embedding row
+        if (a.greedy && warp == 0 && (c == 0 || a.ntok > 1)) {
             float v = -INFINITY;
             uint32_t ix = 0xFFFFFFFFu;
             for (uint32_t p = lane; p < G; p += 32) {
@@ -1181,15 +1202,20 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             }
             if (lane == 0) {
                 if (ix == 0xFFFFFFFFu) ix = 0;
-                *a.token = ix;
-                if (a.sample_out) { a.sample_out[0] = (float)ix; a.sample_out[1] = v; }
-                *a.pos = pos + 1;
-                if (a.hist) a.hist[pos + 1] = ix;
+                s_tok = ix;
+                if (c == 0) {
+                    *a.token = ix;
+                    if (a.sample_out) { a.sample_out[0] = (float)ix; a.sample_out[1] = v; }
+                    *a.pos = pos + 1;
+                    if (a.hist) a.hist[pos + 1] = ix;
+                }
             }
         }
     } else if (c == 0 && tid == 0) {
         *a.pos = pos + 1;
     }
+    tk_sync();  // s_tok before the next position's embedding row
+    }  // token
     if (c == 0 && tid == 0) {
         *a.epoch = base + (uint64_t)nbar * G;
         if (trace) {
