@@ -378,7 +378,7 @@ struct xp_session {
         tk.off_cqkv = off; off += al128(2 * H * 4);
         tk.off_catt = off; off += al128(512 * 4);
         tk.off_cgu = off; off += al128(2 * H * 4);
-        tk.off_rope = off; off += al128(512 * 4);
+        tk.off_rope = off; off += al128(768 * 4);
         tk.off_xn = off; off += al128(std::max<uint32_t>(H, 128) * 4);
         const uint32_t maxnb = std::max(std::max(std::max(tk.qkv.nb, tk.o.nb), std::max(tk.gu.nb, tk.gu.per_cta)), tk.head.nb);
         tk.off_xq = off; off += al128(maxnb * (uint32_t)sizeof(XBlk));

@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     const float* cq = reinterpret_cast<const float*>(sm + a.off_cqkv);
     const float* ca = reinterpret_cast<const float*>(sm + a.off_catt);
     const float* cg = reinterpret_cast<const float*>(sm + a.off_cgu);
-    float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128]
+    float* rope = reinterpret_cast<float*>(sm + a.off_rope);  // [local | global][cos 128 | sin 128], inv freqs
     TkLayInfo* lay = reinterpret_cast<TkLayInfo*>(sm + a.off_lay);
 
     const uint32_t pos0 = *a.pos;
@@ -445,14 +445,17 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         lay[tid] = TkLayInfo{Li.kc, Li.vc, Li.window, Li.global};
     }
     if (tid == 0) s_tok = *a.token;
+    // RoPE inverse frequencies theta^(-2d/256), rounded once from double, once
+    // per launch (rope[512..768): local 128 | global 128)
+    if (tid < 256) rope[512 + tid] = rope_inv_freq(tid & 127, 256, (tid >> 7) ? a.theta_global : a.theta_local);
 #pragma unroll 1
     for (uint32_t tk = 0; tk < a.ntok; ++tk) {
     const uint32_t pos = pos0 + tk;
-    // RoPE table for this position: theta^(-2d/256) rounded once from double,
-    // angle pos * inv in fp32, sin/cos after an exact reduction (llm_transformer.cl:158-179)
+    // RoPE table for this position: angle pos * inv in fp32, sin/cos after an
+    // exact reduction (llm_transformer.cl:158-179)
     if (tid < 256) {
         const uint32_t t = tid >> 7, d = tid & 127;
-        const float inv = rope_inv_freq(d, 256, t ? a.theta_global : a.theta_local);
+        const float inv = rope[512 + tid];
         float s, co;
         rope_sincos((float)pos * inv, &s, &co);
         rope[t * 256 + d] = co;
