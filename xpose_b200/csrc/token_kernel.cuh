@@ -697,23 +697,17 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 }
                 tk_sync();
                 TK_MARK(5)
-                float mv[TK_SPLIT_CAP / 32], lv[TK_SPLIT_CAP / 32];
                 float M = -INFINITY;
-#pragma unroll
-                for (int r = 0; r < TK_SPLIT_CAP / 32; ++r) {
-                    const uint32_t s_ = lane + 32 * r;
-                    mv[r] = s_ < w.nsplit ? mst[s_ * 2] : -INFINITY;
-                    lv[r] = s_ < w.nsplit ? mst[s_ * 2 + 1] : 0.0f;
-                    M = fmaxf(M, mv[r]);
-                }
+#pragma unroll 1
+                for (uint32_t s_ = lane; s_ < w.nsplit; s_ += 32) M = fmaxf(M, mst[s_ * 2]);
                 M = warp_max(M);
                 float Ls = 0.0f;
                 float* wts = red + 1024;  // [TK_SPLIT_CAP]
-#pragma unroll
-                for (int r = 0; r < TK_SPLIT_CAP / 32; ++r) {
-                    const float e = mv[r] == -INFINITY ? 0.0f : expf(mv[r] - M);
-                    Ls += lv[r] * e;
-                    if (warp == 0) wts[lane + 32 * r] = e;
+#pragma unroll 1
+                for (uint32_t s_ = lane; s_ < w.nsplit; s_ += 32) {
+                    const float e = expf(mst[s_ * 2] - M);
+                    Ls += mst[s_ * 2 + 1] * e;
+                    if (warp == 0) wts[s_] = e;
                 }
                 Ls = warp_sum(Ls);
                 tk_sync();
