@@ -10,15 +10,16 @@ decoding toward position 4096 (default K = 3965 timed after W = 3 warm-up
 tokens, so the timed tokens cover positions 131..4095). Every token streams
 562 MB of weights (> the 126 MB L2), so no L2 flush is needed between steps.
 
-value : tokens/s of the device-resident loop (one CUDA graph per token, the
-        sampled token fed back on the device), timed with CUDA events.
+value : tokens/s of the device-resident loop (DecodeSession.generate(): the
+        greedy token kernel decodes up to 512 positions per launch, each
+        position's input token picked on the device), timed with CUDA events.
 e2e   : the same tokens through the public API DecodeSession.decode_step()
         (C ABI xp_session_decode_step): per token a 4-byte host->device copy
         of the input id and a 4-byte device->host read of the sampled id.
 roofline : the persistent token kernel (the only kernel of a decode step):
-        algorithmic bytes per launch = int4 nibbles + bf16 scales of every
-        matrix + the fp16 KV rows attended + embedding row and logits, over its
-        average device duration.
+        algorithmic bytes per position = int4 nibbles + bf16 scales of every
+        matrix + the fp16 KV rows attended + embedding row and logits, over the
+        average device time per position.
 cpu_baseline : the CPU restatement of the same decode (oracle/, "port"),
         timed on this host's cores over a bounded sample.
 batched : BASELINE config 4's batched decode: 64 independent sequences per
@@ -627,14 +628,17 @@ def main():
                        "parallelism": f"dp{world} (independent sequences)" if world > 1 else "single GPU",
                        "l2": "weights 562 MB/token > 126 MB L2; no flush needed"},
             "e2e": e2e,
-            "gpu_launches": kpt * K,
+            # generate() runs the greedy token kernel over up to 512 positions
+            # per cooperative launch (xp_session_generate)
+            "gpu_launches": (K + 511) // 512 if kpt == 1 else kpt * K,
             "kernels_per_token": kpt,
+            "tokens_per_launch": 512 if kpt == 1 else 1,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "token_kernel (persistent, one launch per token: all int4 matvecs, attention, "
-                                   "norms, LM head, argmax)",
-                         "algorithmic_bytes_per_launch": tok_bytes,
-                         "avg_launch_us": round(ms_max / K * 1000.0, 2), "peak_kind": peak_kind},
+                         "kernel": "token_kernel (persistent; each position one pass: all int4 matvecs, attention, "
+                                   "norms, LM head, argmax; up to 512 positions per launch)",
+                         "algorithmic_bytes_per_token": tok_bytes,
+                         "avg_token_us": round(ms_max / K * 1000.0, 2), "peak_kind": peak_kind},
             "clocks": clock_info,
             "cpu_baseline": cpu,
             "matvec": mv,
