@@ -298,7 +298,8 @@ xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n);
 xp_status xp_session_decode_step(xp_session* s, uint32_t* token);
 /* Device-resident generation: n steps back to back with no host round trip
  * (the sampled token feeds the next step on the device); tokens (host) may be
- * NULL. Returns the device time in *ms if non-null. */
+ * NULL. Returns the device time in *ms if non-null. With greedy sampling on
+ * one GPU the token kernel decodes up to 512 positions per launch. */
 xp_status xp_session_generate(xp_session* s, uint32_t n, uint32_t* tokens, float* ms);
 xp_status xp_session_reset(xp_session* s);            /* DecodeSession::reset */
 xp_status xp_session_position(xp_session* s, uint32_t* pos);

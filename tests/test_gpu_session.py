@@ -107,3 +107,30 @@ def test_session_errors():
         sess.decode_step()
     assert e.value.name == "XP_ERR_KV_FULL"
     assert sess.error_word() == 0
+
+
+def test_session_many_splits_and_reset(monkeypatch):
+    """Attention windows of more than 32 splits hand their partials to the O
+    step through a grid barrier, shorter ones as flagged words; a long
+    prompt with 8-row splits runs both kinds in one model (global layers
+    past position 256, local layers within their 16-row window), and a
+    reset must clear the flags so the same positions decode again."""
+    monkeypatch.setenv("XP_TK_CHUNK_MIN", "8")
+    cfg = DecodeConfig(n_layers=3, hidden=256, ffn=512, vocab=4096, max_seq=320, sliding_window=16, global_every=3)
+    seed = 13
+    om = O.OracleModel(cfg, seed)
+    sess = DecodeSession.random(cfg, Sampling(greedy=True), seed=seed)
+    prompt = O.gen_tokens(seed, 77, 290, cfg.vocab)
+    want = None
+    for p, t in enumerate(prompt):
+        want = om.forward(int(t), p, want_logits=(p == len(prompt) - 1))
+    for rep in range(2):
+        sess.prefill(prompt)
+        _check_logits(sess.last_logits(), want)
+        toks, _ = sess.generate(8)
+        if rep == 0:
+            first = list(toks)
+        else:
+            assert list(toks) == first
+        assert sess.error_word() == 0
+        sess.reset()

@@ -63,6 +63,7 @@ constexpr int TK_MAX_RING = 8;
 // slot; the producer waits on them before refilling it
 constexpr int TK_ME_QKV = 16, TK_ME_ATT = 17, TK_ME_O = 18, TK_ME_GU = 19, TK_ME_DOWN = 20, TK_ME_HEAD = 21;
 constexpr int TK_MB_STAGE = 29;  // flash partials staged for the O combine
+constexpr int TK_ME_HEADGO = 30;  // HEAD's input sums are loaded: the LM-head stream may start
 static_assert(TK_ME_HEAD + TK_MAX_RING <= TK_MB_STAGE && TK_MB_STAGE < TK_NMB, "mbarrier count");
 constexpr int TK_SPLIT_CAP = 128;
 // Layers attended in at most TK_LL_SPLITS splits hand the flash partials to
@@ -420,6 +421,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         wait_empty(TK_ME_QKV);
         fill(tk_issue_vec(a.c_head, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
         wait_empty(TK_ME_DOWN);
+        // start the 170 MB stream once HEAD's prologue has its sums: issued
+        // earlier, it queues those L2 loads behind the HBM traffic
+        wait_empty(TK_ME_HEADGO);
         uint32_t i = 0;
         for (uint32_t t = a.head_u0 + c; t < a.head_u1; t += G, ++i) {
             const uint32_t r = i % a.head_ring;
@@ -605,6 +609,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 const float q4 = reduce4(sums.x, sums.y, sums.z, sums.w);
                 if ((lane & 7) == 0) red32[warp * 4 + (lane >> 3)] = q4;
             }
+            if (k == TK_S_HEAD && tid == 0) mbar_arrive(&mb[TK_ME_HEADGO]);
             TK_MARK(4)
             tk_sync();
             TK_MARK(5)
