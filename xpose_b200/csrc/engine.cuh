@@ -371,10 +371,16 @@ struct xp_session {
         tk.off_down = off; off += al128(tk.down.per_cta * tk.down.img_bytes);
         // KV rows of ATTN, then the flash-partial stage of O (512 B per split)
         tk.off_kv = off; off += al128(std::max<uint32_t>(2 * tk.chunk_max * KVD * 2, TK_SPLIT_CAP * 512));
-        const uint32_t ring_bytes = off - tk.off_qkv;
         // a multiple of the LM-head warp groups: each group owns its ring slots
-        tk.head_ring = std::min<uint32_t>(TK_MAX_RING, ring_bytes / tk.head.img_bytes) / TK_HEAD_GROUPS * TK_HEAD_GROUPS;
+        auto ring_slots = [&](uint32_t from) {
+            return std::min<uint32_t>(TK_MAX_RING, (off - from) / tk.head.img_bytes) / TK_HEAD_GROUPS * TK_HEAD_GROUPS;
+        };
+        tk.head_ring = ring_slots(tk.off_qkv);
         if (tk.head_ring == 0) return false;
+        // keep the QKV slot out of the ring when that costs no ring slot: the
+        // next position's layer-0 QKV weights then load while HEAD streams
+        tk.qkv_free = ring_slots(tk.off_o) == tk.head_ring ? 1 : 0;
+        tk.off_ring = tk.qkv_free ? tk.off_o : tk.off_qkv;
         tk.off_cqkv = off; off += al128(2 * H * 4);
         tk.off_catt = off; off += al128(512 * 4);
         tk.off_cgu = off; off += al128(2 * H * 4);

@@ -166,7 +166,9 @@ struct TkArgs {
     uint32_t off_qkv, off_o, off_gu, off_down, off_kv, off_cqkv, off_catt, off_cgu, off_rope;
     uint32_t off_xn, off_xq, off_q, off_sc, off_red, off_misc;
     uint32_t off_lay;     // TkLayInfo per layer, copied to shared memory at launch
-    uint32_t head_ring;   // LM-head ring buffers laid from off_qkv on
+    uint32_t head_ring;   // LM-head ring buffers laid from off_ring on
+    uint32_t off_ring;    // off_qkv, or off_o when the ring fits without the QKV slot
+    int qkv_free;         // the ring leaves the QKV slot alone (it is refilled during HEAD)
     uint32_t head_u0, head_u1;          // this rank's LM-head units [u0, u1)
     uint32_t tp_rank, tp_world;         // tensor-parallel group of the LM head (world 1 = none)
     TkTpSlot* tp_slots[TK_TP_MAX];      // every rank's exchange buffer (peer mappings), TK_TP_MAX slots each
@@ -379,23 +381,29 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         const uint32_t ring_used = min(a.head_ring, (a.head_u1 - a.head_u0 + G - 1 - c) / G);
         for (uint32_t tk = 0; tk < a.ntok; ++tk) {
         const uint32_t pos = pos0 + tk;
+        const TkLayer& L0 = a.layers[0];
         if (tk > 0) {
-            // the previous token's last uses of every slot: its last layer's
-            // ATTN, O and GU steps, the HEAD constants and the LM-head ring
-            wait_empty(TK_ME_ATT);
-            wait_empty(TK_ME_O);
-            wait_empty(TK_ME_GU);
+            // the previous token's last uses of every slot: the HEAD
+            // constants, its last layer's ATTN, GU and O steps and the ring
+            // (the QKV weights of layer 0 went in while the ring streamed)
             wait_empty(TK_ME_QKV);
+            fill(tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
+            wait_empty(TK_ME_ATT);
+            fill(tk_issue_vec(L0.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]), TK_MB_CATT);
+            wait_empty(TK_ME_GU);
+            fill(tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
+            wait_empty(TK_ME_O);
             for (uint32_t r = 0; r < ring_used; ++r) wait_empty(TK_ME_HEAD + r);
-        }
-        {
-            const TkLayer& L0 = a.layers[0];
+            if (!a.qkv_free) fill(tk_issue(L0.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
+        } else {
             fill(tk_issue_vec(L0.c_qkv, 2 * H, (unsigned char*)cq, &mb[TK_MB_CQKV]), TK_MB_CQKV);
             fill(tk_issue(L0.qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
             fill(tk_issue_vec(L0.c_attn, 512, (unsigned char*)ca, &mb[TK_MB_CATT]), TK_MB_CATT);
+            fill(tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
+        }
+        {
             fill(tk_issue_kv(a, L0, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
             fill(tk_issue(L0.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
-            fill(tk_issue_vec(L0.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
             fill(tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
             fill(tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN]), TK_MB_DOWN);
         }
@@ -430,9 +438,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             if (i >= a.head_ring) wait_empty(TK_ME_HEAD + r);
             fence_proxy_async();
             mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
-            bulk_g2s(s_qkv + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
+            bulk_g2s(sm + a.off_ring + (size_t)r * a.head.img_bytes, a.head_img + (size_t)t * a.head.img_bytes,
                      a.head.img_bytes, &mb[TK_MB_HEAD + r]);
         }
+        // the next position's layer-0 QKV weights, into the slot the ring
+        // leaves alone (its last reader, QKV of the last layer, is done)
+        if (a.qkv_free && tk + 1 < a.ntok)
+            fill(tk_issue(a.layers[0].qkv, a.qkv, s_qkv, &mb[TK_MB_QKV]), TK_MB_QKV);
         }  // token
         return;
     }
@@ -1030,7 +1042,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     for (uint32_t i = grp, it = 0; i < ntile; i += TK_HEAD_GROUPS, ++it) {
                         const uint32_t r = i % a.head_ring;
                         wait_slot(TK_MB_HEAD + r);
-                        const unsigned char* img = s_qkv + (size_t)r * P.img_bytes;
+                        const unsigned char* img = sm + a.off_ring + (size_t)r * P.img_bytes;
                         const uint4* nib = reinterpret_cast<const uint4*>(img);
                         const uint16_t* scl = reinterpret_cast<const uint16_t*>(img + (size_t)P.nb * 64 * 16);
                         float a0 = 0.0f, a1 = 0.0f;
