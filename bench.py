@@ -562,7 +562,7 @@ def main():
         try:
             with open(tpath) as f:
                 tr = json.load(f)
-            traffic = tr.get("dram_bytes_per_launch")
+            traffic = tr.get("dram_bytes_per_token")
         except Exception:
             traffic = None
 
