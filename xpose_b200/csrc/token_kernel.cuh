@@ -221,7 +221,7 @@ XP_DEV float tk_dot(const uint4 w, uint16_t s, const XBlk& X) {
 // image keeps the right pair), dotted against limbs whose block carries the
 // 16 values in rows 0-15 and zeros in rows 16-31.
 XP_DEV float tk_dot_half(const uint2 w, uint16_t s, const XBlk& X) {
-    int a0 = 0, a1 = 0, a2 = 0;
+    int a0 = 0, a1 = 0, a2 = X.bias;
     const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -234,7 +234,7 @@ XP_DEV float tk_dot_half(const uint2 w, uint16_t s, const XBlk& X) {
         a2 = __dp4a(lo, X.w[2][i], a2);
         a2 = __dp4a(hi, X.w[2][4 + i], a2);
     }
-    const int d = (a0 * 128 + a1) * 128 + a2 + X.bias;
+    const int d = (a0 * 128 + a1) * 128 + a2;
     return (float)d * (X.f * __uint_as_float((uint32_t)s << 16));
 }
 

@@ -80,7 +80,7 @@ XP_DEV int xq_dot(const uint4 w, const int4* X /* 6 int4 = w[3][8] */, int bias)
     const int x0[8] = {l0a.x, l0a.y, l0a.z, l0a.w, l0b.x, l0b.y, l0b.z, l0b.w};
     const int x1[8] = {l1a.x, l1a.y, l1a.z, l1a.w, l1b.x, l1b.y, l1b.z, l1b.w};
     const int x2[8] = {l2a.x, l2a.y, l2a.z, l2a.w, l2b.x, l2b.y, l2b.z, l2b.w};
-    int a0 = 0, a1 = 0, a2 = 0;
+    int a0 = 0, a1 = 0, a2 = bias;  // the bias rides in the last limb's sum (integer: exact)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int lo = (int)(ws[i] & 0x0F0F0F0Fu);
@@ -92,7 +92,7 @@ XP_DEV int xq_dot(const uint4 w, const int4* X /* 6 int4 = w[3][8] */, int bias)
         a2 = __dp4a(lo, x2[i], a2);
         a2 = __dp4a(hi, x2[4 + i], a2);
     }
-    return (a0 * 128 + a1) * 128 + a2 + bias;
+    return (a0 * 128 + a1) * 128 + a2;
 }
 
 }  // namespace xp
