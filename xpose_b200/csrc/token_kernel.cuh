@@ -1,12 +1,16 @@
-// Persistent token kernel: one cooperative launch decodes one position.
+// Persistent token kernel: one cooperative launch decodes `ntok` positions
+// back to back (one per graph replay for decode_step(), up to 512 for a
+// greedy generate() on one GPU).
 //
 // Grid = one CTA per SM, all co-resident; each CTA is 16 compute warps plus
 // one producer warp. The reference's per-token op order
-// (examples/llm/decode.cpp:1634-1780) runs as four steps per layer separated
-// by grid barriers, then one LM-head step:
+// (examples/llm/decode.cpp:1634-1780) runs as four steps per layer, then one
+// LM-head step:
 //
 //   QKV  : residual + post-FFN norm of layer l-1 (or the embedding), attention
-//          norm, then a K-split int4 matvec unit -> q|k|v sums
+//          norm, then a K-split int4 matvec unit -> q|k|v sums. For l >= 1
+//          the norm is split: the part of the input known a step early is
+//          dotted during the previous barrier wait.
 //   ATTN : QK-norm + RoPE, fp16 KV append (CTA 0), one contiguous chunk of the
 //          attended window per CTA -> flash partials
 //   O    : combine the flash partials of this CTA's 128-dim K range, o-proj
@@ -17,24 +21,27 @@
 //          (the CTA that makes an hb row is the one that consumes it, so the
 //          down-proj needs no grid barrier of its own)
 //   HEAD : residual + post-FFN + final norm, LM-head tiles, per-CTA argmax;
-//          then CTA 0 picks the lowest-index maximum (greedy).
+//          then the lowest-index maximum (greedy).
+//
+// Grid barriers follow QKV, O and GU; one follows ATTN only when the window
+// has more than TK_LL_SPLITS splits, otherwise the partials reach O as
+// flagged 8-byte words and polling them is the wait.
 //
 // Design rules of this kernel, each measured on B200:
-//   * Code size. Every step's code runs once per layer, so a layer loop larger
-//     than the SM's instruction cache refetches all of it every layer (a cold
-//     ~150-instruction loop cost ~1 us). The layer loop is therefore ONE
-//     phase machine: the norm prologue, the limb prep and the 64-column tile
-//     loop each exist once and serve QKV, O and HEAD.
-//   * Grid barriers (~1 us each from the last arrival to the release) are
-//     the dearest thing in a layer, so there are four per layer, the fewest
-//     the data dependences allow.
+//   * Code size. Every step's code runs once per layer and is fetched cold
+//     every layer, so the layer loop is ONE phase machine (the norm prologue,
+//     the limb prep and the 64-column tile loop exist once), and the timeline
+//     instrumentation lives only in the TRACE instance: even predicated-off
+//     instructions cost their fetch.
+//   * Grid barriers (~0.75 us from the last arrival to the release) are the
+//     dearest thing in a layer: three per layer at most.
 //   * K-split sums go through int64 fixed-point accumulators (2^-32 units,
 //     red.add): integer addition is order-independent, so the result is
 //     deterministic, and a consumer loads one vector instead of every partial.
 //   * Everything a step reads that does not depend on this token is in shared
 //     memory before the step starts: weights live in unit-major images (one
 //     bulk copy per CTA and step), per-step norm vectors are contiguous, the
-//     KV rows a CTA attends to are staged ahead, RoPE cos/sin are tabulated
+//     KV rows a CTA attends to are staged ahead, per-layer facts are copied
 //     once per launch. The producer warp issues all of those copies, so no
 //     compute thread ever blocks on issuing one.
 #pragma once
