@@ -736,17 +736,14 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 Ls = warp_sum(Ls);
                 tk_sync();
                 TK_MARK(4)
-                const uint32_t d = tid & 127, g = tid >> 7;
-                float acc = 0.0f;
+                // warp w < 4 combines dims 32w..32w+31 over every split and
+                // makes that block's limbs straight from registers
+                if (warp < 4) {
+                    const uint32_t d = warp * 32 + lane;
+                    float acc = 0.0f;
 #pragma unroll 4
-                for (uint32_t s_ = g; s_ < w.nsplit; s_ += TK_GROUPS) acc += stage[s_ * 128 + d] * wts[s_];
-                red[g * 128 + d] = acc;
-                tk_sync();
-                if (tid < 128) {
-                    float t = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < TK_GROUPS; ++q) t += red[q * 128 + tid];
-                    xn[tid] = t / Ls;
+                    for (uint32_t s_ = 0; s_ < w.nsplit; ++s_) acc += stage[s_ * 128 + d] * wts[s_];
+                    xq_prep_block(acc / Ls, &xq[warp]);
                 }
                 TK_MARK(6)
             }
@@ -942,13 +939,15 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // ---------------- limbs of xn: one shared prep ----------------
             const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
             const bool has = c < P.units;
-            tk_sync();  // xn complete
-            if (has) {
-                const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
+            tk_sync();  // xn complete (O: its limbs, made by the combine)
+            if (k != TK_S_O) {
+                if (has) {
+                    const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
 #pragma unroll 1
-                for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
+                    for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
+                }
+                tk_sync();
             }
-            tk_sync();
             TK_MARK(0)
 
             if (k == TK_S_GU) {
