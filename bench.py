@@ -514,7 +514,17 @@ def main():
         return float(t.item())
 
     # ---- device-resident decode (value) ----
+    # prefill of the 128-token prompt (chunked: 64 positions per tensor-core
+    # pass), host wall clock around the synchronous call, after one untimed
+    # prefill that creates the chunked-prefill engine
+    sess.reset()
+    sess.prefill(prompt)  # warm: creates the chunked-prefill engine once
+    sess.reset()
+    t_pf = time.perf_counter()
     sess.prefill(prompt)
+    pf_ms = (time.perf_counter() - t_pf) * 1000.0
+    prefill = {"tokens": len(prompt), "ms": round(pf_ms, 3), "tok/s": round(len(prompt) / pf_ms * 1000.0, 1),
+               "path": "chunked: 64 prompt positions per pass on the tensor-core batched engine (host wall clock)"}
     sess.generate(W, want_tokens=False)
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev)).split(",")[dev]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else dev
@@ -642,6 +652,7 @@ def main():
             "clocks": clock_info,
             "cpu_baseline": cpu,
             "matvec": mv,
+            "prefill": prefill,
             "batched": bat,
             "tp": tp,
             "long_context": lc,

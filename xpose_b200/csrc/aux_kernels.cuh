@@ -144,7 +144,7 @@ __global__ void greedy_final_kernel(const float* pval, const uint32_t* pidx, uin
     uint32_t bi = 0xFFFFFFFFu;
     for (uint32_t p = threadIdx.x; p < nparts; p += blockDim.x) {
         const float v = pval[p];
-        const uint32_t i = pidx[p];
+        const uint32_t i = pidx ? pidx[p] : p;  // no index array: pval is the logits themselves
         if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
     }
 #pragma unroll

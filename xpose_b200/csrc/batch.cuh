@@ -150,6 +150,13 @@ struct BkAttnArgs {
     uint32_t max_seq, window;
     float theta, eps, scale;
     float inv_freq[128];   // RoPE theta^(-2d/256), from rope_table_host
+    // Batched decode: mode 0, sequence b's cache at kc + b * seq_stride.
+    // Chunked prefill (rows = consecutive positions of one sequence, one
+    // shared cache, seq_stride 0): mode 1 appends every row's k and v (the
+    // q|k|v sums stay), then mode 2 attends with the rows' own k and v read
+    // back from the cache and clears the sums.
+    size_t seq_stride;
+    int mode;
 };
 __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_constant__ BkAttnArgs a) {
     extern __shared__ __align__(16) float bsm_f[];
@@ -173,9 +180,10 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         cs[128 + tid] = s;
     }
     __syncthreads();
-    __half* kcb = a.kc + (size_t)b * a.max_seq * 256;
-    __half* vcb = a.vc + (size_t)b * a.max_seq * 256;
-    if (warp < 6) {
+    __half* kcb = a.kc + (size_t)b * a.seq_stride;
+    __half* vcb = a.vc + (size_t)b * a.seq_stride;
+    const bool want_q = a.mode != 1, want_kv = a.mode != 2;
+    if (warp < 6 && (warp < 4 ? want_q : want_kv)) {
         // warps 0-3: q heads, 4: k, 5: v; lane holds dims 4 lane..+3 and 128 + 4 lane..+3
         long long* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
         float v[8];
@@ -184,7 +192,7 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         for (int i = 0; i < 8; ++i) vr[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)] = 0;
+            if (a.mode != 1) src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)] = 0;
             v[i] = bk_unfix(vr[i]);
         }
         if (warp < 5) {
@@ -222,11 +230,18 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
             }
         }
     }
+    if (a.mode == 2 && (warp == 4 || warp == 5)) {
+        // the rows' k and v are in the cache already: clear their sums
+        long long* src = (warp == 4 ? a.k : a.v) + (size_t)b * 256;
+        for (int i = lane; i < 256; i += 32) src[i] = 0;
+    }
+    if (a.mode == 1) return;
+    const uint32_t pnew = a.mode == 0 ? pos : 0xFFFFFFFFu;  // mode 2 reads row pos from the cache
     __syncthreads();
     // scores: one key per warp, lane holds 8 dims of every head
     for (uint32_t jj = warp; jj < span; jj += BK_THREADS / 32) {
         const uint32_t j = kv_start + jj;
-        const uint4 raw = j == pos ? *reinterpret_cast<const uint4*>(knew + 8 * lane)
+        const uint4 raw = j == pnew ? *reinterpret_cast<const uint4*>(knew + 8 * lane)
                                    : *reinterpret_cast<const uint4*>(kcb + (size_t)j * 256 + 8 * lane);
         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
         float kf[8];
@@ -268,7 +283,7 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         float acc[4][2] = {};
         for (uint32_t jj = qr; jj < span; jj += 4) {
             const uint32_t j = kv_start + jj;
-            const __half2 hv = j == pos ? reinterpret_cast<const __half2*>(vnew)[dp]
+            const __half2 hv = j == pnew ? reinterpret_cast<const __half2*>(vnew)[dp]
                                         : reinterpret_cast<const __half2*>(vcb + (size_t)j * 256)[dp];
             const float2 vf = __half22float2(hv);
 #pragma unroll

@@ -78,6 +78,8 @@ struct xp_session {
     void* samp_scratch = nullptr;
     uint32_t* h_in = nullptr;
     uint32_t* h_out = nullptr;
+    xp_bdec* pre = nullptr;     // chunked prefill (64 prompt positions per pass), made on first use
+    bool pre_failed = false;
     cudaGraphExec_t g_dev = nullptr, g_io = nullptr, g_prefill = nullptr;
     uint32_t* tp_buf = nullptr;              // this rank's LM-head exchange slots (IPC-exported)
     std::vector<void*> tp_peers;             // opened peer mappings
@@ -740,6 +742,7 @@ xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sam
 }
 
 xp_status xp_session_destroy(xp_session* s) {
+    if (s && s->pre) xp_bdec_destroy(s->pre);
     delete s;
     return XP_OK;
 }
@@ -762,11 +765,22 @@ xp_status xp_session_reset(xp_session* s) {
     return XP_OK;
 }
 
+static xp_status prefill_chunked(xp_session* s, const uint32_t* tokens, uint32_t n);
+
 xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n) {
     if (!s) return fail(XP_ERR_INVALID, "null session");
     if (n == 0) return XP_OK;
     if (!tokens) return fail(XP_ERR_INVALID, "decode: null token array");
     cudaSetDevice(s->device);
+    if (n >= (uint32_t)env_int("XP_PREFILL_CHUNK_MIN", 32) && s->use_tk && !s->mv_only && s->tk.tp_world == 1 &&
+        !s->tk.trace && !s->pre_failed && s->host_pos + n <= s->cfg.max_seq) {
+        bool ok = true;
+        for (uint32_t i = 0; i < n && ok; ++i) ok = tokens[i] < s->cfg.vocab;
+        if (ok) {
+            xp_status st = prefill_chunked(s, tokens, n);
+            if (st != XP_ERR_UNSUPPORTED) return st;
+        }
+    }
     for (uint32_t i = 0; i < n; ++i) {
         if (s->host_pos >= s->cfg.max_seq)
             return fail(XP_ERR_KV_FULL, "decode: prompt exceeds max_seq (%u)", s->cfg.max_seq);
@@ -996,6 +1010,9 @@ struct xp_bdec {
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     uint32_t h_pos = 0;  // every sequence is at the same position
+    // chunked prefill of the session's own sequence: row b is position
+    // pos[b] of one sequence, the caches are the session's
+    bool chunk = false;
     // Programmatic dependent launch (XP_BDEC_PDL bit 0: tensor-core launches,
     // which then request their first weights under the previous kernel's tail;
     // bit 1: the per-sequence kernels, measured slightly slower, so off)
@@ -1082,8 +1099,16 @@ struct xp_bdec {
             aa.eps = c.rms_eps;
             aa.scale = ascale;
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
+            aa.seq_stride = chunk ? 0 : (size_t)max_seq * 256;
+            aa.mode = chunk ? 1 : 0;
             if ((e = launch_ex(bk_attn_kernel, dim3(B), dim3(BK_THREADS), (size_t)4 * ms * 4, st, 1, pdl_k, aa)) != cudaSuccess)
                 return e;
+            if (chunk) {
+                // every row's k and v are in the cache before any row attends
+                aa.mode = 2;
+                if ((e = launch_ex(bk_attn_kernel, dim3(B), dim3(BK_THREADS), (size_t)4 * ms * 4, st, 1, pdl_k, aa)) != cudaSuccess)
+                    return e;
+            }
             if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
             if ((e = resid_norm(o, W.norm[1], W.norm[2], 1)) != cudaSuccess) return e;
             if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, op_xn)) != cudaSuccess) return e;
@@ -1130,8 +1155,14 @@ struct xp_bdec {
 
 extern "C" {
 
+static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const xp_sampling* sp, uint64_t seq0,
+                             bool chunk, xp_bdec** out);
 xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const xp_sampling* sp, uint64_t seq0,
                           xp_bdec** out) {
+    return bdec_create(s, nseq, max_seq, sp, seq0, false, out);
+}
+static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const xp_sampling* sp, uint64_t seq0,
+                             bool chunk, xp_bdec** out) {
     if (!s || !sp || !out) return fail(XP_ERR_INVALID, "xp_bdec_create: null argument");
     *out = nullptr;
     if (nseq == 0 || nseq > BMM_MAXN) return fail(XP_ERR_INVALID, "xp_bdec_create: 1..%d sequences (got %u)", BMM_MAXN, nseq);
@@ -1149,6 +1180,7 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     b->max_seq = max_seq;
     b->sp = *sp;
     b->seq0 = seq0;
+    b->chunk = chunk;
     cudaSetDevice(b->device);
     auto bail = [&](xp_status st) { delete b; return st; };
     if (cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess ||
@@ -1171,6 +1203,11 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     b->kc.resize(c.n_layers);
     b->vc.resize(c.n_layers);
     for (uint32_t l = 0; l < c.n_layers; ++l) {
+        if (chunk) {
+            b->kc[l] = s->L[l].kc;
+            b->vc[l] = s->L[l].vc;
+            continue;
+        }
         if ((e = b->alloc(&b->kc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
         if ((e = b->alloc(&b->vc[l], (size_t)nseq * max_seq * 256)) != XP_OK) return bail(e);
     }
@@ -1194,7 +1231,14 @@ xp_status xp_bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, const x
     if (cudaHostAlloc(&b->h_tok, (size_t)nseq * 4, cudaHostAllocDefault) != cudaSuccess)
         return bail(fail(XP_ERR_OOM, "xp_bdec_create: pinned buffer"));
     XP_CUDA_TRY(cudaFuncSetAttribute(bk_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    // warm every kernel once outside capture (attributes, lazy loading)
+    // warm every kernel once outside capture (attributes, lazy loading); a
+    // chunk object must not touch the session's caches here
+    if (chunk) {
+        // every row at the last position: the only cache row written is the
+        // last one, which a real pass at that position writes before reading
+        std::vector<uint32_t> hp(nseq, max_seq - 1);
+        XP_CUDA_TRY(cudaMemcpy(b->pos, hp.data(), (size_t)nseq * 4, cudaMemcpyHostToDevice));
+    }
     if (b->forward() != cudaSuccess) return bail(fail(XP_ERR_CUDA, "xp_bdec_create: warm-up forward failed"));
     XP_CUDA_TRY(cudaMemsetAsync(b->pos, 0, (size_t)nseq * 4, b->st));
     XP_CUDA_TRY(cudaStreamSynchronize(b->st));
@@ -1318,3 +1362,62 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
 }
 
 }  // extern "C"
+
+// Chunked prefill (f1 of the build plan: the prompt as GEMMs). Up to 64 prompt
+// positions per pass run as the rows of the batched engine over the
+// session's own KV caches: tensor-core matvecs for all rows at once, then
+// per layer every row's k and v appended before any row attends (causal over
+// the cache, the window rule per layer). Only the last position's logits are
+// kept; the next token comes from them as after a per-token prefill.
+static xp_status prefill_chunked(xp_session* s, const uint32_t* tokens, uint32_t n) {
+    xp_status st = s->wait_prev();
+    if (st != XP_OK) return st;
+    if (!s->pre) {
+        const xp_sampling sp = s->sp;
+        st = bdec_create(s, BMM_MAXN, s->cfg.max_seq, &sp, 0, true, &s->pre);
+        if (st != XP_OK) {
+            s->pre = nullptr;
+            s->pre_failed = true;
+            return XP_ERR_UNSUPPORTED;  // the caller falls back to one pass per token
+        }
+    }
+    xp_bdec* b = s->pre;
+    const uint32_t B = b->B;
+    std::vector<uint32_t> tk(B), ps(B);
+    uint32_t last = 0;
+    for (uint32_t p = 0; p < n; p += B) {
+        const uint32_t m = std::min(B, n - p);
+        for (uint32_t r = 0; r < B; ++r) {
+            const uint32_t q = p + std::min(r, m - 1);  // rows past the chunk repeat its last position
+            tk[r] = tokens[q];
+            ps[r] = s->host_pos + q;
+        }
+        XP_CUDA_TRY(cudaMemcpyAsync(b->tokens, tk.data(), (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
+        XP_CUDA_TRY(cudaMemcpyAsync(b->pos, ps.data(), (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
+        XP_CUDA_TRY(cudaGraphLaunch(b->g_fwd, b->st));
+        XP_CUDA_TRY(cudaStreamSynchronize(b->st));  // tk / ps are reused
+        last = m - 1;
+    }
+    // the last position's logits become the session's; then what the last
+    // token-kernel pass would have done: the position advances and the next
+    // token is picked (greedy: lowest-index maximum) or sampled
+    const uint32_t V = s->cfg.vocab;
+    const uint32_t endpos = s->host_pos + n;
+    XP_CUDA_TRY(cudaMemcpyAsync(s->logits, b->logits + (size_t)last * V, (size_t)V * 4, cudaMemcpyDeviceToDevice, s->st));
+    // both pickers advance the position from the last prompt position
+    const uint32_t p_last = endpos - 1;
+    XP_CUDA_TRY(cudaMemcpyAsync(s->pos, &p_last, 4, cudaMemcpyHostToDevice, s->st));
+    if (s->sp.greedy) {
+        XP_CUDA_TRY(launch_ex(greedy_final_kernel, dim3(1), dim3(1024), 0, s->st, 1, false, (const float*)s->logits,
+                              (const uint32_t*)nullptr, V, s->token, s->sample_out, s->pos, s->hist));
+    } else {
+        XP_CUDA_TRY(launch_sample_topk(s->token, s->sample_out, s->pos, nullptr, nullptr, s->logits, V, s->sp.top_k,
+                                       s->sp.temperature, s->sp.top_p, s->sp.seed, s->sp.seq_id, s->samp_scratch, s->st,
+                                       false, true, s->hist));
+    }
+    XP_CUDA_TRY(cudaMemcpyAsync(s->h_out, s->token, 4, cudaMemcpyDeviceToHost, s->st));
+    XP_CUDA_TRY(cudaStreamSynchronize(s->st));
+    s->host_pos = endpos;
+    s->have_logits = true;
+    return XP_OK;
+}
