@@ -290,8 +290,12 @@ xp_status xp_session_destroy(xp_session* s);
  * matrices q,k,v,o,gate,up,down; 7..12 the norms; layer = n_layers: 0 embed,
  * 7 final norm. */
 uint64_t xp_session_tensor_stream(uint32_t layer, uint32_t which);
-/* DecodeSession::prefill (decode.cpp:1790-1817): one pass per token, logits
- * only for the last one. Tokens are host memory. */
+/* DecodeSession::prefill (decode.cpp:1790-1817): logits only for the last
+ * token. Tokens are host memory. Prompts of 32 or more tokens (environment
+ * XP_PREFILL_CHUNK_MIN) run 64 positions per pass on the batched tensor-core
+ * engine over the session's KV caches; shorter ones one pass per token. The
+ * first chunked prefill of a session allocates that engine (~80 MB for the
+ * Gemma-3-1B shape); if that fails the call falls back to one pass per token. */
 xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n);
 /* DecodeSession::decode_step (decode.cpp:1819-1866): sample from the
  * previous pass's logits, run the network on it, return the sampled id. */
