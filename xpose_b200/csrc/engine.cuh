@@ -1007,7 +1007,7 @@ struct xp_bdec {
     std::vector<std::pair<uint64_t, unsigned char*>> bscratch;
     uint64_t* cand = nullptr;
     uint32_t ns = 0, nc = 0;
-    cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
+    cudaGraphExec_t g_fwd = nullptr, g_step = nullptr, g_nohead = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     uint32_t h_pos = 0;  // every sequence is at the same position
     // chunked prefill of the session's own sequence: row b is position
@@ -1021,7 +1021,7 @@ struct xp_bdec {
     ~xp_bdec() {
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
-        for (cudaGraphExec_t ge : {g_fwd, g_step})
+        for (cudaGraphExec_t ge : {g_fwd, g_step, g_nohead})
             if (ge) cudaGraphExecDestroy(ge);
         for (cudaEvent_t e : {ev_a, ev_b})
             if (e) cudaEventDestroy(e);
@@ -1075,7 +1075,7 @@ struct xp_bdec {
         return launch_ex(bk_resid_norm_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, x, y, w_post, w_pre, op_xn,
                          s->cfg.hidden, s->cfg.rms_eps, mode);
     }
-    cudaError_t forward() {
+    cudaError_t forward(bool head = true) {
         const xp_model_config& c = s->cfg;
         const uint32_t H = c.hidden, F = c.ffn, L = c.n_layers;
         const float escale = c.embed_scale > 0 ? c.embed_scale : std::sqrt((float)H);
@@ -1116,6 +1116,11 @@ struct xp_bdec {
                 return e;
             if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
         }
+        if (!head) {
+            // a prompt chunk that is not the last: its down-proj sums are
+            // left for nobody, so clear them instead of running the LM head
+            return cudaMemsetAsync(dn, 0, (size_t)B * H * sizeof(long long), st);
+        }
         if ((e = resid_norm(dn, s->L[L - 1].norm[3], s->final_norm, 1)) != cudaSuccess) return e;
         if ((e = mm(logits, op_xn, s->lm)) != cudaSuccess) return e;
         if ((e = launch_ex(bk_pos_inc_kernel, dim3(1), dim3(64), 0, st, 1, pdl_k, pos, B)) != cudaSuccess) return e;
@@ -1136,11 +1141,11 @@ struct xp_bdec {
         if (e != cudaSuccess) return e;
         return cudaGetLastError();
     }
-    xp_status capture(cudaGraphExec_t* out, bool with_sample) {
+    xp_status capture(cudaGraphExec_t* out, bool with_sample, bool head = true) {
         cudaGraph_t gr = nullptr;
         XP_CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         cudaError_t e = with_sample ? sample() : cudaSuccess;
-        if (e == cudaSuccess) e = forward();
+        if (e == cudaSuccess) e = forward(head);
         cudaError_t e2 = cudaStreamEndCapture(st, &gr);
         if (e != cudaSuccess || e2 != cudaSuccess) {
             if (gr) cudaGraphDestroy(gr);
@@ -1244,6 +1249,7 @@ static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, con
     XP_CUDA_TRY(cudaStreamSynchronize(b->st));
     if ((e = b->capture(&b->g_fwd, false)) != XP_OK) return bail(e);
     if ((e = b->capture(&b->g_step, true)) != XP_OK) return bail(e);
+    if (chunk && (e = b->capture(&b->g_nohead, false, false)) != XP_OK) return bail(e);
     *out = b;
     return XP_OK;
 }
@@ -1363,7 +1369,7 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
 
 }  // extern "C"
 
-// Chunked prefill (f1 of the build plan: the prompt as GEMMs). Up to 64 prompt
+// Chunked prefill: the prompt as tensor-core GEMMs. Up to 64 prompt
 // positions per pass run as the rows of the batched engine over the
 // session's own KV caches: tensor-core matvecs for all rows at once, then
 // per layer every row's k and v appended before any row attends (causal over
@@ -1394,7 +1400,7 @@ static xp_status prefill_chunked(xp_session* s, const uint32_t* tokens, uint32_t
         }
         XP_CUDA_TRY(cudaMemcpyAsync(b->tokens, tk.data(), (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
         XP_CUDA_TRY(cudaMemcpyAsync(b->pos, ps.data(), (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
-        XP_CUDA_TRY(cudaGraphLaunch(b->g_fwd, b->st));
+        XP_CUDA_TRY(cudaGraphLaunch(p + m < n ? b->g_nohead : b->g_fwd, b->st));
         XP_CUDA_TRY(cudaStreamSynchronize(b->st));  // tk / ps are reused
         last = m - 1;
     }
