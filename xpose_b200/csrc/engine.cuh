@@ -364,7 +364,7 @@ struct xp_session {
         tk.head = mk_phase(cfg.vocab / 64, nbH, 64, 1, 1, G);
         if (tk.gu.per_cta > 3 || tk.gu.per_cta * 16 > std::max<uint32_t>(H, 128)) return false;
         // attention: at most TK_SPLIT_CAP splits of at least chunk_min rows
-        tk.chunk_min = (uint32_t)std::max(8, env_int("XP_TK_CHUNK_MIN", 16));
+        tk.chunk_min = (uint32_t)std::max(8, env_int("XP_TK_CHUNK_MIN", 32));
         tk.chunk_max = (std::max<uint32_t>(tk.chunk_min, (cfg.max_seq + TK_SPLIT_CAP - 1) / TK_SPLIT_CAP) + 7) & ~7u;
         uint32_t off = 0;
         tk.off_qkv = off; off += al128(tk.qkv.img_bytes);
