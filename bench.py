@@ -78,7 +78,8 @@ def parse():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-long", action="store_true")
-    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm", "batched", "long"], default=None,
+    ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm", "batched", "long", "prefill"],
+                    default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
                          "(4 prompt tokens, 2 decode tokens), 'small' = 4 layers and a 32K vocab, 'multi' = the "
                          "five-kernel graph path on the bench model, 'matvec' = three runs of the config-1 "
@@ -272,6 +273,14 @@ def ncu_case(which):
         print("ncu case long:", r["us_per_step"], "us per step (graph replays of 26 attention calls + sampling)")
         return 0
     from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling
+    if which == "prefill":
+        s = DecodeSession.random(DecodeConfig(max_seq=4096), Sampling(), seed=0)
+        prompt = np.random.default_rng(0).integers(0, s.cfg.vocab, size=PROMPT).astype(np.uint32)
+        s.prefill(prompt)  # creates the chunked-prefill engine
+        s.reset()
+        print("ncu case prefill: second prefill of", PROMPT, "tokens follows")
+        s.prefill(prompt)
+        return 0
     if which == "batched":
         from xpose_b200.decode import BatchDecode
         cfg = DecodeConfig(max_seq=512)

@@ -142,10 +142,26 @@ __global__ void greedy_final_kernel(const float* pval, const uint32_t* pidx, uin
     pdl_wait();
     float bv = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
-    for (uint32_t p = threadIdx.x; p < nparts; p += blockDim.x) {
-        const float v = pval[p];
-        const uint32_t i = pidx ? pidx[p] : p;  // no index array: pval is the logits themselves
-        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    if (!pidx && nparts % 4 == 0) {
+        // pval is the logits themselves: float4 loads, eight in flight
+        const float4* p4 = reinterpret_cast<const float4*>(pval);
+        const uint32_t n4 = nparts / 4;
+#pragma unroll 8
+        for (uint32_t q = threadIdx.x; q < n4; q += blockDim.x) {
+            const float4 v = p4[q];
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const uint32_t i = 4 * q + r;
+                if (vv[r] > bv || (vv[r] == bv && i < bi)) { bv = vv[r]; bi = i; }
+            }
+        }
+    } else {
+        for (uint32_t p = threadIdx.x; p < nparts; p += blockDim.x) {
+            const float v = pval[p];
+            const uint32_t i = pidx ? pidx[p] : p;  // no index array: pval is the logits themselves
+            if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
