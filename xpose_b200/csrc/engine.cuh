@@ -1117,9 +1117,10 @@ struct xp_bdec {
             if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
         }
         if (!head) {
-            // a prompt chunk that is not the last: its down-proj sums are
-            // left for nobody, so clear them instead of running the LM head
-            return cudaMemsetAsync(dn, 0, (size_t)B * H * sizeof(long long), st);
+            // a prompt position (or chunk) before the last: its down-proj sums
+            // are left for nobody, so clear them instead of running the LM head
+            if ((e = cudaMemsetAsync(dn, 0, (size_t)B * H * sizeof(long long), st)) != cudaSuccess) return e;
+            return launch_ex(bk_pos_inc_kernel, dim3(1), dim3(64), 0, st, 1, false, pos, B);
         }
         if ((e = resid_norm(dn, s->L[L - 1].norm[3], s->final_norm, 1)) != cudaSuccess) return e;
         if ((e = mm(logits, op_xn, s->lm)) != cudaSuccess) return e;
@@ -1249,7 +1250,7 @@ static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, con
     XP_CUDA_TRY(cudaStreamSynchronize(b->st));
     if ((e = b->capture(&b->g_fwd, false)) != XP_OK) return bail(e);
     if ((e = b->capture(&b->g_step, true)) != XP_OK) return bail(e);
-    if (chunk && (e = b->capture(&b->g_nohead, false, false)) != XP_OK) return bail(e);
+    if ((e = b->capture(&b->g_nohead, false, false)) != XP_OK) return bail(e);
     *out = b;
     return XP_OK;
 }
@@ -1263,7 +1264,8 @@ xp_status xp_bdec_prefill(xp_bdec* b, const uint32_t* tokens, uint32_t n) {
     for (uint32_t t = 0; t < n; ++t) {
         std::memcpy(b->h_tok, tokens + (size_t)t * b->B, (size_t)b->B * 4);
         XP_CUDA_TRY(cudaMemcpyAsync(b->tokens, b->h_tok, (size_t)b->B * 4, cudaMemcpyHostToDevice, b->st));
-        XP_CUDA_TRY(cudaGraphLaunch(b->g_fwd, b->st));
+        // only the last prompt position's logits are kept
+        XP_CUDA_TRY(cudaGraphLaunch(t + 1 < n ? b->g_nohead : b->g_fwd, b->st));
         XP_CUDA_TRY(cudaStreamSynchronize(b->st));  // h_tok is reused
         ++b->h_pos;
     }
