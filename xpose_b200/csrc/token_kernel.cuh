@@ -115,16 +115,6 @@ struct TkLayer {
     uint32_t global;      // RoPE table: 1 = global theta, 0 = local
 };
 
-// What the compute warps need of a layer in every step, kept in shared
-// memory: global loads there would each cost an L2 round trip after the grid
-// barrier's acquire.
-struct TkLayInfo {
-    __half* kc;
-    __half* vc;
-    uint32_t window;
-    uint32_t global;
-};
-constexpr uint32_t TK_MAX_LAYERS = 64;
 
 // Tensor-parallel LM head: every rank's best (value, index) lands in one slot
 // of every rank's exchange buffer; flag = the launch counter + 1.
@@ -311,6 +301,18 @@ XP_DEV TkWin tk_window(uint32_t pos, uint32_t window, uint32_t chunk_min) {
     return w;
 }
 
+// What the compute warps need of a layer in every step, kept in shared
+// memory: global loads there would each cost an L2 round trip after the grid
+// barrier's acquire.
+struct TkLayInfo {
+    __half* kc;
+    __half* vc;
+    uint32_t window;
+    uint32_t global;
+    TkWin w;  // this position's window and this CTA's split of it (set per position)
+};
+constexpr uint32_t TK_MAX_LAYERS = 64;
+
 // Stage the KV rows [j0, min(j1, pos)) of one layer (producer lane).
 __device__ __noinline__ bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint32_t pos, unsigned char* kvs, uint64_t* bar) {
     const TkWin w = tk_window(pos, L.window, a.chunk_min);
@@ -474,6 +476,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 #pragma unroll 1
     for (uint32_t tk = 0; tk < a.ntok; ++tk) {
     const uint32_t pos = pos0 + tk;
+    if ((uint32_t)tid < a.n_layers) lay[tid].w = tk_window(pos, lay[tid].window, a.chunk_min);
     // RoPE table for this position: angle pos * inv in fp32, sin/cos after an
     // exact reduction (llm_transformer.cl:158-179)
     if (tid < 256) {
@@ -660,7 +663,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // flash combine of this CTA's 128-dim slice over the splits: the
             // slice of every split arrives in one bulk copy while each warp
             // reduces the splits' statistics itself
-            const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            const TkWin w = Ly.w;
             const bool ll = w.nsplit <= TK_LL_SPLITS;
             if (c < a.o.units) {
                 const uint32_t kc = c % a.o.ks, h = kc * 128 / 256;
@@ -749,7 +752,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             }
         } else {
             // ================= ATTN =================
-            const TkWin w = tk_window(pos, Ly.window, a.chunk_min);
+            const TkWin w = Ly.w;
             const bool ll = w.nsplit <= TK_LL_SPLITS;
             wait_slot(TK_MB_CATT);
             if (c < w.nsplit) {
@@ -1117,7 +1120,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 
         // ---------------- grid barrier; the step's slots go back to the producer ----------------
         // (none after ATTN when its partials travel as flagged words)
-        const bool gbar = k != TK_S_ATTN || tk_window(pos, Ly.window, a.chunk_min).nsplit > TK_LL_SPLITS;
+        const bool gbar = k != TK_S_ATTN || Ly.w.nsplit > TK_LL_SPLITS;
         if (gbar) ++nbar;
         tk_sync();
         if (tid == 0) {
