@@ -465,6 +465,17 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     };
 
     __shared__ uint32_t s_tok;  // the input token of the next position (multi-token launches)
+    // this CTA's unit coordinates, fixed for the launch (no divisions in the steps)
+    __shared__ uint32_t s_qkv_b0, s_qkv_col0, s_o_kc, s_o_col0, s_gu_nu;
+    if (tid == 0) {
+        s_qkv_b0 = (c % a.qkv.ks) * a.qkv.nb;
+        s_qkv_col0 = (c / a.qkv.ks) * 64;
+        s_o_kc = c % a.o.ks;
+        s_o_col0 = (c / a.o.ks) * 64;
+        uint32_t nu = 0;
+        for (uint32_t u = c; u < a.gu.units; u += G) ++nu;
+        s_gu_nu = nu;
+    }
     if ((uint32_t)tid < a.n_layers) {
         const TkLayer& Li = a.layers[tid];
         lay[tid] = TkLayInfo{Li.kc, Li.vc, Li.window, Li.global};
@@ -525,7 +536,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // reduction of the norm sums instead of after it.
             const TkPhase& P = a.qkv;
             const bool mine = c < P.units && warp >= 1 && (uint32_t)(warp - 1) < P.nb;
-            const uint32_t bw = warp - 1, b0 = (c % P.ks) * P.nb;
+            const uint32_t bw = warp - 1, b0 = s_qkv_b0;
             float uv[TK_MAXJ], xb[TK_MAXJ];
             float sy = 0.0f, sbu = 0.0f, suu = 0.0f;
 #pragma unroll
@@ -583,7 +594,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 float sum = 0.0f;
 #pragma unroll 1
                 for (uint32_t w = 0; w < P.nb; ++w) sum += wr[w * 64 + tid];
-                const uint32_t col = (c / P.ks) * 64 + tid;
+                const uint32_t col = s_qkv_col0 + tid;
                 if (col < QKVW) red_add_s64(&a.acc_qkv[col], tk_fix(sum * sc2, a.err));
             }
             TK_MARK(2)
@@ -666,7 +677,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             const TkWin w = Ly.w;
             const bool ll = w.nsplit <= TK_LL_SPLITS;
             if (c < a.o.units) {
-                const uint32_t kc = c % a.o.ks, h = kc * 128 / 256;
+                const uint32_t kc = s_o_kc, h = kc * 128 / 256;
                 float* stage = reinterpret_cast<float*>(s_kv);  // [nsplit][128]
                 float* mst = red + 1024 + TK_SPLIT_CAP;        // [nsplit][2] (max, sum) of head h
                 if (ll) {
@@ -945,7 +956,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             tk_sync();  // xn complete (O: its limbs, made by the combine)
             if (k != TK_S_O) {
                 if (has) {
-                    const uint32_t b0 = k == TK_S_QKV ? (c % P.ks) * P.nb : 0;
+                    const uint32_t b0 = k == TK_S_QKV ? s_qkv_b0 : 0;
 #pragma unroll 1
                     for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
                 }
@@ -959,8 +970,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 TK_MARK(1)
                 if (has) {
                     const uint32_t nb = P.nb;
-                    uint32_t nu = 0;
-                    for (uint32_t u = c; u < P.units; u += G) ++nu;
+                    const uint32_t nu = s_gu_nu;
                     // warp w takes blocks w, w + 16, ... and holds that block's limbs
                     // in registers for every unit; lane = (matrix lane / 16,
                     // column lane % 16), so the limb loads are warp-wide broadcasts
@@ -1006,8 +1016,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 wait_slot(TK_MB_DOWN);
                 TK_MARK(3)
                 if (has) {
-                    uint32_t nu = 0;
-                    for (uint32_t u = c; u < P.units; u += G) ++nu;
+                    const uint32_t nu = s_gu_nu;
                     const uint32_t ib = a.down.img_bytes;
                     // unit-outer: each unit's limbs are loaded once per thread
                     float s[TK_MAXJ];
@@ -1109,7 +1118,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     if (has) {
                         tk_tile64(slot, P.nb, xq, red);
                         if (tid < 64) {
-                            const uint32_t col = (c / P.ks) * 64 + tid;
+                            const uint32_t col = (k == TK_S_QKV ? s_qkv_col0 : s_o_col0) + tid;
                             if (col < accw) red_add_s64(&acc[col], tk_fix(red[tid], a.err));
                         }
                     }
@@ -1142,7 +1151,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             const TkPhase& P = a.qkv;
             const uint32_t bw = warp - 1;
             if (c < P.units && warp >= 1 && bw < P.nb) {
-                const uint32_t i = ((c % P.ks) * P.nb + bw) * 32 + lane;
+                const uint32_t i = (s_qkv_b0 + bw) * 32 + lane;
                 xq_prep_block(xr[i] * (1.0f + cq[H + i]), &xq[bw]);
                 __syncwarp();
                 const uint4* nib = reinterpret_cast<const uint4*>(s_qkv);
