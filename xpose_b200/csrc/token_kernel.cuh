@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         wait_empty(TK_ME_HEADGO);
         uint32_t i = 0;
         for (uint32_t t = a.head_u0 + c; t < a.head_u1; t += G, ++i) {
-            const uint32_t r = i % a.head_ring;
+            const uint32_t r = i & (a.head_ring - 1);  // head_ring: 4 or 8
             if (i >= a.head_ring) wait_empty(TK_ME_HEAD + r);
             fence_proxy_async();
             mbar_expect_tx(&mb[TK_MB_HEAD + r], a.head.img_bytes);
@@ -464,6 +464,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         par ^= 1u << i;
     };
 
+    const uint32_t base_g = (uint32_t)(base / G);  // barriers before this launch
+    const float inv_h = 1.0f / (float)H;
     __shared__ uint32_t s_tok;  // the input token of the next position (multi-token launches)
     // this CTA's unit coordinates, fixed for the launch (no divisions in the steps)
     __shared__ uint32_t s_qkv_b0, s_qkv_col0, s_o_kc, s_o_col0, s_gu_nu;
@@ -519,7 +521,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 
         const bool split_qkv = k == TK_S_QKV && l > 0;
         // flag of this layer's flagged words: unique per launch and layer
-        const uint32_t llf = (uint32_t)(base / G) + nbar + 1;
+        const uint32_t llf = base_g + nbar + 1;
         if (k == TK_S_QKV && c == G - 1) {
             // the o-proj sums were consumed by the previous layer's GU step;
             // the QKV -> ATTN barrier orders this before this layer's O red.adds
@@ -575,8 +577,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             t4 += __shfl_xor_sync(0xffffffffu, t4, 16);
             const float tx = __shfl_sync(0xffffffffu, t4, 0), ty = __shfl_sync(0xffffffffu, t4, 1);
             const float tz = __shfl_sync(0xffffffffu, t4, 2);
-            const float s1 = rsqrtf(tx / (float)H + a.eps);
-            const float sc2 = rsqrtf((ss_x1 + 2.0f * s1 * ty + s1 * s1 * tz) / (float)H + a.eps);
+            const float s1 = rsqrtf(tx * inv_h + a.eps);
+            const float sc2 = rsqrtf((ss_x1 + 2.0f * s1 * ty + s1 * s1 * tz) * inv_h + a.eps);
             if (c == 0) {
 #pragma unroll
                 for (int j = 0; j < TK_MAXJ; ++j) {
@@ -654,9 +656,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             t4 += __shfl_xor_sync(0xffffffffu, t4, 16);
             const float tx = __shfl_sync(0xffffffffu, t4, 0), ty = __shfl_sync(0xffffffffu, t4, 1);
             const float tz = __shfl_sync(0xffffffffu, t4, 2), tw = __shfl_sync(0xffffffffu, t4, 3);
-            const float s1 = emb ? 0.0f : rsqrtf(tx / (float)H + a.eps);
+            const float s1 = emb ? 0.0f : rsqrtf(tx * inv_h + a.eps);
             const float ssr = ty + 2.0f * s1 * tz + s1 * s1 * tw;  // sum r^2
-            const float sc2 = rsqrtf(ssr / (float)H + a.eps);
+            const float sc2 = rsqrtf(ssr * inv_h + a.eps);
             if (k == TK_S_GU) ss_x1 = ssr;
             // normalised input -> xn; the shared limb prep below reads it
 #pragma unroll
@@ -1058,7 +1060,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     TK_MARK(1)
 #pragma unroll 1
                     for (uint32_t i = grp, it = 0; i < ntile; i += TK_HEAD_GROUPS, ++it) {
-                        const uint32_t r = i % a.head_ring;
+                        const uint32_t r = i & (a.head_ring - 1);  // head_ring: 4 or 8
                         wait_slot(TK_MB_HEAD + r);
                         const unsigned char* img = sm + a.off_ring + (size_t)r * P.img_bytes;
                         const uint4* nib = reinterpret_cast<const uint4*>(img);
