@@ -195,8 +195,14 @@ xp_status xp_topk4_partial(void* stream, float* cval, uint32_t* cidx, const floa
  * (replaces rmsnorm_heads_gemma x2, rope x2, kv_append x2, attention_scores,
  * softmax_rows, attention_apply: examples/llm/decode.cpp:1676-1731). n_heads
  * must be 4, kv_heads 1, head_dim 256 (Gemma-3-1B). `pos` is a DEVICE
- * pointer. `scratch` needs xp_attention_scratch_bytes(nsplit) bytes and must
- * be zero-initialised once (the kernel leaves it reusable). */
+ * pointer. `max_seq` is the rows each cache holds (the splits are sized for
+ * the window when `window` is non-zero and smaller, else for max_seq).
+ * `scratch` needs xp_attention_scratch_bytes(nsplit) bytes and must
+ * be zero-initialised once (the kernel leaves it reusable). The uint32 at
+ * byte 4 of `scratch` is the call's error word (sticky: bits are only ORed
+ * in): 1 = the split count was too small for max_seq (a prefix was attended),
+ * 4 = a bulk-copy wait ran out, 128 = *pos_dev >= max_seq (nothing was
+ * written: the KV append would have landed past the caches). */
 size_t xp_attention_scratch_bytes(uint32_t nsplit);
 xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, const float* k_raw,
                               const float* v_raw, const float* q_norm, const float* k_norm, uint16_t* kcache_f16,
@@ -211,7 +217,9 @@ xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, cons
  * current device; the first call on a device looks up the array's address, so
  * make that first call before any stream capture. All calls share the one
  * array: calls that overlap on the GPU race. Allocates nothing. No counterpart
- * in the reference. */
+ * in the reference. Every argument check runs before the array is touched.
+ * A device reset (cudaDeviceReset) invalidates the cached address: do not use
+ * this entry point on a device after resetting it. */
 #define XP_ATTN_STATIC_MAX_NSPLIT 64u
 #define XP_ATTN_STATIC_SCRATCH_BYTES (512u + 64u * (4u * 256u * 4u + 8u * 4u))
 xp_status xp_attention_decode_static(void* stream, float* out, const float* q_raw, const float* k_raw,
@@ -219,6 +227,11 @@ xp_status xp_attention_decode_static(void* stream, float* out, const float* q_ra
                                      uint16_t* kcache_f16, uint16_t* vcache_f16, const uint32_t* pos_dev,
                                      uint32_t window, float theta, float eps, float scale, uint32_t nsplit,
                                      uint32_t max_seq);
+/* The error word of the array xp_attention_decode_static uses (same bits as
+ * xp_attention_decode's), copied to host `*word` after the work already on
+ * `stream`; cleared afterwards when `clear` is non-zero. Synchronises
+ * `stream`. Allocates nothing. No counterpart in the reference. */
+xp_status xp_attention_static_error_word(void* stream, uint32_t* word, int clear);
 /* Exact top-k (k <= 64) + temperature + top-p + multinomial over n logits
  * (replaces topk4_partial + host draw(), decode.cpp:1873-1917). `u` index for
  * the seeded uniform is *pos_dev. Writes the chosen id to *token_dev and the

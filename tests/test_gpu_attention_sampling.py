@@ -54,8 +54,9 @@ def test_attention_decode(pos, window, nsplit):
     out = torch.full((NH * HD,), -1e30, device="cuda")
     check(lib().xp_attention_decode(None, ptr(out), ptr(dev(q_raw)), ptr(dev(k_raw)), ptr(dev(v_raw)), ptr(dev(qn)),
                                     ptr(dev(kn)), ptr(dkc), ptr(dvc), ptr(posd), window, theta, 1e-6, 1.0 / 16,
-                                    nsplit, max_seq if window == 0 else min(window, max_seq), ptr(scratch)))
+                                    nsplit, max_seq, ptr(scratch)))
     sync()
+    assert int(host(scratch, np.uint32)[1]) == 0  # the call's error word
     # oracle: QK-norm + RoPE, fp16 append, serial attention over the window
     q = _oracle_qk_post(q_raw, qn, NH, pos, theta)
     k = _oracle_qk_post(k_raw, kn, 1, pos, theta)

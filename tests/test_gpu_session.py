@@ -80,16 +80,18 @@ def test_session_sampling_matches_oracle():
     for p, t in enumerate(prompt):
         want = om.forward(int(t), p, want_logits=(p == len(prompt) - 1))
     pos = len(prompt)
-    agree = 0
     for step in range(16):
         tok = sess.decode_step()
         u = O.oracle().xo_uniform(sp.seed, sp.seq_id, pos - 1)
         exp_tok = O.oracle().xo_sample(want, cfg.vocab, sp.temperature, sp.top_k, sp.top_p, u)
-        agree += tok == exp_tok
+        if tok != exp_tok:
+            # logits agree to ~1e-6, so a different draw is only acceptable
+            # where the uniform sits on a CDF boundary of the oracle's draw
+            lo = O.oracle().xo_sample(want, cfg.vocab, sp.temperature, sp.top_k, sp.top_p, max(0.0, u - 1e-5))
+            hi = O.oracle().xo_sample(want, cfg.vocab, sp.temperature, sp.top_k, sp.top_p, min(1.0, u + 1e-5))
+            assert lo != hi and tok in (lo, hi), (pos, tok, exp_tok)
         want = om.forward(tok, pos)
         pos += 1
-    # logits agree to ~1e-6, so the draws agree except at a boundary within that
-    assert agree >= 15
 
 
 def test_session_errors():
@@ -134,3 +136,32 @@ def test_session_many_splits_and_reset(monkeypatch):
             assert list(toks) == first
         assert sess.error_word() == 0
         sess.reset()
+
+
+def test_five_kernel_graph_matches_oracle(monkeypatch):
+    """The graph of separate kernels per layer (matvec, attention, matvec,
+    matvec per layer; the engine's path for shapes the token kernel does not
+    plan, forced here with XP_ENGINE_MULTI=1) against the oracle."""
+    monkeypatch.setenv("XP_ENGINE_MULTI", "1")
+    cfg = SMALL
+    seed = 17
+    om = O.OracleModel(cfg, seed)
+    sess = DecodeSession.random(cfg, Sampling(greedy=True), seed=seed)
+    monkeypatch.delenv("XP_ENGINE_MULTI")
+    assert sess.stats()["kernels_per_token"] > 1
+    prompt = O.gen_tokens(seed, 501, 10, cfg.vocab)
+    sess.prefill(prompt)
+    want = None
+    for p, t in enumerate(prompt):
+        want = om.forward(int(t), p, want_logits=(p == len(prompt) - 1))
+    _check_logits(sess.last_logits(), want)
+    pos = len(prompt)
+    for _ in range(12):
+        top2 = np.sort(want)[-2:]
+        tok = sess.decode_step()
+        if top2[1] - top2[0] > 1e-4:
+            assert tok == int(np.argmax(want))
+        want = om.forward(tok, pos)
+        pos += 1
+        _check_logits(sess.last_logits(), want)
+    assert sess.error_word() == 0

@@ -121,6 +121,7 @@ _SIGS = {
                                                                         C.c_uint32, C.c_uint32, C.c_void_p]),
     "xp_attention_decode_static": (C.c_int, [C.c_void_p] + [C.c_void_p] * 9 + [C.c_uint32, C.c_float, C.c_float,
                                                                                C.c_float, C.c_uint32, C.c_uint32]),
+    "xp_attention_static_error_word": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_int]),
     "xp_sample_scratch_bytes": (C.c_size_t, [C.c_uint32]),
     "xp_sample_topk": (C.c_int, [C.c_void_p] + [C.c_void_p] * 4 + [C.c_uint32, C.c_uint32, C.c_float, C.c_float,
                                                                    C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),

@@ -42,6 +42,7 @@ struct AttnArgs {
     __half* kcache;        // [max_seq][256]
     __half* vcache;
     const uint32_t* pos;   // device-resident position
+    uint32_t cache_rows;   // rows the K and V caches hold (a position at or past it is refused)
     uint32_t window;       // 0 = global layer
     float theta, eps, scale;
     uint32_t chunk_max;    // smem capacity in positions per CTA
@@ -239,6 +240,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     pdl_wait();
 
     const uint32_t pos = *a.pos;
+    if (pos >= a.cache_rows) {  // the append would land past the caches: flag, write nothing
+        if (tid == 0 && blockIdx.x == 0 && a.err) atomicOr(a.err, TK_ERR_POS);
+        return;
+    }
     const uint32_t seq = pos + 1;
     const uint32_t kv_start = (a.window == 0 || seq <= a.window) ? 0 : seq - a.window;
     const uint32_t span = seq - kv_start;

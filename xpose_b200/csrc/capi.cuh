@@ -866,7 +866,9 @@ xp_status xp_mv_plan_create(const xp_mv_job* jobs, uint32_t n, xp_mv_plan** plan
     p->smem_x = (size_t)nxq * sizeof(XBlk) <= MVS_SMEM_X_MAX;
     int per_sm = 0;
     if (p->smem_x) {
-        cudaFuncSetAttribute(mv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MVS_SMEM_X_MAX);
+        static std::atomic<bool> attr_set[kMaxDevices];
+        if ((e = smem_attr_once(attr_set, mv_stream_kernel<true>, (int)MVS_SMEM_X_MAX)) != cudaSuccess)
+            return cleanup("shared-memory attribute", e);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mv_stream_kernel<true>, MVS_THREADS,
                                                       (size_t)nxq * sizeof(XBlk));
     } else {
@@ -992,28 +994,51 @@ xp_status xp_topk4_partial(void* stream, float* cval, uint32_t* cidx, const floa
 }
 
 size_t xp_attention_scratch_bytes(uint32_t nsplit) { return attn_scratch_bytes(nsplit); }
+}  // extern "C"
+namespace xp {
+// Argument checks of xp_attention_decode, shared with the entry point that
+// keeps its scratch inside the library (which must refuse a call before it
+// touches that shared array).
+inline xp_status attn_validate(const float* out, const float* q_raw, const float* k_raw, const float* v_raw,
+                               const float* q_norm, const float* k_norm, const uint16_t* kc, const uint16_t* vc,
+                               const uint32_t* pos_dev, uint32_t window, uint32_t nsplit, uint32_t max_seq,
+                               const void* scratch) {
+    const void* ptrs[] = {out, q_raw, k_raw, v_raw, q_norm, k_norm, kc, vc, pos_dev, scratch};
+    const char* names[] = {"out", "q_raw", "k_raw", "v_raw", "q_norm", "k_norm", "kcache_f16", "vcache_f16",
+                           "pos_dev", "scratch"};
+    for (int i = 0; i < 10; ++i)
+        if (!ptrs[i]) return fail(XP_ERR_INVALID, "attention_decode: argument '%s' is null", names[i]);
+    if (nsplit == 0 || nsplit > 1024) return fail(XP_ERR_INVALID, "attention_decode: nsplit must be 1..1024");
+    if (max_seq == 0) return fail(XP_ERR_INVALID, "attention_decode: max_seq must be at least 1");
+    if (attn_smem(attn_chunk_max(nsplit, attn_span_max(window, max_seq))) > 200 * 1024)
+        return fail(XP_ERR_INVALID, "attention_decode: max_seq/nsplit too large for shared memory");
+    if (((uintptr_t)out | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)scratch) & 15)
+        return fail(XP_ERR_INVALID, "attention_decode: out, the caches and scratch must be 16-byte aligned");
+    return XP_OK;
+}
+}  // namespace xp
+extern "C" {
 xp_status xp_attention_decode(void* stream, float* out, const float* q_raw, const float* k_raw, const float* v_raw,
                               const float* q_norm, const float* k_norm, uint16_t* kc, uint16_t* vc,
                               const uint32_t* pos_dev, uint32_t window, float theta, float eps, float scale,
                               uint32_t nsplit, uint32_t max_seq, void* scratch) {
-    CHECK_PTR(out); CHECK_PTR(q_raw); CHECK_PTR(k_raw); CHECK_PTR(v_raw); CHECK_PTR(q_norm); CHECK_PTR(k_norm);
-    CHECK_PTR(kc); CHECK_PTR(vc); CHECK_PTR(pos_dev); CHECK_PTR(scratch);
-    if (nsplit == 0 || nsplit > 1024) return fail(XP_ERR_INVALID, "attention_decode: nsplit must be 1..1024");
-    if (attn_smem(attn_chunk_max(nsplit, max_seq)) > 200 * 1024)
-        return fail(XP_ERR_INVALID, "attention_decode: max_seq/nsplit too large for shared memory");
-    if (((uintptr_t)out | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)scratch) & 15)
-        return fail(XP_ERR_INVALID, "attention_decode: out, the caches and scratch must be 16-byte aligned");
+    if (xp_status s = attn_validate(out, q_raw, k_raw, v_raw, q_norm, k_norm, kc, vc, pos_dev, window, nsplit,
+                                    max_seq, scratch);
+        s != XP_OK)
+        return s;
     AttnArgs a{};
     a.q_raw = q_raw; a.k_raw = k_raw; a.v_raw = v_raw; a.q_norm = q_norm; a.k_norm = k_norm;
     a.kcache = reinterpret_cast<__half*>(kc);
     a.vcache = reinterpret_cast<__half*>(vc);
     a.pos = pos_dev;
+    a.cache_rows = max_seq;
     a.window = window; a.theta = theta; a.eps = eps; a.scale = scale;
     a.att = out;
     a.att_xq = nullptr;
     // programmatic dependent launch: the kernel reads nothing before
     // griddepcontrol.wait, so its launch may overlap any predecessor's tail
-    return cuda_status(launch_attn(a, scratch, nsplit, max_seq, (cudaStream_t)stream, true), "attention_decode");
+    return cuda_status(launch_attn(a, scratch, nsplit, attn_span_max(window, max_seq), (cudaStream_t)stream, true),
+                       "attention_decode");
 }
 xp_status xp_selftest_wait_timeout(uint32_t spin_limit, uint32_t* err_word) {
     CHECK_PTR(err_word);

@@ -196,6 +196,7 @@ struct xp_session {
             t.q_norm = w.norm[4]; t.k_norm = w.norm[5];
             t.kcache = w.kc; t.vcache = w.vc;
             t.pos = pos;
+            t.cache_rows = cfg.max_seq;
             const bool glob = is_global(l);
             t.window = glob ? 0 : cfg.sliding_window;
             t.theta = glob ? cfg.rope_theta_global : cfg.rope_theta_local;
@@ -513,7 +514,7 @@ struct xp_session {
         tk.head_u1 = tk.head.units;
         tk.tp_rank = 0;
         tk.tp_world = 1;
-        if ((e = alloc(&tp_buf, TK_TP_MAX * sizeof(TkTpSlot) / 4)) != XP_OK) return e;
+        if ((e = alloc(&tp_buf, TK_TP_SLOTS * sizeof(TkTpSlot) / 4)) != XP_OK) return e;
         if ((e = alloc(&tk.tp_count, 4)) != XP_OK) return e;
         tk.tp_slots[0] = reinterpret_cast<TkTpSlot*>(tp_buf);
         XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
@@ -1362,7 +1363,7 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
     s->tk.head_u1 = (uint32_t)((uint64_t)U * (rank + 1) / world);
     s->tk.tp_rank = rank;
     s->tk.tp_world = world;
-    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, TK_TP_MAX * sizeof(TkTpSlot)));
+    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, TK_TP_SLOTS * sizeof(TkTpSlot)));
     XP_CUDA_TRY(cudaMemset(s->tk.tp_count, 0, 4));
     for (cudaGraphExec_t* g : {&s->g_dev, &s->g_io, &s->g_prefill})
         if (*g) { cudaGraphExecDestroy(*g); *g = nullptr; }

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstring>
@@ -37,15 +38,38 @@ inline xp_status fail(xp_status s, const char* fmt, ...) {
                               __LINE__);                                                           \
     } while (0)
 
+constexpr int kMaxDevices = 64;
+
 inline int sm_count() {
-    static int n = 0;
+    static std::atomic<int> per_dev[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) dev = 0;
+    int n = per_dev[dev].load(std::memory_order_relaxed);
     if (!n) {
-        int dev = 0;
-        cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
         if (n <= 0) n = 148;
+        per_dev[dev].store(n, std::memory_order_relaxed);
     }
     return n;
+}
+
+// Function attributes are held per device: raise `kern`'s dynamic shared
+// memory limit (and optionally allow non-portable cluster sizes) on the
+// current device the first time it launches there. `done` is the call site's
+// per-device flag array.
+template <typename Kern>
+inline cudaError_t smem_attr_once(std::atomic<bool>* done, Kern* kern, int bytes, bool nonportable_cluster = false) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool track = dev >= 0 && dev < kMaxDevices;
+    if (track && done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && nonportable_cluster)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess && track) done[dev].store(true, std::memory_order_release);
+    return e;
 }
 
 // Launch with optional cluster size and programmatic dependent launch.
@@ -84,12 +108,8 @@ inline uint32_t mv_per(const MvArgs& a) {
 }
 
 inline cudaError_t launch_mv(const MvArgs& a, cudaStream_t st, bool pdl, uint32_t max_ctas = 0) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(mv_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        attr_set = true;
-    }
+    static std::atomic<bool> attr_set[kMaxDevices];
+    if (cudaError_t e = smem_attr_once(attr_set, mv_kernel, 200 * 1024, true); e != cudaSuccess) return e;
     const size_t smem = MvSmem::bytes(a, mv_per(a));
     uint32_t grid;
     unsigned cluster = 1;
@@ -112,6 +132,11 @@ constexpr uint32_t attn_cluster(uint32_t grid) { return grid % 8 == 0 ? 8 : grid
 constexpr size_t ATT_SCRATCH_HDR = 512;
 constexpr size_t attn_scratch_bytes(uint32_t nsplit) {
     return ATT_SCRATCH_HDR + (size_t)attn_grid(nsplit) * (4 * 256 * 4 + 8 * 4);
+}
+// Longest span one call attends: the window of a sliding-window layer, else
+// every row the caches hold.
+constexpr uint32_t attn_span_max(uint32_t window, uint32_t max_seq) {
+    return (window != 0 && window < max_seq) ? window : max_seq;
 }
 inline uint32_t attn_chunk_max(uint32_t nsplit, uint32_t max_seq) {
     uint32_t c = (max_seq + nsplit - 1) / nsplit;
@@ -142,11 +167,8 @@ inline void rope_table_host(float theta, float* out) {
 }
 inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint32_t max_seq, cudaStream_t st,
                                bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(attn_decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
+    static std::atomic<bool> attr_set[kMaxDevices];
+    if (cudaError_t e = smem_attr_once(attr_set, attn_decode_kernel<4>, 200 * 1024); e != cudaSuccess) return e;
     char* s = static_cast<char*>(scratch);
     const uint32_t grid = attn_grid(nsplit), cl = attn_cluster(grid);
     a.ticket = reinterpret_cast<uint32_t*>(s);
@@ -170,11 +192,8 @@ inline size_t sample_scratch_bytes(uint32_t n) {
 // one drawing CTA per sequence. `cand` holds nseq * slices * TOPK_TK keys.
 inline cudaError_t launch_topk(const float* logits, uint32_t n, uint32_t nseq, uint64_t* cand,
                                const TopkDrawArgs& da_in, cudaStream_t st, bool pdl) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(topk_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
+    static std::atomic<bool> attr_set[kMaxDevices];
+    if (cudaError_t e = smem_attr_once(attr_set, topk_draw_kernel, 200 * 1024); e != cudaSuccess) return e;
     const uint32_t ns = (n + TOPK_SLICE - 1) / TOPK_SLICE;
     cudaError_t e = launch_ex(topk_cand_kernel, dim3(ns, nseq), dim3(TOPK_THREADS), 0, st, 1, pdl, logits, n, cand);
     if (e != cudaSuccess) return e;

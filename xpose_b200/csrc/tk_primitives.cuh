@@ -14,6 +14,7 @@ constexpr uint32_t TK_ERR_PLAN = 8u;         // a unit did not fit its slot
 constexpr uint32_t TK_ERR_RANGE = 16u;       // a K-split sum outside the fixed-point range
 constexpr uint32_t TK_ERR_TP_WAIT = 32u;     // a tensor-parallel peer's entry never arrived
 constexpr uint32_t TK_ERR_LL_WAIT = 64u;     // a flagged attention partial never arrived
+constexpr uint32_t TK_ERR_POS = 128u;        // a device-resident position at or past the KV caches' rows
 
 // A wait of ~1 s on these loops is far beyond any phase (a token is < 1 ms).
 constexpr uint32_t TK_SPIN_LIMIT = 1u << 22;

@@ -125,6 +125,11 @@ struct TkTpSlot {
     uint32_t pad;
 };
 constexpr uint32_t TK_TP_MAX = 8;
+// Two banks of TK_TP_MAX slots, chosen by the parity of the launch's flag. A
+// peer can run at most one launch ahead of a rank that is still reading its
+// entry (its next-but-one launch needs this rank's next entry), so the entry
+// being read is never the one being rewritten.
+constexpr uint32_t TK_TP_SLOTS = 2 * TK_TP_MAX;
 
 struct TkArgs {
     const TkLayer* layers;
@@ -168,7 +173,7 @@ struct TkArgs {
     int qkv_free;         // the ring leaves the QKV slot alone (it is refilled during HEAD)
     uint32_t head_u0, head_u1;          // this rank's LM-head units [u0, u1)
     uint32_t tp_rank, tp_world;         // tensor-parallel group of the LM head (world 1 = none)
-    TkTpSlot* tp_slots[TK_TP_MAX];      // every rank's exchange buffer (peer mappings), TK_TP_MAX slots each
+    TkTpSlot* tp_slots[TK_TP_MAX];      // every rank's exchange buffer (peer mappings), TK_TP_SLOTS slots each
     uint32_t* tp_count;                 // launches so far (this rank), the exchange flag
 };
 
@@ -1206,8 +1211,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 // [tp_rank] over NVLink, then waits for rank r's entry in our
                 // own buffer (bounded) and the warp keeps the lowest-index max
                 const uint32_t flag = *a.tp_count + 1;
+                const uint32_t bank = (flag & 1u) * TK_TP_MAX;
                 if ((uint32_t)lane < a.tp_world) {
-                    TkTpSlot* dst = a.tp_slots[lane] + a.tp_rank;
+                    TkTpSlot* dst = a.tp_slots[lane] + bank + a.tp_rank;
                     dst->val = v;
                     dst->idx = ix;
                     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(&dst->flag), "r"(flag) : "memory");
@@ -1215,7 +1221,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 float rv = -INFINITY;
                 uint32_t ri = 0xFFFFFFFFu;
                 if ((uint32_t)lane < a.tp_world) {
-                    const TkTpSlot* src = a.tp_slots[a.tp_rank] + lane;
+                    const TkTpSlot* src = a.tp_slots[a.tp_rank] + bank + lane;
                     uint32_t f = 0, it = 0;
                     do {
                         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&src->flag) : "memory");

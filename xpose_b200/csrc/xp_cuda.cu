@@ -13,12 +13,33 @@
 // a `scratch` argument. The array is a fixed XP_ATTN_STATIC_MAX_NSPLIT splits
 // in size and lives on every GPU that loads this library until the process
 // exits. Every call shares it, so calls that overlap on the GPU race.
+//
+// Layout (the kernel's scratch layout): byte 0 the combine ticket (each
+// launch leaves it at zero), byte 4 the error word (sticky: kernels only OR
+// bits into it; xp_attention_static_error_word reads and clears it).
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char g_attn_static_scratch[XP_ATTN_STATIC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kMaxDevices = 64;
-void* g_attn_static_ptr[kMaxDevices] = {};  // device address of the array, per device
+// Device address of the array, per device, looked up once with that device
+// current (concurrent first calls store the same value). cudaDeviceReset
+// destroys the context that owns the array, so a process that resets a device
+// must not use these entry points on it afterwards.
+std::atomic<void*> g_attn_static[kMaxDevices];
+
+xp_status attn_static_scratch(const char* who, void** out) {
+    int dev = 0;
+    XP_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(XP_ERR_NO_DEVICE, "%s: device %d", who, dev);
+    void* p = g_attn_static[dev].load(std::memory_order_acquire);
+    if (!p) {
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+        if (e != cudaSuccess) return fail(XP_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+        g_attn_static[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return XP_OK;
+}
 }  // namespace
 
 extern "C" xp_status xp_attention_decode_static(void* stream, float* out, const float* q_raw, const float* k_raw,
@@ -31,21 +52,28 @@ extern "C" xp_status xp_attention_decode_static(void* stream, float* out, const 
                     nsplit, (unsigned)XP_ATTN_STATIC_MAX_NSPLIT);
     static_assert(XP_ATTN_STATIC_SCRATCH_BYTES >= attn_scratch_bytes(XP_ATTN_STATIC_MAX_NSPLIT),
                   "static scratch smaller than the largest split count needs");
-    int dev = 0;
-    XP_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kMaxDevices) return fail(XP_ERR_NO_DEVICE, "xp_attention_decode_static: device %d", dev);
-    if (!g_attn_static_ptr[dev]) {
-        // first call on this device (the device is current): resolve the
-        // array's device address once
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
-        if (e != cudaSuccess)
-            return fail(XP_ERR_CUDA, "xp_attention_decode_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-        g_attn_static_ptr[dev] = p;
-    }
-    void* scratch = g_attn_static_ptr[dev];
-    // the combine tickets and the error word start at zero for every call
-    XP_CUDA_TRY(cudaMemsetAsync(scratch, 0, ATT_SCRATCH_HDR, (cudaStream_t)stream));
+    void* scratch = nullptr;
+    if (xp_status s = attn_static_scratch("xp_attention_decode_static", &scratch); s != XP_OK) return s;
+    // every check that could refuse the call runs before the shared array is touched
+    if (xp_status s = attn_validate(out, q_raw, k_raw, v_raw, q_norm, k_norm, kcache_f16, vcache_f16, pos_dev,
+                                    window, nsplit, max_seq, scratch);
+        s != XP_OK)
+        return s;
+    // the combine ticket must start at zero (each launch leaves it so; this
+    // covers a launch that never ran to its end). The error word is kept.
+    XP_CUDA_TRY(cudaMemsetAsync(scratch, 0, 4, (cudaStream_t)stream));
     return xp_attention_decode(stream, out, q_raw, k_raw, v_raw, q_norm, k_norm, kcache_f16, vcache_f16, pos_dev,
                                window, theta, eps, scale, nsplit, max_seq, scratch);
+}
+
+extern "C" xp_status xp_attention_static_error_word(void* stream, uint32_t* word, int clear) {
+    if (!word) return fail(XP_ERR_INVALID, "xp_attention_static_error_word: argument 'word' is null");
+    void* scratch = nullptr;
+    if (xp_status s = attn_static_scratch("xp_attention_static_error_word", &scratch); s != XP_OK) return s;
+    uint32_t* err = static_cast<uint32_t*>(scratch) + 1;
+    const cudaStream_t st = (cudaStream_t)stream;
+    XP_CUDA_TRY(cudaMemcpyAsync(word, err, 4, cudaMemcpyDeviceToHost, st));
+    if (clear) XP_CUDA_TRY(cudaMemsetAsync(err, 0, 4, st));
+    XP_CUDA_TRY(cudaStreamSynchronize(st));
+    return XP_OK;
 }
