@@ -120,6 +120,15 @@ def config1_plan(copies=64, rows=1152, cols=6912):
     return plan, keep
 
 
+def measured_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        return 1400.0, "fallback (sustained)"
+
+
 def batched_bench(sess, cfg, rank, world, max_over_ranks, barrier, nseq=64, prompt=128, new=256):
     """BASELINE config 4 (batched part) on this rank's GPU."""
     from xpose_b200.decode import BatchDecode, Sampling
@@ -132,7 +141,23 @@ def batched_bench(sess, cfg, rank, world, max_over_ranks, barrier, nseq=64, prom
         barrier()
         ms = bd.generate(new - 1)
         ms = max_over_ranks(ms)
-        return {"workload": f"{nseq} sequences per GPU, prompt {prompt}, {new} new tokens, top-k 64 / top-p 0.95 / "
+        # per step: every int4 weight byte once (all sequences share it) and
+        # 2 flops per weight per sequence on the tensor cores
+        step_s = ms / (new - 1) / 1000.0
+        wb = cfg.weight_bytes()
+        nweights = wb * 16 // 9  # 4.5 bits per weight (nibble + 1/16 bf16 scale per 32)
+        gbs = wb / step_s / 1e9
+        tfs = 2.0 * nseq * nweights / step_s / 1e12
+        hbm_peak, _ = measured_peak()
+        tc_peak, tc_kind = measured_tflops()
+        hb, tb = gbs / hbm_peak, tfs / tc_peak
+        roof = {"bound": "hbm" if hb >= tb else "tensor", "achieved": round(gbs if hb >= tb else tfs, 1),
+                "peak": hbm_peak if hb >= tb else tc_peak, "unit": "GB/s" if hb >= tb else "TFLOP/s",
+                "frac": round(max(hb, tb), 4), "traffic": None,
+                "hbm": {"achieved_GBps": round(gbs, 1), "frac": round(hb, 4)},
+                "tensor": {"achieved_TFLOPs": round(tfs, 2), "frac": round(tb, 4), "peak_kind": tc_kind},
+                "kernel": "whole batched step (bmm_kernel for every int4 matvec + per-sequence kernels)"}
+        return {"roofline": roof, "workload": f"{nseq} sequences per GPU, prompt {prompt}, {new} new tokens, top-k 64 / top-p 0.95 / "
                             "T 1.0 (BASELINE config 4, batched part)",
                 "value": round(world * nseq * (new - 1) / (ms / 1000.0), 1), "unit": "tok/s",
                 "ms_per_step": round(ms / (new - 1), 3), "sequences": world * nseq,
@@ -194,7 +219,12 @@ def long_context_bench(peak, iters=20):
     ms = e0.elapsed_time(e1) / iters
     nglob = sum(1 for _, gl in layers if gl)
     kv_bytes = (nglob * S + (L - nglob) * 512) * 256 * 2 * 2
-    return {"workload": "26 x single-query GQA attention over 8192-position fp16 caches (5 local w512 : 1 global) + "
+    step_bytes = kv_bytes + vocab * 4  # + the logits the sampler reads
+    gbs = step_bytes / ms / 1e6
+    return {"roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None, "algorithmic_bytes_per_step": step_bytes,
+                         "kernel": "attn_decode_kernel x 26 + topk_cand_kernel + topk_draw_kernel (one graph)"},
+            "workload": "26 x single-query GQA attention over 8192-position fp16 caches (5 local w512 : 1 global) + "
                         "top-k 64 / top-p 0.95 sampling on 262144 logits",
             "us_per_step": round(ms * 1000.0, 1), "kv_bytes": kv_bytes,
             "kv_GB/s": round(kv_bytes / ms / 1e6, 1), "frac": round(kv_bytes / ms / 1e6 / peak, 4),
@@ -229,7 +259,10 @@ def matvec_bench(sess, peak):
     def entry(workload, nbytes, ms):
         gbs = nbytes / ms / 1e6
         return {"workload": workload, "bytes": int(nbytes), "us": round(ms * 1000.0, 2), "GB/s": round(gbs, 1),
-                "frac": round(gbs / peak, 4)}
+                "frac": round(gbs / peak, 4),
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(gbs / peak, 4), "traffic": None,
+                             "kernel": "mv_stream_kernel (one launch per plan run)"}}
     return {"kernel": "mv_stream_kernel (xp_mv_plan_run: limb prep + one persistent streaming launch)",
             "peak": peak, "unit": "GB/s",
             "config1": entry("W 6912x1152 int4 matvec, 64 distinct weight copies per run", b1.value, ms1),
@@ -385,101 +418,357 @@ def steps_default(warmup):
     return TARGET_POS - PROMPT - warmup
 
 
+def depth_buckets(K, W, nb=4):
+    """Where the K timed tokens sit: `nb` equal segments of the decode range
+    [PROMPT + W, TARGET_POS) (positions 131..4095 at W = 3), K/nb tokens
+    centred in each, so a short run still averages over attention depth. At
+    the default K the segments are covered whole (one contiguous sweep).
+    Returns [(first timed position, tokens)]."""
+    lo, hi = PROMPT + W, TARGET_POS
+    if K >= hi - lo:
+        return [(lo, K)]
+    nb = max(1, min(nb, K))
+    out = []
+    for b in range(nb):
+        kb = K // nb + (1 if b < K % nb else 0)
+        s0, s1 = lo + (hi - lo) * b // nb, lo + (hi - lo) * (b + 1) // nb
+        out.append((s0 + max(0, (s1 - s0 - kb) // 2), kb))
+    return out
+
+
+def context_tokens(rank=0):
+    """The token ids that fill the positions before a bucket: the 128-token
+    uniform-random prompt, then uniform-random ids (teacher-forced context)."""
+    rng = np.random.default_rng(1000 + rank)
+    return rng.integers(0, 262144, TARGET_POS + 64, dtype=np.uint32)
+
+
 # ---------------------------------------------------------------------------
-# CPU baseline (oracle restatement, test infrastructure used only as the checker arm)
+# CPU baselines. The checker code under oracle/ (the reference's own kernel
+# sources and DecodeSession compiled for the host, oracle/_ref/libxpref.so, or
+# the C restatement oracle/liboracle.so) is timed here as the reported CPU
+# arm; it is never part of the measured GPU path.
 # ---------------------------------------------------------------------------
-def cpu_decode(n_tokens, warm=1, prompt_len=8):
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _checkers():
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_lib as O
-    from xpose_b200.decode import DecodeConfig
+    have_ref = os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libxpref.so"))
+    return O, have_ref
 
-    cfg = DecodeConfig(max_seq=prompt_len + warm + n_tokens + 1)
-    t0 = time.time()
-    om = O.OracleModel(cfg, seed=0)
-    build_s = time.time() - t0
-    # A short prompt fills the KV rows (time excluded); a decode token's CPU
-    # cost is the 562 MB weight stream, which does not depend on the position.
-    prompt = O.gen_tokens(0, 0x777, prompt_len, cfg.vocab)
+
+def _timed(fn, reps):
+    fn()  # warm
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_decode_port(om, n_tokens, greedy=True, prompt_len=8):
+    """Decode tokens/s of the C restatement (OpenMP over all host cores) on the
+    full-size model, after a short prompt (a decode token's CPU cost is the
+    562 MB weight stream; attention over a short prefix is negligible)."""
+    O, _ = _checkers()
+    prompt = O.gen_tokens(0, 0x777, prompt_len, om.cfg.vocab)
     logits = None
     for p, t in enumerate(prompt):
         logits = om.forward(int(t), p, want_logits=(p == prompt_len - 1))
     pos = prompt_len
-    tok = int(np.argmax(logits))
-    for _ in range(warm):
-        logits = om.forward(tok, pos)
-        tok = int(np.argmax(logits))
-        pos += 1
+
+    def pick(lg, p):
+        if greedy:
+            return int(np.argmax(lg))
+        u = O.oracle().xo_uniform(4242, 0, p)
+        return int(O.oracle().xo_sample(lg, om.cfg.vocab, 1.0, 64, 0.95, u))
+    tok = pick(logits, pos - 1)
+    logits = om.forward(tok, pos)  # warm
+    tok = pick(logits, pos)
+    pos += 1
     t0 = time.perf_counter()
     for _ in range(n_tokens):
         logits = om.forward(tok, pos)
-        tok = int(np.argmax(logits))
+        tok = pick(logits, pos)
         pos += 1
-    dt = time.perf_counter() - t0
-    return n_tokens / dt, build_s, os.cpu_count()
+    return n_tokens / (time.perf_counter() - t0)
 
 
-def ref_engine_decode(n_tokens, warm=1, prompt_len=8):
-    """The reference's own DecodeSession (examples/llm/decode.cpp) and kernels,
-    built from the reference sources into oracle/_ref/libxpref.so, on a
-    full-size seeded GGUF. Returns None when that library was not built."""
+def cpu_matvec_baseline(om):
+    """BASELINE configs 1 and 2 on the host: the reference's `mv_km4_bs`
+    (kernels/llm_matvec.cl, compiled for the CPU, one work item per output
+    column, OpenMP over all cores), else the restatement's xo_mv_km4_bs.
+    Config 1 streams 64 distinct copies of the packed 6912x1152 W per pass
+    (like the GPU case, more than the host's caches); config 2 the model's
+    own 26 layers x 7 matrices + LM head once per pass."""
+    O, have_ref = _checkers()
+    cores = host_cores()
+    kind = "reference" if have_ref else "port"
+
+    def mv(out, x, words, scales, rows, cols):
+        if have_ref:
+            O.ref_launch("mv_km4_bs", cols, out, x, words, scales, rows, cols, threads=cores)
+        else:
+            O.oracle().xo_mv_km4_bs(out, x, words, scales, rows, cols)
+
+    def nbytes(rows, cols):
+        return rows * cols // 2 + rows * cols // 16 + 4 * rows + 4 * cols
+
+    rows, cols = 1152, 6912
+    w = O.gen_normal(0, 1, rows * cols, 0.02)
+    x1 = O.gen_normal(0, 2, rows, 1.0)
+    words, scales = O.pack(w, rows, cols)
+    copies = [(words.copy(), scales.copy()) for _ in range(64)]
+    out1 = np.zeros(cols, np.float32)
+
+    def pass1():
+        for wq, sc in copies:
+            mv(out1, x1, wq, sc, rows, cols)
+    t1 = _timed(pass1, 2)
+    b1 = 64 * nbytes(rows, cols)
+    mats = []
+    for lw in om.layers_np:
+        for m, (r, c) in enumerate(om.cfg.matrix_shapes()):
+            mats.append((lw["words"][m], lw["scales"][m], r, c))
+    mats.append((om.lm_words, om.lm_scales, om.cfg.hidden, om.cfg.vocab))
+    xs = {r: O.gen_normal(0, 3 + r, r, 1.0) for r in {m[2] for m in mats}}
+    outs = {c: np.zeros(c, np.float32) for c in {m[3] for m in mats}}
+
+    def pass2():
+        for wq, sc, r, c in mats:
+            mv(outs[c], xs[r], wq, sc, r, c)
+    t2 = _timed(pass2, 2)
+    b2 = sum(nbytes(r, c) for _, _, r, c in mats)
+    what = ("the reference's mv_km4_bs (kernels/llm_matvec.cl) compiled for the host" if have_ref
+            else "the C restatement xo_mv_km4_bs")
+    return ({"value": round(b1 / t1 / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+             "sample": f"2 passes over 64 copies of W 6912x1152 ({what})"},
+            {"value": round(b2 / t2 / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+             "sample": f"2 sweeps of the 26 x 7 layer matrices + LM head ({what})"})
+
+
+def _softmax_parts(span, min_span=128, max_parts=256):
+    # examples/llm/decode.hpp softmax_parts_for
+    if span < min_span:
+        return 1
+    p = 1
+    while p * p < span and p < max_parts:
+        p *= 2
+    return min(p, span)
+
+
+def cpu_long_context_baseline():
+    """BASELINE config 5 on the host through the reference's own kernels
+    (oracle/_ref): per layer QK-norm (rmsnorm_heads_gemma), rope, kv_append,
+    attention_scores_mq4 + softmax_rows_{partial,finish,scale} +
+    attention_apply_mq4 (split 16) + attention_apply_reduce over fp32 caches
+    (the reference's KV type), the sequence of examples/llm/decode.cpp:1676-1731
+    for spans >= 128; then topk4_partial (1024 chains) and the host draw over
+    its 4096 candidates (decode.cpp:1873-1917, restated in oracle/). Without
+    oracle/_ref: the restatement's xo_attention and xo_sample ("port")."""
+    O, have_ref = _checkers()
+    cores = host_cores()
+    L, S, pos, vocab, hd = 26, 8192, 8191, 262144, 256
+    rng = np.random.default_rng(5)
+    kc = [rng.standard_normal(S * hd, dtype=np.float32) for _ in range(L)]
+    vc = [rng.standard_normal(S * hd, dtype=np.float32) for _ in range(L)]
+    q0 = rng.standard_normal(4 * hd, dtype=np.float32)
+    k0 = rng.standard_normal(hd, dtype=np.float32)
+    qn = (rng.standard_normal(hd, dtype=np.float32) * 0.02).astype(np.float32)
+    logits = (rng.standard_normal(vocab, dtype=np.float32) * 3.0).astype(np.float32)
+    glob = [(l + 1) % 6 == 0 for l in range(L)]
+    q, k, att = np.zeros(4 * hd, np.float32), np.zeros(hd, np.float32), np.zeros(4 * hd, np.float32)
+    scores = np.zeros(4 * S, np.float32)
+    pmax, psum, stats = np.zeros(4 * 256, np.float32), np.zeros(4 * 256, np.float32), np.zeros(8, np.float32)
+    part = np.zeros(16 * 4 * hd, np.float32)
+    cval, cidx = np.zeros(4096, np.float32), np.zeros(4096, np.uint32)
+
+    def step_ref():
+        for l in range(L):
+            seq = pos + 1
+            kv_start = 0 if glob[l] or seq <= 512 else seq - 512
+            span = seq - kv_start
+            theta = 1e6 if glob[l] else 1e4
+            O.ref_launch("rmsnorm_heads_gemma", 4 * hd, q, q0, qn, 4, hd, 1e-6, threads=cores)
+            O.ref_launch("rmsnorm_heads_gemma", hd, k, k0, qn, 1, hd, 1e-6, threads=cores)
+            O.ref_launch("rope", 2 * hd, q, 4, hd, pos, theta, threads=cores)
+            O.ref_launch("rope", hd // 2, k, 1, hd, pos, theta, threads=cores)
+            O.ref_launch("kv_append", hd, kc[l], k, hd, pos, threads=cores)
+            O.ref_launch("kv_append", hd, vc[l], k0, hd, pos, threads=cores)
+            O.ref_launch("attention_scores_mq4", span, scores, q, kc[l], hd, span, 1.0 / 16, kv_start, threads=cores)
+            npt = _softmax_parts(span)
+            O.ref_launch("softmax_rows_partial", 4 * npt, pmax, psum, scores, 4, span, npt, threads=cores)
+            O.ref_launch("softmax_rows_finish", 4, stats, pmax, psum, 4, npt, threads=cores)
+            O.ref_launch("softmax_rows_scale", 4 * span, scores, stats, 4, span, threads=cores)
+            O.ref_launch("attention_apply_mq4", hd * 16, part, scores, vc[l], hd, span, kv_start, 16, threads=cores)
+            O.ref_launch("attention_apply_reduce", 4 * hd, att, part, 4 * hd, 16, threads=cores)
+        O.ref_launch("topk4_partial", 1024, cval, cidx, logits, vocab, 1024, threads=cores)
+        u = O.oracle().xo_uniform(7, 0, pos)
+        O.oracle().xo_sample(cval, 4096, 1.0, 64, 0.95, u)
+
+    kc16 = [a.astype(np.float16).view(np.uint16) for a in kc] if not have_ref else None
+    vc16 = [a.astype(np.float16).view(np.uint16) for a in vc] if not have_ref else None
+
+    def step_port():
+        for l in range(L):
+            seq = pos + 1
+            kv_start = 0 if glob[l] or seq <= 512 else seq - 512
+            O.oracle().xo_attention(att, q0, kc16[l].ctypes.data, vc16[l].ctypes.data, 1, 4, 1, hd, kv_start,
+                                    seq - kv_start, 1.0 / 16)
+        u = O.oracle().xo_uniform(7, 0, pos)
+        O.oracle().xo_sample(logits, vocab, 1.0, 64, 0.95, u)
+
+    t = _timed(step_ref if have_ref else step_port, 5)
+    return {"value": round(t * 1e6, 1), "unit": "us/step", "cores": cores,
+            "kind": "reference" if have_ref else "port",
+            "sample": "5 steps of 26 attention layers at position 8191 (4 global over 8192, 22 local over 512) + "
+                      "sampling 262144 logits"}
+
+
+def ref_engine_session(max_seq, greedy=True):
+    """The reference's own DecodeSession (examples/llm/decode.cpp) and kernel
+    sources, compiled for the host into oracle/_ref/libxpref.so, on the
+    full-size seeded model written as a GGUF file. None when that library was
+    not built."""
     if not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libxpref.so")):
         return None
     import shutil
     import tempfile
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    import oracle_lib as O
+    O, _ = _checkers()
     from xpose_b200.decode import DecodeConfig
-
-    cfg = DecodeConfig(max_seq=prompt_len + warm + n_tokens + 1)
+    cfg = DecodeConfig(max_seq=max_seq)
     tmp = tempfile.mkdtemp(prefix="_refgguf", dir=ROOT)
     try:
         path = os.path.join(tmp, "model.gguf")
         O.write_random_gguf(cfg, 0, path)
-        sess = O.RefSession(path, cfg.max_seq, cfg.global_every)
+        return O.RefSession(path, cfg.max_seq, cfg.global_every, greedy=greedy)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
-    sess.prefill(O.gen_tokens(0, 0x777, prompt_len, cfg.vocab))
-    for _ in range(warm):
-        sess.decode_step()
-    t0 = time.perf_counter()
-    for _ in range(n_tokens):
-        sess.decode_step()
-    dt = time.perf_counter() - t0
-    sess.close()
-    return n_tokens / dt, os.cpu_count()
+
+
+def config_block(W, K, buckets, world):
+    return {"workload": "BASELINE config 3: Gemma-3-1B-shape greedy decode, batch 1, prompt 128, "
+                        "decoding toward position 4096",
+            "timed_positions": [[s, s + k - 1] for s, k in buckets],
+            "parallelism": f"dp{world} (independent sequences)" if world > 1 else "single GPU",
+            "l2": "weights 562 MB/token > 126 MB L2; no flush needed"}
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the decode
+    path on this host's cores, at the same workload as ours: the 128-token
+    prompt, then the same K timed positions in the same depth buckets, each
+    after W untimed tokens (the positions between buckets are filled with the
+    reference's own prefill). Rank 0 alone runs it under torchrun."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    k = min(args.steps or 8, 8)
-    w = min(args.warmup, 1)
-    got = ref_engine_decode(k, warm=w)
-    sample = (f"{k} full-size decode tokens at positions {8 + w}..{8 + w + k - 1} after an 8-token prompt "
-              "(per-token cost is the weight stream, independent of position)")
-    if got is not None:
-        tps, cores = got
-        kind = "reference"
+    W = max(3, args.warmup)
+    K = args.steps if args.steps is not None else steps_default(W)
+    buckets = depth_buckets(K, W)
+    ctx = context_tokens(0)
+    max_seq = max(TARGET_POS, buckets[-1][0] + buckets[-1][1] + 1)
+    cores = host_cores()
+    sess = ref_engine_session(max_seq)
+    kind = "reference"
+    total_s = 0.0
+    if sess is not None:
+        sess.prefill(ctx[:PROMPT])
+        at = PROMPT
+        for start, kb in buckets:
+            if start - W > at:
+                sess.prefill(ctx[at:start - W])
+                at = start - W
+            for _ in range(W):
+                sess.decode_step()
+            t0 = time.perf_counter()
+            for _ in range(kb):
+                sess.decode_step()
+            total_s += time.perf_counter() - t0
+            at = start + kb
+        sess.close()
         note = ("the reference's own DecodeSession and kernel sources (examples/llm/decode.cpp, kernels/*.cl) "
                 "compiled for the host cores (oracle/_ref/libxpref.so), OpenMP over each dispatch's work items; "
                 "its Vulkan runtime and llvmpipe path are unavailable on this box")
     else:
-        tps, _, cores = cpu_decode(k, warm=w)
         kind = "port"
+        O, _ = _checkers()
+        from xpose_b200.decode import DecodeConfig
+        om = O.OracleModel(DecodeConfig(max_seq=max_seq), 0)
+        for p in range(PROMPT):
+            om.forward(int(ctx[p]), p, want_logits=False)
+        at = PROMPT
+        for start, kb in buckets:
+            for p in range(at, start):
+                om.forward(int(ctx[p]), p, want_logits=False)
+            tok = int(ctx[start])
+            t0 = time.perf_counter()
+            for p in range(start, start + kb):
+                tok = int(np.argmax(om.forward(tok, p)))
+            total_s += time.perf_counter() - t0
+            at = start + kb
         note = "CPU restatement of the reference decode path (oracle/xp_oracle.c); oracle/_ref was not built"
+    tps = K / total_s
+    positions = ", ".join(f"{s}..{s + k - 1}" for s, k in buckets)
+    sample = f"{K} greedy decode tokens at positions {positions} after a 128-token prompt"
     line = {
-        "metric": METRIC, "impl": "reference", "value": round(tps, 4), "unit": "tok/s", "n_gpus": 1,
-        "steps": k, "warmup": w, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 compute, fp16 KV",
+        "metric": METRIC, "impl": "reference", "value": round(tps, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 compute, fp32 KV",
         "data": "synthetic (seeded N(0,0.02) random-init weights, uniform-random prompt ids)",
-        "config": {"workload": "Gemma-3-1B-shape greedy decode, batch 1 (BASELINE config 3)", "sample": sample},
+        "config": config_block(W, K, buckets, world),
         "cpu_baseline": {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": note,
+        "note": note + (f"; one process on all {cores} host cores serves every N (the whole host against the "
+                        f"whole {world}-GPU job)" if world > 1 else ""),
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks):
+    """One sequence decoded by all ranks with the LM head's rows split over
+    them. First every rank decodes the same prompt unsharded (its own full
+    head), then sharded; the sharded tokens must equal the unsharded ones and
+    each rank's logit rows must equal the same rows of the unsharded logits
+    (bit-exact: the shard's tiles are the same computation)."""
+    import torch
+    from xpose_b200.tp import shard_lm_head
+    tprompt = np.random.default_rng(77).integers(0, cfg.vocab, PROMPT, dtype=np.uint32)
+    n_check = 64
+    sess.reset()
+    sess.prefill(tprompt)
+    ref_logits = sess.last_logits()
+    ref_toks, _ = sess.generate(n_check)
+    shard_lm_head(sess)
+    sess.reset()
+    sess.prefill(tprompt)
+    logits = sess.last_logits()
+    toks, _ = sess.generate(n_check)
+    units = cfg.vocab // 64
+    u0, u1 = units * rank // world, units * (rank + 1) // world
+    shard_exact = bool(np.array_equal(logits[u0 * 64:u1 * 64], ref_logits[u0 * 64:u1 * 64]))
+    match = bool(np.array_equal(np.asarray(toks), np.asarray(ref_toks)))
+    flags = torch.tensor([int(match), int(shard_exact)], dtype=torch.int32, device="cuda")
+    torch.distributed.all_reduce(flags, op=torch.distributed.ReduceOp.MIN)
+    sess.reset()
+    sess.prefill(tprompt)
+    sess.generate(W, want_tokens=False)
+    kt = min(K, 1000)
+    barrier()
+    _, tms = sess.generate(kt, want_tokens=False)
+    tms = max_over_ranks(tms)
+    assert sess.error_word() == 0
+    return {"workload": f"one sequence, LM head rows split over {world} GPUs (NVLink argmax exchange)",
+            "value": round(kt / (tms / 1000.0), 2), "unit": "tok/s", "ms_per_step": round(tms / kt, 4),
+            "steps": kt, "positions": [PROMPT + W, PROMPT + W + kt - 1], "scaling": "strong",
+            "tokens_match": bool(flags[0].item()), "logit_shard_exact": bool(flags[1].item()),
+            "checked_tokens": n_check}
 
 
 # ---------------------------------------------------------------------------
@@ -489,12 +778,16 @@ def main():
     if args.ncu_case:
         return ncu_case(args.ncu_case)
     if args.impl == "reference":
+        # torchrun sets OMP_NUM_THREADS=1; the reference arm uses every host
+        # core (set before any OpenMP runtime is loaded)
+        os.environ["OMP_NUM_THREADS"] = str(host_cores())
         return run_reference(args)
 
     import torch
 
     W = max(3, args.warmup)
     K = args.steps if args.steps is not None else steps_default(W)
+    buckets = depth_buckets(K, W)
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
@@ -503,12 +796,12 @@ def main():
 
     from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling
 
-    max_seq = max(TARGET_POS, PROMPT + W + K + 1)
+    max_seq = max(TARGET_POS, buckets[-1][0] + buckets[-1][1] + 1)
     max_seq = (max_seq + 63) // 64 * 64
     cfg = DecodeConfig(max_seq=max_seq)
     sess = DecodeSession.random(cfg, Sampling(greedy=True), seed=0, device=dev)
-    rng = np.random.default_rng(1000 + rank)
-    prompt = rng.integers(0, cfg.vocab, PROMPT, dtype=np.uint32)
+    ctx = context_tokens(rank)
+    prompt = ctx[:PROMPT]
 
     def barrier():
         if world > 1:
@@ -522,55 +815,68 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident decode (value) ----
-    # prefill of the 128-token prompt (chunked: 64 positions per tensor-core
-    # pass), host wall clock around the synchronous call, after one untimed
-    # prefill that creates the chunked-prefill engine
+    # ---- prefill of the 128-token prompt (chunked: 64 positions per
+    # tensor-core pass), host wall clock around the synchronous call, after
+    # one untimed prefill that creates the chunked-prefill engine
     sess.reset()
-    sess.prefill(prompt)  # warm: creates the chunked-prefill engine once
+    sess.prefill(prompt)
     sess.reset()
     t_pf = time.perf_counter()
     sess.prefill(prompt)
     pf_ms = (time.perf_counter() - t_pf) * 1000.0
     prefill = {"tokens": len(prompt), "ms": round(pf_ms, 3), "tok/s": round(len(prompt) / pf_ms * 1000.0, 1),
                "path": "chunked: 64 prompt positions per pass on the tensor-core batched engine (host wall clock)"}
-    sess.generate(W, want_tokens=False)
+
+    def to_bucket(start):
+        # the context before the bucket (chunked prefill), then W untimed tokens
+        sess.reset()
+        sess.prefill(ctx[:start - W])
+
+    # ---- device-resident decode (value): K tokens in depth buckets ----
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev)).split(",")[dev]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else dev
     clocks = ClockSampler(gpu_index)
-    barrier()
     clocks.start()
-    _, ms = sess.generate(K, want_tokens=False)
+    ms = 0.0
+    per_bucket = []
+    for start, kb in buckets:
+        to_bucket(start)
+        sess.generate(W, want_tokens=False)
+        barrier()
+        _, bms = sess.generate(kb, want_tokens=False)
+        barrier()
+        ms += bms
+        per_bucket.append({"positions": [start, start + kb - 1], "us_per_token": round(bms / kb * 1000.0, 2)})
     clock_info = clocks.stop()
-    barrier()
     ms_max = max_over_ranks(ms)
     value = world * K / (ms_max / 1000.0)
     kpt = sess.stats()["kernels_per_token"]
     assert sess.error_word() == 0
 
     # ---- roofline of the dominant kernel ----
-    # One launch of the persistent token kernel decodes one position, so its
+    # One pass of the persistent token kernel decodes one position, so its
     # average duration is the device time per token. Algorithmic bytes per
-    # launch = int4 nibbles + bf16 scales of every matrix (562,360,320 B) + the
-    # fp16 K and V rows the layers attend at that position (local layers a
+    # position = int4 nibbles + bf16 scales of every matrix (562,360,320 B) +
+    # the fp16 K and V rows the layers attend at that position (local layers a
     # 512 window, global layers the whole prefix) + the embedding row and the
     # logits, averaged over the timed positions.
     peak, peak_kind = measured_peak()
-    tok_bytes = token_bytes(cfg, PROMPT + W, PROMPT + W + K)
+    tok_bytes = int(sum(token_bytes(cfg, s, s + k) * k for s, k in buckets) / K)
     achieved = tok_bytes / (ms_max / K / 1000.0) / 1e9
 
-    # ---- e2e through the public API ----
+    # ---- e2e through the public API: DecodeSession.decode_step() ----
     e2e = None
     if not args.no_e2e:
-        sess.reset()
-        sess.prefill(prompt)
-        for _ in range(W):
-            sess.decode_step()
-        barrier()
-        sess.timer_start()
-        for _ in range(K):
-            sess.decode_step()
-        e_ms = sess.timer_stop()
+        e_ms = 0.0
+        for start, kb in buckets:
+            to_bucket(start)
+            for _ in range(W):
+                sess.decode_step()
+            barrier()
+            sess.timer_start()
+            for _ in range(kb):
+                sess.decode_step()
+            e_ms += sess.timer_stop()
         e_ms = max_over_ranks(e_ms)
         e2e = {"value": round(world * K / (e_ms / 1000.0), 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                "d2h_bytes_per_step": 4}
@@ -580,38 +886,36 @@ def main():
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
-                tr = json.load(f)
-            traffic = tr.get("dram_bytes_per_token")
+                traffic = json.load(f).get("dram_bytes_per_token")
         except Exception:
             traffic = None
 
-    cpu = None
+    # ---- CPU baselines (rank 0 at N = 1 only) ----
+    cpu = cpu_mv = cpu_bat = cpu_lc = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            tps, build_s, cores = cpu_decode(4, warm=1)
+            O, _ = _checkers()
+            om = O.OracleModel(DecodeConfig(max_seq=64), 0)
+            cores = host_cores()
+            tps = cpu_decode_port(om, 4)
             cpu = {"value": round(tps, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                   "sample": "4 full-size decode tokens at positions 9-12 after an 8-token prompt "
-                             "(OpenMP over all host cores)"}
+                   "sample": "4 full-size greedy decode tokens at positions 9-12 after an 8-token prompt "
+                             "(the C restatement, OpenMP over all host cores)"}
+            tps_s = cpu_decode_port(om, 4, greedy=False)
+            cpu_bat = {"value": round(tps_s, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+                       "sample": "4 sampled (top-k 64 / top-p 0.95 / T 1) decode tokens of one sequence: the "
+                                 "reference decodes sequences one at a time, so its batched rate is its "
+                                 "single-sequence rate"}
+            cpu_mv = cpu_matvec_baseline(om)
+            del om
+            cpu_lc = cpu_long_context_baseline()
         except Exception as e:  # the checker arm must not hide the GPU result
-            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+            cpu = {"value": None, "unit": "tok/s", "cores": host_cores(), "kind": "port", "sample": f"failed: {e}"}
 
     tp = None
     if world > 1 and not args.no_tp:
         try:
-            from xpose_b200.tp import shard_lm_head
-            shard_lm_head(sess)
-            sess.reset()
-            tprompt = np.random.default_rng(77).integers(0, cfg.vocab, PROMPT, dtype=np.uint32)
-            sess.prefill(tprompt)
-            sess.generate(W, want_tokens=False)
-            kt = min(K, 1000)
-            barrier()
-            _, tms = sess.generate(kt, want_tokens=False)
-            tms = max_over_ranks(tms)
-            assert sess.error_word() == 0
-            tp = {"workload": f"one sequence, LM head rows split over {world} GPUs (NVLink argmax exchange)",
-                  "value": round(kt / (tms / 1000.0), 2), "unit": "tok/s", "ms_per_step": round(tms / kt, 4),
-                  "steps": kt, "scaling": "strong"}
+            tp = tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks)
         except Exception as e:
             tp = {"error": str(e)}
 
@@ -619,6 +923,7 @@ def main():
     if not args.no_batched:
         try:
             bat = batched_bench(sess, cfg, rank, world, max_over_ranks, barrier)
+            bat["cpu_baseline"] = cpu_bat
         except Exception as e:  # a failure here must not hide the decode result
             bat = {"error": str(e)}
 
@@ -626,6 +931,7 @@ def main():
     if rank == 0 and not args.no_long:
         try:
             lc = long_context_bench(peak)
+            lc["cpu_baseline"] = cpu_lc
         except Exception as e:
             lc = {"error": str(e)}
 
@@ -633,6 +939,8 @@ def main():
     if rank == 0 and not args.no_matvec:
         try:
             mv = matvec_bench(sess, peak)
+            if cpu_mv:
+                mv["config1"]["cpu_baseline"], mv["config2"]["cpu_baseline"] = cpu_mv
         except Exception as e:  # a failure here must not hide the decode result
             mv = {"error": str(e)}
 
@@ -642,14 +950,12 @@ def main():
             "warmup": W, "ms_per_step": round(ms_max / K, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4 weights (KM4 + bf16 scales), fp32 accumulation, fp16 KV",
             "data": "synthetic (seeded N(0,0.02) random-init weights, uniform-random prompt ids)",
-            "config": {"workload": "BASELINE config 3: Gemma-3-1B-shape greedy decode, batch 1, prompt 128, "
-                                   f"positions {PROMPT + W}..{PROMPT + W + K - 1}",
-                       "parallelism": f"dp{world} (independent sequences)" if world > 1 else "single GPU",
-                       "l2": "weights 562 MB/token > 126 MB L2; no flush needed"},
+            "config": config_block(W, K, buckets, world),
+            "depth_buckets": per_bucket,
             "e2e": e2e,
             # generate() runs the greedy token kernel over up to 512 positions
             # per cooperative launch (xp_session_generate)
-            "gpu_launches": (K + 511) // 512 if kpt == 1 else kpt * K,
+            "gpu_launches": sum((kb + 511) // 512 for _, kb in buckets) if kpt == 1 else kpt * K,
             "kernels_per_token": kpt,
             "tokens_per_launch": 512 if kpt == 1 else 1,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

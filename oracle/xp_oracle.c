@@ -514,3 +514,110 @@ int xo_forward(const xo_model* m, xo_state* st, uint32_t token, uint32_t pos, fl
     free(att); free(hg); free(hu); free(hb);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* prefill shapes: kernels/llm_sampling.cl:495-736 (row-major [row][col])    */
+/* ------------------------------------------------------------------------ */
+/* llm_sampling.cl:527-546: per row (max, sum of exp(x - max)); a fully
+ * masked row gives (0, 1) */
+void xo_softmax_rows_stats(float* stats, const float* x, uint32_t n_rows, uint32_t n_cols) {
+    for (uint32_t r = 0; r < n_rows; ++r) {
+        const float* row = x + (size_t)r * n_cols;
+        float m = -INFINITY;
+        for (uint32_t j = 0; j < n_cols; ++j) m = fmaxf(m, row[j]);
+        if (!isfinite(m)) { stats[2 * r] = 0.0f; stats[2 * r + 1] = 1.0f; continue; }
+        float s = 0.0f;
+        for (uint32_t j = 0; j < n_cols; ++j) s += expf(row[j] - m);
+        stats[2 * r] = m;
+        stats[2 * r + 1] = s;
+    }
+}
+
+/* llm_sampling.cl:549-556 */
+void xo_softmax_rows_apply(float* x, const float* stats, uint32_t n_rows, uint32_t n_cols) {
+    for (uint64_t i = 0; i < (uint64_t)n_rows * n_cols; ++i) {
+        const uint32_t r = (uint32_t)(i / n_cols);
+        x[i] = expf(x[i] - stats[2 * r]) / stats[2 * r + 1];
+    }
+}
+
+/* llm_sampling.cl:574-602: causal + sliding-window masked scores */
+void xo_attention_scores_prefill(float* scores, const float* q, const float* kcache, uint32_t n_heads,
+                                 uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                 uint32_t seq_len, uint32_t q_offset, uint32_t window, float scale) {
+    const uint32_t group = n_heads / kv_heads;
+    for (uint32_t h = 0; h < n_heads; ++h)
+        for (uint32_t qi = 0; qi < n_query; ++qi)
+            for (uint32_t t = 0; t < seq_len; ++t) {
+                const size_t o = ((size_t)h * n_query + qi) * seq_len + t;
+                const uint32_t qpos = q_offset + qi;
+                if (t > qpos || (window != 0u && t + window <= qpos)) { scores[o] = -INFINITY; continue; }
+                const float* qr = q + ((size_t)h * n_query + qi) * head_dim;
+                const float* kr = kcache + ((size_t)t * kv_heads + h / group) * head_dim;
+                float acc = 0.0f;
+                for (uint32_t d = 0; d < head_dim; ++d) acc += qr[d] * kr[d];
+                scores[o] = acc * scale;
+            }
+}
+
+/* llm_sampling.cl:605-630 */
+void xo_attention_apply_prefill(float* out, const float* probs, const float* vcache, uint32_t n_heads,
+                                uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                uint32_t seq_len) {
+    const uint32_t group = n_heads / kv_heads;
+    for (uint32_t h = 0; h < n_heads; ++h)
+        for (uint32_t qi = 0; qi < n_query; ++qi)
+            for (uint32_t d = 0; d < head_dim; ++d) {
+                const float* p = probs + ((size_t)h * n_query + qi) * seq_len;
+                float acc = 0.0f;
+                for (uint32_t t = 0; t < seq_len; ++t)
+                    acc += p[t] * vcache[((size_t)t * kv_heads + h / group) * head_dim + d];
+                out[((size_t)h * n_query + qi) * head_dim + d] = acc;
+            }
+}
+
+/* llm_sampling.cl:634-642 */
+void xo_rmsnorm_rows_sumsq(float* rowss, const float* in, uint32_t n_rows, uint32_t n) {
+    for (uint32_t r = 0; r < n_rows; ++r) {
+        float ss = 0.0f;
+        for (uint32_t j = 0; j < n; ++j) ss += in[(size_t)r * n + j] * in[(size_t)r * n + j];
+        rowss[r] = ss;
+    }
+}
+
+/* llm_sampling.cl:645-656 */
+void xo_rmsnorm_rows_apply_gemma(float* out, const float* in, const float* w, const float* rowss,
+                                 uint32_t n_rows, uint32_t n, float eps) {
+    for (uint32_t r = 0; r < n_rows; ++r) {
+        const float scale = rsqrt_f(rowss[r] / (float)n + eps);
+        for (uint32_t j = 0; j < n; ++j)
+            out[(size_t)r * n + j] = in[(size_t)r * n + j] * scale * (1.0f + w[j]);
+    }
+}
+
+/* llm_sampling.cl:659-675 */
+void xo_rmsnorm_heads_rows_gemma(float* out, const float* in, const float* w, uint32_t n_tokens,
+                                 uint32_t n_heads, uint32_t head_dim, float eps) {
+    xo_rmsnorm_heads_gemma(out, in, w, n_tokens * n_heads, head_dim, eps);
+}
+
+/* llm_sampling.cl:687-711: token ti at position pos0 + ti, the angle of
+ * xo_rope (theta^(-2d/hd) rounded once from double) */
+void xo_rope_prefill(float* x, uint32_t n_tokens, uint32_t n_heads, uint32_t head_dim,
+                     uint32_t pos0, float theta) {
+    const size_t per = (size_t)n_heads * head_dim;
+    for (uint32_t t = 0; t < n_tokens; ++t) xo_rope(x + t * per, n_heads, head_dim, pos0 + t, theta);
+}
+
+/* llm_sampling.cl:714-722 */
+void xo_kv_append_rows(float* cache, const float* src, uint32_t n_tokens, uint32_t row,
+                       uint32_t pos0) {
+    memcpy(cache + (size_t)pos0 * row, src, (size_t)n_tokens * row * sizeof(float));
+}
+
+/* llm_sampling.cl:728-736 */
+void xo_embed_lookup_rows(float* out, const float* table, const uint32_t* tokens,
+                          uint32_t n_tokens, uint32_t n) {
+    for (uint32_t t = 0; t < n_tokens; ++t)
+        memcpy(out + (size_t)t * n, table + (size_t)tokens[t] * n, (size_t)n * sizeof(float));
+}

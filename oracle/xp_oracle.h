@@ -75,6 +75,27 @@ uint32_t xo_topk(const float* x, uint32_t n, uint32_t k, float* vals, uint32_t* 
 uint32_t xo_sample(const float* logits, uint32_t n, float temperature, uint32_t top_k,
                    float top_p, float u);
 
+/* ---- prefill shapes (kernels/llm_sampling.cl:495-736) ------------------ */
+void xo_softmax_rows_stats(float* stats, const float* x, uint32_t n_rows, uint32_t n_cols);
+void xo_softmax_rows_apply(float* x, const float* stats, uint32_t n_rows, uint32_t n_cols);
+void xo_attention_scores_prefill(float* scores, const float* q, const float* kcache, uint32_t n_heads,
+                                 uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                 uint32_t seq_len, uint32_t q_offset, uint32_t window, float scale);
+void xo_attention_apply_prefill(float* out, const float* probs, const float* vcache, uint32_t n_heads,
+                                uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                uint32_t seq_len);
+void xo_rmsnorm_rows_sumsq(float* rowss, const float* in, uint32_t n_rows, uint32_t n);
+void xo_rmsnorm_rows_apply_gemma(float* out, const float* in, const float* w, const float* rowss,
+                                 uint32_t n_rows, uint32_t n, float eps);
+void xo_rmsnorm_heads_rows_gemma(float* out, const float* in, const float* w, uint32_t n_tokens,
+                                 uint32_t n_heads, uint32_t head_dim, float eps);
+void xo_rope_prefill(float* x, uint32_t n_tokens, uint32_t n_heads, uint32_t head_dim,
+                     uint32_t pos0, float theta);
+void xo_kv_append_rows(float* cache, const float* src, uint32_t n_tokens, uint32_t row,
+                       uint32_t pos0);
+void xo_embed_lookup_rows(float* out, const float* table, const uint32_t* tokens,
+                          uint32_t n_tokens, uint32_t n);
+
 /* ---- one decode token (examples/llm/decode.cpp:1634-1780) -------------- */
 typedef struct xo_qweight {
     uint32_t rows, cols; /* K inputs, N outputs */

@@ -54,6 +54,17 @@ def oracle():
         lib.xo_topk.restype = C.c_uint32
         lib.xo_sample.argtypes = [f32p, C.c_uint32, C.c_float, C.c_uint32, C.c_float, C.c_float]
         lib.xo_sample.restype = C.c_uint32
+        u32 = C.c_uint32
+        lib.xo_softmax_rows_stats.argtypes = [f32p, f32p, u32, u32]
+        lib.xo_softmax_rows_apply.argtypes = [f32p, f32p, u32, u32]
+        lib.xo_attention_scores_prefill.argtypes = [f32p, f32p, f32p] + [u32] * 7 + [C.c_float]
+        lib.xo_attention_apply_prefill.argtypes = [f32p, f32p, f32p] + [u32] * 5
+        lib.xo_rmsnorm_rows_sumsq.argtypes = [f32p, f32p, u32, u32]
+        lib.xo_rmsnorm_rows_apply_gemma.argtypes = [f32p, f32p, f32p, f32p, u32, u32, C.c_float]
+        lib.xo_rmsnorm_heads_rows_gemma.argtypes = [f32p, f32p, f32p, u32, u32, u32, C.c_float]
+        lib.xo_rope_prefill.argtypes = [f32p, u32, u32, u32, u32, C.c_float]
+        lib.xo_kv_append_rows.argtypes = [f32p, f32p, u32, u32, u32]
+        lib.xo_embed_lookup_rows.argtypes = [f32p, f32p, u32p, u32, u32]
         _o = lib
     return _o
 

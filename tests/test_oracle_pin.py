@@ -215,3 +215,89 @@ def test_reference_engine_matches_oracle():
                 assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-5
         finally:
             rs.close()
+
+
+# ---- prefill shapes (kernels/llm_sampling.cl:495-736), the shapes of
+# examples/llm/sampling_test.cpp:725-1020 (37 rows: not a multiple of 64)
+T37 = 37
+
+
+def test_prefill_softmax_rows_bitexact():
+    rows, cols = 4 * T37, T37
+    x = urand(rows * cols, -1.5, 1.5)
+    x[5 * cols + 3:5 * cols + 9] = -np.inf  # a partly masked row
+    x[7 * cols:8 * cols] = -np.inf  # a fully masked row
+    st_r, st_o = np.zeros(2 * rows, np.float32), np.zeros(2 * rows, np.float32)
+    O.ref_launch("softmax_rows_stats", rows, st_r, x, rows, cols)
+    O.oracle().xo_softmax_rows_stats(st_o, x, rows, cols)
+    assert np.array_equal(st_r, st_o)
+    xr, xo = x.copy(), x.copy()
+    O.ref_launch("softmax_rows_apply", rows * cols, xr, st_r, rows, cols)
+    O.oracle().xo_softmax_rows_apply(xo, st_o, rows, cols)
+    assert np.array_equal(xr, xo)
+
+
+@pytest.mark.parametrize("window,q_offset", [(0, 0), (8, 0), (0, 20), (16, 40)])
+def test_prefill_attention_bitexact(window, q_offset):
+    nh, kvh, hd, nq = 4, 1, 256, T37
+    seq = q_offset + nq
+    q = urand(nh * nq * hd, -1.5, 1.5)
+    kc, vc = urand(seq * kvh * hd, -1.5, 1.5), urand(seq * kvh * hd, -1.5, 1.5)
+    sr, so = np.zeros(nh * nq * seq, np.float32), np.zeros(nh * nq * seq, np.float32)
+    O.ref_launch("attention_scores_prefill", nh * nq * seq, sr, q, kc, nh, kvh, hd, nq, seq, q_offset, window,
+                 1.0 / 16)
+    O.oracle().xo_attention_scores_prefill(so, q, kc, nh, kvh, hd, nq, seq, q_offset, window, 1.0 / 16)
+    assert np.array_equal(sr, so)
+    st = np.zeros(2 * nh * nq, np.float32)
+    O.oracle().xo_softmax_rows_stats(st, so, nh * nq, seq)
+    O.oracle().xo_softmax_rows_apply(so, st, nh * nq, seq)
+    outr, outo = np.zeros(nh * nq * hd, np.float32), np.zeros(nh * nq * hd, np.float32)
+    O.ref_launch("attention_apply_prefill", nh * nq * hd, outr, so, vc, nh, kvh, hd, nq, seq)
+    O.oracle().xo_attention_apply_prefill(outo, so, vc, nh, kvh, hd, nq, seq)
+    assert np.array_equal(outr, outo)
+
+
+def test_prefill_norms_bitexact():
+    H = 1152
+    x, w = urand(T37 * H, -1.5, 1.5), urand(H, -1.5, 1.5)
+    ssr, sso = np.zeros(T37, np.float32), np.zeros(T37, np.float32)
+    O.ref_launch("rmsnorm_rows_sumsq", T37, ssr, x, T37, H)
+    O.oracle().xo_rmsnorm_rows_sumsq(sso, x, T37, H)
+    assert np.array_equal(ssr, sso)
+    outr, outo = np.zeros(T37 * H, np.float32), np.zeros(T37 * H, np.float32)
+    O.ref_launch("rmsnorm_rows_apply_gemma", T37 * H, outr, x, w, ssr, T37, H, 1e-6)
+    O.oracle().xo_rmsnorm_rows_apply_gemma(outo, x, w, sso, T37, H, 1e-6)
+    assert np.array_equal(outr, outo)
+    x2, w2 = urand(T37 * 4 * 256, -1.5, 1.5), urand(256, -1.5, 1.5)
+    hr, ho = np.zeros_like(x2), np.zeros_like(x2)
+    O.ref_launch("rmsnorm_heads_rows_gemma", x2.size, hr, x2, w2, T37, 4, 256, 1e-6)
+    O.oracle().xo_rmsnorm_heads_rows_gemma(ho, x2, w2, T37, 4, 256, 1e-6)
+    assert np.array_equal(hr, ho)
+
+
+@pytest.mark.parametrize("pos0,theta", [(5, 1e6), (4000, 1e4)])
+def test_prefill_rope_matches(pos0, theta):
+    x = urand(T37 * 4 * 256, -1.5, 1.5)
+    xr, xo = x.copy(), x.copy()
+    O.ref_launch("rope_prefill", T37 * 4 * 128, xr, T37, 4, 256, pos0, theta)
+    O.oracle().xo_rope_prefill(xo, T37, 4, 256, pos0, theta)
+    # theta^(-2d/hd): rounded once from double here, the reference's fp32
+    # exp2/log2 can differ by an ulp, which moves the angle by pos * ulp
+    np.testing.assert_allclose(xo, xr, rtol=0, atol=2e-3 if pos0 > 1000 else 1e-5)
+
+
+def test_prefill_plumbing_bitexact():
+    row, cap, pos0 = 256, 64, 11
+    cache = np.full(row * cap, 7.0, np.float32)
+    src = urand(row * T37)
+    cr, co = cache.copy(), cache.copy()
+    O.ref_launch("kv_append_rows", T37 * row, cr, src, T37, row, pos0)
+    O.oracle().xo_kv_append_rows(co, src, T37, row, pos0)
+    assert np.array_equal(cr, co)
+    vocab, H = 4096, 1152
+    table = (np.arange(vocab * H) % 977).astype(np.float32) * np.float32(0.01)
+    toks = ((np.arange(T37) * 251 + 13) % vocab).astype(np.uint32)
+    er, eo = np.zeros(T37 * H, np.float32), np.zeros(T37 * H, np.float32)
+    O.ref_launch("embed_lookup_rows", T37 * H, er, table, toks, T37, H)
+    O.oracle().xo_embed_lookup_rows(eo, table, toks, T37, H)
+    assert np.array_equal(er, eo)

@@ -133,6 +133,15 @@ cudaError_t launch_mv_split(const xp_arg* a, xp_grid, cudaStream_t st) {
     return launch_mv(m, st, false);
 }
 // argmax tree collapsed: the same out[2] contract as argmax / argmax_final
+// rmsnorm_heads_rows_gemma: grid = n_tokens * n_heads * head_dim in the
+// reference; here one warp per (token, head).
+cudaError_t launch_heads_rows(const xp_arg* a, xp_grid, cudaStream_t st) {
+    const uint32_t nth = arg_as<uint32_t>(a[3]) * arg_as<uint32_t>(a[4]);
+    ops::rmsnorm_heads_rows_gemma<<<(nth + 7) / 8, 256, 0, st>>>(
+        arg_as<float*>(a[0]), arg_as<const float*>(a[1]), arg_as<const float*>(a[2]), arg_as<uint32_t>(a[3]),
+        arg_as<uint32_t>(a[4]), arg_as<uint32_t>(a[5]), arg_as<float>(a[6]));
+    return cudaGetLastError();
+}
 cudaError_t launch_argmax(const xp_arg* a, xp_grid, cudaStream_t st) {
     ops::argmax<<<1, 1024, 0, st>>>(arg_as<float*>(a[0]), arg_as<const float*>(a[1]), arg_as<uint32_t>(a[2]));
     return cudaGetLastError();
@@ -208,6 +217,19 @@ const std::vector<Entry>& registry() {
         E(SM, topp_cutoff, GEO_THREADS, "w,k,p"),
         E(SM, multinomial_sample, GEO_THREADS, "out,idx_out,w,idx,k,u"),
         E(SM, multinomial_strided, GEO_THREADS, "out,idx_out,w,psum,stats,n,nparts,u"),
+        // kernels/llm_sampling.cl, prefill shapes
+        E(SM, softmax_rows_stats, GEO_WARPS, "stats,x,n_rows,n_cols"),
+        E(SM, softmax_rows_apply, GEO_THREADS, "x,stats,n_rows,n_cols"),
+        E(SM, attention_scores_prefill, GEO_WARPS,
+          "scores,q,kcache,n_heads,kv_heads,head_dim,n_query,seq_len,q_offset,window,scale"),
+        E(SM, attention_apply_prefill, GEO_THREADS, "out,probs,vcache,n_heads,kv_heads,head_dim,n_query,seq_len"),
+        E(SM, rmsnorm_rows_sumsq, GEO_WARPS, "rowss,in,n_rows,n"),
+        E(SM, rmsnorm_rows_apply_gemma, GEO_THREADS, "out,in,w,rowss,n_rows,n,eps"),
+        EC(SM, "rmsnorm_heads_rows_gemma", &ops::rmsnorm_heads_rows_gemma, &launch_heads_rows,
+           "out,in,w,n_tokens,n_heads,head_dim,eps"),
+        E(SM, rope_prefill, GEO_THREADS, "x,n_tokens,n_heads,head_dim,pos0,theta"),
+        E(SM, kv_append_rows, GEO_THREADS, "cache,src,n_tokens,row,pos0"),
+        E(SM, embed_lookup_rows, GEO_THREADS, "out,table,tokens,n_tokens,n"),
     };
     return t;
 }

@@ -583,6 +583,156 @@ __global__ void multinomial_strided(float* out, uint32_t* idx_out, const float* 
     idx_out[0] = chosen;
 }
 
+// ---- prefill shapes (llm_sampling.cl:495-736) -------------------------------
+// Row-major [row][col] everywhere, as in the reference. Row reductions run one
+// warp per row (the reference walks a row with one thread); elementwise work is
+// one thread per element.
+XP_DEV uint32_t warp_gid() { return blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); }
+
+// softmax_rows_stats (:527-546): stats[2r] = row max, stats[2r + 1] = row sum
+// of exp(x - max); a fully masked row gives (0, 1).
+__global__ void softmax_rows_stats(float* stats, const float* x, uint32_t n_rows, uint32_t n_cols) {
+    const uint32_t r = warp_gid(), lane = threadIdx.x & 31;
+    if (r >= n_rows) return;
+    const float* row = x + (size_t)r * n_cols;
+    float m = -INFINITY;
+    for (uint32_t j = lane; j < n_cols; j += 32) m = fmaxf(m, row[j]);
+    m = warp_max(m);
+    if (!isfinite(m)) {
+        if (lane == 0) { stats[2 * r] = 0.0f; stats[2 * r + 1] = 1.0f; }
+        return;
+    }
+    float s = 0.0f;
+    for (uint32_t j = lane; j < n_cols; j += 32) s += expf(row[j] - m);
+    s = warp_sum(s);
+    if (lane == 0) { stats[2 * r] = m; stats[2 * r + 1] = s; }
+}
+
+// softmax_rows_apply (:549-556)
+__global__ void softmax_rows_apply(float* x, const float* stats, uint32_t n_rows, uint32_t n_cols) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_rows * n_cols) return;
+    const uint32_t r = (uint32_t)(i / n_cols);
+    x[i] = expf(x[i] - stats[2 * r]) / stats[2 * r + 1];
+}
+
+// attention_scores_prefill (:574-602): scores[(h*n_query + qi)*seq_len + t],
+// causal (t <= q_offset + qi) and sliding-window (t > qpos - window) masks
+// folded in as -inf. One warp per score; lanes split head_dim.
+__global__ void attention_scores_prefill(float* scores, const float* q, const float* kcache, uint32_t n_heads,
+                                         uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                         uint32_t seq_len, uint32_t q_offset, uint32_t window, float scale) {
+    const uint64_t i = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint32_t lane = threadIdx.x & 31;
+    if (i >= (uint64_t)n_heads * n_query * seq_len) return;
+    const uint32_t t = (uint32_t)(i % seq_len);
+    const uint32_t hq = (uint32_t)(i / seq_len);
+    const uint32_t qi = hq % n_query, h = hq / n_query;
+    const uint32_t qpos = q_offset + qi;
+    if (t > qpos || (window != 0u && t + window <= qpos)) {
+        if (lane == 0) scores[i] = -INFINITY;
+        return;
+    }
+    const uint32_t kvh = h / (n_heads / kv_heads);
+    const float* qr = q + (size_t)hq * head_dim;
+    const float* kr = kcache + ((size_t)t * kv_heads + kvh) * head_dim;
+    float acc = 0.0f;
+    for (uint32_t d = lane; d < head_dim; d += 32) acc += qr[d] * kr[d];
+    acc = warp_sum(acc);
+    if (lane == 0) scores[i] = acc * scale;
+}
+
+// attention_apply_prefill (:605-630): out[(h*n_query + qi)*head_dim + d] =
+// sum_t probs[(h*n_query + qi)*seq_len + t] v[t][kvh][d]; one thread per output
+// (a warp shares one probability row and reads 32 consecutive v values).
+__global__ void attention_apply_prefill(float* out, const float* probs, const float* vcache, uint32_t n_heads,
+                                        uint32_t kv_heads, uint32_t head_dim, uint32_t n_query,
+                                        uint32_t seq_len) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_heads * n_query * head_dim) return;
+    const uint32_t d = (uint32_t)(i % head_dim);
+    const uint32_t hq = (uint32_t)(i / head_dim);
+    const uint32_t h = hq / n_query;
+    const uint32_t kvh = h / (n_heads / kv_heads);
+    const float* p = probs + (size_t)hq * seq_len;
+    const size_t vstride = (size_t)kv_heads * head_dim;
+    const float* v = vcache + (size_t)kvh * head_dim + d;
+    float acc = 0.0f;
+    for (uint32_t t = 0; t < seq_len; ++t) acc += p[t] * v[t * vstride];
+    out[i] = acc;
+}
+
+// rmsnorm_rows_sumsq (:634-642): one warp per row
+__global__ void rmsnorm_rows_sumsq(float* rowss, const float* in, uint32_t n_rows, uint32_t n) {
+    const uint32_t r = warp_gid(), lane = threadIdx.x & 31;
+    if (r >= n_rows) return;
+    const float* row = in + (size_t)r * n;
+    float ss = 0.0f;
+    for (uint32_t j = lane; j < n; j += 32) ss += row[j] * row[j];
+    ss = warp_sum(ss);
+    if (lane == 0) rowss[r] = ss;
+}
+
+// rmsnorm_rows_apply_gemma (:645-656): Gemma's (1 + w), w shared across rows
+__global__ void rmsnorm_rows_apply_gemma(float* out, const float* in, const float* w, const float* rowss,
+                                         uint32_t n_rows, uint32_t n, float eps) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_rows * n) return;
+    const uint32_t r = (uint32_t)(i / n), j = (uint32_t)(i - (uint64_t)r * n);
+    const float scale = rsqrtf(rowss[r] / (float)n + eps);
+    out[i] = in[i] * scale * (1.0f + w[j]);
+}
+
+// rmsnorm_heads_rows_gemma (:659-675): QK-norm over [token][head][head_dim];
+// one warp per (token, head) writes its whole head.
+__global__ void rmsnorm_heads_rows_gemma(float* out, const float* in, const float* w, uint32_t n_tokens,
+                                         uint32_t n_heads, uint32_t head_dim, float eps) {
+    const uint32_t th = warp_gid(), lane = threadIdx.x & 31;
+    if (th >= n_tokens * n_heads) return;
+    const float* x = in + (size_t)th * head_dim;
+    float ss = 0.0f;
+    for (uint32_t k = lane; k < head_dim; k += 32) ss += x[k] * x[k];
+    ss = warp_sum(ss);
+    const float scale = rsqrtf(ss / (float)head_dim + eps);
+    for (uint32_t d = lane; d < head_dim; d += 32) out[(size_t)th * head_dim + d] = x[d] * scale * (1.0f + w[d]);
+}
+
+// rope_prefill (:687-711): rotate-half RoPE over [token][head][head_dim], the
+// position of token ti being pos0 + ti; one thread per (token, head, pair),
+// the same angle and expressions as the decode `rope` at that position, so a
+// position rotates bit-identically through either entry point.
+__global__ void rope_prefill(float* x, uint32_t n_tokens, uint32_t n_heads, uint32_t head_dim, uint32_t pos0,
+                             float theta) {
+    const uint32_t half = head_dim >> 1;
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_tokens * n_heads * half) return;
+    const uint32_t d = (uint32_t)(i % half);
+    const uint32_t th = (uint32_t)(i / half);
+    const uint32_t ti = th / n_heads;
+    const size_t base = (size_t)th * head_dim + d;
+    float c, s;
+    rope_cs(d, head_dim, pos0 + ti, theta, c, s);
+    const float lo = x[base], hi = x[base + half];
+    x[base] = lo * c - hi * s;
+    x[base + half] = lo * s + hi * c;
+}
+
+// kv_append_rows (:714-722): n_tokens rows of `row` floats at row pos0
+__global__ void kv_append_rows(float* cache, const float* src, uint32_t n_tokens, uint32_t row, uint32_t pos0) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_tokens * row) return;
+    cache[(size_t)pos0 * row + i] = src[i];
+}
+
+// embed_lookup_rows (:728-736): out[ti][j] = table[tokens[ti]][j]
+__global__ void embed_lookup_rows(float* out, const float* table, const uint32_t* tokens, uint32_t n_tokens,
+                                  uint32_t n) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)n_tokens * n) return;
+    const uint32_t ti = (uint32_t)(i / n), j = (uint32_t)(i - (uint64_t)ti * n);
+    out[i] = table[(size_t)tokens[ti] * n + j];
+}
+
 #undef GID
 }  // namespace ops
 }  // namespace xp
