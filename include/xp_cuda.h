@@ -298,6 +298,30 @@ typedef struct xp_layer_weights {
 xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sampling* sp,
                             const xp_layer_weights* layers, const uint32_t* lm_words, const uint32_t* lm_scales,
                             const float* final_norm, const float* embed, xp_session** out);
+/* A session from a GGUF model file: the reference's real-weight load path
+ * (examples/llm/decode.cpp:1418-1535, DecodeSession::DecodeSession). Shapes
+ * come from the file's metadata (DecodeConfig::from_model, decode.cpp:258-275);
+ * `policy` (may be NULL) supplies max_seq, global_every, sliding_window (if
+ * non-zero), rope_theta_local (if > 0), embed_scale and attn_scale. Tensors of
+ * ggml types F32, F16, BF16, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K and Q6_K are
+ * dequantised on the device and packed to KM4 + bf16 (bit-exact with the
+ * reference packer); norm weights are stored as (1 + w) and loaded as w; the
+ * output head is token_embd unless the file has output.weight. `pack_cache`:
+ * NULL = "<gguf_path>.xpack", "" = no cache, else a path. A valid cache
+ * (the reference's .xpack format, decode.cpp:711-1328, same validation rules)
+ * is loaded instead of packing; otherwise the planes are packed and the cache
+ * is written through "<cache>.tmp" + rename. */
+xp_status xp_session_create_gguf(int device, const char* gguf_path, const xp_model_config* policy,
+                                 const xp_sampling* sp, const char* pack_cache, xp_session** out);
+/* How a GGUF session's weights were loaded: from the cache, whether a cache
+ * was written, and a one-line description (truncated to msg_bytes). */
+xp_status xp_session_load_info(xp_session* s, int* from_cache, int* cache_written, char* msg, uint32_t msg_bytes);
+/* The session's effective model configuration. */
+xp_status xp_session_config(xp_session* s, xp_model_config* cfg);
+/* Dequantise n elements of a ggml block type on the device (src, dst device
+ * pointers): examples/llm/model/gguf.cpp:448-634 GGUFFile::dequantize, bit-exact.
+ * Types as for xp_session_create_gguf. */
+xp_status xp_gguf_dequantize(void* stream, uint32_t ggml_type, const void* src, float* dst, uint64_t n);
 xp_status xp_session_destroy(xp_session* s);
 /* Stream id used for tensor (layer, which) by create_random; which: 0..6 the
  * matrices q,k,v,o,gate,up,down; 7..12 the norms; layer = n_layers: 0 embed,

@@ -37,6 +37,16 @@ int xpref_pack_km4bf16(const float* w_cols_rows, uint32_t rows, uint32_t cols,
 }
 
 float xpref_best_bf16_scale(const float* blk32, float s0) { return best_bf16_scale(blk32, s0); }
+
+// examples/llm/model/gguf.cpp GGUFFile::dequantize, for the GGUF-type pins
+int xpref_gguf_dequantize(uint32_t type, const void* src, float* dst, uint64_t n) {
+    return GGUFFile::dequantize(static_cast<GGMLType>(type), src, dst, (size_t)n) ? 0 : -1;
+}
+// the .xpack payload hash (decode.cpp:784-834)
+uint64_t xpref_xpack_hash(const void* data, uint64_t n) { return xpack_hash(data, (size_t)n); }
+uint64_t xpref_xpack_hash_mt(const void* data, uint64_t n, uint32_t threads) {
+    return xpack_hash_mt(data, (size_t)n, threads);
+}
 uint32_t xpref_quantise(float v, float inv) { return quantise(v, inv); }
 
 uint64_t xpref_plan_weight_bytes(void) {
@@ -52,6 +62,10 @@ struct xpref_session { std::unique_ptr<DecodeSession> s; std::string err; };
 static thread_local std::string g_sess_err;
 const char* xpref_session_error(void) { return g_sess_err.c_str(); }
 
+// The .xpack cache the next xpref_session_create uses (empty: none)
+static std::string g_pack_cache;
+void xpref_set_pack_cache(const char* path) { g_pack_cache = path ? path : ""; }
+
 void* xpref_session_create(const char* gguf_path, const char* kernel_dir, uint32_t max_seq,
                            int greedy, float temperature, uint32_t top_k, float top_p,
                            uint64_t seed, uint32_t global_every) {
@@ -62,7 +76,8 @@ void* xpref_session_create(const char* gguf_path, const char* kernel_dir, uint32
         p.transformer_spv = kd + "/llm_transformer.spv";
         p.sampling_spv = kd + "/llm_sampling.spv";
         p.model_gguf = gguf_path;
-        p.use_pack_cache = false;
+        p.use_pack_cache = !g_pack_cache.empty();
+        p.pack_cache = g_pack_cache;
         DecodeConfig c;
         c.max_seq = max_seq;
         c.sampling.mode = greedy ? SampleMode::Greedy : SampleMode::Temperature;

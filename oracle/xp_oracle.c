@@ -621,3 +621,141 @@ void xo_embed_lookup_rows(float* out, const float* table, const uint32_t* tokens
     for (uint32_t t = 0; t < n_tokens; ++t)
         memcpy(out + (size_t)t * n, table + (size_t)tokens[t] * n, (size_t)n * sizeof(float));
 }
+
+/* ------------------------------------------------------------------------ */
+/* GGUF tensor types: examples/llm/model/gguf.cpp:448-634 (the ggml blocks)  */
+/* ------------------------------------------------------------------------ */
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static uint32_t rd32(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24); }
+
+/* gguf.cpp:431-443: the 6-bit scale and min of Q4_K sub-block j */
+static void k4_scale_min(int j, const uint8_t* q, uint8_t* d, uint8_t* m) {
+    if (j < 4) {
+        *d = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *d = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+        *m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+    }
+}
+
+int xo_gguf_dequantize(uint32_t type, const void* src, float* dst, uint64_t n) {
+    const uint8_t* p = (const uint8_t*)src;
+    switch (type) {
+        case 0: memcpy(dst, p, n * 4); return 0;
+        case 1:
+            for (uint64_t i = 0; i < n; ++i) dst[i] = xo_f16_to_f32(rd16(p + 2 * i));
+            return 0;
+        case 30:
+            for (uint64_t i = 0; i < n; ++i) {
+                const uint32_t b = (uint32_t)rd16(p + 2 * i) << 16;
+                memcpy(dst + i, &b, 4);
+            }
+            return 0;
+        case 2: case 3: case 6: case 7: case 8: {
+            if (n % 32) return -1;
+            const uint32_t bs = type == 2 ? 18 : type == 3 ? 20 : type == 6 ? 22 : type == 7 ? 24 : 34;
+            for (uint64_t b = 0; b < n / 32; ++b) {
+                const uint8_t* blk = p + b * bs;
+                const float d = xo_f16_to_f32(rd16(blk));
+                float* y = dst + b * 32;
+                if (type == 8) {
+                    for (int j = 0; j < 32; ++j) y[j] = (float)(int8_t)blk[2 + j] * d;
+                } else if (type == 2 || type == 3) {
+                    const float m = type == 3 ? xo_f16_to_f32(rd16(blk + 2)) : 0.0f;
+                    const uint8_t* qs = blk + (type == 3 ? 4 : 2);
+                    for (int j = 0; j < 16; ++j) {
+                        if (type == 2) {
+                            y[j] = (float)((int)(qs[j] & 0xF) - 8) * d;
+                            y[j + 16] = (float)((int)(qs[j] >> 4) - 8) * d;
+                        } else {
+                            y[j] = (float)(qs[j] & 0xF) * d + m;
+                            y[j + 16] = (float)(qs[j] >> 4) * d + m;
+                        }
+                    }
+                } else {
+                    const int one = type == 7;
+                    const float m = one ? xo_f16_to_f32(rd16(blk + 2)) : 0.0f;
+                    const uint32_t qh = rd32(blk + (one ? 4 : 2));
+                    const uint8_t* qs = blk + (one ? 8 : 6);
+                    for (int j = 0; j < 16; ++j) {
+                        const int q0 = (qs[j] & 0xF) | (int)(((qh >> j) << 4) & 0x10);
+                        const int q1 = (qs[j] >> 4) | (int)((qh >> (j + 12)) & 0x10);
+                        if (one) {
+                            y[j] = (float)q0 * d + m;
+                            y[j + 16] = (float)q1 * d + m;
+                        } else {
+                            y[j] = (float)(q0 - 16) * d;
+                            y[j + 16] = (float)(q1 - 16) * d;
+                        }
+                    }
+                }
+            }
+            return 0;
+        }
+        case 12:
+            if (n % 256) return -1;
+            for (uint64_t b = 0; b < n / 256; ++b) {
+                const uint8_t* blk = p + b * 144;
+                const float d = xo_f16_to_f32(rd16(blk)), dmin = xo_f16_to_f32(rd16(blk + 2));
+                const uint8_t* sc = blk + 4;
+                for (int e = 0; e < 256; ++e) {
+                    const int c = e / 64, w = e % 64, is = 2 * c + (w >= 32), l = w % 32;
+                    const uint8_t qb = blk[16 + 32 * c + l];
+                    const int q = w < 32 ? (qb & 0xF) : (qb >> 4);
+                    uint8_t s, m;
+                    k4_scale_min(is, sc, &s, &m);
+                    const float d1 = d * (float)s, m1 = dmin * (float)m;
+                    dst[b * 256 + e] = d1 * (float)q - m1;
+                }
+            }
+            return 0;
+        case 14:
+            if (n % 256) return -1;
+            for (uint64_t b = 0; b < n / 256; ++b) {
+                const uint8_t* blk = p + b * 210;
+                const float d = xo_f16_to_f32(rd16(blk + 208));
+                for (int e = 0; e < 256; ++e) {
+                    const int h = e / 128, r = e % 128, g = r / 32, l = r % 32, is = l / 16;
+                    const uint8_t* ql = blk + 64 * h;
+                    const uint8_t qh = blk[128 + 32 * h + l];
+                    const int8_t s = (int8_t)blk[192 + 8 * h + is + 2 * g];
+                    const uint8_t lo = (g & 1) ? ql[l + 32] : ql[l];
+                    const int nib = (g < 2) ? (lo & 0xF) : (lo >> 4);
+                    const int q = (nib | (((qh >> (2 * g)) & 3) << 4)) - 32;
+                    dst[b * 256 + e] = d * (float)s * (float)q;
+                }
+            }
+            return 0;
+        default:
+            return -1;
+    }
+}
+
+/* decode.cpp:784-799 */
+uint64_t xo_xpack_hash(const void* data, uint64_t nbytes) {
+    const uint8_t* p = (const uint8_t*)data;
+    uint64_t h = 1469598103934665603ull ^ nbytes;
+    uint64_t i = 0;
+    for (; i + 8 <= nbytes; i += 8) {
+        uint64_t w;
+        memcpy(&w, p + i, 8);
+        h = (h ^ w) * 1099511628211ull;
+        h ^= h >> 29;
+    }
+    for (; i < nbytes; ++i) h = (h ^ p[i]) * 1099511628211ull;
+    h ^= h >> 32;
+    h *= 0xff51afd7ed558ccdull;
+    h ^= h >> 32;
+    return h;
+}
+
+/* decode.cpp:803-834: per-4-MiB-chunk hashes folded in chunk order */
+uint64_t xo_xpack_hash_chunked(const void* data, uint64_t nbytes) {
+    const uint64_t chunk = 4ull << 20;
+    const uint8_t* p = (const uint8_t*)data;
+    uint64_t acc = 1469598103934665603ull ^ nbytes;
+    for (uint64_t off = 0; off < nbytes; off += chunk)
+        acc = (acc ^ xo_xpack_hash(p + off, nbytes - off < chunk ? nbytes - off : chunk)) * 1099511628211ull;
+    return acc;
+}

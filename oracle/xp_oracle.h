@@ -75,6 +75,16 @@ uint32_t xo_topk(const float* x, uint32_t n, uint32_t k, float* vals, uint32_t* 
 uint32_t xo_sample(const float* logits, uint32_t n, float temperature, uint32_t top_k,
                    float top_p, float u);
 
+/* ---- GGUF tensor types (ggml block formats, examples/llm/model/gguf.cpp:448-634)
+ * type: 0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 6 Q5_0, 7 Q5_1, 8 Q8_0, 12 Q4_K, 14 Q6_K,
+ * 30 BF16. n elements (a multiple of the block size). Returns 0, or -1 for a
+ * type that is not dequantised. */
+int xo_gguf_dequantize(uint32_t type, const void* src, float* dst, uint64_t n);
+/* the .xpack payload hash (examples/llm/decode.cpp:784-834): FNV-1a over
+ * 64-bit words with a final avalanche, folded over 4 MiB chunks */
+uint64_t xo_xpack_hash(const void* data, uint64_t nbytes);
+uint64_t xo_xpack_hash_chunked(const void* data, uint64_t nbytes);
+
 /* ---- prefill shapes (kernels/llm_sampling.cl:495-736) ------------------ */
 void xo_softmax_rows_stats(float* stats, const float* x, uint32_t n_rows, uint32_t n_cols);
 void xo_softmax_rows_apply(float* x, const float* stats, uint32_t n_rows, uint32_t n_cols);

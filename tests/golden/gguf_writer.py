@@ -36,7 +36,8 @@ def write_gguf(path, meta, tensors):
     """meta: list of (key, type, value) or (key, ARR, (elem_type, values)).
     tensors: list of (name, shape_fastest_first, float32 array in row-major
     order of the reversed shape); the array may instead be a callable that
-    returns it, so a large model is generated one tensor at a time."""
+    returns it, so a large model is generated one tensor at a time, or a
+    ("raw", ggml_type, bytes) tuple holding the tensor already encoded."""
     out = bytearray()
     out += struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(meta))
     for key, t, v in meta:
@@ -51,24 +52,29 @@ def write_gguf(path, meta, tensors):
     offs = []
     off = 0
     for name, shape, arr in tensors:
-        nbytes = 4 * int(np.prod(shape))
-        if not callable(arr):
+        raw = isinstance(arr, tuple)
+        nbytes = len(arr[2]) if raw else 4 * int(np.prod(shape))
+        if not raw and not callable(arr):
             assert np.asarray(arr).size * 4 == nbytes
         offs.append(off)
         out += _s(name) + struct.pack("<I", len(shape))
         for d in shape:
             out += struct.pack("<Q", d)
-        out += struct.pack("<IQ", 0, off)  # type F32
+        out += struct.pack("<IQ", arr[1] if raw else 0, off)  # ggml type (0 = F32)
         off += (nbytes + ALIGN - 1) // ALIGN * ALIGN
     pad = (-len(out)) % ALIGN
     out += b"\0" * pad
     with open(path, "wb") as f:
         f.write(out)
         for (name, shape, arr), o in zip(tensors, offs):
-            a = np.ascontiguousarray(arr() if callable(arr) else arr, np.float32)
-            assert a.nbytes == 4 * int(np.prod(shape))
-            f.write(a.tobytes())
-            f.write(b"\0" * ((-a.nbytes) % ALIGN))
+            if isinstance(arr, tuple):
+                b = arr[2]
+            else:
+                a = np.ascontiguousarray(arr() if callable(arr) else arr, np.float32)
+                assert a.nbytes == 4 * int(np.prod(shape))
+                b = a.tobytes()
+            f.write(b)
+            f.write(b"\0" * ((-len(b)) % ALIGN))
 
 
 def gemma3_meta(cfg, rope_base, window):

@@ -301,3 +301,38 @@ def test_prefill_plumbing_bitexact():
     O.ref_launch("embed_lookup_rows", T37 * H, er, table, toks, T37, H)
     O.oracle().xo_embed_lookup_rows(eo, table, toks, T37, H)
     assert np.array_equal(er, eo)
+
+
+# ---- GGUF tensor types (examples/llm/model/gguf.cpp:448-634) and the .xpack
+# payload hash (examples/llm/decode.cpp:784-834)
+@pytest.mark.parametrize("ggml_type", [0, 1, 30, 2, 3, 6, 7, 8, 12, 14])
+def test_gguf_dequantize_bitexact(ggml_type):
+    import ctypes as C
+    from gguf_blocks import random_blocks
+    n = 256 * 37
+    raw = random_blocks(ggml_type, n, seed=ggml_type)
+    want, got = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    lib = O.ref()
+    lib.xpref_gguf_dequantize.argtypes = [C.c_uint32, C.c_char_p, O.f32p, C.c_uint64]
+    assert lib.xpref_gguf_dequantize(ggml_type, raw, want, n) == 0
+    O.oracle().xo_gguf_dequantize.argtypes = [C.c_uint32, C.c_char_p, O.f32p, C.c_uint64]
+    assert O.oracle().xo_gguf_dequantize(ggml_type, raw, got, n) == 0
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("nbytes", [0, 7, 8, 4096 + 3, (4 << 20) * 2 + 12345])
+def test_xpack_hash_matches(nbytes):
+    import ctypes as C
+    data = np.random.default_rng(nbytes).integers(0, 256, nbytes, dtype=np.uint8).tobytes()
+    lib, o = O.ref(), O.oracle()
+    lib.xpref_xpack_hash.restype = C.c_uint64
+    lib.xpref_xpack_hash.argtypes = [C.c_char_p, C.c_uint64]
+    lib.xpref_xpack_hash_mt.restype = C.c_uint64
+    lib.xpref_xpack_hash_mt.argtypes = [C.c_char_p, C.c_uint64, C.c_uint32]
+    o.xo_xpack_hash.restype = C.c_uint64
+    o.xo_xpack_hash.argtypes = [C.c_char_p, C.c_uint64]
+    o.xo_xpack_hash_chunked.restype = C.c_uint64
+    o.xo_xpack_hash_chunked.argtypes = [C.c_char_p, C.c_uint64]
+    assert o.xo_xpack_hash(data, nbytes) == lib.xpref_xpack_hash(data, nbytes)
+    assert o.xo_xpack_hash_chunked(data, nbytes) == lib.xpref_xpack_hash_mt(data, nbytes, 1)
+    assert o.xo_xpack_hash_chunked(data, nbytes) == lib.xpref_xpack_hash_mt(data, nbytes, 4)

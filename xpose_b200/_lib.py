@@ -130,6 +130,11 @@ _SIGS = {
     "xp_stream4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     "xp_session_create_random": (C.c_int, [C.c_int, C.POINTER(ModelConfig), C.POINTER(Sampling), C.c_uint64,
                                            C.POINTER(C.c_void_p)]),
+    "xp_session_create_gguf": (C.c_int, [C.c_int, C.c_char_p, C.POINTER(ModelConfig), C.POINTER(Sampling),
+                                         C.c_char_p, C.POINTER(C.c_void_p)]),
+    "xp_session_load_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_char_p, C.c_uint32]),
+    "xp_session_config": (C.c_int, [C.c_void_p, C.POINTER(ModelConfig)]),
+    "xp_gguf_dequantize": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_uint64]),
     "xp_session_create": (C.c_int, [C.c_int, C.POINTER(ModelConfig), C.POINTER(Sampling), C.POINTER(LayerWeights),
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "xp_session_destroy": (C.c_int, [C.c_void_p]),

@@ -86,6 +86,8 @@ struct xp_session {
     cudaEvent_t ev_done = nullptr, ev_a = nullptr, ev_b = nullptr;
     uint32_t host_pos = 0;
     bool have_logits = false;
+    std::string load_info;                   // how the weights were loaded (GGUF sessions)
+    int load_from_cache = 0, load_cache_written = 0;
     uint32_t kernels_per_token = 0;
     uint64_t weight_bytes = 0;
     uint32_t nsplit_global = 0, nsplit_local = 0;

@@ -1,6 +1,7 @@
 // Single translation unit of libxp_cuda.so (kernels are defined in headers).
 #include "capi.cuh"
 #include "engine.cuh"
+#include "gguf_model.cuh"
 
 // ---------------------------------------------------------------------------
 // Attention without caller-provided scratch.

@@ -97,6 +97,32 @@ class DecodeSession:
         return DecodeSession(h, cfg, sampling)
 
     @staticmethod
+    def from_gguf(path, sampling=None, max_seq=8192, global_every=6, pack_cache=None, device=0, policy=None):
+        """A session from a GGUF model file (C ABI xp_session_create_gguf):
+        shapes from the file, max_seq / global_every (or a whole DecodeConfig
+        `policy`) from the caller. pack_cache: None = "<path>.xpack", "" = no
+        cache, else the cache path."""
+        sampling = sampling or Sampling()
+        pol = policy or DecodeConfig(max_seq=max_seq, global_every=global_every, sliding_window=0)
+        h = C.c_void_p()
+        c, s = pol._c(), sampling._c()
+        pc = None if pack_cache is None else pack_cache.encode()
+        check(lib().xp_session_create_gguf(device, path.encode(), C.byref(c), C.byref(s), pc, C.byref(h)))
+        got = ModelConfig()
+        check(lib().xp_session_config(h, C.byref(got)))
+        cfg = DecodeConfig(got.n_layers, got.hidden, got.ffn, got.n_heads, got.n_kv_heads, got.head_dim, got.vocab,
+                           got.max_seq, got.sliding_window, got.global_every, got.rms_eps, got.rope_theta_global,
+                           got.rope_theta_local, got.embed_scale, got.attn_scale)
+        return DecodeSession(h, cfg, sampling)
+
+    def load_info(self):
+        """(loaded from the cache, wrote the cache, description) of a GGUF session."""
+        fc, cw = C.c_int(), C.c_int()
+        buf = C.create_string_buffer(512)
+        check(lib().xp_session_load_info(self._h, C.byref(fc), C.byref(cw), buf, 512))
+        return bool(fc.value), bool(cw.value), buf.value.decode()
+
+    @staticmethod
     def from_weights(cfg, weights, sampling=None, device=0):
         """weights: dict with 'layers' (list of dicts: words[7], scales[7], norms
         attn/post_attn/ffn/post_ffn/q/k), 'lm_words', 'lm_scales', 'final_norm',
