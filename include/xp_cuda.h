@@ -322,6 +322,39 @@ xp_status xp_session_config(xp_session* s, xp_model_config* cfg);
  * pointers): examples/llm/model/gguf.cpp:448-634 GGUFFile::dequantize, bit-exact.
  * Types as for xp_session_create_gguf. */
 xp_status xp_gguf_dequantize(void* stream, uint32_t ggml_type, const void* src, float* dst, uint64_t n);
+/* ---- tokenizer (examples/llm/model/tokenizer.{hpp,cpp}) --------------------
+ * The SentencePiece vocabulary of a GGUF file (tokenizer.ggml.*): encode with
+ * CONTROL/UNKNOWN tokens cut out first, the leading space marker, best-score
+ * merges (ties: leftmost) and byte fallback; decode with special tokens
+ * optionally skipped and one leading space dropped. Host only (no GPU).
+ * Encode/decode/piece: pass a NULL buffer to get the size first. */
+typedef struct xp_tokenizer xp_tokenizer;
+xp_status xp_tokenizer_create(const char* gguf_path, xp_tokenizer** out);   /* Tokenizer::from_gguf */
+void xp_tokenizer_destroy(xp_tokenizer* t);
+xp_status xp_tokenizer_info(const xp_tokenizer* t, uint32_t* vocab, int32_t* bos, int32_t* eos, int32_t* unk,
+                            int32_t* pad);
+xp_status xp_tokenizer_encode(const xp_tokenizer* t, const char* text, size_t len, int add_bos, int add_eos,
+                              int32_t* ids, uint32_t cap, uint32_t* n);   /* Tokenizer::encode */
+xp_status xp_tokenizer_decode(const xp_tokenizer* t, const int32_t* ids, uint32_t n, int skip_special, char* out,
+                              size_t cap, size_t* len);                    /* Tokenizer::decode */
+xp_status xp_tokenizer_piece(const xp_tokenizer* t, int32_t id, char* out, size_t cap, size_t* len); /* decode_one */
+
+/* ---- chat front-end (android/app/src/main/cpp/llm_jni.cpp:59-186) ---------
+ * create: a GGUF session + its tokenizer; sampling NULL = temperature 0.7,
+ * top-k 64, top-p 0.95, seed 1234. prefill: `text` in the Gemma turn template
+ * ("<start_of_turn>user\n...<end_of_turn>\n<start_of_turn>model\n", a "\n"
+ * before later turns), BOS on the first turn only. step: one token's text, or
+ * *done = 1 at <end_of_turn>, EOS or a full KV cache. metrics: {ms, tok/s,
+ * kernels, submits, position, record_ms, gpu_ms} of the last step. */
+typedef struct xp_chat xp_chat;
+xp_status xp_chat_create(int device, const char* gguf_path, uint32_t max_seq, const xp_sampling* sp,
+                         const char* pack_cache, xp_chat** out);
+xp_status xp_chat_prefill(xp_chat* c, const char* text, uint32_t* n_tokens);
+xp_status xp_chat_step(xp_chat* c, char* piece, size_t cap, int* done);
+xp_status xp_chat_metrics(const xp_chat* c, double out[7]);
+xp_status xp_chat_session(xp_chat* c, xp_session** s);
+xp_status xp_chat_reset(xp_chat* c);
+void xp_chat_destroy(xp_chat* c);
 xp_status xp_session_destroy(xp_session* s);
 /* Stream id used for tensor (layer, which) by create_random; which: 0..6 the
  * matrices q,k,v,o,gate,up,down; 7..12 the norms; layer = n_layers: 0 embed,

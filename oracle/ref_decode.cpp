@@ -62,6 +62,32 @@ struct xpref_session { std::unique_ptr<DecodeSession> s; std::string err; };
 static thread_local std::string g_sess_err;
 const char* xpref_session_error(void) { return g_sess_err.c_str(); }
 
+// examples/llm/model/tokenizer.cpp over a GGUF file, for the tokenizer pins
+struct xpref_tok { GGUFFile f; std::unique_ptr<Tokenizer> t; };
+void* xpref_tok_create(const char* path) {
+    try {
+        auto* h = new xpref_tok{GGUFFile::open(path), nullptr};
+        h->t = std::make_unique<Tokenizer>(Tokenizer::from_gguf(h->f));
+        return h;
+    } catch (const std::exception& e) { g_sess_err = e.what(); return nullptr; }
+}
+void xpref_tok_destroy(void* h) { delete (xpref_tok*)h; }
+int xpref_tok_encode(void* h, const char* text, size_t len, int bos, int eos, int32_t* out, uint32_t cap) {
+    auto v = ((xpref_tok*)h)->t->encode(std::string_view(text, len), bos != 0, eos != 0);
+    for (size_t i = 0; i < v.size() && i < cap; ++i) out[i] = v[i];
+    return (int)v.size();
+}
+long xpref_tok_piece(void* h, int32_t id, char* out, size_t cap) {
+    std::string s = ((xpref_tok*)h)->t->decode_one(id);
+    if (s.size() + 1 <= cap) std::memcpy(out, s.c_str(), s.size() + 1);
+    return (long)s.size();
+}
+long xpref_tok_decode(void* h, const int32_t* ids, uint32_t n, int skip, char* out, size_t cap) {
+    std::string s = ((xpref_tok*)h)->t->decode(std::vector<int32_t>(ids, ids + n), skip != 0);
+    if (s.size() + 1 <= cap) std::memcpy(out, s.c_str(), s.size() + 1);
+    return (long)s.size();
+}
+
 // The .xpack cache the next xpref_session_create uses (empty: none)
 static std::string g_pack_cache;
 void xpref_set_pack_cache(const char* path) { g_pack_cache = path ? path : ""; }

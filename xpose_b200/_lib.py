@@ -130,6 +130,21 @@ _SIGS = {
     "xp_stream4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     "xp_session_create_random": (C.c_int, [C.c_int, C.POINTER(ModelConfig), C.POINTER(Sampling), C.c_uint64,
                                            C.POINTER(C.c_void_p)]),
+    "xp_tokenizer_create": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "xp_tokenizer_destroy": (None, [C.c_void_p]),
+    "xp_tokenizer_info": (C.c_int, [C.c_void_p] + [C.c_void_p] * 5),
+    "xp_tokenizer_encode": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_uint32,
+                                      C.POINTER(C.c_uint32)]),
+    "xp_tokenizer_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_int, C.c_char_p, C.c_size_t,
+                                      C.POINTER(C.c_size_t)]),
+    "xp_tokenizer_piece": (C.c_int, [C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "xp_chat_create": (C.c_int, [C.c_int, C.c_char_p, C.c_uint32, C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+    "xp_chat_prefill": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_uint32)]),
+    "xp_chat_step": (C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t, C.POINTER(C.c_int)]),
+    "xp_chat_metrics": (C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
+    "xp_chat_session": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "xp_chat_reset": (C.c_int, [C.c_void_p]),
+    "xp_chat_destroy": (None, [C.c_void_p]),
     "xp_session_create_gguf": (C.c_int, [C.c_int, C.c_char_p, C.POINTER(ModelConfig), C.POINTER(Sampling),
                                          C.c_char_p, C.POINTER(C.c_void_p)]),
     "xp_session_load_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_char_p, C.c_uint32]),

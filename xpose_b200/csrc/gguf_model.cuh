@@ -139,6 +139,9 @@ struct GgufValue {
     double f = 0;        // floats
     std::string s;       // strings
     uint64_t count = 0;  // arrays: element count
+    uint32_t elem_type = 0;         // arrays: element type
+    std::vector<std::string> strs;  // string arrays
+    std::vector<double> nums;       // numeric arrays
 };
 
 class GgufFile {
@@ -258,15 +261,21 @@ class GgufFile {
                 uint64_t n = 0;
                 if (!rd(et) || !rd(n)) return bad("truncated array");
                 v.count = n;
-                for (uint64_t k = 0; k < n; ++k) {
-                    if (et == 8) {
-                        std::string s;
-                        if (!rd_str(s, version)) return bad("truncated string array");
-                    } else {
-                        const size_t sz = scalar_size(et);
-                        if (!sz || !need(sz * (n - k))) return bad("truncated or nested array");
-                        pos += sz * (n - k);
-                        break;
+                v.elem_type = et;
+                if (et == 8) {
+                    if (n > size) return bad("implausible string array");
+                    v.strs.resize(n);
+                    for (uint64_t k = 0; k < n; ++k)
+                        if (!rd_str(v.strs[k], version)) return bad("truncated string array");
+                } else {
+                    const size_t sz = scalar_size(et);
+                    if (!sz || n > size || !need(sz * n)) return bad("truncated or nested array");
+                    v.nums.resize(n);
+                    for (uint64_t k = 0; k < n; ++k) {
+                        GgufValue e;
+                        rd_scalar(et, e);
+                        v.nums[k] = (et == 6 || et == 12) ? e.f : (et == 1 || et == 3 || et == 5 || et == 11)
+                                                                      ? (double)(int64_t)e.u : (double)e.u;
                     }
                 }
             } else if (!rd_scalar(t, v)) {

@@ -2,6 +2,7 @@
 #include "capi.cuh"
 #include "engine.cuh"
 #include "gguf_model.cuh"
+#include "tokenizer.cuh"
 
 // ---------------------------------------------------------------------------
 // Attention without caller-provided scratch.
