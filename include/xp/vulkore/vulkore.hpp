@@ -12,6 +12,7 @@
 // Covers the API surface the reference's LLM engine uses. Not thread-safe per
 // Context (the reference's Context is single-threaded too).
 #pragma once
+#include <array>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -24,6 +25,12 @@
 #include <vector>
 
 #include "../../xp_cuda.h"
+
+#ifndef VK_VERSION_1_0
+// Vulkan's byte-size type, used by callers of the reference's buffer API
+// (include/vulkore/buffer.hpp) for offsets and sizes.
+typedef uint64_t VkDeviceSize;
+#endif
 
 namespace vulkore {
 
@@ -123,6 +130,10 @@ class Kernel {
   bool valid() const { return id_ >= 0; }
   const std::string& name() const { return name_; }
   xp_kernel id() const { return id_; }
+  // The reference's workgroup size query (include/vulkore/program.hpp:76):
+  // a Grid counts global threads, rounded up to groups of 64; the kernels
+  // here choose their own CTA shapes, so 64 is the grouping callers see.
+  std::array<uint32_t, 3> local_size() const { return {64u, 1u, 1u}; }
   Context& context() const { return *ctx_; }
 
  private:
