@@ -106,6 +106,8 @@ const std::vector<Entry>& table() {
         K(M_MV, ref_matvec, mv_reduce), K(M_MV, ref_matvec, mv_kmn),
         K(M_MV, ref_matvec, mv_km), K(M_MV, ref_matvec, mv_km4),
         K(M_MV, ref_matvec, mv_km4_c2), K(M_MV, ref_matvec, mv_km4_c4),
+        K(M_MV, ref_matvec, mv_km4_wg32), K(M_MV, ref_matvec, mv_km4_wg128),
+        K(M_MV, ref_matvec, mv_km4_wg256), K(M_MV, ref_matvec, mv_km4_c2_wg32),
         K(M_MV, ref_matvec, mv_km4_split), K(M_MV, ref_matvec, stream4),
         K(M_MV, ref_matvec, mv_km4_bs), K(M_MV, ref_matvec, mv_km4_bs_split),
         K(M_TF, ref_transformer, rmsnorm), K(M_TF, ref_transformer, rmsnorm_gemma),

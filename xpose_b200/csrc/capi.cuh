@@ -142,6 +142,22 @@ cudaError_t launch_heads_rows(const xp_arg* a, xp_grid, cudaStream_t st) {
         arg_as<uint32_t>(a[4]), arg_as<uint32_t>(a[5]), arg_as<float>(a[6]));
     return cudaGetLastError();
 }
+// The layout-study matvecs: one warp per (column, split); the reference grid
+// (a thread per column, per column pair or per (column, split)) is ignored.
+template <int L, bool SPLIT>
+cudaError_t launch_mv_layout(const xp_arg* a, xp_grid, cudaStream_t st) {
+    const uint32_t cols = arg_as<uint32_t>(a[5]), split = SPLIT ? arg_as<uint32_t>(a[6]) : 1u;
+    const uint64_t warps = (uint64_t)cols * split;
+    ops::mv_layout<L><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+        arg_as<float*>(a[0]), arg_as<const float*>(a[1]), arg_as<const uint32_t*>(a[2]), arg_as<const float*>(a[3]),
+        arg_as<uint32_t>(a[4]), cols, split);
+    return cudaGetLastError();
+}
+cudaError_t launch_stream_read(const xp_arg* a, xp_grid, cudaStream_t st) {
+    ops::stream_read<<<65536 / 256, 256, 0, st>>>(arg_as<float*>(a[0]), arg_as<const uint32_t*>(a[1]),
+                                                  arg_as<uint32_t>(a[2]));
+    return cudaGetLastError();
+}
 cudaError_t launch_argmax(const xp_arg* a, xp_grid, cudaStream_t st) {
     ops::argmax<<<1, 1024, 0, st>>>(arg_as<float*>(a[0]), arg_as<const float*>(a[1]), arg_as<uint32_t>(a[2]));
     return cudaGetLastError();
@@ -154,6 +170,7 @@ cudaError_t launch_stream4(const xp_arg* a, xp_grid g, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+#define LLM "kernels/llm.spv"
 #define MV "kernels/llm_matvec.spv"
 #define TF "kernels/llm_transformer.spv"
 #define SM "kernels/llm_sampling.spv"
@@ -165,10 +182,36 @@ __global__ void proto_mv(float*, const float*, const uint4*, const uint2*, uint3
 __global__ void proto_mv_split(float*, const float*, const uint4*, const uint2*, uint32_t, uint32_t, uint32_t) {}
 __global__ void proto_heads(float*, const float*, const float*, uint32_t, uint32_t, float) {}
 __global__ void proto_rms(float*, const float*, const float*, uint32_t, float) {}
+__global__ void proto_mvl(float*, const float*, const uint32_t*, const float*, uint32_t, uint32_t) {}
+__global__ void proto_mvl4(float*, const float*, const uint4*, const float*, uint32_t, uint32_t) {}
+__global__ void proto_mvl_split(float*, const float*, const uint32_t*, const float*, uint32_t, uint32_t, uint32_t) {}
+__global__ void proto_mvl4_split(float*, const float*, const uint4*, const float*, uint32_t, uint32_t, uint32_t) {}
 
 const std::vector<Entry>& registry() {
     static const std::vector<Entry> t = {
+        // kernels/llm.cl (the first, column-nibble matvec module)
+        E(LLM, matvec_f32, GEO_THREADS, "out,in,w,rows,cols"),
+        EC(LLM, "matvec_q4", &proto_mvl, (&launch_mv_layout<ops::MVL_COL, false>), "out,in,wq,scale,rows,cols"),
+        EC(LLM, "stream_read", &ops::stream_read, &launch_stream_read, "out,src,n"),
+        EC(LLM, "matvec_q4_split", &proto_mvl_split, (&launch_mv_layout<ops::MVL_COL, true>),
+           "partial,in,wq,scale,rows,cols,split"),
+        Entry{LLM, "matvec_reduce", "out,partial,cols,split", Gen<&ops::mv_reduce, GEO_THREADS>::specs(),
+              &Gen<&ops::mv_reduce, GEO_THREADS>::launch},
         // kernels/llm_matvec.cl
+        EC(MV, "mv_ref", &proto_mvl, (&launch_mv_layout<ops::MVL_COL, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_ref_split", &proto_mvl_split, (&launch_mv_layout<ops::MVL_COL, true>),
+           "partial,in,wq,scale,rows,cols,split"),
+        EC(MV, "mv_kmn", &proto_mvl, (&launch_mv_layout<ops::MVL_KMN, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km", &proto_mvl, (&launch_mv_layout<ops::MVL_KM, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_wg128", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_wg256", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_wg32", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_c2", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_c2_wg32", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_c4", &proto_mvl4, (&launch_mv_layout<ops::MVL_KM4, false>), "out,in,wq,scale,rows,cols"),
+        EC(MV, "mv_km4_split", &proto_mvl4_split, (&launch_mv_layout<ops::MVL_KM4, true>),
+           "partial,in,wq,scale,rows,cols,split"),
         EC(MV, "mv_km4_bs", &proto_mv, &launch_mv_plain, "out,in,wq,sc,rows,cols"),
         EC(MV, "mv_km4_bs_split", &proto_mv_split, &launch_mv_split, "partial,in,wq,sc,rows,cols,split"),
         E(MV, mv_reduce, GEO_THREADS, "out,partial,cols,split"),

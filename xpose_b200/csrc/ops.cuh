@@ -583,11 +583,70 @@ __global__ void multinomial_strided(float* out, uint32_t* idx_out, const float* 
     idx_out[0] = chosen;
 }
 
+// ---- matvec layouts of the layout study (llm_matvec.cl:25-366, llm.cl:12-117) --
+// fp32 scales [block][col]; the nibble of weight (k, j) sits at:
+//   COL  word[(k*cols + j) / 8], nibble j % 8                 (llm.cl, mv_ref*)
+//   KMN  word[j*(rows/8) + k/8], nibble k % 8                  (mv_kmn)
+//   KM   word[((j/64)*(rows/8) + k/8)*64 + j%64], nibble k % 8  (mv_km)
+//   KM4  uint4[((j/64)*(rows/32) + k/32)*64 + j%64], word (k/8)%4, nibble k % 8
+//                                                    (mv_km4 and its variants)
+// One warp per (output column, K split); lanes take 32-row blocks in turn, each
+// block's (sum in*(nibble - 8)) * scale added to the lane's sum, then a warp sum.
+XP_DEV uint32_t warp_gid() { return blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); }
+enum MvLayout : int { MVL_COL = 0, MVL_KMN = 1, MVL_KM = 2, MVL_KM4 = 3 };
+template <int L>
+XP_DEV uint32_t mvl_nibble(const uint32_t* w, uint32_t k, uint32_t j, uint32_t rows, uint32_t cols) {
+    if (L == MVL_COL) return (w[((size_t)k * cols + j) >> 3] >> ((j & 7u) * 4u)) & 15u;
+    const uint32_t sh = (k & 7u) * 4u;
+    if (L == MVL_KMN) return (w[(size_t)j * (rows >> 3) + (k >> 3)] >> sh) & 15u;
+    if (L == MVL_KM) return (w[(((size_t)(j >> 6) * (rows >> 3) + (k >> 3)) << 6) + (j & 63u)] >> sh) & 15u;
+    return (w[((((size_t)(j >> 6) * (rows >> 5) + (k >> 5)) << 6) + (j & 63u)) * 4 + ((k >> 3) & 3u)] >> sh) & 15u;
+}
+template <int L>
+__global__ void mv_layout(float* out, const float* in, const uint32_t* wq, const float* scale, uint32_t rows,
+                          uint32_t cols, uint32_t split) {
+    const uint32_t w = warp_gid(), lane = threadIdx.x & 31;
+    if (w >= cols * split) return;
+    const uint32_t j = w % cols, p = w / cols, nblk = rows / 32;
+    const uint32_t per = (nblk + split - 1) / split, b0 = p * per, b1 = min(b0 + per, nblk);
+    float acc = 0.0f;
+    for (uint32_t b = b0 + lane; b < b1; b += 32) {
+        float part = 0.0f;
+        for (uint32_t t = 0; t < 32; ++t) {
+            const uint32_t k = b * 32 + t;
+            part += in[k] * ((float)mvl_nibble<L>(wq, k, j, rows, cols) - 8.0f);
+        }
+        acc += part * scale[(size_t)b * cols + j];
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) out[(size_t)p * cols + j] = acc;
+}
+
+// matvec_f32 (llm.cl:12-19): out[j] = sum_k in[k] w[k*cols + j]; thread per
+// column (consecutive threads read consecutive w)
+__global__ void matvec_f32(float* out, const float* in, const float* w, uint32_t rows, uint32_t cols) {
+    const uint32_t j = GID();
+    if (j >= cols) return;
+    float acc = 0.0f;
+    for (uint32_t k = 0; k < rows; ++k) acc += in[k] * w[(size_t)k * cols + j];
+    out[j] = acc;
+}
+// stream_read (llm.cl:60-66): a load probe over 65536 strided lanes; out[0]
+// = lane 0's sum (src[0] + src[65536] + ...), as the reference writes it. The
+// other lanes store only on a sum they cannot reach, so their loads stay live.
+__global__ void stream_read(float* out, const uint32_t* src, uint32_t n) {
+    const uint32_t i = GID();
+    if (i >= 65536u) return;
+    uint32_t acc = 0;
+    for (uint32_t k = i; k < n; k += 65536u) acc += __ldg(src + k);
+    if (i == 0) out[0] = (float)acc;
+    else if (acc == 0xDEADBEEFu && n == 0u) out[1] = 0.0f;
+}
+
 // ---- prefill shapes (llm_sampling.cl:495-736) -------------------------------
 // Row-major [row][col] everywhere, as in the reference. Row reductions run one
 // warp per row (the reference walks a row with one thread); elementwise work is
 // one thread per element.
-XP_DEV uint32_t warp_gid() { return blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); }
 
 // softmax_rows_stats (:527-546): stats[2r] = row max, stats[2r + 1] = row sum
 // of exp(x - max); a fully masked row gives (0, 1).
