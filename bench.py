@@ -731,21 +731,23 @@ def run_reference(args):
     return 0
 
 
-def tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks):
-    """One sequence decoded by all ranks with the LM head's rows split over
-    them. First every rank decodes the same prompt unsharded (its own full
-    head), then sharded; the sharded tokens must equal the unsharded ones and
-    each rank's logit rows must equal the same rows of the unsharded logits
-    (bit-exact: the shard's tiles are the same computation)."""
+def tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks, shard_ffn=False):
+    """One sequence decoded by all ranks with the LM head's rows (and with
+    shard_ffn the FFN's gate|up columns and down-proj rows) split over them.
+    First every rank decodes the same prompt unsharded, then sharded; the
+    sharded tokens must equal the unsharded ones and each rank's logit rows
+    must equal the same rows of the unsharded logits (bit-exact)."""
     import torch
     from xpose_b200.tp import shard_lm_head
     tprompt = np.random.default_rng(77).integers(0, cfg.vocab, PROMPT, dtype=np.uint32)
     n_check = 64
     sess.reset()
+    # the same (tensor-parallel) kernel at one rank is the bit-exact reference
+    sess.tp_attach(0, 1, [sess.tp_handle()], shard_ffn=True)
     sess.prefill(tprompt)
     ref_logits = sess.last_logits()
     ref_toks, _ = sess.generate(n_check)
-    shard_lm_head(sess)
+    shard_lm_head(sess, shard_ffn=shard_ffn)
     sess.reset()
     sess.prefill(tprompt)
     logits = sess.last_logits()
@@ -764,7 +766,8 @@ def tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks):
     _, tms = sess.generate(kt, want_tokens=False)
     tms = max_over_ranks(tms)
     assert sess.error_word() == 0
-    return {"workload": f"one sequence, LM head rows split over {world} GPUs (NVLink argmax exchange)",
+    what = "LM head rows and FFN gate|up columns / down-proj rows" if shard_ffn else "LM head rows"
+    return {"workload": f"one sequence, {what} split over {world} GPUs (exchanges over NVLink inside the token kernel)",
             "value": round(kt / (tms / 1000.0), 2), "unit": "tok/s", "ms_per_step": round(tms / kt, 4),
             "steps": kt, "positions": [PROMPT + W, PROMPT + W + kt - 1], "scaling": "strong",
             "tokens_match": bool(flags[0].item()), "logit_shard_exact": bool(flags[1].item()),
@@ -916,6 +919,7 @@ def main():
     if world > 1 and not args.no_tp:
         try:
             tp = tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks)
+            tp["ffn_sharded"] = tp_bench(sess, cfg, K, W, world, rank, barrier, max_over_ranks, shard_ffn=True)
         except Exception as e:
             tp = {"error": str(e)}
 

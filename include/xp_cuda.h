@@ -413,6 +413,15 @@ xp_status xp_selftest_wait_timeout(uint32_t spin_limit, uint32_t* err_word);
  * reference, which runs on one device. */
 xp_status xp_session_tp_handle(xp_session* s, void* handle64);
 xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, const void* handles);
+/* As xp_session_tp_attach; flags: XP_TP_SHARD_FFN also splits the FFN over
+ * the ranks (gate|up columns and the matching down-proj rows; the down-proj
+ * sums are exchanged between the ranks inside every launch in int64). Its
+ * token kernel fixes each 16-row down-proj unit's partial sum separately, so
+ * logits are bit-identical for every world size, including one rank attached
+ * with this flag (the single-GPU default kernel groups units per CTA before
+ * fixing: the same tokens, logits equal to fp32 rounding). Greedy only. */
+#define XP_TP_SHARD_FFN 1u
+xp_status xp_session_tp_attach_ex(xp_session* s, uint32_t rank, uint32_t world, const void* handles, uint32_t flags);
 
 /* ---- batched decode ---------------------------------------------------------
  * nseq (<= 64) independent sequences advance one position together over the

@@ -1,7 +1,13 @@
-"""Tensor-parallel LM head on two GPUs: with the head's rows split over two
-processes, greedy decoding produces the same tokens as one GPU and each rank's
-logits shard equals the same rows of the unsharded logits (bit-exact: the
-shard's tiles are the same computation). Skipped with fewer than two GPUs."""
+"""Tensor parallelism on two GPUs: with the LM head's rows split over two
+processes (and, in the second mode, the FFN's gate|up columns and down-proj
+rows too, the down-proj sums exchanged between the ranks in int64), greedy
+decoding produces the same tokens as one GPU and each rank's logits shard
+equals the same rows of the unsharded logits (bit-exact: the shard's tiles
+are the same computation, and the per-unit int64 down-proj sums do not depend
+on their order; the FFN mode's one-GPU reference is the same kernel attached
+at one rank).
+Prefill (launches without logits) and decode both run sharded. Skipped with
+fewer than two GPUs."""
 import os
 import socket
 
@@ -13,7 +19,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, shard_ffn):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -24,14 +30,16 @@ def _worker(rank, world, port, q):
     cfg = DecodeConfig(n_layers=3, vocab=32768, max_seq=128)
     s = DecodeSession.random(cfg, Sampling(greedy=True), seed=9, device=rank)
     prompt = np.arange(10, dtype=np.uint32) * 997 % cfg.vocab
+    # the tensor-parallel kernel at one rank: the bit-exact reference
+    s.tp_attach(0, 1, [s.tp_handle()], shard_ffn=True)
     s.prefill(prompt)
     ref_logits = s.last_logits()
-    ref_toks, _ = s.generate(6)
+    ref_toks, _ = s.generate(12)
     s.reset()
-    shard_lm_head(s)
+    shard_lm_head(s, shard_ffn=shard_ffn)
     s.prefill(prompt)
     logits = s.last_logits()
-    toks, _ = s.generate(6)
+    toks, _ = s.generate(12)
     units = cfg.vocab // 64
     u0, u1 = units * rank // world, units * (rank + 1) // world
     same_shard = bool(np.array_equal(logits[u0 * 64:u1 * 64], ref_logits[u0 * 64:u1 * 64]))
@@ -40,7 +48,8 @@ def _worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_sharded_lm_head_matches_one_gpu():
+@pytest.mark.parametrize("shard_ffn", [False, True])
+def test_sharded_decode_matches_one_gpu(shard_ffn):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -49,7 +58,7 @@ def test_sharded_lm_head_matches_one_gpu():
         port = so.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shard_ffn)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)

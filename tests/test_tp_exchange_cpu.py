@@ -18,8 +18,9 @@ class FakeSession:
     def tp_handle(self):
         return bytes([self.rank]) * 64
 
-    def tp_attach(self, rank, world, handles):
+    def tp_attach(self, rank, world, handles, shard_ffn=False):
         self.attached = (rank, world, list(handles))
+        self.shard_ffn = shard_ffn
 
 
 def _worker(rank, world, port, q):

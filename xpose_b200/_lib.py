@@ -92,6 +92,7 @@ _SIGS = {
     "xp_selftest_wait_timeout": (C.c_int, [C.c_uint32, C.POINTER(C.c_uint32)]),
     "xp_session_tp_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
     "xp_session_tp_attach": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "xp_session_tp_attach_ex": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_uint32]),
     "xp_bdec_create": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(Sampling), C.c_uint64,
                                  C.POINTER(C.c_void_p)]),
     "xp_bdec_prefill": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),

@@ -81,11 +81,13 @@ struct xp_session {
     xp_bdec* pre = nullptr;     // chunked prefill (64 prompt positions per pass), made on first use
     bool pre_failed = false;
     cudaGraphExec_t g_dev = nullptr, g_io = nullptr, g_prefill = nullptr;
-    uint32_t* tp_buf = nullptr;              // this rank's LM-head exchange slots (IPC-exported)
+    uint32_t* tp_buf = nullptr;              // this rank's exchange area (IPC-exported): argmax slots, then the down-sum receive area
+    size_t tp_buf_bytes() const { return TK_TP_SLOTS * sizeof(TkTpSlot) + tk_dn_rx_words(cfg.hidden) * 8; }
     std::vector<void*> tp_peers;             // opened peer mappings
     cudaEvent_t ev_done = nullptr, ev_a = nullptr, ev_b = nullptr;
     uint32_t host_pos = 0;
     bool have_logits = false;
+    bool tk_tp_instance = false;             // run the tensor-parallel token kernel (also at one rank)
     std::string load_info;                   // how the weights were loaded (GGUF sessions)
     int load_from_cache = 0, load_cache_written = 0;
     uint32_t kernels_per_token = 0;
@@ -514,13 +516,17 @@ struct xp_session {
         // LM head unsharded until xp_session_tp_attach
         tk.head_u0 = 0;
         tk.head_u1 = tk.head.units;
+        tk.gu_u0 = 0;
+        tk.gu_u1 = tk.gu.units;
+        tk.ffn_shard = 0;
         tk.tp_rank = 0;
         tk.tp_world = 1;
-        if ((e = alloc(&tp_buf, TK_TP_SLOTS * sizeof(TkTpSlot) / 4)) != XP_OK) return e;
-        if ((e = alloc(&tk.tp_count, 4)) != XP_OK) return e;
+        if ((e = alloc(&tp_buf, tp_buf_bytes() / 4)) != XP_OK) return e;
+        if ((e = alloc(&tk.tp_count, 8)) != XP_OK) return e;
         tk.tp_slots[0] = reinterpret_cast<TkTpSlot*>(tp_buf);
-        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
-        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
+        XP_CUDA_TRY(cudaFuncSetAttribute(token_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tk_smem));
         XP_CUDA_TRY(cudaStreamSynchronize(st));
         return XP_OK;
     }
@@ -540,7 +546,9 @@ struct xp_session {
         c.attrs = at;
         c.numAttrs = 1;
         ++launches;
-        cudaError_t e = a.trace ? cudaLaunchKernelEx(&c, token_kernel<true>, a) : cudaLaunchKernelEx(&c, token_kernel<false>, a);
+        cudaError_t e = a.trace              ? cudaLaunchKernelEx(&c, token_kernel<true, false>, a)
+                        : (a.tp_world > 1 || tk_tp_instance) ? cudaLaunchKernelEx(&c, token_kernel<false, true>, a)
+                                         : cudaLaunchKernelEx(&c, token_kernel<false, false>, a);
         if (e != cudaSuccess || !want_logits || sp.greedy) return e;
         launches += 2;
         return launch_sample_topk(token, sample_out, pos, nullptr, nullptr, logits, cfg.vocab, sp.top_k,
@@ -775,7 +783,7 @@ xp_status xp_session_prefill(xp_session* s, const uint32_t* tokens, uint32_t n) 
     if (n == 0) return XP_OK;
     if (!tokens) return fail(XP_ERR_INVALID, "decode: null token array");
     cudaSetDevice(s->device);
-    if (n >= (uint32_t)env_int("XP_PREFILL_CHUNK_MIN", 32) && s->use_tk && !s->mv_only && s->tk.tp_world == 1 &&
+    if (n >= (uint32_t)env_int("XP_PREFILL_CHUNK_MIN", 32) && s->use_tk && !s->mv_only && !s->tk_tp_instance &&
         !s->tk.trace && !s->pre_failed && s->host_pos + n <= s->cfg.max_seq) {
         bool ok = true;
         for (uint32_t i = 0; i < n && ok; ++i) ok = tokens[i] < s->cfg.vocab;
@@ -1336,6 +1344,10 @@ xp_status xp_session_tp_handle(xp_session* s, void* handle) {
 }
 
 xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, const void* handles) {
+    return xp_session_tp_attach_ex(s, rank, world, handles, 0u);
+}
+
+xp_status xp_session_tp_attach_ex(xp_session* s, uint32_t rank, uint32_t world, const void* handles, uint32_t flags) {
     if (!s || !handles) return fail(XP_ERR_INVALID, "xp_session_tp_attach: null argument");
     if (!s->use_tk) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: needs the persistent token kernel path");
     if (!s->sp.greedy) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: the sharded LM head exchanges argmax only (greedy)");
@@ -1350,6 +1362,7 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
     for (uint32_t r = 0; r < world; ++r) {
         if (r == rank) {
             s->tk.tp_slots[r] = reinterpret_cast<TkTpSlot*>(s->tp_buf);
+            s->tk.dn_rx[r] = reinterpret_cast<unsigned long long*>(s->tk.tp_slots[r] + TK_TP_SLOTS);
             continue;
         }
         cudaIpcMemHandle_t h;
@@ -1358,6 +1371,7 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
         XP_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
         s->tp_peers.push_back(p);
         s->tk.tp_slots[r] = static_cast<TkTpSlot*>(p);
+        s->tk.dn_rx[r] = reinterpret_cast<unsigned long long*>(s->tk.tp_slots[r] + TK_TP_SLOTS);
     }
     // units of 64 vocabulary rows split evenly; every rank runs the same launches
     const uint32_t U = s->tk.head.units;
@@ -1365,8 +1379,20 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
     s->tk.head_u1 = (uint32_t)((uint64_t)U * (rank + 1) / world);
     s->tk.tp_rank = rank;
     s->tk.tp_world = world;
-    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, TK_TP_SLOTS * sizeof(TkTpSlot)));
-    XP_CUDA_TRY(cudaMemset(s->tk.tp_count, 0, 4));
+    // FFN row shard: gate|up units of 16 GeGLU rows split evenly, the
+    // down-proj K rows with them (its sums exchanged inside the launch)
+    const bool ffn = (flags & XP_TP_SHARD_FFN) && world > 1;
+    const uint32_t GU = s->tk.gu.units;
+    s->tk.gu_u0 = ffn ? (uint32_t)((uint64_t)GU * rank / world) : 0u;
+    s->tk.gu_u1 = ffn ? (uint32_t)((uint64_t)GU * (rank + 1) / world) : GU;
+    s->tk.ffn_shard = ffn ? 1 : 0;
+    // The tensor-parallel kernel fixes every down-proj unit's partial sum on
+    // its own, so its results do not depend on how units fall on ranks; one
+    // rank attached with XP_TP_SHARD_FFN runs it too (the reference for the
+    // sharded runs, bit for bit).
+    s->tk_tp_instance = world > 1 || (flags & XP_TP_SHARD_FFN);
+    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, s->tp_buf_bytes()));
+    XP_CUDA_TRY(cudaMemset(s->tk.tp_count, 0, 8));
     for (cudaGraphExec_t* g : {&s->g_dev, &s->g_io, &s->g_prefill})
         if (*g) { cudaGraphExecDestroy(*g); *g = nullptr; }
     return s->build_graphs();

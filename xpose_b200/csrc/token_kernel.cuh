@@ -56,6 +56,10 @@ namespace xp {
 #define XP_TK_THREADS 512
 #endif
 constexpr int TK_THREADS = XP_TK_THREADS;    // compute threads
+#ifndef XP_TK_FIX_PER_UNIT
+#define XP_TK_FIX_PER_UNIT 0
+#endif
+constexpr bool TK_FIX_PER_UNIT = XP_TK_FIX_PER_UNIT;
 constexpr int TK_WARPS = TK_THREADS / 32;
 constexpr int TK_BLOCK = TK_THREADS + 32;      // + one producer warp that issues every bulk copy
 constexpr int TK_MAXJ = (1536 + TK_THREADS - 1) / TK_THREADS;  // hidden and q|k|v width <= 1536
@@ -174,8 +178,20 @@ struct TkArgs {
     uint32_t head_u0, head_u1;          // this rank's LM-head units [u0, u1)
     uint32_t tp_rank, tp_world;         // tensor-parallel group of the LM head (world 1 = none)
     TkTpSlot* tp_slots[TK_TP_MAX];      // every rank's exchange buffer (peer mappings), TK_TP_SLOTS slots each
-    uint32_t* tp_count;                 // launches so far (this rank), the exchange flag
+    uint32_t* tp_count;                 // [0] launches so far (the argmax exchange flag), [1] down-sum exchanges so far
+    // FFN row shard (tensor parallel): this rank's gate|up units [gu_u0, gu_u1)
+    // (16 GeGLU rows each) and the matching down-proj K rows. Each rank's
+    // down-proj sums then cover only its rows; after the GU barrier every CTA
+    // sends its stripe of them to each peer as flagged 32-bit halves
+    // (dn_rx of the peer: [bank][sender][H][2] words, bank = layer parity)
+    // and every reader adds the peers' parts to its own (int64, exact, so the
+    // result is bit-identical to one GPU).
+    uint32_t gu_u0, gu_u1;
+    int ffn_shard;
+    unsigned long long* dn_rx[TK_TP_MAX];  // every rank's receive area (peer mappings)
 };
+// words of the down-sum receive area: 2 banks x TK_TP_MAX senders x H x 2
+constexpr size_t tk_dn_rx_words(uint32_t H) { return (size_t)2 * TK_TP_MAX * H * 2; }
 
 // ---- helpers -------------------------------------------------------------------
 // CTA barrier of the 16 compute warps only (named barrier 1); the producer
@@ -207,6 +223,19 @@ XP_DEV long long tk_fix(float v, uint32_t* err) {
         return 0;
     }
     return __float2ll_rn(s);
+}
+// tk_fix without a 64-bit conversion instruction: v * 2^32 is an integer
+// already once |v * 2^32| >= 2^23 (its mantissa shifted left), and fits a
+// 32-bit round-to-nearest conversion below that, so the result equals
+// tk_fix's. Out of range (|v| >= 2^31, or NaN): 0 and *bad = true.
+XP_DEV long long tk_fix_fast(float v, bool& bad) {
+    const float f = v * 4294967296.0f;
+    const uint32_t u = __float_as_uint(f), e = (u >> 23) & 0xFFu;
+    if (e < 150u) return (long long)__float2int_rn(f);
+    const bool ok = e < 190u;
+    bad |= !ok;
+    const long long m = (long long)((u & 0x7FFFFFu) | 0x800000u) << (ok ? e - 150u : 0u);
+    return ok ? ((u >> 31) ? -m : m) : 0;
 }
 XP_DEV float tk_unfix(long long x) { return __ll2float_rn(x) * 2.3283064365386963e-10f; }
 XP_DEV void red_add_s64(long long* p, long long v) {
@@ -268,17 +297,65 @@ XP_DEV void tk_tile64(const unsigned char* img, uint32_t nb, const XBlk* xq, flo
 
 // Issue the bulk copies of this CTA's units of a phase into its slot
 // (producer lane). Returns whether anything was armed on `bar`.
-__device__ __noinline__ bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar) {
+// Units [u0, u1) of the phase (all of them unless the phase is sharded): CTA
+// c takes u0 + c, u0 + c + G, ...
+__device__ __noinline__ bool tk_issue(const unsigned char* imgs, const TkPhase& P, unsigned char* slot, uint64_t* bar,
+                                      uint32_t u0 = 0, uint32_t u1 = 0xFFFFFFFFu) {
     const uint32_t G = gridDim.x, c = blockIdx.x;
-    if (c >= P.units) return false;
+    if (u1 > P.units) u1 = P.units;
+    if (u0 + c >= u1) return false;
     uint32_t n = 0;
-    for (uint32_t u = c; u < P.units; u += G) ++n;
+    for (uint32_t u = u0 + c; u < u1; u += G) ++n;
     fence_proxy_async();
     mbar_expect_tx(bar, n * P.img_bytes);
     uint32_t i = 0;
-    for (uint32_t u = c; u < P.units; u += G, ++i)
+    for (uint32_t u = u0 + c; u < u1; u += G, ++i)
         bulk_g2s(slot + (size_t)i * P.img_bytes, imgs + (size_t)u * P.img_bytes, P.img_bytes, bar);
     return true;
+}
+
+// ---- FFN shard: the down-proj sums across ranks ---------------------------------
+XP_DEV void st_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+XP_DEV unsigned long long ld_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Send this CTA's stripe of the local down-proj sums (complete after the GU
+// barrier) to every peer: element i as two flagged words (low, high half).
+XP_DEV void tk_dn_send(const TkArgs& a, uint32_t bank, uint32_t flag) {
+    const uint32_t G = gridDim.x, c = blockIdx.x, W = a.tp_world;
+    const uint32_t per = (a.H + G - 1) / G;
+    for (uint32_t t = threadIdx.x; t < per * W; t += TK_THREADS) {
+        const uint32_t r = t % W, i = c * per + t / W;
+        if (r == a.tp_rank || i >= a.H) continue;
+        const unsigned long long v = (unsigned long long)a.acc_dn[i];
+        unsigned long long* dst = a.dn_rx[r] + (((size_t)bank * TK_TP_MAX + a.tp_rank) * a.H + i) * 2;
+        st_sys_u64(dst, ((unsigned long long)flag << 32) | (v & 0xFFFFFFFFull));
+        st_sys_u64(dst + 1, ((unsigned long long)flag << 32) | (v >> 32));
+    }
+}
+// The full down-proj sum of element i: the local part plus every peer's part
+// (polled: the flag is the wait; bounded).
+XP_DEV long long tk_dn(const TkArgs& a, uint32_t i, uint32_t bank, uint32_t flag) {
+    long long v = a.acc_dn[i];
+    if (!a.ffn_shard) return v;
+    const unsigned long long* rx = a.dn_rx[a.tp_rank] + (size_t)bank * TK_TP_MAX * a.H * 2;
+    for (uint32_t r = 0; r < a.tp_world; ++r) {
+        if (r == a.tp_rank) continue;
+        const unsigned long long* p = rx + ((size_t)r * a.H + i) * 2;
+        unsigned long long lo, hi;
+        uint32_t it = 0;
+        do {
+            lo = ld_sys_u64(p);
+            hi = ld_sys_u64(p + 1);
+            if (++it > TK_SPIN_LIMIT) { atomicOr(a.err, TK_ERR_TP_WAIT); break; }
+        } while ((uint32_t)(lo >> 32) != flag || (uint32_t)(hi >> 32) != flag);
+        v += (long long)(((hi & 0xFFFFFFFFull) << 32) | (lo & 0xFFFFFFFFull));
+    }
+    return v;
 }
 XP_DEV bool tk_issue_vec(const float* src, uint32_t n, unsigned char* slot, uint64_t* bar) {
     fence_proxy_async();
@@ -336,9 +413,12 @@ __device__ __noinline__ bool tk_issue_kv(const TkArgs& a, const TkLayer& L, uint
 // ---------------------------------------------------------------------------------
 // TRACE: record the phase timeline into a.trace (XP_TRACE); the production
 // instance carries none of that code.
-template <bool TRACE>
+template <bool TRACE, bool TP>
 __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constant__ TkArgs a) {
     uint64_t* const trace = TRACE ? a.trace : nullptr;
+    // tensor-parallel code exists only in the TP instance (code size: every
+    // layer's code is fetched cold)
+    const bool ffn = TP && a.ffn_shard;
     extern __shared__ __align__(128) unsigned char sm[];
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -418,8 +498,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         {
             fill(tk_issue_kv(a, L0, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
             fill(tk_issue(L0.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
-            fill(tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
-            fill(tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN]), TK_MB_DOWN);
+            fill(tk_issue(L0.gu, a.gu, s_gu, &mb[TK_MB_GU], a.gu_u0, a.gu_u1), TK_MB_GU);
+            fill(tk_issue(L0.down, a.down, s_down, &mb[TK_MB_DOWN], a.gu_u0, a.gu_u1), TK_MB_DOWN);
         }
         for (uint32_t l = 0; l + 1 < L; ++l) {
             const TkLayer& Ln = a.layers[l + 1];
@@ -432,10 +512,10 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             fill(tk_issue(Ln.o, a.o, s_o, &mb[TK_MB_O]), TK_MB_O);
             fill(tk_issue_kv(a, Ln, pos, s_kv, &mb[TK_MB_KV]), TK_MB_KV);
             wait_empty(TK_ME_GU);
-            fill(tk_issue(Ln.gu, a.gu, s_gu, &mb[TK_MB_GU]), TK_MB_GU);
+            fill(tk_issue(Ln.gu, a.gu, s_gu, &mb[TK_MB_GU], a.gu_u0, a.gu_u1), TK_MB_GU);
             fill(tk_issue_vec(Ln.c_gu, 2 * H, (unsigned char*)cg, &mb[TK_MB_CGU]), TK_MB_CGU);
             wait_empty(TK_ME_DOWN);
-            fill(tk_issue(Ln.down, a.down, s_down, &mb[TK_MB_DOWN]), TK_MB_DOWN);
+            fill(tk_issue(Ln.down, a.down, s_down, &mb[TK_MB_DOWN], a.gu_u0, a.gu_u1), TK_MB_DOWN);
         }
         if (!a.want_logits) return;
         // last layer: the head constants once QKV is done with its slot, the
@@ -470,6 +550,12 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     };
 
     const uint32_t base_g = (uint32_t)(base / G);  // barriers before this launch
+    // FFN shard: flags of this launch's down-sum exchanges (one per layer;
+    // a tensor-parallel launch decodes one position)
+    // FFN shard: exchanges are numbered across launches (tp_count[1] counts
+    // them), so consecutive exchanges alternate between the two banks and a
+    // peer can never be more than one exchange ahead of a reader
+    const uint32_t dn_flag0 = ffn ? a.tp_count[1] + 1u : 0u;
     const float inv_h = 1.0f / (float)H;
     __shared__ uint32_t s_tok;  // the input token of the next position (multi-token launches)
     // this CTA's unit coordinates, fixed for the launch (no divisions in the steps)
@@ -480,7 +566,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         s_o_kc = c % a.o.ks;
         s_o_col0 = (c / a.o.ks) * 64;
         uint32_t nu = 0;
-        for (uint32_t u = c; u < a.gu.units; u += G) ++nu;
+        for (uint32_t u = a.gu_u0 + c; u < a.gu_u1; u += G) ++nu;
         s_gu_nu = nu;
     }
     if ((uint32_t)tid < a.n_layers) {
@@ -543,13 +629,16 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // reduction of the norm sums instead of after it.
             const TkPhase& P = a.qkv;
             const bool mine = c < P.units && warp >= 1 && (uint32_t)(warp - 1) < P.nb;
+            // FFN shard: the previous layer's down-proj sums, completed by the peers' parts
+            const uint32_t dn_flag = dn_flag0 + l - 1, dn_bank = dn_flag & 1u;
+            if (ffn) tk_dn_send(a, dn_bank, dn_flag);
             const uint32_t bw = warp - 1, b0 = s_qkv_b0;
             float uv[TK_MAXJ], xb[TK_MAXJ];
             float sy = 0.0f, sbu = 0.0f, suu = 0.0f;
 #pragma unroll
             for (int j = 0; j < TK_MAXJ; ++j) {
                 const uint32_t i = tid + j * TK_THREADS;
-                const float y = i < H ? tk_unfix(a.acc_dn[i]) : 0.0f;
+                const float y = i < H ? tk_unfix(ffn ? tk_dn(a, i, dn_bank, dn_flag) : a.acc_dn[i]) : 0.0f;
                 xb[j] = i < H ? xr[i] : 0.0f;
                 uv[j] = i < H ? y * (1.0f + cq[i]) : 0.0f;
                 sy += y * y;
@@ -559,7 +648,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             float bq0 = 0.0f, bq1 = 0.0f;
             if (mine) {
                 const uint32_t i = (b0 + bw) * 32 + lane;
-                const float yb = tk_unfix(a.acc_dn[i]);
+                const float yb = tk_unfix(ffn ? tk_dn(a, i, dn_bank, dn_flag) : a.acc_dn[i]);
                 xq_prep_block(yb * (1.0f + cq[i]) * (1.0f + cq[H + i]), &xq[bw]);
                 __syncwarp();
                 const uint4* nib = reinterpret_cast<const uint4*>(s_qkv);
@@ -630,10 +719,13 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     sums.y += rv[j] * rv[j];
                 }
             } else {
+                const bool head_dn = k == TK_S_HEAD && ffn;
+                const uint32_t dn_flag = dn_flag0 + L - 1, dn_bank = dn_flag & 1u;
+                if (head_dn) tk_dn_send(a, dn_bank, dn_flag);
 #pragma unroll
                 for (int j = 0; j < TK_MAXJ; ++j) {
                     const uint32_t i = tid + j * TK_THREADS;
-                    const float y = i < H ? tk_unfix(acc[i]) : 0.0f;
+                    const float y = i < H ? tk_unfix(head_dn ? tk_dn(a, i, dn_bank, dn_flag) : acc[i]) : 0.0f;
                     rv[j] = i < H ? bsrc[i] : 0.0f;
                     uv[j] = i < H ? y * (1.0f + wv[i]) : 0.0f;
                     sums.x += y * y;
@@ -959,7 +1051,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
         if (k != TK_S_ATTN && !split_qkv) {
             // ---------------- limbs of xn: one shared prep ----------------
             const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
-            const bool has = c < P.units;
+            const bool has = c < (k == TK_S_GU ? a.gu_u1 - a.gu_u0 : P.units);
             tk_sync();  // xn complete (O: its limbs, made by the combine)
             if (k != TK_S_O) {
                 if (has) {
@@ -1025,10 +1117,18 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 if (has) {
                     const uint32_t nu = s_gu_nu;
                     const uint32_t ib = a.down.img_bytes;
-                    // unit-outer: each unit's limbs are loaded once per thread
-                    float s[TK_MAXJ];
+                    // unit-outer: each unit's limbs are loaded once per thread.
+                    // Each unit's partial is fixed-point on its own and the
+                    // units are added as integers, so the sums do not depend
+                    // on which CTA (or rank) holds which unit.
+                    long long s[TK_MAXJ];
+                    float f[TK_MAXJ];
+                    bool bad = false;
 #pragma unroll
-                    for (int jj = 0; jj < TK_MAXJ; ++jj) s[jj] = 0.0f;
+                    for (int jj = 0; jj < TK_MAXJ; ++jj) {
+                        s[jj] = 0;
+                        f[jj] = 0.0f;
+                    }
 #pragma unroll 1
                     for (uint32_t ui = 0; ui < nu; ++ui) {
                         const XBlk& X = xq[ui];
@@ -1036,15 +1136,23 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 #pragma unroll
                         for (int jj = 0; jj < TK_MAXJ; ++jj) {
                             const uint32_t j = tid + jj * TK_THREADS;
-                            if (j < H)
-                                s[jj] += tk_dot_half(reinterpret_cast<const uint2*>(img)[j],
-                                                     reinterpret_cast<const uint16_t*>(img + (size_t)H * 8)[j], X);
+                            if (j < H) {
+                                const float d = tk_dot_half(reinterpret_cast<const uint2*>(img)[j],
+                                                            reinterpret_cast<const uint16_t*>(img + (size_t)H * 8)[j], X);
+                                if (TK_FIX_PER_UNIT || TP) s[jj] += tk_fix_fast(d, bad);
+                                else f[jj] += d;
+                            }
                         }
                     }
+                    if (!(TK_FIX_PER_UNIT || TP)) {
+#pragma unroll
+                        for (int jj = 0; jj < TK_MAXJ; ++jj) s[jj] = tk_fix_fast(f[jj], bad);
+                    }
+                    if (bad) atomicOr(a.err, TK_ERR_RANGE);
 #pragma unroll
                     for (int jj = 0; jj < TK_MAXJ; ++jj) {
                         const uint32_t j = tid + jj * TK_THREADS;
-                        if (j < H) red_add_s64(&a.acc_dn[j], tk_fix(s[jj], a.err));
+                        if (j < H) red_add_s64(&a.acc_dn[j], s[jj]);
                     }
                 }
                 // the q|k|v sums were consumed by this layer's ATTN step
@@ -1206,7 +1314,7 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 const uint32_t oi = __shfl_xor_sync(0xffffffffu, ix, o);
                 if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
             }
-            if (a.tp_world > 1) {
+            if (TP && a.tp_world > 1) {
                 // lane r publishes this rank's best into rank r's slot
                 // [tp_rank] over NVLink, then waits for rank r's entry in our
                 // own buffer (bounded) and the warp keeps the lowest-index max
@@ -1258,6 +1366,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
     }  // token
     if (c == 0 && tid == 0) {
         *a.epoch = base + (uint64_t)nbar * G;
+        // this launch's down-sum exchanges: one per layer consumed (L - 1, or
+        // L when HEAD ran); every CTA read tp_count[1] before the first barrier
+        if (ffn) a.tp_count[1] += a.want_logits ? L : L - 1;
         if (trace) {
             trace[0] = nbar;
             trace[509] = trace[2 * nbar + 2] = globaltimer_ns();

@@ -233,11 +233,12 @@ class DecodeSession:
         check(lib().xp_session_tp_handle(self._h, buf))
         return bytes(buf)
 
-    def tp_attach(self, rank, world, handles):
-        """Shard the LM head over `world` ranks (handles in rank order)."""
+    def tp_attach(self, rank, world, handles, shard_ffn=False):
+        """Shard the LM head (and with shard_ffn the FFN) over `world` ranks
+        (handles in rank order)."""
         blob = b"".join(handles)
         assert len(blob) == 64 * world
-        check(lib().xp_session_tp_attach(self._h, rank, world, blob))
+        check(lib().xp_session_tp_attach_ex(self._h, rank, world, blob, 1 if shard_ffn else 0))
 
     def error_word(self):
         w = C.c_uint32()
