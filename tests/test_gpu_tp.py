@@ -6,8 +6,10 @@ equals the same rows of the unsharded logits (bit-exact: the shard's tiles
 are the same computation, and the per-unit int64 down-proj sums do not depend
 on their order; the FFN mode's one-GPU reference is the same kernel attached
 at one rank).
-Prefill (launches without logits) and decode both run sharded. Skipped with
-fewer than two GPUs."""
+Sampled decoding (top-k 64 / top-p 0.95) gathers every shard's candidate
+lists over peer memory and draws the same tokens as one GPU. Prefill
+(launches without logits) and decode both run sharded. Skipped with fewer
+than two GPUs."""
 import os
 import socket
 
@@ -19,7 +21,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _worker(rank, world, port, q, shard_ffn):
+def _worker(rank, world, port, q, shard_ffn, greedy):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -28,7 +30,8 @@ def _worker(rank, world, port, q, shard_ffn):
     from xpose_b200.decode import DecodeConfig, DecodeSession, Sampling
     from xpose_b200.tp import shard_lm_head
     cfg = DecodeConfig(n_layers=3, vocab=32768, max_seq=128)
-    s = DecodeSession.random(cfg, Sampling(greedy=True), seed=9, device=rank)
+    sp = Sampling(greedy=True) if greedy else Sampling(greedy=False, temperature=1.0, top_k=64, top_p=0.95, seed=5)
+    s = DecodeSession.random(cfg, sp, seed=9, device=rank)
     prompt = np.arange(10, dtype=np.uint32) * 997 % cfg.vocab
     # the tensor-parallel kernel at one rank: the bit-exact reference
     s.tp_attach(0, 1, [s.tp_handle()], shard_ffn=True)
@@ -48,8 +51,8 @@ def _worker(rank, world, port, q, shard_ffn):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shard_ffn", [False, True])
-def test_sharded_decode_matches_one_gpu(shard_ffn):
+@pytest.mark.parametrize("shard_ffn,greedy", [(False, True), (True, True), (True, False)])
+def test_sharded_decode_matches_one_gpu(shard_ffn, greedy):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -58,7 +61,7 @@ def test_sharded_decode_matches_one_gpu(shard_ffn):
         port = so.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shard_ffn)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, shard_ffn, greedy)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)

@@ -346,8 +346,11 @@ XP_DEV void append_key(bool take, uint64_t key, uint64_t* list, uint32_t* count,
 // of TOPK_THREADS * 8 logits, in descending order. Any global top-k element
 // (k <= TOPK_TK) survives in its slice's list. Only keys >= a lower bound L on
 // the slice's 64th largest key are ranked (L from a sample of warp maxima).
-// cand: [sequence][slices][TOPK_TK].
-__global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* logits, uint32_t n, uint64_t* cand) {
+// cand: [sequence][slices][TOPK_TK]. The launch covers slices
+// [s0, s0 + gridDim.x) of ns slices (all of them unless the logits are
+// sharded: then only this rank's slices are valid).
+__global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* logits, uint32_t n, uint64_t* cand,
+                                                                 uint32_t s0, uint32_t ns) {
     constexpr uint32_t SL = TOPK_THREADS * 8, TK = 64, NW = TOPK_THREADS / 32;
     static_assert(NW * 8 >= TK, "the sample holds at least 64 keys");
     __shared__ uint64_t keys[SL];  // radix fallback only
@@ -359,7 +362,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* lo
     pdl_launch_dependents();
     pdl_wait();
     const float* lg = logits + (size_t)blockIdx.y * n;
-    const uint32_t base = blockIdx.x * SL;
+    const uint32_t base = (blockIdx.x + s0) * SL;
     uint64_t k[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -396,7 +399,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* lo
     for (int j = 0; j < 8; ++j) append_key(k[j] >= L, k[j], fc, &fcount, TOPK_FAST_MAX);
     __syncthreads();
     const uint32_t m = fcount;
-    uint64_t* out = cand + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * TK;
+    uint64_t* out = cand + ((size_t)blockIdx.y * ns + blockIdx.x + s0) * TK;
     if (m <= TOPK_FAST_MAX) {
         rank_place(fc, m, TK, out);
         return;
@@ -408,6 +411,47 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cand_kernel(const float* lo
     block_select(keys, SL, TK, s, prefix, mask);
     block_collect(keys, SL, TK, prefix, mask, s, fc);
     rank_place(fc, TK, TK, out);
+}
+
+// Tensor-parallel sampling: every rank copies its slices' candidate lists
+// [s0, s1) (TOPK_TK keys each) into every rank's candidate area (peer
+// mappings; its own too), publishes `flag` to every rank and waits, bounded,
+// for every rank's flag; then copies the whole vocabulary's lists back into
+// `cand`, from which it draws the same token as every other rank. Areas and
+// flags have two banks, chosen by the flag's parity: a rank can be at most
+// one exchange ahead of another (the next needs everyone's flag). One CTA.
+struct TpCandArgs {
+    uint64_t* cand;               // this rank's lists, [ns][TOPK_TK]; receives all of them
+    uint32_t s0, s1, ns;          // this rank's slices of ns
+    uint32_t rank, world;
+    uint64_t* area[8];            // every rank's candidate area: 2 banks of ns * TOPK_TK keys
+    uint32_t* flags[8];           // every rank's flag words: 2 banks of 8
+    uint32_t* count;              // exchanges so far (this rank); advanced here
+    uint32_t* err;
+};
+__global__ void tp_cand_exchange_kernel(TpCandArgs a) {
+    pdl_wait();
+    const uint32_t flag = *a.count + 1, bank = flag & 1u;
+    const size_t W = (size_t)a.ns * 64, lo = (size_t)a.s0 * 64, hi = (size_t)a.s1 * 64;
+    for (uint32_t r = 0; r < a.world; ++r)
+        for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x)
+            asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.area[r] + bank * W + i), "l"(a.cand[i]) : "memory");
+    __syncthreads();
+    if (threadIdx.x < a.world) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flags[threadIdx.x] + bank * 8 + a.rank), "r"(flag)
+                     : "memory");
+        uint32_t f = 0, it = 0;
+        do {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(a.flags[a.rank] + bank * 8 + threadIdx.x)
+                         : "memory");
+            if (++it > (1u << 22)) { atomicOr(a.err, 32u); break; }
+        } while (f != flag);
+    }
+    __syncthreads();
+    const uint64_t* mine = a.area[a.rank] + bank * W;
+    for (size_t i = threadIdx.x; i < W; i += blockDim.x) a.cand[i] = mine[i];
+    if (threadIdx.x == 0) *a.count = flag;
 }
 
 // Phase 2 (one CTA per sequence): exact top-k of the candidates, then

@@ -82,7 +82,11 @@ struct xp_session {
     bool pre_failed = false;
     cudaGraphExec_t g_dev = nullptr, g_io = nullptr, g_prefill = nullptr;
     uint32_t* tp_buf = nullptr;              // this rank's exchange area (IPC-exported): argmax slots, then the down-sum receive area
-    size_t tp_buf_bytes() const { return TK_TP_SLOTS * sizeof(TkTpSlot) + tk_dn_rx_words(cfg.hidden) * 8; }
+    // [argmax slots | down-sum receive area | candidate area (2 banks) | candidate flags (2 x 8)]
+    size_t tp_off_cand() const { return TK_TP_SLOTS * sizeof(TkTpSlot) + tk_dn_rx_words(cfg.hidden) * 8; }
+    size_t tp_cand_keys() const { return (size_t)((cfg.vocab + TOPK_SLICE - 1) / TOPK_SLICE) * TOPK_TK; }
+    size_t tp_off_cflags() const { return tp_off_cand() + 2 * tp_cand_keys() * 8; }
+    size_t tp_buf_bytes() const { return tp_off_cflags() + 2 * 8 * 4; }
     std::vector<void*> tp_peers;             // opened peer mappings
     cudaEvent_t ev_done = nullptr, ev_a = nullptr, ev_b = nullptr;
     uint32_t host_pos = 0;
@@ -551,8 +555,24 @@ struct xp_session {
                                          : cudaLaunchKernelEx(&c, token_kernel<false, false>, a);
         if (e != cudaSuccess || !want_logits || sp.greedy) return e;
         launches += 2;
+        TpCandArgs tpa{};
+        const bool tp = tk.tp_world > 1;
+        if (tp) {  // this rank's logits are its LM-head shard: gather the candidates
+            tpa.s0 = tk.head_u0 * 64 / TOPK_SLICE;
+            tpa.s1 = tk.head_u1 * 64 / TOPK_SLICE;
+            tpa.rank = tk.tp_rank;
+            tpa.world = tk.tp_world;
+            for (uint32_t r = 0; r < tk.tp_world; ++r) {
+                unsigned char* b = reinterpret_cast<unsigned char*>(tk.tp_slots[r]);
+                tpa.area[r] = reinterpret_cast<uint64_t*>(b + tp_off_cand());
+                tpa.flags[r] = reinterpret_cast<uint32_t*>(b + tp_off_cflags());
+            }
+            tpa.count = tk.tp_count;
+            tpa.err = tk.err;
+        }
         return launch_sample_topk(token, sample_out, pos, nullptr, nullptr, logits, cfg.vocab, sp.top_k,
-                                  sp.temperature, sp.top_p, sp.seed, sp.seq_id, samp_scratch, st, false, true, hist);
+                                  sp.temperature, sp.top_p, sp.seed, sp.seq_id, samp_scratch, st, false, true, hist,
+                                  tp ? &tpa : nullptr);
     }
 
     xp_status validate_cfg() {
@@ -1350,7 +1370,6 @@ xp_status xp_session_tp_attach(xp_session* s, uint32_t rank, uint32_t world, con
 xp_status xp_session_tp_attach_ex(xp_session* s, uint32_t rank, uint32_t world, const void* handles, uint32_t flags) {
     if (!s || !handles) return fail(XP_ERR_INVALID, "xp_session_tp_attach: null argument");
     if (!s->use_tk) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: needs the persistent token kernel path");
-    if (!s->sp.greedy) return fail(XP_ERR_UNSUPPORTED, "xp_session_tp_attach: the sharded LM head exchanges argmax only (greedy)");
     if (world == 0 || world > TK_TP_MAX || rank >= world)
         return fail(XP_ERR_INVALID, "xp_session_tp_attach: rank %u of %u (world 1..%u)", rank, world, TK_TP_MAX);
     cudaSetDevice(s->device);
@@ -1377,6 +1396,13 @@ xp_status xp_session_tp_attach_ex(xp_session* s, uint32_t rank, uint32_t world, 
     const uint32_t U = s->tk.head.units;
     s->tk.head_u0 = (uint32_t)((uint64_t)U * rank / world);
     s->tk.head_u1 = (uint32_t)((uint64_t)U * (rank + 1) / world);
+    // sampling draws from every shard's candidate lists, made per sampler
+    // slice: the shards must split the vocabulary on slice boundaries
+    if (!s->sp.greedy && world > 1 &&
+        ((s->tk.head_u0 * 64) % TOPK_SLICE || (s->tk.head_u1 * 64) % TOPK_SLICE))
+        return fail(XP_ERR_UNSUPPORTED,
+                    "xp_session_tp_attach: sampled decoding needs the vocabulary (%u) split on %u-row slices over %u ranks",
+                    s->cfg.vocab, TOPK_SLICE, world);
     s->tk.tp_rank = rank;
     s->tk.tp_world = world;
     // FFN row shard: gate|up units of 16 GeGLU rows split evenly, the

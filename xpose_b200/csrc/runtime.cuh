@@ -191,14 +191,24 @@ inline size_t sample_scratch_bytes(uint32_t n) {
 // Two launches over nseq sequences of n logits each: slice candidates, then
 // one drawing CTA per sequence. `cand` holds nseq * slices * TOPK_TK keys.
 inline cudaError_t launch_topk(const float* logits, uint32_t n, uint32_t nseq, uint64_t* cand,
-                               const TopkDrawArgs& da_in, cudaStream_t st, bool pdl) {
+                               const TopkDrawArgs& da_in, cudaStream_t st, bool pdl,
+                               const TpCandArgs* tp = nullptr) {
     static std::atomic<bool> attr_set[kMaxDevices];
     if (cudaError_t e = smem_attr_once(attr_set, topk_draw_kernel, 200 * 1024); e != cudaSuccess) return e;
     const uint32_t ns = (n + TOPK_SLICE - 1) / TOPK_SLICE;
-    cudaError_t e = launch_ex(topk_cand_kernel, dim3(ns, nseq), dim3(TOPK_THREADS), 0, st, 1, pdl, logits, n, cand);
+    const uint32_t s0 = tp ? tp->s0 : 0u, s1 = tp ? tp->s1 : ns;
+    cudaError_t e = launch_ex(topk_cand_kernel, dim3(s1 - s0, nseq), dim3(TOPK_THREADS), 0, st, 1, pdl, logits, n, cand,
+                              s0, ns);
     if (e != cudaSuccess) return e;
     TopkDrawArgs da = da_in;
     da.cand = cand;
+    if (tp) {  // sharded logits: gather every rank's candidate lists into cand, then draw from them
+        TpCandArgs x = *tp;
+        x.cand = cand;
+        x.ns = ns;
+        e = launch_ex(tp_cand_exchange_kernel, dim3(1), dim3(1024), 0, st, 1, true, x);
+        if (e != cudaSuccess) return e;
+    }
     da.ncand = ns * TOPK_TK;
     if (da.top_k == 0 || da.top_k > TOPK_TK) da.top_k = TOPK_TK;
     return launch_ex(topk_draw_kernel, dim3(nseq), dim3(TOPK_THREADS), (size_t)da.ncand * 8, st, 1, true, da);
@@ -206,7 +216,8 @@ inline cudaError_t launch_topk(const float* logits, uint32_t n, uint32_t nseq, u
 inline cudaError_t launch_sample_topk(uint32_t* token, float* sample_out, uint32_t* pos_dev, float* out_vals,
                                       uint32_t* out_idx, const float* logits, uint32_t n, uint32_t top_k,
                                       float temperature, float top_p, uint64_t seed, uint64_t seq_id, void* scratch,
-                                      cudaStream_t st, bool pdl, bool advance, uint32_t* hist = nullptr) {
+                                      cudaStream_t st, bool pdl, bool advance, uint32_t* hist = nullptr,
+                                      const TpCandArgs* tp = nullptr) {
     TopkDrawArgs da{};
     da.top_k = top_k;
     da.temperature = temperature;
@@ -222,7 +233,7 @@ inline cudaError_t launch_sample_topk(uint32_t* token, float* sample_out, uint32
     da.out_vals = out_vals;
     da.out_idx = out_idx;
     da.hist = hist;
-    return launch_topk(logits, n, 1, static_cast<uint64_t*>(scratch), da, st, pdl);
+    return launch_topk(logits, n, 1, static_cast<uint64_t*>(scratch), da, st, pdl, tp);
 }
 
 }  // namespace xp
