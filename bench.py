@@ -184,7 +184,7 @@ def long_context_bench(peak, iters=20):
     out = torch.empty(1024, device="cuda")
     posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
     tok = torch.empty(1, dtype=torch.int32, device="cuda")
-    ns_g, ns_l = 64, 8
+    ns_g, ns_l = 64, 16
     scr = torch.zeros(lib().xp_attention_scratch_bytes(ns_g) // 4 + 64, dtype=torch.int32, device="cuda")
     sscr = torch.zeros(lib().xp_sample_scratch_bytes(vocab) // 4 + 64, dtype=torch.int32, device="cuda")
     layers = [(l, (l + 1) % 6 == 0) for l in range(L)]

@@ -14,12 +14,13 @@
 //     bulk copies (cp.async.bulk, 32 positions = 16 KB a stage) issued before
 //     the q/k work, and computes scores, a softmax partial (max, sum) and the
 //     unnormalised P.V for its chunk;
-//   * the combine is two-level: the CTAs of a thread-block cluster (up to 8)
-//     leave their partials in shared memory and the cluster's first CTA
-//     merges them through distributed shared memory; with more than one
-//     cluster, the last cluster to finish (atomic ticket) merges the cluster
-//     results in cluster order and writes the attention output and its matvec
-//     limbs. Fixed merge order: deterministic.
+//   * the combine is two-level: the CTAs of a thread-block cluster (up to 16)
+//     push their partials into the cluster leader's shared memory (st.async,
+//     completing on the leader's mbarrier; no cluster-wide barrier after the
+//     work) and the leader merges them; with more than one cluster, the last
+//     cluster to finish (atomic ticket) merges the cluster results in cluster
+//     order and writes the attention output and its matvec limbs. Fixed merge
+//     order: deterministic.
 // Shape: n_heads = NH query heads sharing one kv head, head_dim = 256.
 #pragma once
 #include <cooperative_groups.h>
@@ -30,7 +31,12 @@
 
 namespace xp {
 
-constexpr int ATT_THREADS = 256;
+#ifndef XP_ATT_THREADS
+#define XP_ATT_THREADS 256
+#endif
+constexpr int ATT_THREADS = XP_ATT_THREADS;  // 256 or 512
+constexpr int ATT_MT = 256;                  // threads of the combine and merge: one float4 of outputs each
+constexpr int ATT_PVG = ATT_THREADS / 128;   // P.V row groups (a thread owns a dim pair)
 constexpr int ATT_HD = 256;
 
 struct AttnArgs {
@@ -132,6 +138,36 @@ XP_DEV float reduce4(float v0, float v1, float v2, float v3) {
     return kk;
 }
 
+// Phase timestamps for latency studies, compiled only with XP_ATT_TRACE:
+// [launch][cta][10] globaltimer values (entry, after the grid dependency,
+// position read, q/k ready, scores, softmax, P.V, partials published, cluster
+// merged, final merge).
+#ifdef XP_ATT_TRACE
+__device__ unsigned long long g_att_trace[64 * 160 * 16];
+__device__ uint32_t g_att_launch;
+#define ATT_STAMP(i) do { if (threadIdx.x == 0) tr_[i] = globaltimer_ns(); } while (0)
+#else
+#define ATT_STAMP(i) do { } while (0)
+#endif
+
+// Cluster primitives of the push merge: each CTA stores its partial into the
+// cluster leader's shared memory with st.async, which completes bytes on the
+// leader's mbarrier, so only the leader waits and no cluster-wide barrier
+// follows the merge.
+XP_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+XP_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+XP_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+XP_DEV void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(addr), "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+                   "r"(__float_as_uint(v.w)), "r"(bar)
+                 : "memory");
+}
+
 constexpr uint32_t ATT_TILE = 32;    // positions per bulk-copy stage (16 KB of K or V)
 constexpr uint32_t ATT_STAGES = 4;
 
@@ -142,65 +178,23 @@ struct AttnSmem {
     static constexpr size_t qs = ring + (size_t)ATT_STAGES * ATT_TILE * 512;
     static constexpr size_t knv = qs + 4 * 256 * 4;
     static constexpr size_t accs = knv + 2 * 256 * 2;
-    static constexpr size_t sc = accs + 2 * 4 * 256 * 4;
-    static constexpr size_t bytes(uint32_t chunk_max) { return sc + (size_t)4 * chunk_max * 4; }
+    static constexpr size_t sc = accs + (size_t)ATT_PVG * 4 * 256 * 4;
+    // cluster leader only: one slot per cluster CTA, [NH][256] partial | (max, sum) x NH
+    static constexpr size_t slot_bytes = 4 * 256 * 4 + 4 * 2 * 4;
+    __host__ __device__ static constexpr size_t slots(uint32_t chunk_max) { return sc + (size_t)4 * chunk_max * 4; }
+    static constexpr size_t bytes(uint32_t chunk_max, uint32_t cluster) {
+        return slots(chunk_max) + (cluster > 1 ? (size_t)cluster * slot_bytes : 0);
+    }
 };
 
-// Merge `cnt` flash-decode partials (unnormalised P.V [NH][256] and (max, sum)
-// per head) in index order; part(b) and stat(b) give partial b's arrays (global
-// memory, or a cluster peer's shared memory when DSMEM). Each thread owns four
-// consecutive outputs of one head and recomputes that head's max, weights
-// e^(m_b - M) and sum itself, so the merge needs no block synchronisation.
-// final: out = (sum_b P_b e^(m_b - M)) / L, with matvec limbs when xq is set
-// (accs: 1024 floats of staging); else the merged partial and its (M, L).
-template <int NH, bool DSMEM, class PF, class SF>
-__device__ __noinline__ void attn_merge(PF part, SF stat, uint32_t cnt, float* out, float* ostat, XBlk* xq, bool final,
-                                        float* accs) {
+// Finish a merged flash-decode partial (thread's float4 o of [NH][256], its
+// head's max M and sum L). final: out = o / L, with matvec limbs when xq is set
+// (accs: 1024 floats of staging); else the partial and its (M, L). Run by
+// threads 0..ATT_MT-1 only.
+template <int NH>
+XP_DEV void attn_finish(float4 o, float M, float L, float* out, float* ostat, XBlk* xq, bool final, float* accs) {
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    static_assert(NH * 256 == 4 * ATT_THREADS, "one float4 of outputs per thread");
     const uint32_t h = (4 * tid) >> 8;
-    auto ld4 = [&](uint32_t b) {
-        const float4* p = reinterpret_cast<const float4*>(part(b)) + tid;
-        return DSMEM ? *p : __ldcg(p);
-    };
-    auto ld2 = [&](uint32_t b) {
-        const float2* p = reinterpret_cast<const float2*>(stat(b)) + h;
-        return DSMEM ? *p : __ldcg(p);
-    };
-    float M = -INFINITY, L = 0.0f;
-    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (DSMEM) {
-        // a cluster holds at most 8 partials: every load in one round trip
-        float4 v[8];
-        float2 st[8];
-#pragma unroll
-        for (int b = 0; b < 8; ++b)
-            if ((uint32_t)b < cnt) { v[b] = ld4(b); st[b] = ld2(b); }
-#pragma unroll
-        for (int b = 0; b < 8; ++b)
-            if ((uint32_t)b < cnt && st[b].y > 0.0f) M = fmaxf(M, st[b].x);
-#pragma unroll
-        for (int b = 0; b < 8; ++b)
-            if ((uint32_t)b < cnt) {
-                const float w = st[b].y > 0.0f ? expf(st[b].x - M) : 0.0f;
-                L += st[b].y * w;
-                o.x += v[b].x * w; o.y += v[b].y * w; o.z += v[b].z * w; o.w += v[b].w * w;
-            }
-    } else {
-#pragma unroll 4
-        for (uint32_t b = 0; b < cnt; ++b) {
-            const float2 st = ld2(b);
-            if (st.y > 0.0f) M = fmaxf(M, st.x);
-        }
-#pragma unroll 4
-        for (uint32_t b = 0; b < cnt; ++b) {
-            const float4 v = ld4(b);
-            const float2 st = ld2(b);
-            const float w = st.y > 0.0f ? expf(st.x - M) : 0.0f;
-            L += st.y * w;
-            o.x += v.x * w; o.y += v.y * w; o.z += v.z * w; o.w += v.w * w;
-        }
-    }
     if (!final) {
         reinterpret_cast<float4*>(out)[tid] = o;
         if ((tid & 63) == 0) { ostat[h * 2] = M; ostat[h * 2 + 1] = L; }
@@ -211,9 +205,84 @@ __device__ __noinline__ void attn_merge(PF part, SF stat, uint32_t cnt, float* o
     reinterpret_cast<float4*>(out)[tid] = o;
     if (xq) {
         reinterpret_cast<float4*>(accs)[tid] = o;
-        __syncthreads();
-        for (uint32_t bb = warp; bb < NH * 256 / 32; bb += ATT_THREADS / 32) xq_prep_block(accs[bb * 32 + lane], &xq[bb]);
+        asm volatile("bar.sync 1, %0;" ::"n"(ATT_MT) : "memory");  // the merging threads only
+        for (uint32_t bb = warp; bb < NH * 256 / 32; bb += ATT_MT / 32) xq_prep_block(accs[bb * 32 + lane], &xq[bb]);
     }
+}
+
+// Merge `cnt` flash-decode partials (unnormalised P.V [NH][256] and (max, sum)
+// per head) in index order: M = max of the non-empty partials' maxima, then
+// o = sum_b P_b e^(m_b - M) and L = sum_b l_b e^(m_b - M). Each thread owns
+// four consecutive outputs of one head and recomputes that head's M itself,
+// so the merge needs no block synchronisation.
+//
+// Cluster partials in global memory (the last cluster merges them): a loop.
+template <int NH>
+__device__ __noinline__ void attn_merge_global(const float* part, const float* stat, uint32_t cnt, float* out,
+                                               XBlk* xq, float* accs) {
+    const uint32_t tid = threadIdx.x;
+    static_assert(NH * 256 == 4 * ATT_MT, "one float4 of outputs per merging thread");
+    const uint32_t h = (4 * tid) >> 8;
+    float M = -INFINITY, L = 0.0f;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 4
+    for (uint32_t b = 0; b < cnt; ++b) {
+        const float2 st = __ldcg(reinterpret_cast<const float2*>(stat + (size_t)b * NH * 2) + h);
+        if (st.y > 0.0f) M = fmaxf(M, st.x);
+    }
+#pragma unroll 4
+    for (uint32_t b = 0; b < cnt; ++b) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(part + (size_t)b * NH * 256) + tid);
+        const float2 st = __ldcg(reinterpret_cast<const float2*>(stat + (size_t)b * NH * 2) + h);
+        const float w = st.y > 0.0f ? expf(st.x - M) : 0.0f;
+        L += st.y * w;
+        o.x += v.x * w; o.y += v.y * w; o.z += v.z * w; o.w += v.w * w;
+    }
+    attn_finish<NH>(o, M, L, out, nullptr, xq, true, accs);
+}
+
+// The cluster's partials in the leader's shared-memory slots (cnt <= MAXP
+// = 16). The weights e^(m_b - M) depend only on (head, partial), so lane b of
+// half-warp h computes head h's weight for partial b once (M by a max over
+// the half-warp, L summed in partial order by lane 0) into wsh[NH][16] and
+// lsh[NH]; then every thread accumulates its float4 in partial order. The
+// same operations in the same order as the loop above, 1/64 of the exps.
+template <int NH, int MAXP>
+XP_DEV void attn_merge_slots(const float* slots, uint32_t cnt, float4& o, float& M, float& L, float* wsh,
+                             float* lsh) {
+    static_assert(MAXP == 16 && NH * 16 <= ATT_MT, "a half-warp per head");
+    const uint32_t tid = threadIdx.x;
+    constexpr uint32_t SF = AttnSmem::slot_bytes / 4;
+    if (tid < NH * 16) {
+        const uint32_t h = tid >> 4, b = tid & 15;
+        const float2 st = b < cnt ? reinterpret_cast<const float2*>(slots + b * SF + NH * 256)[h] : make_float2(0.0f, 0.0f);
+        float m = st.y > 0.0f ? st.x : -INFINITY;
+#pragma unroll
+        for (int d = 8; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+        const float w = st.y > 0.0f ? expf(st.x - m) : 0.0f;
+        wsh[h * 16 + b] = w;
+        // L in partial order (lane 0 of the half-warp gathers the terms)
+        float l = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MAXP; ++k) {
+            const float yk = __shfl_sync(0xffffffffu, st.y, (tid & 16) + k);
+            const float wk = __shfl_sync(0xffffffffu, w, (tid & 16) + k);
+            if ((uint32_t)k < cnt) l += yk * wk;
+        }
+        if (b == 0) { lsh[h * 2] = m; lsh[h * 2 + 1] = l; }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(ATT_MT) : "memory");
+    const uint32_t h = (4 * tid) >> 8;
+    M = lsh[h * 2];
+    L = lsh[h * 2 + 1];
+    o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int b = 0; b < MAXP; ++b)
+        if ((uint32_t)b < cnt) {
+            const float4 v = reinterpret_cast<const float4*>(slots + b * SF)[tid];
+            const float w = wsh[h * 16 + b];
+            o.x += v.x * w; o.y += v.y * w; o.z += v.z * w; o.w += v.w * w;
+        }
 }
 
 template <int NH>
@@ -225,21 +294,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     float* qs = reinterpret_cast<float*>(smem + AttnSmem::qs);         // [NH][256], pre-scaled
     __half* kn = reinterpret_cast<__half*>(smem + AttnSmem::knv);     // [256] new k (fp16)
     __half* vn = kn + 256;                                            // [256] new v (fp16)
-    float* accs = reinterpret_cast<float*>(smem + AttnSmem::accs);     // [2][NH][256] P.V halves
+    float* accs = reinterpret_cast<float*>(smem + AttnSmem::accs);     // [ATT_PVG][NH][256] P.V by row group
     float* sc = reinterpret_cast<float*>(smem + AttnSmem::sc);         // [chunk_max][NH] scores / probs
     __shared__ __align__(16) float stat[NH * 2];  // (max, sum) per head, read as float2 by the merge
     __shared__ float rcs[256];  // RoPE cos | sin of this position
+    __shared__ float wsh[NH * 16 + NH * 2];  // merge weights [NH][16] | (M, L) per head
     __shared__ uint32_t s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#ifdef XP_ATT_TRACE
+    unsigned long long tr_[16] = {};
+    ATT_STAMP(0);
+#endif
     if (tid == 0) {
-        for (uint32_t s = 0; s < ATT_STAGES; ++s) mbar_init(&bar[s], 1);
+        for (uint32_t s = 0; s <= ATT_STAGES; ++s) mbar_init(&bar[s], 1);  // copy ring + merge
         fence_mbar_init();
     }
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    const uint32_t csize = cl.num_blocks(), crank = cl.block_rank();
+    if (csize > 1) cluster_arrive_relaxed();  // the leader's merge barrier is initialised
     pdl_launch_dependents();
     pdl_wait();
+    ATT_STAMP(1);
+#ifdef XP_ATT_TRACE
+    const uint32_t launch_ = *(volatile uint32_t*)&g_att_launch & 63;
+    auto flush_ = [&]() {
+        if (tid == 0 && blockIdx.x < 160)
+            for (int i = 0; i < 16; ++i) g_att_trace[((size_t)launch_ * 160 + blockIdx.x) * 16 + i] = tr_[i];
+    };
+#endif
 
     const uint32_t pos = *a.pos;
+    ATT_STAMP(2);
     if (pos >= a.cache_rows) {  // the append would land past the caches: flag, write nothing
         if (tid == 0 && blockIdx.x == 0 && a.err) atomicOr(a.err, TK_ERR_POS);
         return;
@@ -268,9 +355,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
         mbar_expect_tx(b, rows * 512);
         bulk_g2s(ring + (size_t)(u % ATT_STAGES) * ATT_TILE * 256, src, rows * 512, b);
     };
-    __syncthreads();  // barriers initialised
+    // thread 0 initialised the barriers, so it issues the first copies at once;
+    // every other thread's first wait comes after the block barrier below
     if (tid == 0)
         for (uint32_t u = 0; u < min(2 * nt, ATT_STAGES); ++u) issue(u);
+    ATT_STAMP(10);
 
     // ---- q, k, v post-processing (overlaps the first copies) ------------------------------
     // The position's RoPE table is computed once (one angle per thread); the
@@ -311,6 +400,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
         }
     }
     __syncthreads();
+    ATT_STAMP(3);
+
 
     // ---- scores: one warp per key, lane owns dims 8*lane..8*lane+7 ----------------
     float q[NH][8];
@@ -320,14 +411,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
         for (int i = 0; i < 8; ++i) q[h][i] = qs[h * 256 + 8 * lane + i];
     for (uint32_t u = 0; u < nt; ++u) {
         mbar_wait(&bar[u % ATT_STAGES], (u / ATT_STAGES) & 1, a.err);
+#ifdef XP_ATT_TRACE
+        if (u < 2) ATT_STAMP(11 + u);
+#endif
         const __half* tile = ring + (size_t)(u % ATT_STAGES) * ATT_TILE * 256;
         const uint32_t rows = min(ATT_TILE, n - u * ATT_TILE);
-        static_assert(ATT_TILE == 4 * (ATT_THREADS / 32), "four rows of a tile per warp");
-        // rows 4 warp .. 4 warp + 3: four independent dot products and reductions
-        float tot[4];
+        constexpr int RPW = ATT_TILE / (ATT_THREADS / 32);  // rows of a tile per warp
+        static_assert(RPW * (ATT_THREADS / 32) == ATT_TILE, "whole rows per warp");
+        // rows RPW warp .. RPW warp + RPW - 1: independent dot products and reductions
+        float tot[RPW];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-            const uint32_t r = 4 * warp + rr;
+        for (int rr = 0; rr < RPW; ++rr) {
+            const uint32_t r = RPW * warp + rr;
             const uint32_t jj = u * ATT_TILE + r;
             uint4 raw = make_uint4(0u, 0u, 0u, 0u);
             if (r < rows)
@@ -354,13 +449,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
         if ((lane & 7) == 0) {
             const int h = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr)
-                if (4 * warp + rr < rows) sc[(u * ATT_TILE + 4 * warp + rr) * NH + h] = tot[rr];
+            for (int rr = 0; rr < RPW; ++rr)
+                if (RPW * warp + rr < rows) sc[(u * ATT_TILE + RPW * warp + rr) * NH + h] = tot[rr];
         }
         __syncthreads();  // stage consumed
         if (tid == 0 && u + ATT_STAGES < 2 * nt) issue(u + ATT_STAGES);
     }
 
+    ATT_STAMP(4);
     // ---- chunk softmax statistics ---------------------------------------------------
     if (warp < NH) {
         float m = -INFINITY;
@@ -376,16 +472,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
         if (lane == 0) { stat[warp * 2] = m; stat[warp * 2 + 1] = l; }
     }
     __syncthreads();
+    ATT_STAMP(5);
 
-    // ---- P.V: thread owns a dim pair, alternate rows of each tile ------------------------
+    // ---- P.V: thread owns a dim pair and every ATT_PVG-th row of each tile -----------------
     {
-        const uint32_t dp = tid & 127, half = tid >> 7;
+        const uint32_t dp = tid & 127, grp = tid >> 7;
         float acc[NH][2];
 #pragma unroll
         for (int h = 0; h < NH; ++h) acc[h][0] = acc[h][1] = 0.0f;
         for (uint32_t t = 0; t < nt; ++t) {
             const uint32_t u = nt + t;
             mbar_wait(&bar[u % ATT_STAGES], (u / ATT_STAGES) & 1, a.err);
+#ifdef XP_ATT_TRACE
+            if (t < 2) ATT_STAMP(13 + t);
+#endif
             const __half* tile = ring + (size_t)(u % ATT_STAGES) * ATT_TILE * 256;
             const uint32_t rows = min(ATT_TILE, n - t * ATT_TILE);
             auto row = [&](uint32_t r) {
@@ -403,50 +503,97 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
             };
             if (rows == ATT_TILE) {
 #pragma unroll
-                for (uint32_t r0 = 0; r0 < ATT_TILE; r0 += 2) row(r0 + half);
+                for (uint32_t r0 = 0; r0 < ATT_TILE; r0 += ATT_PVG) row(r0 + grp);
             } else {
 #pragma unroll 1
-                for (uint32_t r = half; r < rows; r += 2) row(r);
+                for (uint32_t r = grp; r < rows; r += ATT_PVG) row(r);
             }
             __syncthreads();  // stage consumed
             if (tid == 0 && u + ATT_STAGES < 2 * nt) issue(u + ATT_STAGES);
         }
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
-            accs[(half * NH + h) * 256 + 2 * dp] = acc[h][0];
-            accs[(half * NH + h) * 256 + 2 * dp + 1] = acc[h][1];
+            accs[(grp * NH + h) * 256 + 2 * dp] = acc[h][0];
+            accs[(grp * NH + h) * 256 + 2 * dp + 1] = acc[h][1];
         }
     }
     __syncthreads();
-    // ---- combine: cluster peers through DSMEM, then clusters through global memory ----------------
-    for (uint32_t i = tid; i < NH * 256; i += ATT_THREADS) accs[i] += accs[NH * 256 + i];
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    const uint32_t csize = cl.num_blocks(), crank = cl.block_rank();
+    ATT_STAMP(6);
+    // ---- combine: push to the cluster leader, then clusters through global memory ----------------
+    // threads 0..ATT_MT-1 own one float4 of the [NH][256] partial each
     const uint32_t ncl = nblk / csize, ci = blockIdx.x / csize;
-    cl.sync();  // every CTA's partial (accs, stat) is in its shared memory
-    if (crank == 0) {
-        auto ppart = [&](uint32_t b) { return cl.map_shared_rank(accs, b); };
-        auto pstat = [&](uint32_t b) { return cl.map_shared_rank(&stat[0], b); };
-        // the merged cluster partial goes to the second half of accs (unused by peers)
-        if (ncl == 1)
-            attn_merge<NH, true>(ppart, pstat, csize, a.att, nullptr, a.att_xq, true, accs + NH * 256);
-        else
-            attn_merge<NH, true>(ppart, pstat, csize, a.part + (size_t)ci * NH * 256, a.pstat + (size_t)ci * NH * 2,
-                                 nullptr, false, accs + NH * 256);
+    float* slots = reinterpret_cast<float*>(smem + AttnSmem::slots(a.chunk_max));
+    constexpr uint32_t SLOT_F = AttnSmem::slot_bytes / 4;
+    const bool mt = tid < ATT_MT;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (mt)
+#pragma unroll
+        for (int g = 0; g < ATT_PVG; ++g) {
+            const float4 x = reinterpret_cast<const float4*>(accs)[g * NH * 64 + tid];
+            o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
+        }
+    if (csize > 1) {
+        cluster_wait();
+        if (crank != 0) {
+            // this CTA's partial and statistics into the leader's slot `crank`;
+            // the leader waits on its barrier for every peer's bytes
+            if (!mt) return;
+            const uint32_t dst = mapa_shared(smem_u32(slots + crank * SLOT_F), 0);
+            const uint32_t rb = mapa_shared(smem_u32(&bar[ATT_STAGES]), 0);
+            st_async_v4(dst + 16 * tid, o, rb);
+            if (tid < NH / 2) st_async_v4(dst + NH * 256 * 4 + 16 * tid, reinterpret_cast<const float4*>(stat)[tid], rb);
+            ATT_STAMP(7);
+#ifdef XP_ATT_TRACE
+            flush_();
+#endif
+            return;
+        }
+        if (mt) reinterpret_cast<float4*>(slots)[tid] = o;
+        if (tid < NH / 2) reinterpret_cast<float4*>(slots + NH * 256)[tid] = reinterpret_cast<const float4*>(stat)[tid];
+        if (tid == 0) mbar_expect_tx(&bar[ATT_STAGES], (csize - 1) * (uint32_t)AttnSmem::slot_bytes);
+        __syncthreads();
+        mbar_wait(&bar[ATT_STAGES], 0, a.err);
     }
-    cl.sync();  // peers keep their shared memory until the first CTA has read it
-    if (ncl == 1 || crank != 0) return;
+    ATT_STAMP(7);
+    // the cluster's merged partial (a lone CTA's own partial as it stands:
+    // the merge of one partial is the identity); the second half of accs
+    // stages the matvec limbs
+    if (mt) {
+        float M, L;
+        if (csize > 1) {
+            attn_merge_slots<NH, 16>(slots, csize, o, M, L, wsh, wsh + NH * 16);
+        } else {
+            const float2 st = reinterpret_cast<const float2*>(stat)[(4 * tid) >> 8];
+            const bool live = st.y > 0.0f;
+            M = live ? st.x : -INFINITY;
+            L = live ? st.y : 0.0f;
+            if (!live) o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        attn_finish<NH>(o, M, L, ncl == 1 ? a.att : a.part + (size_t)ci * NH * 256,
+                        a.pstat + (size_t)ci * NH * 2, ncl == 1 ? a.att_xq : nullptr, ncl == 1, accs + NH * 256);
+#ifdef XP_ATT_TRACE
+        if (tid == 0) tr_[14] = globaltimer_ns();
+#endif
+    }
+    ATT_STAMP(8);
+#ifdef XP_ATT_TRACE
+    flush_();
+    if (ncl == 1 && tid == 0) { __threadfence(); atomicAdd(&g_att_launch, 1u); }
+#endif
+    if (ncl == 1) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = (atomicAdd(a.ticket, 1u) == ncl - 1) ? 1u : 0u;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    auto gpart = [&](uint32_t b) { return a.part + (size_t)b * NH * 256; };
-    auto gstat = [&](uint32_t b) { return a.pstat + (size_t)b * NH * 2; };
-    attn_merge<NH, false>(gpart, gstat, ncl, a.att, nullptr, a.att_xq, true, accs);
+    if (mt) attn_merge_global<NH>(a.part, a.pstat, ncl, a.att, a.att_xq, accs);
     if (tid == 0) *a.ticket = 0;
+#ifdef XP_ATT_TRACE
+    ATT_STAMP(9);
+    flush_();
+    if (tid == 0) { __threadfence(); atomicAdd(&g_att_launch, 1u); }
+#endif
 }
 
 }  // namespace xp

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstring>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "../../include/xp_cuda.h"
@@ -125,9 +126,22 @@ inline cudaError_t launch_mv(const MvArgs& a, cudaStream_t st, bool pdl, uint32_
 
 // ---- attention -------------------------------------------------------------------------
 // CTAs per split launch: nsplit, rounded up to a multiple of 8 above 64 so
-// that large grids form clusters of 8 (else 4, 2 or 1 CTAs).
+// that large grids form clusters of 8 (else 4, 2 or 1 CTAs). A grid that is a
+// multiple of 16 forms clusters of 16 (a non-portable size: one GPC), one
+// merge level fewer at 16 and 128 splits; XP_ATTN_CLUSTER=8 keeps clusters
+// within the portable 8.
 constexpr uint32_t attn_grid(uint32_t nsplit) { return nsplit <= 64 ? nsplit : (nsplit + 7) & ~7u; }
-constexpr uint32_t attn_cluster(uint32_t grid) { return grid % 8 == 0 ? 8 : grid % 4 == 0 ? 4 : grid % 2 == 0 ? 2 : 1; }
+inline uint32_t attn_cluster_max() {
+    static const uint32_t c = [] {
+        const char* e = std::getenv("XP_ATTN_CLUSTER");
+        return (e && std::atoi(e) == 8) ? 8u : 16u;
+    }();
+    return c;
+}
+inline uint32_t attn_cluster(uint32_t grid) {
+    if (attn_cluster_max() == 16 && grid % 16 == 0) return 16;
+    return grid % 8 == 0 ? 8 : grid % 4 == 0 ? 4 : grid % 2 == 0 ? 2 : 1;
+}
 // scratch: [ticket u32 | error word u32 | pad to 512][cluster partials | cluster stats]
 constexpr size_t ATT_SCRATCH_HDR = 512;
 constexpr size_t attn_scratch_bytes(uint32_t nsplit) {
@@ -142,7 +156,7 @@ inline uint32_t attn_chunk_max(uint32_t nsplit, uint32_t max_seq) {
     uint32_t c = (max_seq + nsplit - 1) / nsplit;
     return (c + 7) & ~7u;
 }
-inline size_t attn_smem(uint32_t chunk_max) { return AttnSmem::bytes(chunk_max); }
+inline size_t attn_smem(uint32_t chunk_max, uint32_t cluster) { return AttnSmem::bytes(chunk_max, cluster); }
 // RoPE inverse frequencies theta^(-2d/256), d < 128, with log2 and exp2 each
 // rounded once from double (the oracle's formula, computed on the host so the
 // device table matches it bit for bit). Small per-thread cache: decode
@@ -168,7 +182,7 @@ inline void rope_table_host(float theta, float* out) {
 inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint32_t max_seq, cudaStream_t st,
                                bool pdl) {
     static std::atomic<bool> attr_set[kMaxDevices];
-    if (cudaError_t e = smem_attr_once(attr_set, attn_decode_kernel<4>, 200 * 1024); e != cudaSuccess) return e;
+    if (cudaError_t e = smem_attr_once(attr_set, attn_decode_kernel<4>, 200 * 1024, true); e != cudaSuccess) return e;
     char* s = static_cast<char*>(scratch);
     const uint32_t grid = attn_grid(nsplit), cl = attn_cluster(grid);
     a.ticket = reinterpret_cast<uint32_t*>(s);
@@ -177,7 +191,7 @@ inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint3
     a.pstat = a.part + (size_t)(grid / cl) * 4 * 256;
     a.chunk_max = attn_chunk_max(grid, max_seq);
     rope_table_host(a.theta, a.inv_freq);
-    return launch_ex(attn_decode_kernel<4>, dim3(grid), dim3(ATT_THREADS), attn_smem(a.chunk_max), st, cl, pdl, a);
+    return launch_ex(attn_decode_kernel<4>, dim3(grid), dim3(ATT_THREADS), attn_smem(a.chunk_max, cl), st, cl, pdl, a);
 }
 
 // ---- sampling ----------------------------------------------------------------------------
