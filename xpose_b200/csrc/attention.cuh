@@ -169,7 +169,12 @@ XP_DEV void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
 }
 
 constexpr uint32_t ATT_TILE = 32;    // positions per bulk-copy stage (16 KB of K or V)
-constexpr uint32_t ATT_STAGES = 4;
+#ifndef XP_ATT_STAGES
+#define XP_ATT_STAGES 4
+#endif
+constexpr uint32_t ATT_STAGES = XP_ATT_STAGES;  // copies in flight per CTA
+static_assert(ATT_STAGES + 1 <= 16, "the ring and merge barriers fit the 128-byte barrier area");
+constexpr size_t ATT_SMEM_MAX = 225 * 1024;  // dynamic shared memory a launch may ask for
 
 // Shared-memory layout of attn_decode_kernel (bytes from the dynamic base).
 struct AttnSmem {

@@ -1075,7 +1075,7 @@ inline xp_status attn_validate(const float* out, const float* q_raw, const float
         if (!ptrs[i]) return fail(XP_ERR_INVALID, "attention_decode: argument '%s' is null", names[i]);
     if (nsplit == 0 || nsplit > 1024) return fail(XP_ERR_INVALID, "attention_decode: nsplit must be 1..1024");
     if (max_seq == 0) return fail(XP_ERR_INVALID, "attention_decode: max_seq must be at least 1");
-    if (attn_smem(attn_chunk_max(nsplit, attn_span_max(window, max_seq)), attn_cluster(attn_grid(nsplit))) > 200 * 1024)
+    if (attn_smem(attn_chunk_max(nsplit, attn_span_max(window, max_seq)), attn_cluster(attn_grid(nsplit))) > ATT_SMEM_MAX)
         return fail(XP_ERR_INVALID, "attention_decode: max_seq/nsplit too large for shared memory");
     if (((uintptr_t)out | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)scratch) & 15)
         return fail(XP_ERR_INVALID, "attention_decode: out, the caches and scratch must be 16-byte aligned");

@@ -182,7 +182,7 @@ inline void rope_table_host(float theta, float* out) {
 inline cudaError_t launch_attn(AttnArgs a, void* scratch, uint32_t nsplit, uint32_t max_seq, cudaStream_t st,
                                bool pdl) {
     static std::atomic<bool> attr_set[kMaxDevices];
-    if (cudaError_t e = smem_attr_once(attr_set, attn_decode_kernel<4>, 200 * 1024, true); e != cudaSuccess) return e;
+    if (cudaError_t e = smem_attr_once(attr_set, attn_decode_kernel<4>, (int)ATT_SMEM_MAX, true); e != cudaSuccess) return e;
     char* s = static_cast<char*>(scratch);
     const uint32_t grid = attn_grid(nsplit), cl = attn_cluster(grid);
     a.ticket = reinterpret_cast<uint32_t*>(s);
