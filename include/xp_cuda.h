@@ -322,6 +322,19 @@ xp_status xp_session_config(xp_session* s, xp_model_config* cfg);
  * pointers): examples/llm/model/gguf.cpp:448-634 GGUFFile::dequantize, bit-exact.
  * Types as for xp_session_create_gguf. */
 xp_status xp_gguf_dequantize(void* stream, uint32_t ggml_type, const void* src, float* dst, uint64_t n);
+/* Element counts of the planes examples/llm/quant_repack.cpp repack() makes
+ * for a rows x cols tensor of ggml type Q8_0 (8), Q5_0 (6), Q4_K (12) or
+ * Q6_K (14): sizes[0] quant words, [1] high words, [2] fp32 scales,
+ * [3] fp32 biases (0 where the type has no such plane). XP_ERR_INVALID for
+ * another type, cols not a multiple of 32 (256 for the K types) or rows 0. */
+xp_status xp_quant_repack_sizes(uint32_t ggml_type, uint32_t rows, uint32_t cols, uint64_t* sizes);
+/* That repack on the device (every pointer a device pointer): native GGUF
+ * blocks -> the interleaved planes the kernels/llm_quant.spv matvec_rq*
+ * entries read, bit-identical to the host repack (quant_repack.cpp:130-210),
+ * padding rows written as zeros. `quant` 16-byte aligned; `high` and `bias`
+ * may be NULL for types without them. */
+xp_status xp_quant_repack(void* stream, uint32_t ggml_type, const void* src, uint32_t rows, uint32_t cols,
+                          uint32_t* quant, uint32_t* high, float* scale, float* bias);
 /* ---- tokenizer (examples/llm/model/tokenizer.{hpp,cpp}) --------------------
  * The SentencePiece vocabulary of a GGUF file (tokenizer.ggml.*): encode with
  * CONTROL/UNKNOWN tokens cut out first, the leading space marker, best-score

@@ -14,6 +14,8 @@
 #include <cstring>
 #include <memory>
 
+#include "quant_repack.hpp"
+
 using namespace vulkore::llm;
 
 extern "C" {
@@ -48,6 +50,24 @@ uint64_t xpref_xpack_hash_mt(const void* data, uint64_t n, uint32_t threads) {
     return xpack_hash_mt(data, (size_t)n, threads);
 }
 uint32_t xpref_quantise(float v, float inv) { return quantise(v, inv); }
+
+// examples/llm/quant_repack.cpp repack(): native GGUF blocks -> the planes of
+// the matvec_rq* kernels. sizes[4] receives the element counts of quant,
+// high, scale and bias; each output pointer may be null (size query).
+int xpref_quant_repack(uint32_t type, const void* src, uint32_t rows, uint32_t cols, uint32_t* quant,
+                       uint32_t* high, float* scale, float* bias, uint64_t* sizes) {
+    RepackedTensor t;
+    if (!repack(static_cast<GGMLType>(type), src, rows, cols, t)) return -1;
+    sizes[0] = t.quant.size();
+    sizes[1] = t.high.size();
+    sizes[2] = t.scale.size();
+    sizes[3] = t.bias.size();
+    if (quant) std::memcpy(quant, t.quant.data(), t.quant.size() * 4);
+    if (high) std::memcpy(high, t.high.data(), t.high.size() * 4);
+    if (scale) std::memcpy(scale, t.scale.data(), t.scale.size() * 4);
+    if (bias) std::memcpy(bias, t.bias.data(), t.bias.size() * 4);
+    return 0;
+}
 
 uint64_t xpref_plan_weight_bytes(void) {
     return plan_token(DecodeConfig::gemma3_1b(), MatvecConfig{}).weight_bytes;

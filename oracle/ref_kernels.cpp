@@ -1,5 +1,6 @@
 // CPU checker: the reference's own OpenCL C kernels (kernels/llm_matvec.cl,
-// kernels/llm_transformer.cl, kernels/llm_sampling.cl, kernels/llm.cl)
+// kernels/llm_transformer.cl, kernels/llm_sampling.cl, kernels/llm.cl,
+// kernels/llm_quant.cl)
 // compiled VERBATIM as host C++ through cl_shim.hpp, and dispatched over the
 // same global grids the reference runtime uses (src/launch.cpp:21-35: grid =
 // global thread count, every kernel bound-checks its id).
@@ -39,6 +40,14 @@ namespace ref_transformer {
 namespace ref_sampling {
 #include STR(REF_DIR/kernels/llm_sampling.cl)
 }
+namespace ref_quant {
+#include STR(REF_DIR/kernels/llm_quant.cl)
+}
+#undef NIB8
+#undef N5_8
+#undef N6_8
+#undef B4
+#undef SPLIT_PROLOGUE
 #undef kernel
 #undef global
 #undef constant
@@ -96,6 +105,7 @@ const char* M_LLM = "kernels/llm.spv";
 const char* M_MV = "kernels/llm_matvec.spv";
 const char* M_TF = "kernels/llm_transformer.spv";
 const char* M_SM = "kernels/llm_sampling.spv";
+const char* M_QT = "kernels/llm_quant.spv";
 
 const std::vector<Entry>& table() {
     static const std::vector<Entry> t = {
@@ -137,6 +147,13 @@ const std::vector<Entry>& table() {
         K(M_SM, ref_sampling, rmsnorm_rows_sumsq), K(M_SM, ref_sampling, rmsnorm_rows_apply_gemma),
         K(M_SM, ref_sampling, rmsnorm_heads_rows_gemma), K(M_SM, ref_sampling, rope_prefill),
         K(M_SM, ref_sampling, kv_append_rows), K(M_SM, ref_sampling, embed_lookup_rows),
+        K(M_QT, ref_quant, fp16_decode), K(M_QT, ref_quant, dequant_q8_0), K(M_QT, ref_quant, matvec_q8_0),
+        K(M_QT, ref_quant, dequant_q5_0), K(M_QT, ref_quant, matvec_q5_0), K(M_QT, ref_quant, dequant_q4_k),
+        K(M_QT, ref_quant, matvec_q4_k), K(M_QT, ref_quant, dequant_q6_k), K(M_QT, ref_quant, matvec_q6_k),
+        K(M_QT, ref_quant, matvec_rq4_k), K(M_QT, ref_quant, matvec_rq5_0), K(M_QT, ref_quant, matvec_rq6_k),
+        K(M_QT, ref_quant, matvec_rq8_0), K(M_QT, ref_quant, matvec_rq4_k_split),
+        K(M_QT, ref_quant, matvec_rq5_0_split), K(M_QT, ref_quant, matvec_rq6_k_split),
+        K(M_QT, ref_quant, matvec_rq8_0_split), K(M_QT, ref_quant, mv_reduce),
     };
     return t;
 }

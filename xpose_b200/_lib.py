@@ -151,6 +151,8 @@ _SIGS = {
     "xp_session_load_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_char_p, C.c_uint32]),
     "xp_session_config": (C.c_int, [C.c_void_p, C.POINTER(ModelConfig)]),
     "xp_gguf_dequantize": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_uint64]),
+    "xp_quant_repack_sizes": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(C.c_uint64)]),
+    "xp_quant_repack": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32] + [C.c_void_p] * 4),
     "xp_session_create": (C.c_int, [C.c_int, C.POINTER(ModelConfig), C.POINTER(Sampling), C.POINTER(LayerWeights),
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "xp_session_destroy": (C.c_int, [C.c_void_p]),

@@ -16,6 +16,7 @@
 #include "bmm.cuh"
 #include "mv_stream.cuh"
 #include "ops.cuh"
+#include "quant.cuh"
 #include "runtime.cuh"
 
 using namespace xp;
@@ -170,10 +171,49 @@ cudaError_t launch_stream4(const xp_arg* a, xp_grid g, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// kernels/llm_quant.cl: element-wise dequant on the ggml element decoder,
+// native-layout matvecs a warp per row, repacked matvecs a CTA per 64-row group
+template <uint32_t TYPE>
+cudaError_t launch_dequant(const xp_arg* a, xp_grid, cudaStream_t st) {
+    return gguf_dequant(st, TYPE, a[1].ptr, arg_as<float*>(a[0]), arg_as<uint32_t>(a[2]));
+}
+template <void (*K)(float*, const float*, const uint32_t*, uint32_t, uint32_t)>
+cudaError_t launch_mvq(const xp_arg* a, xp_grid, cudaStream_t st) {
+    const uint32_t rows = arg_as<uint32_t>(a[3]);
+    K<<<(rows + 7) / 8, 256, 0, st>>>(arg_as<float*>(a[0]), arg_as<const float*>(a[1]), arg_as<const uint32_t*>(a[2]),
+                                      rows, arg_as<uint32_t>(a[4]));
+    return cudaGetLastError();
+}
+template <int F, bool SPLIT>
+cudaError_t launch_rqv(const xp_arg* a, xp_grid, cudaStream_t st) {
+    quant::RqArgs r{};
+    r.out = arg_as<float*>(a[0]);
+    r.x = arg_as<const float4*>(a[1]);
+    r.q = arg_as<const uint4*>(a[2]);
+    uint32_t i = 3;
+    if (F == quant::RQ50 || F == quant::RQ6K) r.hi = arg_as<const uint32_t*>(a[i++]);
+    r.scale = arg_as<const float*>(a[i++]);
+    if (F == quant::RQ4K) r.bias = arg_as<const float*>(a[i++]);
+    r.rows = arg_as<uint32_t>(a[i++]);
+    r.cols = arg_as<uint32_t>(a[i++]);
+    r.split = SPLIT ? arg_as<uint32_t>(a[i]) : 1u;
+    if (r.split == 0 || r.rows == 0) return cudaErrorInvalidValue;
+    return quant::launch_rq(F, r, st);
+}
+__global__ void proto_rq4k(float*, const float4*, const uint4*, const float*, const float*, uint32_t, uint32_t) {}
+__global__ void proto_rq4k_split(float*, const float4*, const uint4*, const float*, const float*, uint32_t, uint32_t,
+                                 uint32_t) {}
+__global__ void proto_rqhi(float*, const float4*, const uint4*, const uint32_t*, const float*, uint32_t, uint32_t) {}
+__global__ void proto_rqhi_split(float*, const float4*, const uint4*, const uint32_t*, const float*, uint32_t,
+                                 uint32_t, uint32_t) {}
+__global__ void proto_rq80(float*, const float4*, const uint4*, const float*, uint32_t, uint32_t) {}
+__global__ void proto_rq80_split(float*, const float4*, const uint4*, const float*, uint32_t, uint32_t, uint32_t) {}
+
 #define LLM "kernels/llm.spv"
 #define MV "kernels/llm_matvec.spv"
 #define TF "kernels/llm_transformer.spv"
 #define SM "kernels/llm_sampling.spv"
+#define QT "kernels/llm_quant.spv"
 #define E(mod, fn, geo, names) Entry{mod, #fn, names, Gen<&ops::fn, geo>::specs(), &Gen<&ops::fn, geo>::launch}
 #define EC(mod, fn, proto, launcher, names) Entry{mod, fn, names, Gen<proto, GEO_CUSTOM>::specs(), launcher}
 
@@ -273,6 +313,31 @@ const std::vector<Entry>& registry() {
         E(SM, rope_prefill, GEO_THREADS, "x,n_tokens,n_heads,head_dim,pos0,theta"),
         E(SM, kv_append_rows, GEO_THREADS, "cache,src,n_tokens,row,pos0"),
         E(SM, embed_lookup_rows, GEO_THREADS, "out,table,tokens,n_tokens,n"),
+        // kernels/llm_quant.cl
+        Entry{QT, "fp16_decode", "out,src,n", Gen<&quant::fp16_decode, GEO_THREADS>::specs(),
+              &Gen<&quant::fp16_decode, GEO_THREADS>::launch},
+        EC(QT, "dequant_q8_0", &quant::fp16_decode, &launch_dequant<8>, "out,src,n"),
+        EC(QT, "dequant_q5_0", &quant::fp16_decode, &launch_dequant<6>, "out,src,n"),
+        EC(QT, "dequant_q4_k", &quant::fp16_decode, &launch_dequant<12>, "out,src,n"),
+        EC(QT, "dequant_q6_k", &quant::fp16_decode, &launch_dequant<14>, "out,src,n"),
+        EC(QT, "matvec_q8_0", &quant::matvec_q32<true>, &launch_mvq<&quant::matvec_q32<true>>, "out,in,w,rows,cols"),
+        EC(QT, "matvec_q5_0", &quant::matvec_q32<false>, &launch_mvq<&quant::matvec_q32<false>>, "out,in,w,rows,cols"),
+        EC(QT, "matvec_q4_k", &quant::matvec_q4_k, &launch_mvq<&quant::matvec_q4_k>, "out,in,w,rows,cols"),
+        EC(QT, "matvec_q6_k", &quant::matvec_q6_k, &launch_mvq<&quant::matvec_q6_k>, "out,in,w,rows,cols"),
+        EC(QT, "matvec_rq4_k", &proto_rq4k, (&launch_rqv<quant::RQ4K, false>), "out,in,q,scale,bias,rows,cols"),
+        EC(QT, "matvec_rq5_0", &proto_rqhi, (&launch_rqv<quant::RQ50, false>), "out,in,q,hi,scale,rows,cols"),
+        EC(QT, "matvec_rq6_k", &proto_rqhi, (&launch_rqv<quant::RQ6K, false>), "out,in,q,hi,scale,rows,cols"),
+        EC(QT, "matvec_rq8_0", &proto_rq80, (&launch_rqv<quant::RQ80, false>), "out,in,q,scale,rows,cols"),
+        EC(QT, "matvec_rq4_k_split", &proto_rq4k_split, (&launch_rqv<quant::RQ4K, true>),
+           "partial,in,q,scale,bias,rows,cols,split"),
+        EC(QT, "matvec_rq5_0_split", &proto_rqhi_split, (&launch_rqv<quant::RQ50, true>),
+           "partial,in,q,hi,scale,rows,cols,split"),
+        EC(QT, "matvec_rq6_k_split", &proto_rqhi_split, (&launch_rqv<quant::RQ6K, true>),
+           "partial,in,q,hi,scale,rows,cols,split"),
+        EC(QT, "matvec_rq8_0_split", &proto_rq80_split, (&launch_rqv<quant::RQ80, true>),
+           "partial,in,q,scale,rows,cols,split"),
+        Entry{QT, "mv_reduce", "out,partial,rows,split", Gen<&quant::rq_reduce, GEO_THREADS>::specs(),
+              &Gen<&quant::rq_reduce, GEO_THREADS>::launch},
     };
     return t;
 }

@@ -27,97 +27,9 @@
 #include <vector>
 
 #include "engine.cuh"
+#include "quant.cuh"
 
 namespace xp {
-
-// ---- ggml tensor types (block sizes are the ggml ABI) -------------------------
-struct GgmlType {
-    uint32_t id, block, bytes;
-    const char* name;
-};
-inline const GgmlType* ggml_type(uint32_t id) {
-    static const GgmlType t[] = {{0, 1, 4, "F32"},      {1, 1, 2, "F16"},      {30, 1, 2, "BF16"},
-                                 {2, 32, 18, "Q4_0"},   {3, 32, 20, "Q4_1"},   {6, 32, 22, "Q5_0"},
-                                 {7, 32, 24, "Q5_1"},   {8, 32, 34, "Q8_0"},   {12, 256, 144, "Q4_K"},
-                                 {14, 256, 210, "Q6_K"}};
-    for (const auto& e : t)
-        if (e.id == id) return &e;
-    return nullptr;
-}
-
-XP_DEV float gg_f16(const uint8_t* p) { return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8)))); }
-
-// One element of a ggml block tensor (the formats of gguf.cpp:448-634).
-// Products and sums are rounded one operation at a time (no contraction), as
-// the host formula does, so the values are bit-identical to it.
-XP_DEV float gg_elem(uint32_t type, const uint8_t* src, uint64_t i) {
-    switch (type) {
-        case 1: return gg_f16(src + 2 * i);
-        case 30: return __uint_as_float((uint32_t)(src[2 * i] | (src[2 * i + 1] << 8)) << 16);
-        case 8: {
-            const uint8_t* b = src + (i / 32) * 34;
-            return __fmul_rn((float)(int8_t)b[2 + i % 32], gg_f16(b));
-        }
-        case 2: case 3: {
-            const uint32_t bs = type == 2 ? 18 : 20, j = i % 32;
-            const uint8_t* b = src + (i / 32) * bs;
-            const uint8_t q = b[(type == 2 ? 2 : 4) + (j & 15)];
-            const int v = j < 16 ? (q & 0xF) : (q >> 4);
-            if (type == 2) return __fmul_rn((float)(v - 8), gg_f16(b));
-            return __fadd_rn(__fmul_rn((float)v, gg_f16(b)), gg_f16(b + 2));
-        }
-        case 6: case 7: {
-            const bool one = type == 7;
-            const uint32_t j = i % 32, jj = j & 15;
-            const uint8_t* b = src + (i / 32) * (one ? 24 : 22);
-            const uint8_t* h = b + (one ? 4 : 2);
-            const uint32_t qh = h[0] | (h[1] << 8) | (h[2] << 16) | ((uint32_t)h[3] << 24);
-            const uint8_t q = b[(one ? 8 : 6) + jj];
-            const int v = j < 16 ? ((q & 0xF) | (int)(((qh >> jj) << 4) & 0x10))
-                                 : ((q >> 4) | (int)((qh >> (jj + 12)) & 0x10));
-            if (!one) return __fmul_rn((float)(v - 16), gg_f16(b));
-            return __fadd_rn(__fmul_rn((float)v, gg_f16(b)), gg_f16(b + 2));
-        }
-        case 12: {
-            const uint8_t* b = src + (i / 256) * 144;
-            const uint32_t e = i % 256, c = e / 64, w = e % 64, is = 2 * c + (w >= 32), l = w % 32;
-            const uint8_t* sc = b + 4;
-            uint32_t s, m;  // the 6-bit scale and min of sub-block `is`
-            if (is < 4) {
-                s = sc[is] & 63;
-                m = sc[is + 4] & 63;
-            } else {
-                s = (sc[is + 4] & 0xF) | ((sc[is - 4] >> 6) << 4);
-                m = (sc[is + 4] >> 4) | ((sc[is] >> 6) << 4);
-            }
-            const uint8_t qb = b[16 + 32 * c + l];
-            const float q = (float)(w < 32 ? (qb & 0xF) : (qb >> 4));
-            return __fsub_rn(__fmul_rn(__fmul_rn(gg_f16(b), (float)s), q), __fmul_rn(gg_f16(b + 2), (float)m));
-        }
-        case 14: {
-            const uint8_t* b = src + (i / 256) * 210;
-            const uint32_t e = i % 256, h = e / 128, r = e % 128, g = r / 32, l = r % 32;
-            const uint8_t lo = b[64 * h + l + ((g & 1) ? 32 : 0)];
-            const uint32_t nib = g < 2 ? (lo & 0xF) : (lo >> 4);
-            const int q = (int)(nib | (((b[128 + 32 * h + l] >> (2 * g)) & 3) << 4)) - 32;
-            const int8_t s = (int8_t)b[192 + 8 * h + l / 16 + 2 * g];
-            return __fmul_rn(__fmul_rn(gg_f16(b + 208), (float)s), (float)q);
-        }
-        default: return __int_as_float(((const int*)src)[i]);  // F32
-    }
-}
-
-__global__ void gguf_dequant_kernel(uint32_t type, const uint8_t* src, float* dst, uint64_t n) {
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
-        dst[i] = gg_elem(type, src, i);
-}
-
-inline cudaError_t gguf_dequant(cudaStream_t st, uint32_t type, const void* src, float* dst, uint64_t n) {
-    const uint64_t blocks = std::min<uint64_t>((n + 255) / 256, (uint64_t)sm_count() * 16);
-    gguf_dequant_kernel<<<(unsigned)std::max<uint64_t>(blocks, 1), 256, 0, st>>>(
-        type, static_cast<const uint8_t*>(src), dst, n);
-    return cudaGetLastError();
-}
 
 // ---- GGUF reader (the published v2/v3 layout) ----------------------------------
 struct GgufTensor {
@@ -521,6 +433,38 @@ xp_status xp_gguf_dequantize(void* stream, uint32_t type_id, const void* src, fl
                                   (unsigned long long)n, g->name);
     if (n == 0) return XP_OK;
     return cuda_status(gguf_dequant((cudaStream_t)stream, type_id, src, dst, n), "gguf_dequantize");
+}
+
+xp_status xp_quant_repack_sizes(uint32_t type_id, uint32_t rows, uint32_t cols, uint64_t* sizes) {
+    using namespace xp;
+    if (!sizes) return fail(XP_ERR_INVALID, "xp_quant_repack_sizes: null sizes");
+    if (!quant::repack_sizes(type_id, rows, cols, sizes))
+        return fail(XP_ERR_INVALID, "xp_quant_repack: type %u with %u x %u is not repackable (Q8_0, Q5_0: cols %% 32; "
+                    "Q4_K, Q6_K: cols %% 256)", type_id, rows, cols);
+    return XP_OK;
+}
+
+xp_status xp_quant_repack(void* stream, uint32_t type_id, const void* src, uint32_t rows, uint32_t cols, uint32_t* q,
+                          uint32_t* high, float* scale, float* bias) {
+    using namespace xp;
+    uint64_t sizes[4];
+    if (xp_status e = xp_quant_repack_sizes(type_id, rows, cols, sizes); e != XP_OK) return e;
+    if (!src || !q || !scale || (sizes[1] && !high) || (sizes[3] && !bias))
+        return fail(XP_ERR_INVALID, "xp_quant_repack: null pointer for a plane this type has");
+    if (((uintptr_t)q) & 15) return fail(XP_ERR_INVALID, "xp_quant_repack: the quant plane must be 16-byte aligned");
+    quant::RepackArgs a{};
+    a.src = static_cast<const uint8_t*>(src);
+    a.quant = reinterpret_cast<uint4*>(q);
+    a.high = high;
+    a.scale = scale;
+    a.bias = bias;
+    a.type = type_id;
+    a.rows = rows;
+    a.cols = cols;
+    a.nkb = cols / 32;
+    a.slots = (uint32_t)(sizes[2] / (type_id == 14 ? 2 : 1));
+    quant::repack_kernel<<<(a.slots + 255) / 256, 256, 0, (cudaStream_t)stream>>>(a);
+    return cuda_status(cudaGetLastError(), "quant_repack");
 }
 
 xp_status xp_session_create_gguf(int device, const char* gguf_path, const xp_model_config* policy,
