@@ -506,7 +506,11 @@ xp_status xp_alloc(xp_context* c, size_t bytes, xp_usage usage, void** dptr, voi
     } else {
         void* d = nullptr;
         XP_CUDA_TRY(cudaMalloc(&d, bytes));
-        XP_CUDA_TRY(cudaMemset(d, 0, bytes));
+        // zero-filled on the context's own stream: it is non-blocking, so a
+        // fill on the legacy default stream would not be ordered before the
+        // uploads and launches that follow and could land after them
+        XP_CUDA_TRY(cudaMemsetAsync(d, 0, bytes, c->stream));
+        XP_CUDA_TRY(cudaStreamSynchronize(c->stream));
         c->allocs[d] = {XP_DEVICE_LOCAL, nullptr};
         *dptr = d;
         if (host_ptr) *host_ptr = nullptr;
@@ -971,7 +975,7 @@ xp_status xp_mv_plan_create(const xp_mv_job* jobs, uint32_t n, xp_mv_plan** plan
     if (part_floats) {
         if ((e = cudaMalloc(&p->part, part_floats * 4)) != cudaSuccess) return cleanup("partials", e);
         if ((e = cudaMalloc(&p->arrive, arrive_words * 4)) != cudaSuccess) return cleanup("counters", e);
-        if ((e = cudaMemset(p->arrive, 0, arrive_words * 4)) != cudaSuccess) return cleanup("counters", e);
+        if ((e = zero_fill_sync(p->arrive, arrive_words * 4)) != cudaSuccess) return cleanup("counters", e);
         size_t po = 0, ao = 0;
         for (auto& j : hj)
             if (j.ksplit > 1) {
@@ -984,9 +988,9 @@ xp_status xp_mv_plan_create(const xp_mv_job* jobs, uint32_t n, xp_mv_plan** plan
     if ((e = cudaMalloc(&p->jobs, n * sizeof(MvsJob))) != cudaSuccess) return cleanup("jobs", e);
     if ((e = cudaMalloc(&p->src, hs.size() * sizeof(MvsSrc))) != cudaSuccess) return cleanup("sources", e);
     if ((e = cudaMalloc(&p->next, 16)) != cudaSuccess) return cleanup("counter", e);
-    if ((e = cudaMemcpy(p->jobs, hj.data(), n * sizeof(MvsJob), cudaMemcpyHostToDevice)) != cudaSuccess)
+    if ((e = h2d_sync(p->jobs, hj.data(), n * sizeof(MvsJob))) != cudaSuccess)
         return cleanup("upload", e);
-    if ((e = cudaMemcpy(p->src, hs.data(), hs.size() * sizeof(MvsSrc), cudaMemcpyHostToDevice)) != cudaSuccess)
+    if ((e = h2d_sync(p->src, hs.data(), hs.size() * sizeof(MvsSrc))) != cudaSuccess)
         return cleanup("upload", e);
     p->njobs = n;
     p->nstrips = strips;

@@ -133,7 +133,10 @@ struct xp_session {
         cudaError_t e = cudaMalloc(&d, count * sizeof(T) + 16);
         if (e != cudaSuccess) return fail(XP_ERR_OOM, "decode: cudaMalloc(%zu) failed: %s", count * sizeof(T),
                                           cudaGetErrorString(e));
-        cudaMemset(d, 0, count * sizeof(T) + 16);
+        if ((e = zero_fill_sync(d, count * sizeof(T) + 16)) != cudaSuccess) {
+            cudaFree(d);
+            return fail(XP_ERR_CUDA, "decode: zero fill failed: %s", cudaGetErrorString(e));
+        }
         allocs.push_back(d);
         *p = static_cast<T*>(d);
         return XP_OK;
@@ -482,7 +485,7 @@ struct xp_session {
         if ((e = alloc(&tk_head, (size_t)tk.head.units * tk.head.img_bytes)) != XP_OK) return e;
         if ((e = repack(lm, tk_head, tk.head, 0, 0)) != XP_OK) return e;
         if ((e = alloc(&tk_layers_dev, cfg.n_layers)) != XP_OK) return e;
-        XP_CUDA_TRY(cudaMemcpy(tk_layers_dev, tk_layers.data(), sizeof(TkLayer) * cfg.n_layers, cudaMemcpyHostToDevice));
+        XP_CUDA_TRY(h2d_sync(tk_layers_dev, tk_layers.data(), sizeof(TkLayer) * cfg.n_layers));
         float *attp, *atts, *amv2;
         long long *aq, *ao, *ad;
         uint32_t* ami2;
@@ -747,7 +750,7 @@ xp_status xp_session_create(int device, const xp_model_config* cfg, const xp_sam
     const uint32_t H = s->cfg.hidden;
     auto up = [&](void* dst, const void* src, size_t bytes) -> xp_status {
         if (!src) return fail(XP_ERR_INVALID, "decode: null weight pointer");
-        XP_CUDA_TRY(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+        XP_CUDA_TRY(h2d_sync(dst, src, bytes));
         return XP_OK;
     };
     for (uint32_t l = 0; l < s->cfg.n_layers && st == XP_OK; ++l) {
@@ -1008,7 +1011,7 @@ xp_status xp_session_error_word(xp_session* s, uint32_t* w) {
     // the attention error word follows the ticket at the head of the scratch
     uint32_t* err = static_cast<uint32_t*>(s->attn_scratch) + 1;
     XP_CUDA_TRY(cudaMemcpy(w, err, 4, cudaMemcpyDeviceToHost));
-    XP_CUDA_TRY(cudaMemset(err, 0, 4));
+    XP_CUDA_TRY(zero_fill_sync(err, 4));
     return XP_OK;
 }
 
@@ -1065,7 +1068,10 @@ struct xp_bdec {
         cudaError_t e = cudaMalloc(&d, count * sizeof(T) + 256);
         if (e != cudaSuccess) return fail(XP_ERR_OOM, "batch: cudaMalloc(%zu) failed: %s", count * sizeof(T),
                                           cudaGetErrorString(e));
-        cudaMemset(d, 0, count * sizeof(T) + 256);
+        if ((e = zero_fill_sync(d, count * sizeof(T) + 256)) != cudaSuccess) {
+            cudaFree(d);
+            return fail(XP_ERR_CUDA, "batch: zero fill failed: %s", cudaGetErrorString(e));
+        }
         allocs.push_back(d);
         *p = static_cast<T*>(d);
         return XP_OK;
@@ -1274,7 +1280,7 @@ static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, con
         // every row at the last position: the only cache row written is the
         // last one, which a real pass at that position writes before reading
         std::vector<uint32_t> hp(nseq, max_seq - 1);
-        XP_CUDA_TRY(cudaMemcpy(b->pos, hp.data(), (size_t)nseq * 4, cudaMemcpyHostToDevice));
+        XP_CUDA_TRY(h2d_sync(b->pos, hp.data(), (size_t)nseq * 4));
     }
     if (b->forward() != cudaSuccess) return bail(fail(XP_ERR_CUDA, "xp_bdec_create: warm-up forward failed"));
     XP_CUDA_TRY(cudaMemsetAsync(b->pos, 0, (size_t)nseq * 4, b->st));
@@ -1417,8 +1423,8 @@ xp_status xp_session_tp_attach_ex(xp_session* s, uint32_t rank, uint32_t world, 
     // rank attached with XP_TP_SHARD_FFN runs it too (the reference for the
     // sharded runs, bit for bit).
     s->tk_tp_instance = world > 1 || (flags & XP_TP_SHARD_FFN);
-    XP_CUDA_TRY(cudaMemset(s->tp_buf, 0, s->tp_buf_bytes()));
-    XP_CUDA_TRY(cudaMemset(s->tk.tp_count, 0, 8));
+    XP_CUDA_TRY(zero_fill_sync(s->tp_buf, s->tp_buf_bytes()));
+    XP_CUDA_TRY(zero_fill_sync(s->tk.tp_count, 8));
     for (cudaGraphExec_t* g : {&s->g_dev, &s->g_io, &s->g_prefill})
         if (*g) { cudaGraphExecDestroy(*g); *g = nullptr; }
     return s->build_graphs();

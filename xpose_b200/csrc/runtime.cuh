@@ -73,6 +73,24 @@ inline cudaError_t smem_attr_once(std::atomic<bool>* done, Kern* kern, int bytes
     return e;
 }
 
+// Zero-fill device memory and wait for it. cudaMemset runs on the legacy
+// default stream, which the library's non-blocking streams do not order
+// against: without the wait, a fill could land after the first uploads or
+// kernels on those streams. Set-up paths only.
+inline cudaError_t zero_fill_sync(void* d, size_t bytes) {
+    cudaError_t e = cudaMemset(d, 0, bytes);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
+    return e;
+}
+// Host -> device copy that has landed when it returns: a plain cudaMemcpy from
+// pageable memory may return once the data is staged, before the DMA that
+// work on the non-blocking streams would not wait for. Set-up paths only.
+inline cudaError_t h2d_sync(void* dst, const void* src, size_t bytes) {
+    cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
+    return e;
+}
+
 // Launch with optional cluster size and programmatic dependent launch.
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_ex(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
