@@ -76,3 +76,30 @@ def test_batch_scratch_shared_across_shapes():
         for s in (0, n - 1):
             want = O.mv(xs[s], words, scales, rows, cols)
             assert rel_l2(got[s], want) < 1e-5, (i, rows, cols, s, rel_l2(got[s], want))
+
+
+@pytest.mark.parametrize("tiny", [False, True])
+def test_batch_operand_modes(tiny):
+    """Scaled operand mode (every bf16 scale in [2^-14, 8160]: the dequantised
+    weight is an exact fp16) and the integer mode the kernel falls back to when
+    one block's scale is below 2^-14 (here one 32-row block of weights near
+    1e-7): both must match the oracle at the same bar."""
+    rows, cols, n = 1152, 1024, 64
+    w = O.gen_normal(91, 1, rows * cols, 0.02).reshape(cols, rows)  # [cols][rows]
+    if tiny:
+        w[5, 32:64] *= 5e-6
+    words, scales = O.pack(w.reshape(-1), rows, cols)
+    xs = np.stack([O.gen_normal(91, 100 + s, rows, 1.0) for s in range(n)])
+    nbytes = lib().xp_mv_km4_bs_batch_scratch_bytes(rows, cols, n)
+    scratch = torch.zeros(nbytes // 4 + 64, dtype=torch.int32, device="cuda")
+    out = torch.full((n * cols,), -1e30, device="cuda")
+    check(lib().xp_mv_km4_bs_batch(None, ptr(out), ptr(dev(xs.reshape(-1))), ptr(dev(words)), ptr(dev(scales)),
+                                   rows, cols, n, ptr(scratch)))
+    sync()
+    sc = host(scratch, np.uint32)
+    assert int(sc[64]) == 0, "pipeline wait ran out"
+    assert int(sc[96]) == (1 if tiny else 0), "scale-range flag of the call"
+    got = host(out).reshape(n, cols)
+    for s in (0, 31, n - 1):
+        want = O.mv(xs[s], words, scales, rows, cols)
+        assert rel_l2(got[s], want) < 1e-5, (tiny, s, rel_l2(got[s], want))

@@ -4,14 +4,23 @@
 // (kernels/llm_matvec.cl:422-434) for every sequence at once. This is the
 // skinny GEMM (M = weight columns, N = sequences, K = rows) of batched decode.
 //
-// Exactness. The reference dequantises (nibble - 8) * bf16(scale) in fp32. A
-// 16-bit MMA operand cannot hold that product exactly, so the tensor cores
-// multiply the exact integers (nibble - 8) in fp16 and the per-32-row block
-// scale is applied afterwards in fp32: one K = 32 block per accumulator, an
-// epilogue adds scale(j, b) * D_b to a register sum. The activation enters as
-// x / 2^e = hi + lo, two fp16 halves (about 22 significant bits), with one
-// power-of-two e per sequence applied at the end; hi and lo are two MMAs into
-// the same accumulator.
+// Exactness. The reference dequantises (nibble - 8) * bf16(scale) in fp32.
+// The activation enters as x / 2^e = hi + lo, two fp16 halves (about 22
+// significant bits), with one power-of-two e per sequence applied at the end.
+// Two operand modes, chosen per launch:
+//   scaled  (every scale s of the launch's matrices is 0 or 2^-14 <= |s| <=
+//            8160): (nibble - 8) * s has at most 8 + 3 significant bits and
+//            stays a normal fp16 below 65504, so the dequant warps write the
+//            exact dequantised weight as the fp16 A operand, one TMEM
+//            accumulator runs over the item's whole K range, and the epilogue
+//            runs once per item. hi and lo are the two halves of one MMA's N
+//            (N' = 2N columns: hi sums, then lo sums).
+//   integer (any other scale): A holds the exact integers (nibble - 8), one
+//            K = 32 block per accumulator, and the epilogue adds
+//            scale(j, b) * D_b to a register sum per block; hi and lo are two
+//            MMAs into the same accumulator.
+// Both give fp32 products of exact operands; they differ only in the fp32
+// summation order.
 //
 // CTA (448 threads) per work item = 128 output columns x one K range:
 //   warp 0   producer: bulk copies of the nibbles (2 x 1 KB per block, the
@@ -19,12 +28,12 @@
 //   warp 1   MMA issuer (one thread) + TMEM owner (alloc/dealloc, 4N columns)
 //   warps 2-5  dequant: thread = column j, 32 nibbles -> fp16 A tile
 //   warps 6-13 epilogue: thread = column j x half of the sequences,
-//            tcgen05.ld of the block's sums, scale and accumulate; the item's
-//            result goes to out (one K range) or to int64 fixed-point sums
-//            (K split across CTAs)
-// Four A tiles and four accumulator slots keep the MMA up to four blocks
-// ahead of the epilogue; two CTAs share an SM. Waiting warps poll with one
-// lane.
+//            tcgen05.ld of the sums (per item, or per block and scaled); the
+//            item's result goes to out (one K range) or to int64 fixed-point
+//            sums (K split across CTAs)
+// Four A tiles and four accumulator slots (two of 2N columns in scaled mode)
+// keep the MMA ahead of the epilogue; two CTAs share an SM. Waiting warps
+// poll with one lane.
 // Shared-memory operands use the K-major, no-swizzle canonical layout: 8 rows x
 // 16 bytes per core matrix. Within each 8-element K chunk the order is the
 // nibble extraction order (k0 k4 k1 k5 k2 k6 k3 k7) on both operands.
@@ -62,13 +71,15 @@ constexpr int BMM_MAXPARTS = 3;
 struct BmmArgs {
     BmmPart part[BMM_MAXPARTS];
     uint32_t nparts;
-    const unsigned char* xb;  // prepared activations: [nblk][hi, lo][chunk 4][N][16 B]
+    const unsigned char* xb;  // prepared activations: [nblk][chunk 4][hi, lo][N][16 B]
     const float* xs;          // [N] per-sequence power-of-two scale 2^e
     uint32_t nblk, N;         // N = padded sequence count (32 or 64)
     uint32_t nreal;           // sequences actually present (rows of out)
     uint32_t ksplit, cb;      // K ranges per tile, blocks per range
     uint32_t nitems;          // tiles * ksplit
     uint32_t raw;             // 1: leave the result in acc as fixed-point sums (the consumer converts)
+    uint32_t scaled;          // 1: scaled-operand mode (every scale in the fp16-exact range)
+    const uint32_t* fbflag;   // if set, the mode is read here instead: 0 scaled, else integer
     uint32_t* err;
 };
 // The matrix holding launch tile `tile`, and the tile's index within it.
@@ -165,11 +176,39 @@ XP_DEV uint4 bmm_unpack8(uint32_t w) {
     return r;
 }
 
+// bf16 scale magnitudes for which (nibble - 8) * s is an exact normal fp16:
+// 0, or 2^-14 (0x3880) <= |s| <= 8160 (0x45FF; 8 * 8160 <= 65504)
+XP_DEV bool bmm_scale_exact16(uint32_t bits16) {
+    const uint32_t m = bits16 & 0x7FFFu;
+    return m == 0 || (m >= 0x3880u && m <= 0x45FFu);
+}
+// Any scale of the plane (nwords uint4 = 8 bf16 each) outside that range ->
+// *flag |= 1 (the flag is cleared before the launch).
+__global__ void bmm_scale_check_kernel(const uint4* sc, size_t nwords, uint32_t* flag) {
+    bool bad = false;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords; i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 w = __ldg(sc + i);
+        const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) bad = bad || !bmm_scale_exact16(v[k] & 0xFFFFu) || !bmm_scale_exact16(v[k] >> 16);
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1u);
+}
+// 8 nibbles -> 8 fp16 (nibble - 8) * s, exact for s in the range above
+XP_DEV uint4 bmm_unpack8s(uint32_t w, __half2 s2) {
+    uint4 r = bmm_unpack8(w);
+    *reinterpret_cast<__half2*>(&r.x) = __hmul2(*reinterpret_cast<__half2*>(&r.x), s2);
+    *reinterpret_cast<__half2*>(&r.y) = __hmul2(*reinterpret_cast<__half2*>(&r.y), s2);
+    *reinterpret_cast<__half2*>(&r.z) = __hmul2(*reinterpret_cast<__half2*>(&r.z), s2);
+    *reinterpret_cast<__half2*>(&r.w) = __hmul2(*reinterpret_cast<__half2*>(&r.w), s2);
+    return r;
+}
+
 // Activation prep, pass 1: per sequence the power-of-two 2^e >= max |x| (one
 // warp per sequence); also zeroes the fixed-point sums of this call.
 // Activations of one call, one CTA per (padded) sequence: the power-of-two
 // scale 2^e > max |x| of the sequence, then x / 2^e as hi + lo fp16 in the
-// B-operand layout [nblk][hi, lo][chunk 4][N][8 halves]. Padded sequences get
+// B-operand layout [nblk][chunk 4][hi, lo][N][8 halves]. Padded sequences get
 // zeros. CTA 0 also clears the call's error word. Rows up to 8 x 1024 are
 // loaded once into registers (every load in flight together).
 constexpr int BMM_XP_THREADS = 1024, BMM_XP_PER = 8;
@@ -180,8 +219,8 @@ XP_DEV void bmm_xput(unsigned char* xb, uint32_t Npad, uint32_t n, uint32_t i, f
     const __half hi = __float2half_rn(y);
     const __half lo = __float2half_rn(y - __half2float(hi));
     __half* base = reinterpret_cast<__half*>(xb + (size_t)b * 2 * 4 * Npad * 16);
-    base[((0 * 4 + c) * Npad + n) * 8 + pos] = hi;
-    base[((1 * 4 + c) * Npad + n) * 8 + pos] = lo;
+    base[((c * 2 + 0) * Npad + n) * 8 + pos] = hi;
+    base[((c * 2 + 1) * Npad + n) * 8 + pos] = lo;
 }
 // The same operand written by the kernel that produces the activations: the
 // calling CTA holds sequence n, element i = threadIdx.x + j * blockDim.x in
@@ -305,6 +344,8 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t G = gridDim.x;
+    // operand mode of the launch (uniform over the CTA)
+    const bool S = a.fbflag ? (*reinterpret_cast<const volatile uint32_t*>(a.fbflag) == 0u) : (a.scaled != 0u);
 
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
@@ -349,35 +390,67 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
-            const uint32_t idesc = bmm_idesc(N);
-            uint32_t t = 0;
-            for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-                const uint32_t kc = item % a.ksplit;
-                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
-                for (uint32_t b = b0; b < b1; ++b, ++t) {
-                    const uint32_t s = t % BMM_STAGES, p = t % BMM_NA, q = t % BMM_ND;
-                    bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);       // A tile of block t dequantised
-                    bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);    // activations of block t landed
-                    if (t >= BMM_ND) bmm_wait(&dempty[q], ((t / BMM_ND) - 1) & 1, a.err);  // slot q read
-                    tc_fence_after();
-                    const uint32_t ab = smem_u32(atile + p * 8192);
-                    const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
-                    const uint32_t d = tmem + q * N;
-                    uint32_t acc = 0;
+            uint32_t t = 0, it = 0;  // blocks, items of this CTA
+            if (S) {
+                // one accumulator of 2N columns (hi sums | lo sums) per item,
+                // over the item's whole K range; two slots alternate
+                const uint32_t idesc = bmm_idesc(2 * N);
+                for (uint32_t item = blockIdx.x; item < a.nitems; item += G, ++it) {
+                    const uint32_t kc = item % a.ksplit;
+                    const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                    const uint32_t q = it & 1;
+                    if (it >= 2) bmm_wait(&dempty[q], ((it >> 1) - 1) & 1, a.err);  // slot q drained
+                    const uint32_t d = tmem + q * 2 * N;
+                    for (uint32_t b = b0; b < b1; ++b, ++t) {
+                        const uint32_t s = t % BMM_STAGES, p = t % BMM_NA;
+                        bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);
+                        bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);
+                        tc_fence_after();
+                        const uint32_t ab = smem_u32(atile + p * 8192);
+                        const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-                        for (int hl = 0; hl < 2; ++hl) {
-                            // A: chunks 2kk, 2kk+1 of 128 columns (chunk stride 2 KB, 8-row groups 128 B)
+                        for (int kk = 0; kk < 2; ++kk) {
                             const uint64_t ad = bmm_desc(ab + kk * 4096, 2048, 128);
-                            // B: chunks 2kk, 2kk+1 of N sequences (chunk stride 16N B, 8-row groups 128 B)
-                            const uint64_t bd = bmm_desc(xbase + (hl * 4 + 2 * kk) * N * 16, N * 16, 128);
-                            bmm_mma(d, ad, bd, idesc, acc);
-                            acc = 1;
+                            // B: chunks 2kk, 2kk+1, rows hi 0..N-1 then lo N..2N-1
+                            // (chunk stride 32N B, 8-row groups 128 B)
+                            const uint64_t bd = bmm_desc(xbase + (2 * kk) * 2 * N * 16, 2 * N * 16, 128);
+                            bmm_mma(d, ad, bd, idesc, (b != b0 || kk != 0) ? 1u : 0u);
                         }
-                    bmm_commit(&dfull[q]);   // accumulator of block t ready
-                    bmm_commit(&aempty[p]);  // A tile p free
-                    bmm_commit(&empty[s]);   // activations of stage s no longer read
+                        bmm_commit(&aempty[p]);
+                        bmm_commit(&empty[s]);
+                    }
+                    bmm_commit(&dfull[q]);  // the item's sums are complete
+                }
+            } else {
+                const uint32_t idesc = bmm_idesc(N);
+                for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
+                    const uint32_t kc = item % a.ksplit;
+                    const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                    for (uint32_t b = b0; b < b1; ++b, ++t) {
+                        const uint32_t s = t % BMM_STAGES, p = t % BMM_NA, q = t % BMM_ND;
+                        bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);       // A tile of block t dequantised
+                        bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);    // activations of block t landed
+                        if (t >= BMM_ND) bmm_wait(&dempty[q], ((t / BMM_ND) - 1) & 1, a.err);  // slot q read
+                        tc_fence_after();
+                        const uint32_t ab = smem_u32(atile + p * 8192);
+                        const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
+                        const uint32_t d = tmem + q * N;
+                        uint32_t acc = 0;
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+                            for (int hl = 0; hl < 2; ++hl) {
+                                // A: chunks 2kk, 2kk+1 of 128 columns (chunk stride 2 KB, 8-row groups 128 B)
+                                const uint64_t ad = bmm_desc(ab + kk * 4096, 2048, 128);
+                                // B: chunks 2kk, 2kk+1 of half hl, N sequences (chunk stride 32N B, 8-row groups 128 B)
+                                const uint64_t bd = bmm_desc(xbase + (2 * kk * 2 + hl) * N * 16, 2 * N * 16, 128);
+                                bmm_mma(d, ad, bd, idesc, acc);
+                                acc = 1;
+                            }
+                        bmm_commit(&dfull[q]);   // accumulator of block t ready
+                        bmm_commit(&aempty[p]);  // A tile p free
+                        bmm_commit(&empty[s]);   // activations of stage s no longer read
+                    }
                 }
             }
         }
@@ -386,18 +459,47 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         const uint32_t j = tid - 64;  // column within the tile, 0..127
         uint32_t t = 0;
         for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-            const uint32_t kc = item % a.ksplit;
+            const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
             const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+            uint2 sw{}, sw_next{};
+            const uint2* scp = nullptr;
+            uint32_t cols = 0;
+            if (S) {
+                // this column's scales, one quad of blocks ahead
+                uint32_t lt;
+                const BmmPart& P = bmm_part(a, tile, lt);
+                cols = P.cols;
+                scp = P.sc + lt * BMM_M + j;
+                sw = __ldg(scp + (size_t)(b0 >> 2) * cols);
+                sw_next = b0 + 4 < b1 ? __ldg(scp + (size_t)((b0 >> 2) + 1) * cols) : sw;
+            }
             for (uint32_t b = b0; b < b1; ++b, ++t) {
                 const uint32_t s = t % BMM_STAGES, p = t % BMM_NA;
+                __half2 s2;
+                if (S) {
+                    if ((b & 3) == 0 && b != b0) {
+                        sw = sw_next;
+                        if (b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * cols);
+                    }
+                    const uint32_t word = (b & 2) ? sw.y : sw.x;
+                    const __half h = __float2half_rn((b & 1) ? bf16_hi(word) : bf16_lo(word));  // exact in range
+                    s2 = __halves2half2(h, h);
+                }
                 bmm_wait_warp(&full[s], (t / BMM_STAGES) & 1, a.err);
                 const uint4 w = *reinterpret_cast<const uint4*>(stage0 + s * sbytes + (j >> 6) * 1024 + (j & 63) * 16);
                 if (t >= BMM_NA) bmm_wait_warp(&aempty[p], ((t / BMM_NA) - 1) & 1, a.err);
                 unsigned char* at = atile + p * 8192 + j * 16;
-                *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8(w.x);
-                *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8(w.y);
-                *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8(w.z);
-                *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8(w.w);
+                if (S) {
+                    *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8s(w.x, s2);
+                    *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8s(w.y, s2);
+                    *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8s(w.z, s2);
+                    *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8s(w.w, s2);
+                } else {
+                    *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8(w.x);
+                    *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8(w.y);
+                    *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8(w.z);
+                    *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8(w.w);
+                }
                 fence_proxy_async();  // generic smem writes -> async-proxy MMA reads
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 if (j == 0) {
@@ -414,7 +516,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         const uint32_t j = q4 * 32 + lane;           // column within the tile
         const uint32_t half = e >> 2;                // sequences [half * N/2, +N/2)
         const uint32_t nh = N / 2;                   // 16 or 32
-        uint32_t t = 0;
+        uint32_t t = 0, it = 0;
         for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
             const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
             const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
@@ -422,6 +524,24 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             const BmmPart& P = bmm_part(a, tile, lt);
             const uint32_t col = lt * BMM_M + j;
             float sum[BMM_MAXN / 2];
+            if (S) {
+                // one read of the item's accumulator: hi sums + lo sums
+                const uint32_t q = it & 1;
+                bmm_wait_warp(&dfull[q], (it >> 1) & 1, a.err);
+                tc_fence_after();
+                float v[32];
+                const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * 2 * N + half * nh;
+                if (nh == 32) tmem_ld32(taddr, sum);
+                else tmem_ld16(taddr, sum);
+                if (nh == 32) tmem_ld32(taddr + N, v);
+                else tmem_ld16(taddr + N, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sum[i] += v[i];
+                tc_fence_before();
+                asm volatile("bar.sync 3, 256;" ::: "memory");
+                if (tid == 192) bmm_arrive(&dempty[q]);
+                ++it;
+            } else {
 #pragma unroll
             for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
             // scales one quad ahead: the scale plane is read from HBM
@@ -446,6 +566,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 tc_fence_before();
                 asm volatile("bar.sync 3, 256;" ::: "memory");
                 if (tid == 192) bmm_arrive(&dempty[q]);
+            }
             }
 #pragma unroll
             for (int i = 0; i < BMM_MAXN / 2; ++i) {

@@ -832,8 +832,27 @@ struct BmmPrep {
     const float* xs;
     const unsigned char* xb;
 };
+// Operand mode (bmm.cuh): BMM_MODE_SCALED when the caller knows every scale of
+// the matrices lies in the fp16-exact range (bmm_scales_exact16), else
+// BMM_MODE_INTEGER; BMM_MODE_CHECK scans the scale planes on the stream first
+// and lets the kernel pick. XP_BMM_SCALED=0 forces the integer mode.
+enum { BMM_MODE_INTEGER = 0, BMM_MODE_SCALED = 1, BMM_MODE_CHECK = 2 };
+constexpr size_t BMM_OFF_FLAG = 384;  // scratch word: scale-range violation flag of a checking call
+static void bmm_launch_scale_check(cudaStream_t st, const uint32_t* sc, uint32_t rows, uint32_t cols, uint32_t* flag) {
+    const size_t nwords = (size_t)(rows / 32) * cols / 8;
+    const uint32_t grid = (uint32_t)std::min<size_t>((nwords + 255) / 256, 4 * (size_t)sm_count());
+    bmm_scale_check_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const uint4*>(sc), nwords, flag);
+}
+static bool bmm_scaled_allowed() {
+    static const bool on = [] {
+        const char* v = std::getenv("XP_BMM_SCALED");
+        return !(v && *v && std::atoi(v) == 0);
+    }();
+    return on;
+}
 static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, bool raw, const float* in, uint32_t rows,
-                         uint32_t n, void* scratch, const BmmPrep* prep = nullptr, bool pdl = false) {
+                         uint32_t n, void* scratch, const BmmPrep* prep = nullptr, bool pdl = false,
+                         int mode = BMM_MODE_CHECK) {
     if (nmat == 0 || nmat > (uint32_t)BMM_MAXPARTS || (!raw && nmat != 1))
         return fail(XP_ERR_INVALID, "bmm_run: %u matrices", nmat);
     uint32_t cols = 0;
@@ -862,6 +881,17 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
     }
     if (!prep) {
         bmm_xprep_kernel<<<p.npad, BMM_XP_THREADS, 0, st>>>(in, rows, n, p.npad, xs, xb, err);
+        XP_CUDA_TRY(cudaGetLastError());
+    }
+    if (!bmm_scaled_allowed()) mode = BMM_MODE_INTEGER;
+    uint32_t* fbflag = nullptr;
+    if (mode == BMM_MODE_CHECK) {
+        // the kernel reads the flag at its start: a programmatic launch could
+        // read it before the check wrote it
+        pdl = false;
+        fbflag = reinterpret_cast<uint32_t*>(base + BMM_OFF_FLAG);
+        XP_CUDA_TRY(cudaMemsetAsync(fbflag, 0, 4, st));
+        for (uint32_t m = 0; m < nmat; ++m) bmm_launch_scale_check(st, mats[m].sc, rows, mats[m].cols, fbflag);
         XP_CUDA_TRY(cudaGetLastError());
     }
     static size_t attr_set[64] = {};
@@ -894,6 +924,8 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
     a.cb = p.cb;
     a.nitems = p.nitems;
     a.err = err;
+    a.scaled = mode == BMM_MODE_SCALED ? 1u : 0u;
+    a.fbflag = fbflag;
     const uint32_t grid = std::min<uint32_t>(p.nitems, 2 * (uint32_t)sm_count());
     XP_CUDA_TRY(launch_ex(bmm_kernel, dim3(grid), dim3(BMM_THREADS), p.smem, st, 1, pdl, a));
     if (acc) {
@@ -902,6 +934,20 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
         XP_CUDA_TRY(cudaGetLastError());
     }
     return XP_OK;
+}
+// Set-up time: true when every scale of the plane is in the fp16-exact range
+// (the scaled operand mode applies); synchronous on the stream.
+static cudaError_t bmm_scales_exact16(cudaStream_t st, const void* sc, uint32_t rows, uint32_t cols, uint32_t* dflag,
+                                      bool* ok) {
+    cudaError_t e = cudaMemsetAsync(dflag, 0, 4, st);
+    if (e != cudaSuccess) return e;
+    bmm_launch_scale_check(st, static_cast<const uint32_t*>(sc), rows, cols, dflag);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    uint32_t h = 1;
+    if ((e = cudaMemcpyAsync(&h, dflag, 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
+    *ok = h == 0;
+    return cudaSuccess;
 }
 xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
                              uint32_t rows, uint32_t cols, uint32_t n, void* scratch) {

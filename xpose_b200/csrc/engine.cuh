@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <initializer_list>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "runtime.cuh"
@@ -1041,6 +1042,13 @@ struct xp_bdec {
     std::vector<std::pair<uint64_t, unsigned char*>> bscratch;
     uint64_t* cand = nullptr;
     uint32_t ns = 0, nc = 0;
+    // per scale plane: every scale in the fp16-exact range, so its matvecs use
+    // the tensor-core kernel's scaled operand mode (checked once at creation)
+    std::unordered_map<const void*, bool> s16;
+    int mode_of(const QW& w) const {
+        auto it = s16.find(w.sc);
+        return it != s16.end() && it->second ? BMM_MODE_SCALED : BMM_MODE_INTEGER;
+    }
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr, g_nohead = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
     uint32_t h_pos = 0;  // every sequence is at the same position
@@ -1088,15 +1096,18 @@ struct xp_bdec {
         if (!scr) return cudaErrorInvalidValue;
         const BmmMat m{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols, out, nullptr};
         const BmmPrep pr{in.xs, in.xb};
-        return bmm_run(st, &m, 1, false, nullptr, w.rows, B, scr, &pr, pdl_mm) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        return bmm_run(st, &m, 1, false, nullptr, w.rows, B, scr, &pr, pdl_mm, mode_of(w)) == XP_OK ? cudaSuccess
+                                                                                                   : cudaErrorUnknown;
     }
     // raw[i] (fixed-point sums, zero on entry) = in x W[i] for every sequence:
     // matrices with the same rows in one launch
     cudaError_t mm_raw(std::initializer_list<std::pair<long long*, const QW*>> parts, const BkOperand& in) {
         BmmMat m[BMM_MAXPARTS];
         uint32_t n = 0, cols = 0, rows = 0;
+        int mode = BMM_MODE_SCALED;
         for (auto& pr : parts) {
             const QW& w = *pr.second;
+            if (mode_of(w) != BMM_MODE_SCALED) mode = BMM_MODE_INTEGER;
             m[n++] = BmmMat{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols,
                             nullptr, pr.first};
             cols += w.cols;
@@ -1105,7 +1116,7 @@ struct xp_bdec {
         unsigned char* scr = scratch_for(rows, cols);
         if (!scr) return cudaErrorInvalidValue;
         const BmmPrep pr{in.xs, in.xb};
-        return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr, pdl_mm) == XP_OK ? cudaSuccess : cudaErrorUnknown;
+        return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr, pdl_mm, mode) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
     cudaError_t resid_norm(long long* y, const float* w_post, const float* w_pre, int mode) {
@@ -1267,6 +1278,24 @@ static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, con
         unsigned char* scr = nullptr;
         if ((e = b->alloc(&scr, sb)) != XP_OK) return bail(e);
         b->bscratch.push_back({key, scr});
+    }
+    {
+        // operand mode per matrix: scan each scale plane once
+        uint32_t* dflag = nullptr;
+        if ((e = b->alloc(&dflag, 1)) != XP_OK) return bail(e);
+        auto check = [&](const QW& w) -> cudaError_t {
+            if (!w.sc || b->s16.count(w.sc)) return cudaSuccess;
+            bool ok = false;
+            const cudaError_t ce = bmm_scales_exact16(b->st, w.sc, w.rows, w.cols, dflag, &ok);
+            b->s16[w.sc] = ok;
+            return ce;
+        };
+        cudaError_t ce = check(s->lm);
+        for (uint32_t l = 0; l < c.n_layers && ce == cudaSuccess; ++l)
+            for (const QW& w : s->L[l].m)
+                if (ce == cudaSuccess) ce = check(w);
+        if (ce != cudaSuccess)
+            return bail(fail(XP_ERR_CUDA, "xp_bdec_create: scale-range check failed: %s", cudaGetErrorString(ce)));
     }
     b->ns = (uint32_t)((V + TOPK_SLICE - 1) / TOPK_SLICE);
     b->nc = b->ns * TOPK_TK;
