@@ -15,11 +15,34 @@ namespace xp {
 
 constexpr int BK_THREADS = 512;
 
-// Matvec results arrive as int64 fixed-point sums (2^-32 units) that the
-// tensor-core kernel adds into; each is read once by the consuming kernel and
-// left zero for the next step. Kernels load all of theirs before clearing any,
-// so the loads are in flight together.
-XP_DEV float bk_unfix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
+// Matvec results arrive as fp32 partial sums, one per K range of the
+// tensor-core launch ([ks][B][cols], plain stores); the consuming kernel adds
+// them in K-range order, so the result is deterministic. Loads are issued in
+// groups (all of a group in flight together) before any add.
+struct BkSums {
+    const float* p;
+    uint32_t ks;       // K ranges (partials)
+    uint32_t stride;   // floats between consecutive partials (B x cols)
+};
+// v[j] = element idx[j] (< 0: none, v = 0) summed over the partials
+template <int J, int KU>
+XP_DEV void bk_gather(const BkSums& s, const long long (&idx)[J], float (&v)[J]) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) v[j] = 0.0f;
+#pragma unroll 1
+    for (uint32_t k0 = 0; k0 < s.ks; k0 += KU) {
+        float t[KU][J];
+#pragma unroll
+        for (int k = 0; k < KU; ++k)
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                t[k][j] = (k0 + k < s.ks && idx[j] >= 0) ? __ldcg(s.p + (size_t)(k0 + k) * s.stride + idx[j]) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < KU; ++k)
+#pragma unroll
+            for (int j = 0; j < J; ++j) v[j] += t[k][j];
+    }
+}
 
 // Every kernel of a batched step may be launched programmatically (its
 // launch overlapping the previous kernel's tail): each one lets its
@@ -44,9 +67,9 @@ struct BkOperand {
 };
 
 // mode 0: xn = rmsnorm_gemma(x, w_pre)
-// mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)  (y: fixed-point sums)
+// mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)  (y: partial sums)
 // xn goes out as the next matvec's operand.
-__global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, long long* y, const float* w_post,
+__global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, BkSums y, const float* w_post,
                                                                  const float* w_pre, BkOperand xn, uint32_t H, float eps,
                                                                  int mode) {
     __shared__ float red[32];
@@ -54,24 +77,19 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, lon
     pdl_wait();
     const uint32_t b = blockIdx.x;
     float* xb = x + (size_t)b * H;
-    long long* yb = y + (size_t)b * H;
     constexpr int J = 4;  // H <= 2048
     float r[J];
     if (mode == 1) {
         float yv[J], ss = 0.0f;
-        long long yr[J];
+        long long idx[J];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
             const uint32_t i = threadIdx.x + j * BK_THREADS;
-            yr[j] = i < H ? yb[i] : 0;
+            idx[j] = i < H ? (long long)b * H + i : -1;
         }
+        bk_gather<J, 8>(y, idx, yv);
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const uint32_t i = threadIdx.x + j * BK_THREADS;
-            if (i < H) yb[i] = 0;
-            yv[j] = bk_unfix(yr[j]);
-            ss += yv[j] * yv[j];
-        }
+        for (int j = 0; j < J; ++j) ss += yv[j] * yv[j];
         ss = block_sum(ss, red);
         const float sc = rsqrtf(ss / (float)H + eps);
         __syncthreads();
@@ -111,25 +129,24 @@ __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
 // hb = gelu(g) * u for one sequence per CTA (F <= BK_THREADS * BK_GJ), left
 // as the down-proj operand
 constexpr int BK_GJ = 16;
-__global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(long long* g, long long* u, BkOperand hb, uint32_t F) {
+__global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(BkSums g, BkSums u, BkOperand hb, uint32_t F) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t b = blockIdx.x;
-    long long* gb = g + (size_t)b * F;
-    long long* ub = u + (size_t)b * F;
-    long long gr[BK_GJ], ur[BK_GJ];
+    long long idx[BK_GJ];
 #pragma unroll
     for (int j = 0; j < BK_GJ; ++j) {
         const uint32_t i = threadIdx.x + j * BK_THREADS;
-        gr[j] = i < F ? gb[i] : 0;
-        ur[j] = i < F ? ub[i] : 0;
+        idx[j] = i < F ? (long long)b * F + i : -1;
     }
+    float gv[BK_GJ], uv[BK_GJ];
+    bk_gather<BK_GJ, 2>(g, idx, gv);
+    bk_gather<BK_GJ, 2>(u, idx, uv);
     float h[BK_GJ];
 #pragma unroll
     for (int j = 0; j < BK_GJ; ++j) {
         const uint32_t i = threadIdx.x + j * BK_THREADS;
-        if (i < F) { gb[i] = 0; ub[i] = 0; }
-        h[j] = i < F ? gelu_tanh_ref(bk_unfix(gr[j])) * bk_unfix(ur[j]) : 0.0f;
+        h[j] = i < F ? gelu_tanh_ref(gv[j]) * uv[j] : 0.0f;
     }
     bmm_put_seq(h, F, b, hb.Npad, hb.xs, hb.xb);
 }
@@ -138,9 +155,9 @@ __global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(long long* g, long
 // append at pos[b], then 4-head attention over [kv_start, pos] of this
 // sequence's cache (window 0 = global). Dynamic smem: 4 * span_max floats.
 struct BkAttnArgs {
-    long long* q;          // [B][1024] raw, fixed-point sums
-    long long* k;          // [B][256]
-    long long* v;          // [B][256]
+    BkSums q;              // [B][1024] raw q, partial sums
+    BkSums k;              // [B][256]
+    BkSums v;              // [B][256]
     const float* qn;       // [256] q_norm weights
     const float* kn;       // [256] k_norm weights
     __half* kc;            // [B][max_seq][256]
@@ -179,22 +196,50 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         cs[tid] = c;
         cs[128 + tid] = s;
     }
+    // this sequence's q|k|v: every thread gathers three of the 1536 sums (all
+    // partial loads in flight together) into shared memory (the P.V partials'
+    // buffer, free until the scores are done)
+    float* qkv_s = red;
+    {
+        const bool want_q = a.mode != 1, want_kv = a.mode != 2;
+        long long idx[3];
+        const BkSums* src[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) {
+            const uint32_t i = tid + r * BK_THREADS;  // 0..1023 q, 1024..1279 k, 1280..1535 v
+            const bool isq = i < 1024;
+            src[r] = isq ? &a.q : (i < 1280 ? &a.k : &a.v);
+            idx[r] = (isq ? want_q : want_kv) ? (isq ? (long long)b * 1024 + i : (long long)b * 256 + ((i - 1024) & 255)) : -1;
+        }
+        // q, k and v come from one launch: the same K ranges, their own strides
+        float v3[3] = {0.0f, 0.0f, 0.0f};
+        const uint32_t ks = a.q.ks;
+#pragma unroll 1
+        for (uint32_t k0 = 0; k0 < ks; k0 += 16) {
+            float t[3][16];
+#pragma unroll
+            for (int r = 0; r < 3; ++r)
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    t[r][k] = (k0 + k < ks && idx[r] >= 0) ? __ldcg(src[r]->p + (size_t)(k0 + k) * src[r]->stride + idx[r]) : 0.0f;
+#pragma unroll
+            for (int r = 0; r < 3; ++r)
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v3[r] += t[r][k];
+        }
+#pragma unroll
+        for (int r = 0; r < 3; ++r) qkv_s[tid + r * BK_THREADS] = v3[r];
+    }
     __syncthreads();
     __half* kcb = a.kc + (size_t)b * a.seq_stride;
     __half* vcb = a.vc + (size_t)b * a.seq_stride;
     const bool want_q = a.mode != 1, want_kv = a.mode != 2;
     if (warp < 6 && (warp < 4 ? want_q : want_kv)) {
         // warps 0-3: q heads, 4: k, 5: v; lane holds dims 4 lane..+3 and 128 + 4 lane..+3
-        long long* src = warp < 4 ? a.q + (size_t)b * 1024 + warp * 256 : (warp == 4 ? a.k : a.v) + (size_t)b * 256;
+        const float* src = qkv_s + (warp < 4 ? warp * 256 : (warp == 4 ? 1024 : 1280));
         float v[8];
-        long long vr[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) vr[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (a.mode != 1) src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)] = 0;
-            v[i] = bk_unfix(vr[i]);
-        }
+        for (int i = 0; i < 8; ++i) v[i] = src[i < 4 ? 4 * lane + i : 128 + 4 * lane + (i - 4)];
         if (warp < 5) {
             const float* w = warp < 4 ? a.qn : a.kn;
             float ss = 0.0f;
@@ -229,11 +274,6 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
                 cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
             }
         }
-    }
-    if (a.mode == 2 && (warp == 4 || warp == 5)) {
-        // the rows' k and v are in the cache already: clear their sums
-        long long* src = (warp == 4 ? a.k : a.v) + (size_t)b * 256;
-        for (int i = lane; i < 256; i += 32) src[i] = 0;
     }
     if (a.mode == 1) return;
     const uint32_t pnew = a.mode == 0 ? pos : 0xFFFFFFFFu;  // mode 2 reads row pos from the cache

@@ -29,11 +29,13 @@
 //   warps 2-5  dequant: thread = column j, 32 nibbles -> fp16 A tile
 //   warps 6-13 epilogue: thread = column j x half of the sequences,
 //            tcgen05.ld of the sums (per item, or per block and scaled); the
-//            item's result goes to out (one K range) or to int64 fixed-point
-//            sums (K split across CTAs)
-// Four A tiles and four accumulator slots (two of 2N columns in scaled mode)
-// keep the MMA ahead of the epilogue; two CTAs share an SM. Waiting warps
-// poll with one lane.
+//            item's result goes to out (one K range), to int64 fixed-point
+//            sums (K split across CTAs), or, for the batched-decode engine, to
+//            its K range's fp32 partial that the consuming kernel adds
+// A pipeline stage is two 32-row blocks (one bulk copy per KM4 group and one
+// for the activations); three stages, each with its own A tile, and four
+// accumulator slots (two of 2N columns in scaled mode) keep the MMA ahead of
+// the epilogue; two CTAs share an SM. Waiting warps poll with one lane.
 // Shared-memory operands use the K-major, no-swizzle canonical layout: 8 rows x
 // 16 bytes per core matrix. Within each 8-element K chunk the order is the
 // nibble extraction order (k0 k4 k1 k5 k2 k6 k3 k7) on both operands.
@@ -47,9 +49,10 @@ namespace xp {
 
 constexpr int BMM_THREADS = 448;     // producer, MMA, 4 dequant, 8 epilogue warps
 constexpr int BMM_M = 128;           // output columns per tile
-constexpr int BMM_STAGES = 4;        // copy ring depth (blocks)
-constexpr int BMM_NA = 4;            // A tiles (dequantised blocks) in flight
-constexpr int BMM_ND = 4;            // TMEM accumulator slots in flight
+constexpr int BMM_SB = 2;            // 32-row blocks per pipeline stage
+constexpr int BMM_STAGES = 3;        // copy ring depth (stages), one A tile each
+constexpr int BMM_ABYTES = BMM_SB * 8192;  // dequantised A tile of a stage: 128 columns x 64 rows fp16
+constexpr int BMM_ND = 4;            // TMEM accumulator slots (integer mode; two of 2N columns when scaled)
 constexpr int BMM_MAXN = 64;
 // sequences padded to the MMA's N (32 or 64)
 inline uint32_t bmm_npad(uint32_t n) { return n <= 32 ? 32u : 64u; }
@@ -63,7 +66,8 @@ struct BmmPart {
     const uint4* wq;          // nibble plane of the matrix (reference layout)
     const uint2* sc;          // bf16 scale plane
     float* out;               // [N][cols] (ksplit == 1 and not raw)
-    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1 or raw), zero at launch
+    long long* acc;           // [N][cols] fixed-point sums (ksplit > 1, not raw), zero at launch
+    float* part;              // raw: [ksplit][nreal][cols] fp32 sums of each K range (plain stores)
     uint32_t cols;            // columns of this matrix
     uint32_t tile0;           // first tile of this matrix in the launch
 };
@@ -77,7 +81,7 @@ struct BmmArgs {
     uint32_t nreal;           // sequences actually present (rows of out)
     uint32_t ksplit, cb;      // K ranges per tile, blocks per range
     uint32_t nitems;          // tiles * ksplit
-    uint32_t raw;             // 1: leave the result in acc as fixed-point sums (the consumer converts)
+    uint32_t raw;             // 1: leave the result as per-K-range partial sums in part (the consumer adds them)
     uint32_t scaled;          // 1: scaled-operand mode (every scale in the fp16-exact range)
     const uint32_t* fbflag;   // if set, the mode is read here instead: 0 scaled, else integer
     uint32_t* err;
@@ -287,6 +291,17 @@ __global__ void __launch_bounds__(BMM_XP_THREADS) bmm_xprep_kernel(const float* 
     }
 }
 
+// Per-role timeline of the first CTAs (a build with BMM_TRACE only):
+// [cta][role][stage] %globaltimer ns; roles: 0 producer issued, 1 MMA inputs
+// ready, 2 MMA issued, 3 dequant input ready, 4 dequant done.
+#ifdef BMM_TRACE
+__device__ unsigned long long g_bmm_trace[4][6][64];
+#define BMM_TR(role, t) \
+    if (blockIdx.x < 4 && (t) < 64) g_bmm_trace[blockIdx.x][role][t] = globaltimer_ns();
+#else
+#define BMM_TR(role, t)
+#endif
+
 XP_DEV void bmm_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -302,19 +317,21 @@ __global__ void bmm_finish_kernel(long long* acc, float* out, size_t n) {
 
 __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_constant__ BmmArgs a) {
     extern __shared__ __align__(1024) unsigned char bsm[];
+    __shared__ float s_xs[BMM_MAXN];  // per-sequence scales 2^e (epilogue)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) { BMM_TR(5, 0) }
     const uint32_t N = a.N;
-    const uint32_t xbytes = 2 * 4 * N * 16;   // activations per block
-    const uint32_t sbytes = 2048 + xbytes;    // one stage: nibbles + activations
-    // layout: [stages][nibbles 2 KB | activations] [A tiles 2 x 8 KB] [mbarriers] [tmem addr]
+    const uint32_t xbytes = 2 * 4 * N * 16;              // activations per block
+    const uint32_t sbytes = BMM_SB * 2048 + BMM_SB * xbytes;  // one stage: nibbles + activations of two blocks
+    // layout: [stages][nibbles: group 0 blocks b, b+1 | group 1 blocks b, b+1 | activations b, b+1]
+    //         [A tiles, one per stage] [mbarriers] [tmem addr]
     unsigned char* stage0 = bsm;
     unsigned char* atile = bsm + BMM_STAGES * sbytes;
-    uint64_t* mb = reinterpret_cast<uint64_t*>(atile + BMM_NA * 8192);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(atile + BMM_STAGES * BMM_ABYTES);
     uint64_t* full = mb;                         // [STAGES] producer -> dequant, MMA
-    uint64_t* empty = mb + BMM_STAGES;           // [STAGES] dequant + MMA commit -> producer
-    uint64_t* afull = mb + 2 * BMM_STAGES;       // [NA] dequant -> MMA
-    uint64_t* aempty = afull + BMM_NA;           // [NA] MMA commit -> dequant
-    uint64_t* dfull = aempty + BMM_NA;           // [ND] MMA commit -> epilogue
+    uint64_t* empty = mb + BMM_STAGES;           // [STAGES] dequant + MMA commit -> producer, dequant (stage and A tile free)
+    uint64_t* afull = mb + 2 * BMM_STAGES;       // [STAGES] dequant -> MMA
+    uint64_t* dfull = afull + BMM_STAGES;        // [ND] MMA commit -> epilogue
     uint64_t* dempty = dfull + BMM_ND;           // [ND] epilogue -> MMA
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + BMM_ND);
 
@@ -322,10 +339,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         for (int i = 0; i < BMM_STAGES; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 2);
-        }
-        for (int i = 0; i < BMM_NA; ++i) {
             mbar_init(&afull[i], 1);
-            mbar_init(&aempty[i], 1);
         }
         for (int i = 0; i < BMM_ND; ++i) {
             mbar_init(&dfull[i], 1);
@@ -354,7 +368,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             // activations do: the first stages' nibbles are requested before
             // griddepcontrol.wait (under the previous kernel's tail when this
             // launch is programmatic), their activations after it.
-            uint32_t t = 0;  // global block counter of this CTA
+            uint32_t t = 0;  // stage counter of this CTA (two blocks each)
             uint32_t deferred[BMM_STAGES];
             uint32_t ndef = 0;
             bool waited = false;
@@ -362,14 +376,15 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 pdl_wait();
                 waited = true;
                 for (uint32_t i = 0; i < ndef; ++i)
-                    bulk_g2s(stage0 + i * sbytes + 2048, a.xb + (size_t)deferred[i] * xbytes, xbytes, &full[i]);
+                    bulk_g2s(stage0 + i * sbytes + BMM_SB * 2048, a.xb + (size_t)deferred[i] * xbytes, BMM_SB * xbytes,
+                             &full[i]);
             };
             for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
                 const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
                 const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
                 uint32_t lt;
                 const uint4* wq = bmm_part(a, tile, lt).wq;
-                for (uint32_t b = b0; b < b1; ++b, ++t) {
+                for (uint32_t b = b0; b < b1; b += BMM_SB, ++t) {
                     const uint32_t s = t % BMM_STAGES;
                     if (t >= BMM_STAGES) {
                         if (!waited) release();
@@ -377,83 +392,77 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                     }
                     unsigned char* st = stage0 + s * sbytes;
                     fence_proxy_async();
-                    mbar_expect_tx(&full[s], 2048 + xbytes);
-                    // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups
-                    bulk_g2s(st, wq + ((size_t)(2 * lt) * a.nblk + b) * 64, 1024, &full[s]);
-                    bulk_g2s(st + 1024, wq + ((size_t)(2 * lt + 1) * a.nblk + b) * 64, 1024, &full[s]);
-                    if (waited) bulk_g2s(st + 2048, a.xb + (size_t)b * xbytes, xbytes, &full[s]);
+                    mbar_expect_tx(&full[s], sbytes);
+                    // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups;
+                    // a group's consecutive blocks are contiguous (1 KB each)
+                    bulk_g2s(st, wq + ((size_t)(2 * lt) * a.nblk + b) * 64, BMM_SB * 1024, &full[s]);
+                    bulk_g2s(st + BMM_SB * 1024, wq + ((size_t)(2 * lt + 1) * a.nblk + b) * 64, BMM_SB * 1024, &full[s]);
+                    if (waited) bulk_g2s(st + BMM_SB * 2048, a.xb + (size_t)b * xbytes, BMM_SB * xbytes, &full[s]);
                     else deferred[ndef++] = b;  // stage s == ndef while t < BMM_STAGES
+                    BMM_TR(0, t)
                 }
             }
             if (!waited) release();
         }
+        __syncwarp();  // the whole warp reaches the closing CTA barrier together
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
         if (lane == 0) {
-            uint32_t t = 0, it = 0;  // blocks, items of this CTA
-            if (S) {
-                // one accumulator of 2N columns (hi sums | lo sums) per item,
-                // over the item's whole K range; two slots alternate
-                const uint32_t idesc = bmm_idesc(2 * N);
-                for (uint32_t item = blockIdx.x; item < a.nitems; item += G, ++it) {
-                    const uint32_t kc = item % a.ksplit;
-                    const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
-                    const uint32_t q = it & 1;
-                    if (it >= 2) bmm_wait(&dempty[q], ((it >> 1) - 1) & 1, a.err);  // slot q drained
-                    const uint32_t d = tmem + q * 2 * N;
-                    for (uint32_t b = b0; b < b1; ++b, ++t) {
-                        const uint32_t s = t % BMM_STAGES, p = t % BMM_NA;
-                        bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);
-                        bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);
-                        tc_fence_after();
-                        const uint32_t ab = smem_u32(atile + p * 8192);
-                        const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
+            uint32_t t = 0, tb = 0, it = 0;  // stages, blocks, items of this CTA
+            const uint32_t idesc = bmm_idesc(S ? 2 * N : N);
+            for (uint32_t item = blockIdx.x; item < a.nitems; item += G, ++it) {
+                const uint32_t kc = item % a.ksplit;
+                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+                // scaled: one accumulator of 2N columns (hi sums | lo sums) per
+                // item over its whole K range; two slots alternate
+                const uint32_t qi = it & 1;
+                if (S && it >= 2) bmm_wait(&dempty[qi], ((it >> 1) - 1) & 1, a.err);  // slot drained
+                for (uint32_t b = b0; b < b1; b += BMM_SB, ++t) {
+                    const uint32_t s = t % BMM_STAGES;
+                    bmm_wait(&afull[s], (t / BMM_STAGES) & 1, a.err);  // A tile of the stage dequantised
+                    bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);   // activations landed
+                    BMM_TR(1, t)
+                    tc_fence_after();
+                    const uint32_t ab = smem_u32(atile + s * BMM_ABYTES);
+                    const uint32_t xbase = smem_u32(stage0 + s * sbytes + BMM_SB * 2048);
+                    if (S) {
+                        const uint32_t d = tmem + qi * 2 * N;
 #pragma unroll
-                        for (int kk = 0; kk < 2; ++kk) {
+                        for (int kk = 0; kk < 2 * BMM_SB; ++kk) {
+                            // A: K chunks 2kk, 2kk+1 of 128 columns (chunk stride 2 KB, 8-row groups 128 B)
                             const uint64_t ad = bmm_desc(ab + kk * 4096, 2048, 128);
-                            // B: chunks 2kk, 2kk+1, rows hi 0..N-1 then lo N..2N-1
-                            // (chunk stride 32N B, 8-row groups 128 B)
-                            const uint64_t bd = bmm_desc(xbase + (2 * kk) * 2 * N * 16, 2 * N * 16, 128);
+                            // B: the same K chunks, rows hi 0..N-1 then lo N..2N-1
+                            // (chunk stride 32N B, 8-row groups 128 B; blocks follow each other)
+                            const uint64_t bd = bmm_desc(xbase + kk * 4 * N * 16, 2 * N * 16, 128);
                             bmm_mma(d, ad, bd, idesc, (b != b0 || kk != 0) ? 1u : 0u);
                         }
-                        bmm_commit(&aempty[p]);
-                        bmm_commit(&empty[s]);
-                    }
-                    bmm_commit(&dfull[q]);  // the item's sums are complete
-                }
-            } else {
-                const uint32_t idesc = bmm_idesc(N);
-                for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-                    const uint32_t kc = item % a.ksplit;
-                    const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
-                    for (uint32_t b = b0; b < b1; ++b, ++t) {
-                        const uint32_t s = t % BMM_STAGES, p = t % BMM_NA, q = t % BMM_ND;
-                        bmm_wait(&afull[p], (t / BMM_NA) & 1, a.err);       // A tile of block t dequantised
-                        bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);    // activations of block t landed
-                        if (t >= BMM_ND) bmm_wait(&dempty[q], ((t / BMM_ND) - 1) & 1, a.err);  // slot q read
-                        tc_fence_after();
-                        const uint32_t ab = smem_u32(atile + p * 8192);
-                        const uint32_t xbase = smem_u32(stage0 + s * sbytes + 2048);
-                        const uint32_t d = tmem + q * N;
-                        uint32_t acc = 0;
+                    } else {
+                        for (uint32_t h = 0; h < BMM_SB; ++h, ++tb) {
+                            const uint32_t q = tb % BMM_ND;
+                            if (tb >= BMM_ND) bmm_wait(&dempty[q], ((tb / BMM_ND) - 1) & 1, a.err);  // slot q read
+                            tc_fence_after();
+                            const uint32_t d = tmem + q * N;
+                            uint32_t acc = 0;
 #pragma unroll
-                        for (int kk = 0; kk < 2; ++kk)
+                            for (int kk = 0; kk < 2; ++kk)
 #pragma unroll
-                            for (int hl = 0; hl < 2; ++hl) {
-                                // A: chunks 2kk, 2kk+1 of 128 columns (chunk stride 2 KB, 8-row groups 128 B)
-                                const uint64_t ad = bmm_desc(ab + kk * 4096, 2048, 128);
-                                // B: chunks 2kk, 2kk+1 of half hl, N sequences (chunk stride 32N B, 8-row groups 128 B)
-                                const uint64_t bd = bmm_desc(xbase + (2 * kk * 2 + hl) * N * 16, 2 * N * 16, 128);
-                                bmm_mma(d, ad, bd, idesc, acc);
-                                acc = 1;
-                            }
-                        bmm_commit(&dfull[q]);   // accumulator of block t ready
-                        bmm_commit(&aempty[p]);  // A tile p free
-                        bmm_commit(&empty[s]);   // activations of stage s no longer read
+                                for (int hl = 0; hl < 2; ++hl) {
+                                    const uint64_t ad = bmm_desc(ab + (2 * h + kk) * 4096, 2048, 128);
+                                    // B: chunks 2kk, 2kk+1 of block h, half hl, N sequences
+                                    const uint64_t bd = bmm_desc(xbase + h * xbytes + (2 * kk * 2 + hl) * N * 16, 2 * N * 16, 128);
+                                    bmm_mma(d, ad, bd, idesc, acc);
+                                    acc = 1;
+                                }
+                            bmm_commit(&dfull[q]);  // accumulator of block tb ready
+                        }
                     }
+                    bmm_commit(&empty[s]);  // stage s and its A tile no longer read
+                    BMM_TR(2, t)
                 }
+                if (S) bmm_commit(&dfull[qi]);  // the item's sums are complete
             }
         }
+        __syncwarp();
     } else if (warp < 6) {
         // ------------------------------ dequant ------------------------------
         const uint32_t j = tid - 64;  // column within the tile, 0..127
@@ -465,52 +474,68 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             const uint2* scp = nullptr;
             uint32_t cols = 0;
             if (S) {
-                // this column's scales, one quad of blocks ahead
+                // this column's scales (one uint2 = four blocks)
                 uint32_t lt;
                 const BmmPart& P = bmm_part(a, tile, lt);
                 cols = P.cols;
                 scp = P.sc + lt * BMM_M + j;
                 sw = __ldg(scp + (size_t)(b0 >> 2) * cols);
-                sw_next = b0 + 4 < b1 ? __ldg(scp + (size_t)((b0 >> 2) + 1) * cols) : sw;
             }
-            for (uint32_t b = b0; b < b1; ++b, ++t) {
-                const uint32_t s = t % BMM_STAGES, p = t % BMM_NA;
-                __half2 s2;
+            for (uint32_t b = b0; b < b1; b += BMM_SB, ++t) {
+                const uint32_t s = t % BMM_STAGES;
+                __half2 s2[BMM_SB];
                 if (S) {
-                    if ((b & 3) == 0 && b != b0) {
-                        sw = sw_next;
-                        if (b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * cols);
+                    // the next quad's scales load while this stage is dequantised
+                    if ((b & 3) == 0 && b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * cols);
+#pragma unroll
+                    for (int h = 0; h < BMM_SB; ++h) {
+                        const uint32_t bb = b + h;
+                        const uint32_t word = (bb & 2) ? sw.y : sw.x;
+                        const __half v = __float2half_rn((bb & 1) ? bf16_hi(word) : bf16_lo(word));  // exact in range
+                        s2[h] = __halves2half2(v, v);
                     }
-                    const uint32_t word = (b & 2) ? sw.y : sw.x;
-                    const __half h = __float2half_rn((b & 1) ? bf16_hi(word) : bf16_lo(word));  // exact in range
-                    s2 = __halves2half2(h, h);
                 }
                 bmm_wait_warp(&full[s], (t / BMM_STAGES) & 1, a.err);
-                const uint4 w = *reinterpret_cast<const uint4*>(stage0 + s * sbytes + (j >> 6) * 1024 + (j & 63) * 16);
-                if (t >= BMM_NA) bmm_wait_warp(&aempty[p], ((t / BMM_NA) - 1) & 1, a.err);
-                unsigned char* at = atile + p * 8192 + j * 16;
-                if (S) {
-                    *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8s(w.x, s2);
-                    *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8s(w.y, s2);
-                    *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8s(w.z, s2);
-                    *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8s(w.w, s2);
-                } else {
-                    *reinterpret_cast<uint4*>(at + 0 * 2048) = bmm_unpack8(w.x);
-                    *reinterpret_cast<uint4*>(at + 1 * 2048) = bmm_unpack8(w.y);
-                    *reinterpret_cast<uint4*>(at + 2 * 2048) = bmm_unpack8(w.z);
-                    *reinterpret_cast<uint4*>(at + 3 * 2048) = bmm_unpack8(w.w);
+                if (j == 0) { BMM_TR(3, t) }
+                const unsigned char* nb = stage0 + s * sbytes + (j >> 6) * (BMM_SB * 1024) + (j & 63) * 16;
+                uint4 w[BMM_SB];
+#pragma unroll
+                for (int h = 0; h < BMM_SB; ++h) w[h] = *reinterpret_cast<const uint4*>(nb + h * 1024);
+                if (t >= BMM_STAGES) bmm_wait_warp(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);  // A tile free
+                unsigned char* at = atile + s * BMM_ABYTES + j * 16;
+#pragma unroll
+                for (int h = 0; h < BMM_SB; ++h) {
+                    unsigned char* ah = at + h * 4 * 2048;
+                    if (S) {
+                        *reinterpret_cast<uint4*>(ah + 0 * 2048) = bmm_unpack8s(w[h].x, s2[h]);
+                        *reinterpret_cast<uint4*>(ah + 1 * 2048) = bmm_unpack8s(w[h].y, s2[h]);
+                        *reinterpret_cast<uint4*>(ah + 2 * 2048) = bmm_unpack8s(w[h].z, s2[h]);
+                        *reinterpret_cast<uint4*>(ah + 3 * 2048) = bmm_unpack8s(w[h].w, s2[h]);
+                    } else {
+                        *reinterpret_cast<uint4*>(ah + 0 * 2048) = bmm_unpack8(w[h].x);
+                        *reinterpret_cast<uint4*>(ah + 1 * 2048) = bmm_unpack8(w[h].y);
+                        *reinterpret_cast<uint4*>(ah + 2 * 2048) = bmm_unpack8(w[h].z);
+                        *reinterpret_cast<uint4*>(ah + 3 * 2048) = bmm_unpack8(w[h].w);
+                    }
                 }
+                if (S && ((b + BMM_SB) & 3) == 0) sw = sw_next;
                 fence_proxy_async();  // generic smem writes -> async-proxy MMA reads
                 asm volatile("bar.sync 2, 128;" ::: "memory");
                 if (j == 0) {
-                    bmm_arrive(&afull[p]);
+                    bmm_arrive(&afull[s]);
                     bmm_arrive(&empty[s]);
+                    BMM_TR(4, t)
                 }
             }
         }
     } else {
         // ------------------------------ epilogue ------------------------------
         pdl_wait();  // the sequence scales and the sums it adds into follow the previous kernel
+        if (tid == 192) { BMM_TR(5, 3) }
+        // the sequences' scales in shared memory: a global load after the
+        // output stores (which may alias it) would wait for each of them
+        if (tid - 192 < BMM_MAXN) s_xs[tid - 192] = tid - 192 < (int)N ? a.xs[tid - 192] : 0.0f;
+        asm volatile("bar.sync 3, 256;" ::: "memory");
         const uint32_t e = warp - 6;
         const uint32_t q4 = warp & 3;                // TMEM lane quadrant of this warp
         const uint32_t j = q4 * 32 + lane;           // column within the tile
@@ -527,7 +552,9 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             if (S) {
                 // one read of the item's accumulator: hi sums + lo sums
                 const uint32_t q = it & 1;
+                if (tid == 192) { BMM_TR(5, 8 + it) }
                 bmm_wait_warp(&dfull[q], (it >> 1) & 1, a.err);
+                if (tid == 192) { BMM_TR(5, 16 + it) }
                 tc_fence_after();
                 float v[32];
                 const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * 2 * N + half * nh;
@@ -540,18 +567,21 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 tc_fence_before();
                 asm volatile("bar.sync 3, 256;" ::: "memory");
                 if (tid == 192) bmm_arrive(&dempty[q]);
+                if (tid == 192) { BMM_TR(5, 24 + it) }
                 ++it;
             } else {
 #pragma unroll
             for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
             // scales one quad ahead: the scale plane is read from HBM
-            uint2 sw = __ldg(P.sc + (size_t)(b0 >> 2) * P.cols + col);
-            uint2 sw_next = b0 + 4 < b1 ? __ldg(P.sc + (size_t)((b0 >> 2) + 1) * P.cols + col) : sw;
+            const uint2* scp = P.sc + col;
+            const size_t scs = P.cols;
+            uint2 sw = __ldg(scp + (size_t)(b0 >> 2) * scs);
+            uint2 sw_next = b0 + 4 < b1 ? __ldg(scp + (size_t)((b0 >> 2) + 1) * scs) : sw;
             for (uint32_t b = b0; b < b1; ++b, ++t) {
                 const uint32_t q = t % BMM_ND;
                 if ((b & 3) == 0 && b != b0) {
                     sw = sw_next;
-                    if (b + 4 < b1) sw_next = __ldg(P.sc + (size_t)((b >> 2) + 1) * P.cols + col);
+                    if (b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * scs);
                 }
                 const uint32_t word = (b & 2) ? sw.y : sw.x;
                 const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
@@ -568,28 +598,37 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 if (tid == 192) bmm_arrive(&dempty[q]);
             }
             }
+            // output addresses in registers: P lives in parameter space behind a
+            // generic pointer, and a load through it after a store would wait
+            // for that store
+            const size_t cstride = P.cols;
+            float* dst = a.raw ? P.part + (size_t)kc * a.nreal * cstride + col : P.out + col;
+            long long* accp = P.acc + col;
 #pragma unroll
             for (int i = 0; i < BMM_MAXN / 2; ++i) {
                 const uint32_t n = half * nh + i;
                 if ((uint32_t)i < nh && n < a.nreal) {
-                    const float v = sum[i] * a.xs[n];
-                    if (a.ksplit == 1 && !a.raw) {
-                        P.out[(size_t)n * P.cols + col] = v;
+                    const float v = sum[i] * s_xs[n];
+                    if (a.raw || a.ksplit == 1) {
+                        // raw: the consumer adds the ksplit partials in K-range order
+                        dst[(size_t)n * cstride] = v;
                     } else {
                         const float f = v * 4294967296.0f;
                         long long fx = 0;
                         if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
                         else atomicOr(a.err, TK_ERR_RANGE);
-                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(P.acc + (size_t)n * P.cols + col),
+                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(accp + (size_t)n * cstride),
                                      "l"(fx) : "memory");
                     }
                 }
             }
         }
     }
+    if (tid == 64 + 128) { BMM_TR(5, 1) }
     pdl_launch_dependents();
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) { BMM_TR(5, 2) }
     if (warp == 1) {
         tc_fence_after();
         const uint32_t ncols = BMM_ND * N;

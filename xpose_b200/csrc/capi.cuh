@@ -799,7 +799,7 @@ BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     p.off_xb = 512;
     p.off_acc = p.off_xb + (size_t)p.nblk * 2 * 4 * p.npad * 16;
     p.bytes = p.off_acc + (p.ksplit > 1 ? (size_t)p.npad * cols * 8 : 0);
-    p.smem = (size_t)BMM_STAGES * (2048 + 2 * 4 * p.npad * 16) + BMM_NA * 8192 + 8 * (2 * BMM_STAGES + 2 * BMM_NA + 2 * BMM_ND) + 16;
+    p.smem = (size_t)BMM_STAGES * (BMM_SB * (2048 + 2 * 4 * p.npad * 16) + BMM_ABYTES) + 8 * (3 * BMM_STAGES + 2 * BMM_ND) + 16;
     return p;
 }
 }  // namespace
@@ -809,22 +809,25 @@ void xp_bmm_trace_read(unsigned long long* out) {
     cudaMemcpyFromSymbol(out, g_bmm_trace, sizeof(g_bmm_trace));
 }
 #endif
+// K ranges of a launch over `cols` total columns (the raw partial count)
+static uint32_t bmm_ksplit(uint32_t rows, uint32_t cols, uint32_t n) { return bmm_plan(rows, cols, n).ksplit; }
 size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n) {
     if (rows == 0 || rows % 128 || cols == 0 || cols % 128 || n == 0 || n > BMM_MAXN) return 0;
     return bmm_plan(rows, cols, n).bytes;
 }
 // One batched matvec launch over up to BMM_MAXPARTS matrices that share the
 // input (same rows): activation prep once, then the tensor-core kernel over
-// every matrix's column tiles. raw: each matrix's result stays as fixed-point
-// sums in its raw buffer (zero at entry; the consumer converts and re-zeroes
-// them). Otherwise (one matrix) out gets fp32, K-split sums going through the
-// scratch and a finish launch that leaves them zero.
+// every matrix's column tiles. raw: each matrix's result stays as ksplit fp32
+// partial sums in its part buffer ([ksplit][n][cols], bmm_ksplit), which the
+// consumer adds in K-range order. Otherwise (one matrix) out gets fp32,
+// K-split sums going through the scratch and a finish launch that leaves them
+// zero.
 struct BmmMat {
     const uint32_t* wq;
     const uint32_t* sc;
     uint32_t cols;
     float* out;
-    long long* raw;
+    float* part;
 };
 // prep: the activation operand already written by its producer (xs, xb of
 // bmm_put_seq); then `in` is unused and no prep launch runs.
@@ -908,7 +911,8 @@ static xp_status bmm_run(cudaStream_t st, const BmmMat* mats, uint32_t nmat, boo
         P.wq = reinterpret_cast<const uint4*>(mats[m].wq);
         P.sc = reinterpret_cast<const uint2*>(mats[m].sc);
         P.out = mats[m].out;
-        P.acc = raw ? mats[m].raw : acc;
+        P.acc = acc;
+        P.part = mats[m].part;
         P.cols = mats[m].cols;
         P.tile0 = tile0;
         tile0 += mats[m].cols / BMM_M;

@@ -1032,9 +1032,11 @@ struct xp_bdec {
     float *x = nullptr, *logits = nullptr;
     // matvec inputs, written as tensor-core operands by the kernels that make them
     BkOperand op_xn{}, op_att{}, op_hb{};
-    // matvec results as int64 fixed-point sums (2^-32): the tensor-core kernel
-    // adds into them, the consuming kernel converts and re-zeroes them
-    long long *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *g = nullptr, *u = nullptr, *dn = nullptr;
+    // matvec results as fp32 partial sums, one per K range of the tensor-core
+    // launch ([ks][B][cols]); the consuming kernel adds them
+    float *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *g = nullptr, *u = nullptr, *dn = nullptr;
+    uint32_t ks_qkv = 1, ks_o = 1, ks_gu = 1, ks_dn = 1;
+    BkSums sums(const float* p, uint32_t ks, uint32_t cols) const { return BkSums{p, ks, B * cols}; }
     std::vector<__half*> kc, vc;
     uint32_t *tokens = nullptr, *pos = nullptr, *h_tok = nullptr;
     // one tensor-core scratch per matrix shape: a call leaves its fixed-point
@@ -1101,7 +1103,7 @@ struct xp_bdec {
     }
     // raw[i] (fixed-point sums, zero on entry) = in x W[i] for every sequence:
     // matrices with the same rows in one launch
-    cudaError_t mm_raw(std::initializer_list<std::pair<long long*, const QW*>> parts, const BkOperand& in) {
+    cudaError_t mm_raw(std::initializer_list<std::pair<float*, const QW*>> parts, const BkOperand& in) {
         BmmMat m[BMM_MAXPARTS];
         uint32_t n = 0, cols = 0, rows = 0;
         int mode = BMM_MODE_SCALED;
@@ -1109,7 +1111,7 @@ struct xp_bdec {
             const QW& w = *pr.second;
             if (mode_of(w) != BMM_MODE_SCALED) mode = BMM_MODE_INTEGER;
             m[n++] = BmmMat{reinterpret_cast<const uint32_t*>(w.wq), reinterpret_cast<const uint32_t*>(w.sc), w.cols,
-                            nullptr, pr.first};
+                            nullptr, pr.first};  // partials [ks][B][cols]
             cols += w.cols;
             rows = w.rows;
         }
@@ -1119,7 +1121,7 @@ struct xp_bdec {
         return bmm_run(st, m, n, true, nullptr, rows, B, scr, &pr, pdl_mm, mode) == XP_OK ? cudaSuccess : cudaErrorUnknown;
     }
     // one position for every sequence: tokens -> logits, pos += 1
-    cudaError_t resid_norm(long long* y, const float* w_post, const float* w_pre, int mode) {
+    cudaError_t resid_norm(BkSums y, const float* w_post, const float* w_pre, int mode) {
         return launch_ex(bk_resid_norm_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, x, y, w_post, w_pre, op_xn,
                          s->cfg.hidden, s->cfg.rms_eps, mode);
     }
@@ -1134,11 +1136,13 @@ struct xp_bdec {
             return e;
         for (uint32_t l = 0; l < L; ++l) {
             const LayerDev& W = s->L[l];
-            if ((e = resid_norm(dn, l == 0 ? nullptr : s->L[l - 1].norm[3], W.norm[0], l == 0 ? 0 : 1)) != cudaSuccess)
+            if ((e = resid_norm(sums(dn, ks_dn, H), l == 0 ? nullptr : s->L[l - 1].norm[3], W.norm[0], l == 0 ? 0 : 1)) !=
+                cudaSuccess)
                 return e;
             if ((e = mm_raw({{q, &W.m[0]}, {k, &W.m[1]}, {v, &W.m[2]}}, op_xn)) != cudaSuccess) return e;
             BkAttnArgs aa{};
-            aa.q = q; aa.k = k; aa.v = v; aa.qn = W.norm[4]; aa.kn = W.norm[5];
+            aa.q = sums(q, ks_qkv, 1024); aa.k = sums(k, ks_qkv, 256); aa.v = sums(v, ks_qkv, 256);
+            aa.qn = W.norm[4]; aa.kn = W.norm[5];
             aa.kc = kc[l]; aa.vc = vc[l]; aa.pos = pos; aa.att = op_att; aa.max_seq = max_seq;
             const bool glob = s->is_global(l);
             aa.window = glob ? 0 : c.sliding_window;
@@ -1158,19 +1162,18 @@ struct xp_bdec {
                     return e;
             }
             if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
-            if ((e = resid_norm(o, W.norm[1], W.norm[2], 1)) != cudaSuccess) return e;
+            if ((e = resid_norm(sums(o, ks_o, H), W.norm[1], W.norm[2], 1)) != cudaSuccess) return e;
             if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, op_xn)) != cudaSuccess) return e;
-            if ((e = launch_ex(bk_geglu_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, g, u, op_hb, F)) != cudaSuccess)
+            if ((e = launch_ex(bk_geglu_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, sums(g, ks_gu, F),
+                               sums(u, ks_gu, F), op_hb, F)) != cudaSuccess)
                 return e;
             if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
         }
         if (!head) {
-            // a prompt position (or chunk) before the last: its down-proj sums
-            // are left for nobody, so clear them instead of running the LM head
-            if ((e = cudaMemsetAsync(dn, 0, (size_t)B * H * sizeof(long long), st)) != cudaSuccess) return e;
+            // a prompt position (or chunk) before the last: no LM head
             return launch_ex(bk_pos_inc_kernel, dim3(1), dim3(64), 0, st, 1, false, pos, B);
         }
-        if ((e = resid_norm(dn, s->L[L - 1].norm[3], s->final_norm, 1)) != cudaSuccess) return e;
+        if ((e = resid_norm(sums(dn, ks_dn, H), s->L[L - 1].norm[3], s->final_norm, 1)) != cudaSuccess) return e;
         if ((e = mm(logits, op_xn, s->lm)) != cudaSuccess) return e;
         if ((e = launch_ex(bk_pos_inc_kernel, dim3(1), dim3(64), 0, st, 1, pdl_k, pos, B)) != cudaSuccess) return e;
         return cudaGetLastError();
@@ -1244,8 +1247,14 @@ static xp_status bdec_create(xp_session* s, uint32_t nseq, uint32_t max_seq, con
     const size_t H = c.hidden, F = c.ffn, QD = s->q_dim(), KVD = s->kv_dim(), V = c.vocab;
     xp_status e;
 #define BA(p, n) if ((e = b->alloc(&b->p, (n))) != XP_OK) return bail(e)
-    BA(x, nseq * H); BA(q, nseq * QD); BA(k, nseq * KVD); BA(v, nseq * KVD);
-    BA(o, nseq * H); BA(g, nseq * F); BA(u, nseq * F); BA(dn, nseq * H); BA(logits, nseq * V);
+    // partial-sum buffers: one per K range of the launch that fills them
+    b->ks_qkv = bmm_ksplit((uint32_t)H, (uint32_t)(QD + 2 * KVD), nseq);
+    b->ks_o = bmm_ksplit((uint32_t)QD, (uint32_t)H, nseq);
+    b->ks_gu = bmm_ksplit((uint32_t)H, (uint32_t)(2 * F), nseq);
+    b->ks_dn = bmm_ksplit((uint32_t)F, (uint32_t)H, nseq);
+    BA(x, nseq * H); BA(q, b->ks_qkv * nseq * QD); BA(k, b->ks_qkv * nseq * KVD); BA(v, b->ks_qkv * nseq * KVD);
+    BA(o, b->ks_o * nseq * H); BA(g, b->ks_gu * nseq * F); BA(u, b->ks_gu * nseq * F); BA(dn, b->ks_dn * nseq * H);
+    BA(logits, nseq * V);
     for (auto pr : {std::make_pair(&b->op_xn, H), std::make_pair(&b->op_att, QD), std::make_pair(&b->op_hb, F)}) {
         BkOperand& op = *pr.first;
         op.Npad = bmm_npad(nseq);
