@@ -14,13 +14,14 @@
 //     bulk copies (cp.async.bulk, 32 positions = 16 KB a stage) issued before
 //     the q/k work, and computes scores, a softmax partial (max, sum) and the
 //     unnormalised P.V for its chunk;
-//   * the combine is two-level: the CTAs of a thread-block cluster (up to 16)
-//     push their partials into the cluster leader's shared memory (st.async,
-//     completing on the leader's mbarrier; no cluster-wide barrier after the
-//     work) and the leader merges them; with more than one cluster, the last
-//     cluster to finish (atomic ticket) merges the cluster results in cluster
-//     order and writes the attention output and its matvec limbs. Fixed merge
-//     order: deterministic.
+//   * the combine is two-level: within a thread-block cluster (up to 16
+//     CTAs) the output is cut into one slice per CTA; every CTA pushes slice
+//     k of its partial into CTA k's shared memory (st.async, completing on
+//     CTA k's mbarrier; no cluster-wide barrier after the work) and each CTA
+//     merges its slice; with more than one cluster, the last CTA to finish
+//     (atomic ticket) merges the cluster results in cluster order and writes
+//     the attention output and its matvec limbs. Fixed merge order:
+//     deterministic.
 // Shape: n_heads = NH query heads sharing one kv head, head_dim = 256.
 #pragma once
 #include <cooperative_groups.h>
@@ -150,10 +151,10 @@ __device__ uint32_t g_att_launch;
 #define ATT_STAMP(i) do { } while (0)
 #endif
 
-// Cluster primitives of the push merge: each CTA stores its partial into the
-// cluster leader's shared memory with st.async, which completes bytes on the
-// leader's mbarrier, so only the leader waits and no cluster-wide barrier
-// follows the merge.
+// Cluster primitives of the push merge: each CTA stores a slice of its
+// partial into the shared memory of the CTA that merges that slice with
+// st.async, which completes bytes on the receiver's mbarrier, so only
+// receivers wait and no cluster-wide barrier follows the merge.
 XP_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 XP_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 XP_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
@@ -184,11 +185,12 @@ struct AttnSmem {
     static constexpr size_t knv = qs + 4 * 256 * 4;
     static constexpr size_t accs = knv + 2 * 256 * 2;
     static constexpr size_t sc = accs + (size_t)ATT_PVG * 4 * 256 * 4;
-    // cluster leader only: one slot per cluster CTA, [NH][256] partial | (max, sum) x NH
-    static constexpr size_t slot_bytes = 4 * 256 * 4 + 4 * 2 * 4;
+    // merge slots: one per cluster CTA, its slice of this CTA's part of the
+    // output (4 KB / cluster) | (max, sum) x NH
+    static constexpr size_t slot_bytes(uint32_t cluster) { return 4 * 256 * 4 / cluster + 4 * 2 * 4; }
     __host__ __device__ static constexpr size_t slots(uint32_t chunk_max) { return sc + (size_t)4 * chunk_max * 4; }
     static constexpr size_t bytes(uint32_t chunk_max, uint32_t cluster) {
-        return slots(chunk_max) + (cluster > 1 ? (size_t)cluster * slot_bytes : 0);
+        return slots(chunk_max) + (cluster > 1 ? (size_t)cluster * slot_bytes(cluster) : 0);
     }
 };
 
@@ -246,49 +248,9 @@ __device__ __noinline__ void attn_merge_global(const float* part, const float* s
     attn_finish<NH>(o, M, L, out, nullptr, xq, true, accs);
 }
 
-// The cluster's partials in the leader's shared-memory slots (cnt <= MAXP
-// = 16). The weights e^(m_b - M) depend only on (head, partial), so lane b of
-// half-warp h computes head h's weight for partial b once (M by a max over
-// the half-warp, L summed in partial order by lane 0) into wsh[NH][16] and
-// lsh[NH]; then every thread accumulates its float4 in partial order. The
-// same operations in the same order as the loop above, 1/64 of the exps.
-template <int NH, int MAXP>
-XP_DEV void attn_merge_slots(const float* slots, uint32_t cnt, float4& o, float& M, float& L, float* wsh,
-                             float* lsh) {
-    static_assert(MAXP == 16 && NH * 16 <= ATT_MT, "a half-warp per head");
-    const uint32_t tid = threadIdx.x;
-    constexpr uint32_t SF = AttnSmem::slot_bytes / 4;
-    if (tid < NH * 16) {
-        const uint32_t h = tid >> 4, b = tid & 15;
-        const float2 st = b < cnt ? reinterpret_cast<const float2*>(slots + b * SF + NH * 256)[h] : make_float2(0.0f, 0.0f);
-        float m = st.y > 0.0f ? st.x : -INFINITY;
-#pragma unroll
-        for (int d = 8; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
-        const float w = st.y > 0.0f ? expf(st.x - m) : 0.0f;
-        wsh[h * 16 + b] = w;
-        // L in partial order (lane 0 of the half-warp gathers the terms)
-        float l = 0.0f;
-#pragma unroll
-        for (int k = 0; k < MAXP; ++k) {
-            const float yk = __shfl_sync(0xffffffffu, st.y, (tid & 16) + k);
-            const float wk = __shfl_sync(0xffffffffu, w, (tid & 16) + k);
-            if ((uint32_t)k < cnt) l += yk * wk;
-        }
-        if (b == 0) { lsh[h * 2] = m; lsh[h * 2 + 1] = l; }
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(ATT_MT) : "memory");
-    const uint32_t h = (4 * tid) >> 8;
-    M = lsh[h * 2];
-    L = lsh[h * 2 + 1];
-    o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-    for (int b = 0; b < MAXP; ++b)
-        if ((uint32_t)b < cnt) {
-            const float4 v = reinterpret_cast<const float4*>(slots + b * SF)[tid];
-            const float w = wsh[h * 16 + b];
-            o.x += v.x * w; o.y += v.y * w; o.z += v.z * w; o.w += v.w * w;
-        }
-}
+// The RoPE table again when the position changed after the speculative one
+// (rare: out of line, so its code is not fetched on the common path).
+__device__ __noinline__ void rope_table_again(float ang, float* s, float* c) { rope_sincos(ang, s, c); }
 
 template <int NH>
 __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
@@ -303,7 +265,6 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     float* sc = reinterpret_cast<float*>(smem + AttnSmem::sc);         // [chunk_max][NH] scores / probs
     __shared__ __align__(16) float stat[NH * 2];  // (max, sum) per head, read as float2 by the merge
     __shared__ float rcs[256];  // RoPE cos | sin of this position
-    __shared__ float wsh[NH * 16 + NH * 2];  // merge weights [NH][16] | (M, L) per head
     __shared__ uint32_t s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -318,8 +279,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     const uint32_t csize = cl.num_blocks(), crank = cl.block_rank();
-    if (csize > 1) cluster_arrive_relaxed();  // the leader's merge barrier is initialised
+    if (csize > 1) cluster_arrive_relaxed();  // this CTA's merge barrier is initialised
     pdl_launch_dependents();
+    // Before the grid dependency resolves (this launch may overlap the tail
+    // of the kernel before it): the position read here may be stale, so it
+    // only steers an L2 prefetch of this CTA's K and V rows (a hint: what the
+    // copies below read is unaffected) and a RoPE table that is recomputed
+    // if the position turns out different.
+    const uint32_t pos_early = __ldcg(a.pos);
+    if (pos_early < a.cache_rows) {
+        const uint32_t seq_e = pos_early + 1;
+        const uint32_t ks_e = (a.window == 0 || seq_e <= a.window) ? 0 : seq_e - a.window;
+        const uint32_t span_e = seq_e - ks_e;
+        uint32_t ch = (span_e + gridDim.x - 1) / gridDim.x;
+        ch = min((ch + 7) & ~7u, a.chunk_max);
+        const uint32_t r0 = ks_e + min(blockIdx.x * ch, span_e), r1 = ks_e + min((blockIdx.x + 1) * ch, span_e);
+        if (tid == 0 && r1 > r0) {
+            bulk_prefetch_l2(a.kcache + (size_t)r0 * 256, (r1 - r0) * 512);
+            bulk_prefetch_l2(a.vcache + (size_t)r0 * 256, (r1 - r0) * 512);
+        }
+        if (tid < 128) rope_sincos((float)pos_early * a.inv_freq[tid], &rcs[128 + tid], &rcs[tid]);
+    }
     pdl_wait();
     ATT_STAMP(1);
 #ifdef XP_ATT_TRACE
@@ -330,6 +310,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     };
 #endif
 
+    // q, k, v and the norm weights load together with the position (they do
+    // not depend on it)
+    float v[8], wv[8];
+    if (warp <= NH + 1) {
+        const float* src = warp < NH ? a.q_raw + warp * 256 : (warp == NH ? a.k_raw : a.v_raw);
+        const float* wsrc = warp < NH ? a.q_norm : a.k_norm;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[i] = src[4 * lane + i];
+            v[4 + i] = src[128 + 4 * lane + i];
+            wv[i] = wsrc[4 * lane + i];
+            wv[4 + i] = wsrc[128 + 4 * lane + i];
+        }
+    }
     const uint32_t pos = *a.pos;
     ATT_STAMP(2);
     if (pos >= a.cache_rows) {  // the append would land past the caches: flag, write nothing
@@ -369,19 +363,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     // ---- q, k, v post-processing (overlaps the first copies) ------------------------------
     // The position's RoPE table is computed once (one angle per thread); the
     // q, k, v loads are in flight meanwhile.
-    float v[8], wv[8];
-    if (warp <= NH + 1) {
-        const float* src = warp < NH ? a.q_raw + warp * 256 : (warp == NH ? a.k_raw : a.v_raw);
-        const float* wsrc = warp < NH ? a.q_norm : a.k_norm;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            v[i] = src[4 * lane + i];
-            v[4 + i] = src[128 + 4 * lane + i];
-            wv[i] = wsrc[4 * lane + i];
-            wv[4 + i] = wsrc[128 + 4 * lane + i];
-        }
-    }
-    if (tid < 128) rope_sincos((float)pos * a.inv_freq[tid], &rcs[128 + tid], &rcs[tid]);
+    if (tid < 128 && pos != pos_early) rope_table_again((float)pos * a.inv_freq[tid], &rcs[128 + tid], &rcs[tid]);
     __syncthreads();
     if (warp <= NH) qk_norm_rope(v, wv, a.eps, rcs);
     if (warp < NH) {
@@ -524,11 +506,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     }
     __syncthreads();
     ATT_STAMP(6);
-    // ---- combine: push to the cluster leader, then clusters through global memory ----------------
+    // ---- combine: slices pushed to the CTAs that merge them, then clusters through global memory ----
     // threads 0..ATT_MT-1 own one float4 of the [NH][256] partial each
     const uint32_t ncl = nblk / csize, ci = blockIdx.x / csize;
     float* slots = reinterpret_cast<float*>(smem + AttnSmem::slots(a.chunk_max));
-    constexpr uint32_t SLOT_F = AttnSmem::slot_bytes / 4;
     const bool mt = tid < ATT_MT;
     float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (mt)
@@ -537,58 +518,94 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
             const float4 x = reinterpret_cast<const float4*>(accs)[g * NH * 64 + tid];
             o.x += x.x; o.y += x.y; o.z += x.z; o.w += x.w;
         }
+    // Distributed merge: the cluster's [NH][256] output is cut into csize
+    // slices of S4 float4s; slice k is merged by cluster CTA k. Every CTA
+    // stores slice k of its partial (and its per-head statistics) into CTA
+    // k's slot for it with st.async, which completes bytes on CTA k's merge
+    // barrier, so each CTA receives 4 KB in total (plus 32 B of statistics
+    // per peer) instead of one CTA receiving every partial.
+    const uint32_t S4 = (uint32_t)ATT_MT / csize;      // float4s per slice
+    const uint32_t SLOT4 = S4 + 2;                      // slice + (max, sum) x NH
+    float4* slots4 = reinterpret_cast<float4*>(slots);  // [csize][SLOT4]
     if (csize > 1) {
-        cluster_wait();
-        if (crank != 0) {
-            // this CTA's partial and statistics into the leader's slot `crank`;
-            // the leader waits on its barrier for every peer's bytes
-            if (!mt) return;
-            const uint32_t dst = mapa_shared(smem_u32(slots + crank * SLOT_F), 0);
-            const uint32_t rb = mapa_shared(smem_u32(&bar[ATT_STAGES]), 0);
-            st_async_v4(dst + 16 * tid, o, rb);
-            if (tid < NH / 2) st_async_v4(dst + NH * 256 * 4 + 16 * tid, reinterpret_cast<const float4*>(stat)[tid], rb);
-            ATT_STAMP(7);
-#ifdef XP_ATT_TRACE
-            flush_();
-#endif
-            return;
+        cluster_wait();  // every CTA's merge barrier is initialised
+        if (mt) {
+            const uint32_t k = tid / S4;
+            const uint32_t dst = mapa_shared(smem_u32(slots4 + crank * SLOT4), k);
+            const uint32_t rb = mapa_shared(smem_u32(&bar[ATT_STAGES]), k);
+            st_async_v4(dst + 16 * (tid % S4), o, rb);
+            if (tid % S4 == 0) {
+                st_async_v4(dst + 16 * S4, reinterpret_cast<const float4*>(stat)[0], rb);
+                st_async_v4(dst + 16 * S4 + 16, reinterpret_cast<const float4*>(stat)[1], rb);
+            }
         }
-        if (mt) reinterpret_cast<float4*>(slots)[tid] = o;
-        if (tid < NH / 2) reinterpret_cast<float4*>(slots + NH * 256)[tid] = reinterpret_cast<const float4*>(stat)[tid];
-        if (tid == 0) mbar_expect_tx(&bar[ATT_STAGES], (csize - 1) * (uint32_t)AttnSmem::slot_bytes);
-        __syncthreads();
+        if (tid == 0) mbar_expect_tx(&bar[ATT_STAGES], csize * SLOT4 * 16);
         mbar_wait(&bar[ATT_STAGES], 0, a.err);
     }
     ATT_STAMP(7);
-    // the cluster's merged partial (a lone CTA's own partial as it stands:
-    // the merge of one partial is the identity); the second half of accs
-    // stages the matvec limbs
-    if (mt) {
-        float M, L;
+    // This CTA's merged slice (a lone CTA's own partial as it stands: the
+    // merge of one partial is the identity), in partial order: M = max of the
+    // non-empty partials' maxima, w_b = e^(m_b - M), L = sum l_b w_b,
+    // o = sum P_b w_b.
+    const uint32_t nmine = csize > 1 ? S4 : (uint32_t)ATT_MT;  // float4s this CTA finishes
+    const uint32_t e4 = (csize > 1 ? crank * S4 : 0u) + tid;    // float4 index in [NH][256]
+    const bool fin = tid < nmine;
+    float M = -INFINITY, L = 0.0f;
+    if (fin) {
+        const uint32_t h = (4 * e4) >> 8;
         if (csize > 1) {
-            attn_merge_slots<NH, 16>(slots, csize, o, M, L, wsh, wsh + NH * 16);
+            const float* sf = reinterpret_cast<const float*>(slots4);
+            for (uint32_t b = 0; b < csize; ++b) {
+                const float2 st = reinterpret_cast<const float2*>(sf + (b * SLOT4 + S4) * 4)[h];
+                if (st.y > 0.0f) M = fmaxf(M, st.x);
+            }
+            o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (uint32_t b = 0; b < csize; ++b) {
+                const float2 st = reinterpret_cast<const float2*>(sf + (b * SLOT4 + S4) * 4)[h];
+                const float w = st.y > 0.0f ? expf(st.x - M) : 0.0f;
+                const float4 v = slots4[b * SLOT4 + tid];
+                L += st.y * w;
+                o.x += v.x * w; o.y += v.y * w; o.z += v.z * w; o.w += v.w * w;
+            }
         } else {
-            const float2 st = reinterpret_cast<const float2*>(stat)[(4 * tid) >> 8];
+            const float2 st = reinterpret_cast<const float2*>(stat)[h];
             const bool live = st.y > 0.0f;
             M = live ? st.x : -INFINITY;
             L = live ? st.y : 0.0f;
             if (!live) o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        attn_finish<NH>(o, M, L, ncl == 1 ? a.att : a.part + (size_t)ci * NH * 256,
-                        a.pstat + (size_t)ci * NH * 2, ncl == 1 ? a.att_xq : nullptr, ncl == 1, accs + NH * 256);
-#ifdef XP_ATT_TRACE
-        if (tid == 0) tr_[14] = globaltimer_ns();
-#endif
+        if (ncl > 1) {
+            // the cluster's partial slice and, once per head, its (M, L)
+            reinterpret_cast<float4*>(a.part + (size_t)ci * NH * 256)[e4] = o;
+            if ((e4 & 63) == 0) { a.pstat[((size_t)ci * NH + h) * 2] = M; a.pstat[((size_t)ci * NH + h) * 2 + 1] = L; }
+        } else {
+            const float inv = 1.0f / L;
+            o.x *= inv; o.y *= inv; o.z *= inv; o.w *= inv;
+            reinterpret_cast<float4*>(a.att)[e4] = o;
+            if (a.att_xq) reinterpret_cast<float4*>(accs + NH * 256)[e4] = o;
+        }
     }
+    if (ncl == 1 && a.att_xq) {
+        // matvec limbs of this CTA's output blocks (32 floats each)
+        __syncthreads();
+        const uint32_t b0 = (csize > 1 ? crank * S4 : 0u) / 8, nb = nmine / 8;
+        for (uint32_t bb = warp; bb < nb; bb += ATT_THREADS / 32)
+            xq_prep_block(accs[NH * 256 + (b0 + bb) * 32 + lane], &a.att_xq[b0 + bb]);
+    }
+#ifdef XP_ATT_TRACE
+    if (tid == 0) tr_[14] = globaltimer_ns();
+#endif
     ATT_STAMP(8);
 #ifdef XP_ATT_TRACE
     flush_();
     if (ncl == 1 && tid == 0) { __threadfence(); atomicAdd(&g_att_launch, 1u); }
 #endif
     if (ncl == 1) return;
+    // every CTA of every cluster wrote a slice: the last of them merges the
+    // clusters
     __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(a.ticket, 1u) == ncl - 1) ? 1u : 0u;
+    if (tid == 0) s_last = (atomicAdd(a.ticket, 1u) == nblk - 1) ? 1u : 0u;
     __syncthreads();
     if (!s_last) return;
     __threadfence();

@@ -803,6 +803,12 @@ BmmPlan bmm_plan(uint32_t rows, uint32_t cols, uint32_t n) {
     return p;
 }
 }  // namespace
+#ifdef XP_ATT_TRACE
+void xp_att_trace_read(unsigned long long* out) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(out, g_att_trace, sizeof(g_att_trace));
+}
+#endif
 #ifdef BMM_TRACE
 void xp_bmm_trace_read(unsigned long long* out) {
     cudaDeviceSynchronize();

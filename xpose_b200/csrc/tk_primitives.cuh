@@ -42,6 +42,12 @@ XP_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
         : "memory");
 }
 
+// L2 prefetch of a global range (16-byte aligned, size a multiple of 16): a
+// hint with no effect on what later loads read.
+XP_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 XP_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
