@@ -117,21 +117,8 @@ XP_DEV void bmm_commit(uint64_t* bar) {
 }
 XP_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 XP_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-XP_DEV void tmem_ld32(uint32_t taddr, float v[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-XP_DEV void tmem_ld16(uint32_t taddr, float v[32]) {
+// 16 columns of the warp's 32 TMEM lanes into v[0..15]
+XP_DEV void tmem_ld16(uint32_t taddr, float* v) {
     uint32_t r[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -141,8 +128,6 @@ XP_DEV void tmem_ld16(uint32_t taddr, float v[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-#pragma unroll
-    for (int i = 16; i < 32; ++i) v[i] = 0.0f;
 }
 // bounded wait that records the failure and returns
 XP_DEV void bmm_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
@@ -360,6 +345,13 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
     const uint32_t G = gridDim.x;
     // operand mode of the launch (uniform over the CTA)
     const bool S = a.fbflag ? (*reinterpret_cast<const volatile uint32_t*>(a.fbflag) == 0u) : (a.scaled != 0u);
+    // launch scalars in registers: `a` has its address taken (bmm_part), and a
+    // load through that generic pointer after a store or an asm memory
+    // clobber would be issued again each time
+    const uint32_t nitems = a.nitems, ksplit = a.ksplit, cbk = a.cb, nblk = a.nblk, nreal = a.nreal;
+    const bool raw = a.raw != 0u;
+    uint32_t* const err = a.err;
+    const unsigned char* const xb = a.xb;
 
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
@@ -376,28 +368,28 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                 pdl_wait();
                 waited = true;
                 for (uint32_t i = 0; i < ndef; ++i)
-                    bulk_g2s(stage0 + i * sbytes + BMM_SB * 2048, a.xb + (size_t)deferred[i] * xbytes, BMM_SB * xbytes,
+                    bulk_g2s(stage0 + i * sbytes + BMM_SB * 2048, xb + (size_t)deferred[i] * xbytes, BMM_SB * xbytes,
                              &full[i]);
             };
-            for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-                const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
-                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+            for (uint32_t item = blockIdx.x; item < nitems; item += G) {
+                const uint32_t tile = item / ksplit, kc = item % ksplit;
+                const uint32_t b0 = kc * cbk, b1 = min(b0 + cbk, nblk);
                 uint32_t lt;
                 const uint4* wq = bmm_part(a, tile, lt).wq;
                 for (uint32_t b = b0; b < b1; b += BMM_SB, ++t) {
                     const uint32_t s = t % BMM_STAGES;
                     if (t >= BMM_STAGES) {
                         if (!waited) release();
-                        bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);
+                        bmm_wait(&empty[s], ((t / BMM_STAGES) - 1) & 1, err);
                     }
                     unsigned char* st = stage0 + s * sbytes;
                     fence_proxy_async();
                     mbar_expect_tx(&full[s], sbytes);
                     // columns 128 tile .. +63 and +64 .. +127 are two KM4 groups;
                     // a group's consecutive blocks are contiguous (1 KB each)
-                    bulk_g2s(st, wq + ((size_t)(2 * lt) * a.nblk + b) * 64, BMM_SB * 1024, &full[s]);
-                    bulk_g2s(st + BMM_SB * 1024, wq + ((size_t)(2 * lt + 1) * a.nblk + b) * 64, BMM_SB * 1024, &full[s]);
-                    if (waited) bulk_g2s(st + BMM_SB * 2048, a.xb + (size_t)b * xbytes, BMM_SB * xbytes, &full[s]);
+                    bulk_g2s(st, wq + ((size_t)(2 * lt) * nblk + b) * 64, BMM_SB * 1024, &full[s]);
+                    bulk_g2s(st + BMM_SB * 1024, wq + ((size_t)(2 * lt + 1) * nblk + b) * 64, BMM_SB * 1024, &full[s]);
+                    if (waited) bulk_g2s(st + BMM_SB * 2048, xb + (size_t)b * xbytes, BMM_SB * xbytes, &full[s]);
                     else deferred[ndef++] = b;  // stage s == ndef while t < BMM_STAGES
                     BMM_TR(0, t)
                 }
@@ -410,17 +402,17 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         if (lane == 0) {
             uint32_t t = 0, tb = 0, it = 0;  // stages, blocks, items of this CTA
             const uint32_t idesc = bmm_idesc(S ? 2 * N : N);
-            for (uint32_t item = blockIdx.x; item < a.nitems; item += G, ++it) {
-                const uint32_t kc = item % a.ksplit;
-                const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+            for (uint32_t item = blockIdx.x; item < nitems; item += G, ++it) {
+                const uint32_t kc = item % ksplit;
+                const uint32_t b0 = kc * cbk, b1 = min(b0 + cbk, nblk);
                 // scaled: one accumulator of 2N columns (hi sums | lo sums) per
                 // item over its whole K range; two slots alternate
                 const uint32_t qi = it & 1;
-                if (S && it >= 2) bmm_wait(&dempty[qi], ((it >> 1) - 1) & 1, a.err);  // slot drained
+                if (S && it >= 2) bmm_wait(&dempty[qi], ((it >> 1) - 1) & 1, err);  // slot drained
                 for (uint32_t b = b0; b < b1; b += BMM_SB, ++t) {
                     const uint32_t s = t % BMM_STAGES;
-                    bmm_wait(&afull[s], (t / BMM_STAGES) & 1, a.err);  // A tile of the stage dequantised
-                    bmm_wait(&full[s], (t / BMM_STAGES) & 1, a.err);   // activations landed
+                    bmm_wait(&afull[s], (t / BMM_STAGES) & 1, err);  // A tile of the stage dequantised
+                    bmm_wait(&full[s], (t / BMM_STAGES) & 1, err);   // activations landed
                     BMM_TR(1, t)
                     tc_fence_after();
                     const uint32_t ab = smem_u32(atile + s * BMM_ABYTES);
@@ -439,7 +431,7 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                     } else {
                         for (uint32_t h = 0; h < BMM_SB; ++h, ++tb) {
                             const uint32_t q = tb % BMM_ND;
-                            if (tb >= BMM_ND) bmm_wait(&dempty[q], ((tb / BMM_ND) - 1) & 1, a.err);  // slot q read
+                            if (tb >= BMM_ND) bmm_wait(&dempty[q], ((tb / BMM_ND) - 1) & 1, err);  // slot q read
                             tc_fence_after();
                             const uint32_t d = tmem + q * N;
                             uint32_t acc = 0;
@@ -467,9 +459,9 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         // ------------------------------ dequant ------------------------------
         const uint32_t j = tid - 64;  // column within the tile, 0..127
         uint32_t t = 0;
-        for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-            const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
-            const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+        for (uint32_t item = blockIdx.x; item < nitems; item += G) {
+            const uint32_t tile = item / ksplit, kc = item % ksplit;
+            const uint32_t b0 = kc * cbk, b1 = min(b0 + cbk, nblk);
             uint2 sw{}, sw_next{};
             const uint2* scp = nullptr;
             uint32_t cols = 0;
@@ -495,13 +487,13 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
                         s2[h] = __halves2half2(v, v);
                     }
                 }
-                bmm_wait_warp(&full[s], (t / BMM_STAGES) & 1, a.err);
+                bmm_wait_warp(&full[s], (t / BMM_STAGES) & 1, err);
                 if (j == 0) { BMM_TR(3, t) }
                 const unsigned char* nb = stage0 + s * sbytes + (j >> 6) * (BMM_SB * 1024) + (j & 63) * 16;
                 uint4 w[BMM_SB];
 #pragma unroll
                 for (int h = 0; h < BMM_SB; ++h) w[h] = *reinterpret_cast<const uint4*>(nb + h * 1024);
-                if (t >= BMM_STAGES) bmm_wait_warp(&empty[s], ((t / BMM_STAGES) - 1) & 1, a.err);  // A tile free
+                if (t >= BMM_STAGES) bmm_wait_warp(&empty[s], ((t / BMM_STAGES) - 1) & 1, err);  // A tile free
                 unsigned char* at = atile + s * BMM_ABYTES + j * 16;
 #pragma unroll
                 for (int h = 0; h < BMM_SB; ++h) {
@@ -531,7 +523,6 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
     } else {
         // ------------------------------ epilogue ------------------------------
         pdl_wait();  // the sequence scales and the sums it adds into follow the previous kernel
-        if (tid == 192) { BMM_TR(5, 3) }
         // the sequences' scales in shared memory: a global load after the
         // output stores (which may alias it) would wait for each of them
         if (tid - 192 < BMM_MAXN) s_xs[tid - 192] = tid - 192 < (int)N ? a.xs[tid - 192] : 0.0f;
@@ -542,85 +533,94 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
         const uint32_t half = e >> 2;                // sequences [half * N/2, +N/2)
         const uint32_t nh = N / 2;                   // 16 or 32
         uint32_t t = 0, it = 0;
-        for (uint32_t item = blockIdx.x; item < a.nitems; item += G) {
-            const uint32_t tile = item / a.ksplit, kc = item % a.ksplit;
-            const uint32_t b0 = kc * a.cb, b1 = min(b0 + a.cb, a.nblk);
+        for (uint32_t item = blockIdx.x; item < nitems; item += G) {
+            const uint32_t tile = item / ksplit, kc = item % ksplit;
+            const uint32_t b0 = kc * cbk, b1 = min(b0 + cbk, nblk);
             uint32_t lt;
             const BmmPart& P = bmm_part(a, tile, lt);
             const uint32_t col = lt * BMM_M + j;
-            float sum[BMM_MAXN / 2];
-            if (S) {
-                // one read of the item's accumulator: hi sums + lo sums
-                const uint32_t q = it & 1;
-                if (tid == 192) { BMM_TR(5, 8 + it) }
-                bmm_wait_warp(&dfull[q], (it >> 1) & 1, a.err);
-                if (tid == 192) { BMM_TR(5, 16 + it) }
-                tc_fence_after();
-                float v[32];
-                const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * 2 * N + half * nh;
-                if (nh == 32) tmem_ld32(taddr, sum);
-                else tmem_ld16(taddr, sum);
-                if (nh == 32) tmem_ld32(taddr + N, v);
-                else tmem_ld16(taddr + N, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sum[i] += v[i];
-                tc_fence_before();
-                asm volatile("bar.sync 3, 256;" ::: "memory");
-                if (tid == 192) bmm_arrive(&dempty[q]);
-                if (tid == 192) { BMM_TR(5, 24 + it) }
-                ++it;
-            } else {
-#pragma unroll
-            for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
-            // scales one quad ahead: the scale plane is read from HBM
-            const uint2* scp = P.sc + col;
-            const size_t scs = P.cols;
-            uint2 sw = __ldg(scp + (size_t)(b0 >> 2) * scs);
-            uint2 sw_next = b0 + 4 < b1 ? __ldg(scp + (size_t)((b0 >> 2) + 1) * scs) : sw;
-            for (uint32_t b = b0; b < b1; ++b, ++t) {
-                const uint32_t q = t % BMM_ND;
-                if ((b & 3) == 0 && b != b0) {
-                    sw = sw_next;
-                    if (b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * scs);
-                }
-                const uint32_t word = (b & 2) ? sw.y : sw.x;
-                const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
-                bmm_wait_warp(&dfull[q], (t / BMM_ND) & 1, a.err);
-                tc_fence_after();
-                float v[32];
-                const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * N + half * nh;
-                if (nh == 32) tmem_ld32(taddr, v);
-                else tmem_ld16(taddr, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) sum[i] = fmaf(scale, v[i], sum[i]);
-                tc_fence_before();
-                asm volatile("bar.sync 3, 256;" ::: "memory");
-                if (tid == 192) bmm_arrive(&dempty[q]);
-            }
-            }
             // output addresses in registers: P lives in parameter space behind a
             // generic pointer, and a load through it after a store would wait
             // for that store
             const size_t cstride = P.cols;
-            float* dst = a.raw ? P.part + (size_t)kc * a.nreal * cstride + col : P.out + col;
+            float* dst = raw ? P.part + (size_t)kc * nreal * cstride + col : P.out + col;
             long long* accp = P.acc + col;
+            // sequences n0 .. n0 + 15 of this thread's column: x 2^e, then out
+            // (raw: this K range's partial, which the consumer adds in order;
+            // one K range: the result) or the fixed-point sums
+            auto emit16 = [&](uint32_t n0, const float* val) {
 #pragma unroll
-            for (int i = 0; i < BMM_MAXN / 2; ++i) {
-                const uint32_t n = half * nh + i;
-                if ((uint32_t)i < nh && n < a.nreal) {
-                    const float v = sum[i] * s_xs[n];
-                    if (a.raw || a.ksplit == 1) {
-                        // raw: the consumer adds the ksplit partials in K-range order
-                        dst[(size_t)n * cstride] = v;
-                    } else {
-                        const float f = v * 4294967296.0f;
-                        long long fx = 0;
-                        if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
-                        else atomicOr(a.err, TK_ERR_RANGE);
-                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(accp + (size_t)n * cstride),
-                                     "l"(fx) : "memory");
+                for (int i = 0; i < 16; ++i) {
+                    const uint32_t n = n0 + i;
+                    if (n < nreal) {
+                        const float v = val[i] * s_xs[n];
+                        if (raw || ksplit == 1) {
+                            dst[(size_t)n * cstride] = v;
+                        } else {
+                            const float f = v * 4294967296.0f;
+                            long long fx = 0;
+                            if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
+                            else atomicOr(err, TK_ERR_RANGE);
+                            asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(accp + (size_t)n * cstride),
+                                         "l"(fx) : "memory");
+                        }
                     }
                 }
+            };
+            if (S) {
+                // one read of the item's accumulator, 16 sequences at a time:
+                // hi sums + lo sums, out; the slot is released after the last
+                const uint32_t q = it & 1;
+                bmm_wait_warp(&dfull[q], (it >> 1) & 1, err);
+                tc_fence_after();
+                const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * 2 * N + half * nh;
+                for (uint32_t c = 0; c < nh; c += 16) {
+                    float hi[16], lo[16];
+                    tmem_ld16(taddr + c, hi);
+                    tmem_ld16(taddr + N + c, lo);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) hi[i] += lo[i];
+                    emit16(half * nh + c, hi);
+                }
+                tc_fence_before();
+                asm volatile("bar.sync 3, 256;" ::: "memory");
+                if (tid == 192) bmm_arrive(&dempty[q]);
+                ++it;
+            } else {
+                float sum[BMM_MAXN / 2];
+#pragma unroll
+                for (int n = 0; n < BMM_MAXN / 2; ++n) sum[n] = 0.0f;
+                // scales one quad ahead: the scale plane is read from HBM
+                const uint2* scp = P.sc + col;
+                const size_t scs = P.cols;
+                uint2 sw = __ldg(scp + (size_t)(b0 >> 2) * scs);
+                uint2 sw_next = b0 + 4 < b1 ? __ldg(scp + (size_t)((b0 >> 2) + 1) * scs) : sw;
+                for (uint32_t b = b0; b < b1; ++b, ++t) {
+                    const uint32_t q = t % BMM_ND;
+                    if ((b & 3) == 0 && b != b0) {
+                        sw = sw_next;
+                        if (b + 4 < b1) sw_next = __ldg(scp + (size_t)((b >> 2) + 1) * scs);
+                    }
+                    const uint32_t word = (b & 2) ? sw.y : sw.x;
+                    const float scale = (b & 1) ? bf16_hi(word) : bf16_lo(word);
+                    bmm_wait_warp(&dfull[q], (t / BMM_ND) & 1, err);
+                    tc_fence_after();
+                    const uint32_t taddr = tmem + ((q4 * 32) << 16) + q * N + half * nh;
+                    float v[16];
+                    tmem_ld16(taddr, v);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) sum[i] = fmaf(scale, v[i], sum[i]);
+                    if (nh == 32) {
+                        tmem_ld16(taddr + 16, v);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) sum[16 + i] = fmaf(scale, v[i], sum[16 + i]);
+                    }
+                    tc_fence_before();
+                    asm volatile("bar.sync 3, 256;" ::: "memory");
+                    if (tid == 192) bmm_arrive(&dempty[q]);
+                }
+                emit16(half * nh, sum);
+                if (nh == 32) emit16(half * nh + 16, sum + 16);
             }
         }
     }
