@@ -78,6 +78,9 @@ def parse():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-long", action="store_true")
+    ap.add_argument("--attn-layer-cost", action="store_true",
+                    help="print the in-graph cost of one xp_attention_decode layer (slope of 1 vs 26 launches) "
+                         "for local and global layers at several split counts, then exit")
     ap.add_argument("--ncu-case", choices=["full", "small", "multi", "matvec", "bmm", "batched", "long", "prefill"],
                     default=None,
                     help="run only a short untimed decode as an ncu capture target: 'full' = the bench model "
@@ -229,6 +232,55 @@ def long_context_bench(peak, iters=20):
             "us_per_step": round(ms * 1000.0, 1), "kv_bytes": kv_bytes,
             "kv_GB/s": round(kv_bytes / ms / 1e6, 1), "frac": round(kv_bytes / ms / 1e6 / peak, 4),
             "launches_per_step": 2 * L + 2}
+
+
+def attn_layer_cost():
+    """In-graph cost of one attention layer at position 8191: a CUDA graph of 1
+    and of 26 xp_attention_decode launches (4 distinct 8192-position caches,
+    so global layers are partly L2-resident), per layer = the slope."""
+    import torch
+    from xpose_b200._lib import check, lib
+    S, pos = 8192, 8191
+    g = torch.Generator(device="cuda").manual_seed(5)
+    kc = [torch.randn(S * 256, generator=g, device="cuda").half() for _ in range(4)]
+    vc = [torch.randn(S * 256, generator=g, device="cuda").half() for _ in range(4)]
+    q, k, v = (torch.randn(n, generator=g, device="cuda") for n in (1024, 256, 256))
+    qn, kn = (torch.randn(256, generator=g, device="cuda") * 0.02 for _ in range(2))
+    out = torch.empty(1024, device="cuda")
+    posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    scr = torch.zeros(lib().xp_attention_scratch_bytes(128) // 4 + 64, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def run(n, glob, ns):
+        for l in range(n):
+            check(lib().xp_attention_decode(stream.cuda_stream, out.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                            v.data_ptr(), qn.data_ptr(), kn.data_ptr(), kc[l % 4].data_ptr(),
+                                            vc[l % 4].data_ptr(), posd.data_ptr(), 0 if glob else 512,
+                                            1e6 if glob else 1e4, 1e-6, 1.0 / 16, ns, S, scr.data_ptr()))
+
+    def us(n, glob, ns, iters=50):
+        with torch.cuda.stream(stream):
+            run(n, glob, ns)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            run(n, glob, ns)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0.record(stream)
+            for _ in range(iters):
+                gr.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1000.0
+
+    for glob, splits in ((False, (1, 2, 4, 8, 16, 32)), (True, (16, 32, 64, 128))):
+        for ns in splits:
+            t1, t26 = us(1, glob, ns), us(26, glob, ns)
+            print(json.dumps({"layer": "global" if glob else "local", "splits": ns, "us_1": round(t1, 2),
+                              "us_26": round(t26, 2), "us_per_layer": round((t26 - t1) / 25, 2)}))
+    return 0
 
 
 def matvec_bench(sess, peak):
@@ -780,6 +832,8 @@ def main():
     rank, world, local = dist_env()
     if args.ncu_case:
         return ncu_case(args.ncu_case)
+    if args.attn_layer_cost:
+        return attn_layer_cost()
     if args.impl == "reference":
         # torchrun sets OMP_NUM_THREADS=1; the reference arm uses every host
         # core (set before any OpenMP runtime is loaded)

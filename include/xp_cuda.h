@@ -126,13 +126,17 @@ xp_status xp_mv_reduce(void* stream, float* out, const float* partial, uint32_t 
 /* ---- one matrix, many sequences, on the tensor cores ------------------------
  * out[s][j] = sum_k in[s][k] W[k][j] for s < n (<= 64): the skinny GEMM of
  * batched decode, each row the value kernels/llm_matvec.cl:422-434 computes for
- * that sequence (same planes, bf16 scales applied in fp32 per 32-row block).
+ * that sequence (same planes; products of exact operands summed in fp32: when
+ * every bf16 scale is 0 or within [2^-14, 8160] the dequantised weight itself
+ * is the fp16 operand, otherwise the scale is applied in fp32 per 32-row
+ * block; each call scans the scale plane on the stream to choose).
  * in is [n][rows], out [n][cols]; rows % 128 == 0, cols % 128 == 0. `scratch`
  * (256-byte aligned, xp_mv_km4_bs_batch_scratch_bytes) is caller-owned and
  * must be zero-initialised once (every call leaves it reusable; switching a
  * scratch to another shape costs one memset, so keep one per shape); its 32-bit
  * word at byte offset 256 is nonzero after a call whose tensor-core pipeline
- * wait ran out. No counterpart entry in the reference (which
+ * wait ran out, and the word at byte offset 384 is 1 after a call that took
+ * the per-block scale path. No counterpart entry in the reference (which
  * dispatches mv_km4_bs once per sequence). */
 size_t xp_mv_km4_bs_batch_scratch_bytes(uint32_t rows, uint32_t cols, uint32_t n);
 xp_status xp_mv_km4_bs_batch(void* stream, float* out, const float* in, const uint32_t* wq, const uint32_t* sc,
