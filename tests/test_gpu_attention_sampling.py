@@ -28,7 +28,10 @@ def _oracle_qk_post(raw, w, n_heads, pos, theta, eps=1e-6):
 
 # (pos, window, nsplit): kSeqLen 131 (examples/llm/kernel_tests.cpp:43), a
 # windowed case past the window, position 0, and a long global span.
-CASES = [(130, 0, 16), (700, 512, 16), (0, 512, 16), (130, 16, 4), (4095, 0, 64), (8191, 0, 128)]
+# split counts cover every cluster size of the merge: 16 (one or several
+# clusters), 8, 4, 2, and lone CTAs (3 clusters of one; a single CTA)
+CASES = [(130, 0, 16), (700, 512, 16), (0, 512, 16), (130, 16, 4), (4095, 0, 64), (8191, 0, 128),
+         (300, 0, 8), (300, 512, 6), (200, 0, 3), (8191, 512, 1)]
 
 
 @pytest.mark.parametrize("pos,window,nsplit", CASES)

@@ -549,21 +549,41 @@ __global__ void __launch_bounds__(BMM_THREADS, 2) bmm_kernel(const __grid_consta
             // (raw: this K range's partial, which the consumer adds in order;
             // one K range: the result) or the fixed-point sums
             auto emit16 = [&](uint32_t n0, const float* val) {
+                if (raw || ksplit == 1) {
+                    // 4 x 4 transposes within groups of four lanes (two
+                    // butterfly stages of shuffles), so each lane stores a
+                    // float4: 4 columns of one sequence. A warp store is then
+                    // 512 B of 4 rows instead of 128 B of one, a quarter of
+                    // the store instructions.
+                    const bool b0 = lane & 1, b1 = (lane & 2) != 0;
+                    const uint32_t row = (b1 ? 2u : 0u) + (b0 ? 1u : 0u);
+                    float* colbase = dst - lane + (lane & ~3u);  // this lane's 4 columns, sequence 0
+#pragma unroll
+                    for (int r = 0; r < 16; r += 4) {
+                        const float v0 = val[r] * s_xs[n0 + r], v1 = val[r + 1] * s_xs[n0 + r + 1];
+                        const float v2 = val[r + 2] * s_xs[n0 + r + 2], v3 = val[r + 3] * s_xs[n0 + r + 3];
+                        const float a0 = __shfl_xor_sync(0xffffffffu, b0 ? v0 : v1, 1);
+                        const float a1 = __shfl_xor_sync(0xffffffffu, b0 ? v2 : v3, 1);
+                        const float2 p0 = b0 ? make_float2(a0, v1) : make_float2(v0, a0);  // sequence r + b0
+                        const float2 p1 = b0 ? make_float2(a1, v3) : make_float2(v2, a1);  // sequence r + 2 + b0
+                        const float2 sd = b1 ? p0 : p1;
+                        const float rx = __shfl_xor_sync(0xffffffffu, sd.x, 2), ry = __shfl_xor_sync(0xffffffffu, sd.y, 2);
+                        const float4 o4 = b1 ? make_float4(rx, ry, p1.x, p1.y) : make_float4(p0.x, p0.y, rx, ry);
+                        const uint32_t n = n0 + r + row;
+                        if (n < nreal) *reinterpret_cast<float4*>(colbase + (size_t)n * cstride) = o4;
+                    }
+                    return;
+                }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const uint32_t n = n0 + i;
                     if (n < nreal) {
-                        const float v = val[i] * s_xs[n];
-                        if (raw || ksplit == 1) {
-                            dst[(size_t)n * cstride] = v;
-                        } else {
-                            const float f = v * 4294967296.0f;
-                            long long fx = 0;
-                            if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
-                            else atomicOr(err, TK_ERR_RANGE);
-                            asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(accp + (size_t)n * cstride),
-                                         "l"(fx) : "memory");
-                        }
+                        const float f = val[i] * s_xs[n] * 4294967296.0f;
+                        long long fx = 0;
+                        if (fabsf(f) < 9.2e18f) fx = __float2ll_rn(f);
+                        else atomicOr(err, TK_ERR_RANGE);
+                        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(accp + (size_t)n * cstride),
+                                     "l"(fx) : "memory");
                     }
                 }
             };
