@@ -1059,7 +1059,11 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
 #pragma unroll 1
                     for (uint32_t b = warp; b < P.nb; b += TK_WARPS) xq_prep_block(xn[(b0 + b) * 32 + lane], &xq[b]);
                 }
-                tk_sync();
+                // QKV (layer 0) and GU dot exactly the blocks each warp just
+                // prepared (block b on warp b mod 16); the LM head's warp
+                // groups read every block
+                if (k == TK_S_HEAD) tk_sync();
+                else __syncwarp();
             }
             TK_MARK(0)
 
