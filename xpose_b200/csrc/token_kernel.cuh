@@ -765,7 +765,17 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                     const float r = rv[j] + s1 * uv[j];
                     if (x_out && c == 0) x_out[i] = r;
                     if (k == TK_S_GU) xr[i] = r;
-                    xn[i] = r * sc2 * (1.0f + wv[H + i]);
+                    else xn[i] = r * sc2 * (1.0f + wv[H + i]);
+                }
+            }
+            if (k == TK_S_GU && s_gu_nu) {
+                // GU's limbs straight from registers: block warp + 16 j holds
+                // exactly this warp's element j, and the gate|up dot reads only
+                // the blocks its own warp made (no xn round trip, no CTA barrier)
+#pragma unroll
+                for (int j = 0; j < TK_MAXJ; ++j) {
+                    const uint32_t i = tid + j * TK_THREADS;
+                    if (i < H) xq_prep_block((rv[j] + s1 * uv[j]) * sc2 * (1.0f + wv[H + i]), &xq[warp + j * TK_WARPS]);
                 }
             }
             TK_MARK(6)
@@ -1052,8 +1062,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
             // ---------------- limbs of xn: one shared prep ----------------
             const TkPhase& P = k == TK_S_QKV ? a.qkv : k == TK_S_O ? a.o : k == TK_S_GU ? a.gu : a.head;
             const bool has = c < (k == TK_S_GU ? a.gu_u1 - a.gu_u0 : P.units);
-            tk_sync();  // xn complete (O: its limbs, made by the combine)
-            if (k != TK_S_O) {
+            if (k != TK_S_GU) tk_sync();  // xn complete (O: its limbs, made by the combine)
+            if (k != TK_S_O && k != TK_S_GU) {
                 if (has) {
                     const uint32_t b0 = k == TK_S_QKV ? s_qkv_b0 : 0;
 #pragma unroll 1
@@ -1064,6 +1074,8 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                 // groups read every block
                 if (k == TK_S_HEAD) tk_sync();
                 else __syncwarp();
+            } else if (k == TK_S_GU) {
+                __syncwarp();
             }
             TK_MARK(0)
 
@@ -1133,8 +1145,9 @@ __global__ void __launch_bounds__(TK_BLOCK, 1) token_kernel(const __grid_constan
                         s[jj] = 0;
                         f[jj] = 0.0f;
                     }
-#pragma unroll 1
-                    for (uint32_t ui = 0; ui < nu; ++ui) {
+#pragma unroll
+                    for (uint32_t ui = 0; ui < 3; ++ui) {
+                        if (ui >= nu) break;
                         const XBlk& X = xq[ui];
                         const unsigned char* img = s_down + (size_t)ui * ib;
 #pragma unroll

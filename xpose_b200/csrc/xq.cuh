@@ -63,11 +63,12 @@ XP_DEV void xq_prep_block(float v, XBlk* dst) {
     reinterpret_cast<int8_t*>(&dst->w[0][slot])[byte] = (int8_t)d0;
     reinterpret_cast<int8_t*>(&dst->w[1][slot])[byte] = (int8_t)d1;
     reinterpret_cast<int8_t*>(&dst->w[2][slot])[byte] = (int8_t)d2;
-    const int s0 = __reduce_add_sync(0xffffffffu, d0);
-    const int s1 = __reduce_add_sync(0xffffffffu, d1);
-    const int s2 = __reduce_add_sync(0xffffffffu, d2);
+    // one reduction of the combined limb value (|d0 16384 + d1 128 + d2| <
+    // 2^21 per lane, < 2^26 over the block): the same integer as summing
+    // each limb and combining afterwards
+    const int sc = __reduce_add_sync(0xffffffffu, (d0 * 16384 + d1 * 128) + d2);
     if (lane == 0) {
-        dst->bias = -8 * (s0 * 16384 + s1 * 128 + s2);
+        dst->bias = -8 * sc;
         dst->f = f;
     }
 }
