@@ -7,6 +7,7 @@
 // theta^(-2d/256) rounded once from double, fp16 KV cache, max-subtracted
 // softmax, tanh-approximate GeGLU.
 #pragma once
+#include <cooperative_groups.h>
 #include "attention.cuh"
 #include "bmm.cuh"
 #include "common.cuh"
@@ -126,29 +127,61 @@ __global__ void bk_pos_inc_kernel(uint32_t* pos, uint32_t B) {
     if (threadIdx.x < B) pos[threadIdx.x] += 1;
 }
 
-// hb = gelu(g) * u for one sequence per CTA (F <= BK_THREADS * BK_GJ), left
-// as the down-proj operand
+// hb = gelu(g) * u, left as the down-proj operand (F <= BK_THREADS * BK_GJ).
+// One cluster of BK_GC CTAs per sequence: CTA rank r takes elements
+// t + (r * BK_GJC + j) * BK_THREADS, and the operand's power-of-two scale
+// comes from the exact maximum of |hb| over the cluster (each CTA's block
+// maximum read from the others' shared memory), so every stored value is the
+// same as one CTA per sequence would store, on a quarter of the latency chain.
 constexpr int BK_GJ = 16;
+constexpr int BK_GC = 4;
+constexpr int BK_GJC = BK_GJ / BK_GC;
+static_assert(BK_GJ % BK_GC == 0, "elements per thread split over the cluster");
 __global__ void __launch_bounds__(BK_THREADS) bk_geglu_kernel(BkSums g, BkSums u, BkOperand hb, uint32_t F) {
+    namespace cg = cooperative_groups;
+    __shared__ float wmax[BK_THREADS / 32];
+    __shared__ float cmax;
+    cg::cluster_group cl = cg::this_cluster();
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t b = blockIdx.x;
-    long long idx[BK_GJ];
+    const uint32_t b = blockIdx.x / BK_GC, r = cl.block_rank();
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    long long idx[BK_GJC];
 #pragma unroll
-    for (int j = 0; j < BK_GJ; ++j) {
-        const uint32_t i = threadIdx.x + j * BK_THREADS;
+    for (int j = 0; j < BK_GJC; ++j) {
+        const uint32_t i = tid + (r * BK_GJC + j) * BK_THREADS;
         idx[j] = i < F ? (long long)b * F + i : -1;
     }
-    float gv[BK_GJ], uv[BK_GJ];
-    bk_gather<BK_GJ, 2>(g, idx, gv);
-    bk_gather<BK_GJ, 2>(u, idx, uv);
-    float h[BK_GJ];
+    float gv[BK_GJC], uv[BK_GJC];
+    bk_gather<BK_GJC, 2>(g, idx, gv);
+    bk_gather<BK_GJC, 2>(u, idx, uv);
+    float h[BK_GJC];
+    float am = 0.0f;
 #pragma unroll
-    for (int j = 0; j < BK_GJ; ++j) {
-        const uint32_t i = threadIdx.x + j * BK_THREADS;
-        h[j] = i < F ? gelu_tanh_ref(gv[j]) * uv[j] : 0.0f;
+    for (int j = 0; j < BK_GJC; ++j) {
+        h[j] = idx[j] >= 0 ? gelu_tanh_ref(gv[j]) * uv[j] : 0.0f;
+        am = fmaxf(am, fabsf(h[j]));
     }
-    bmm_put_seq(h, F, b, hb.Npad, hb.xs, hb.xb);
+    am = warp_max(am);
+    if (lane == 0) wmax[warp] = am;
+    __syncthreads();
+    if (warp == 0) {
+        am = warp_max(lane < BK_THREADS / 32 ? wmax[lane] : 0.0f);
+        if (lane == 0) cmax = am;
+    }
+    cl.sync();  // every CTA's maximum is in its shared memory
+    float m = 0.0f;
+#pragma unroll
+    for (int q = 0; q < BK_GC; ++q) m = fmaxf(m, *cl.map_shared_rank(&cmax, q));
+    cl.sync();  // no CTA leaves while a peer may still read its maximum
+    const int eb = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+    const float sc = eb > 0 && eb < 253 ? __uint_as_float((uint32_t)(eb + 1) << 23) : 1.0f;
+    if (r == 0 && tid == 0) hb.xs[b] = sc;
+#pragma unroll
+    for (int j = 0; j < BK_GJC; ++j) {
+        const uint32_t i = tid + (r * BK_GJC + j) * BK_THREADS;
+        if (i < F) bmm_xput(hb.xb, hb.Npad, b, i, h[j] / sc);  // exact: power of two
+    }
 }
 
 // One CTA per sequence: QK-norm + RoPE of the raw q (4 heads) and k, fp16 KV

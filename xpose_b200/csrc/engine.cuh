@@ -1164,7 +1164,7 @@ struct xp_bdec {
             if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
             if ((e = resid_norm(sums(o, ks_o, H), W.norm[1], W.norm[2], 1)) != cudaSuccess) return e;
             if ((e = mm_raw({{g, &W.m[4]}, {u, &W.m[5]}}, op_xn)) != cudaSuccess) return e;
-            if ((e = launch_ex(bk_geglu_kernel, dim3(B), dim3(BK_THREADS), 0, st, 1, pdl_k, sums(g, ks_gu, F),
+            if ((e = launch_ex(bk_geglu_kernel, dim3(B * BK_GC), dim3(BK_THREADS), 0, st, BK_GC, pdl_k, sums(g, ks_gu, F),
                                sums(u, ks_gu, F), op_hb, F)) != cudaSuccess)
                 return e;
             if ((e = mm_raw({{dn, &W.m[6]}}, op_hb)) != cudaSuccess) return e;
