@@ -69,19 +69,28 @@ struct BkOperand {
 
 // mode 0: xn = rmsnorm_gemma(x, w_pre)
 // mode 1: x += rmsnorm_gemma(y, w_post); xn = rmsnorm_gemma(x, w_pre)  (y: partial sums)
-// xn goes out as the next matvec's operand.
+// xn goes out as the next matvec's operand. One block reduction serves both
+// norms: with u = y (1 + w_post) and s1 = rsqrt(sum y^2 / H + eps), the
+// residual is r = x + s1 u and sum r^2 = sum x^2 + 2 s1 sum x u + s1^2 sum u^2;
+// x is loaded beside the partial sums.
 __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, BkSums y, const float* w_post,
                                                                  const float* w_pre, BkOperand xn, uint32_t H, float eps,
                                                                  int mode) {
-    __shared__ float red[32];
+    __shared__ float4 red4[BK_THREADS / 32];
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t b = blockIdx.x;
+    const uint32_t b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float* xb = x + (size_t)b * H;
     constexpr int J = 4;  // H <= 2048
-    float r[J];
+    float xv[J], uv[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const uint32_t i = threadIdx.x + j * BK_THREADS;
+        xv[j] = i < H ? xb[i] : 0.0f;
+    }
+    float4 s4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // y^2, x^2, x u, u^2
     if (mode == 1) {
-        float yv[J], ss = 0.0f;
+        float yv[J];
         long long idx[J];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
@@ -90,33 +99,43 @@ __global__ void __launch_bounds__(BK_THREADS) bk_resid_norm_kernel(float* x, BkS
         }
         bk_gather<J, 8>(y, idx, yv);
 #pragma unroll
-        for (int j = 0; j < J; ++j) ss += yv[j] * yv[j];
-        ss = block_sum(ss, red);
-        const float sc = rsqrtf(ss / (float)H + eps);
-        __syncthreads();
-#pragma unroll
         for (int j = 0; j < J; ++j) {
             const uint32_t i = threadIdx.x + j * BK_THREADS;
-            r[j] = i < H ? xb[i] + yv[j] * sc * (1.0f + w_post[i]) : 0.0f;
-            if (i < H) xb[i] = r[j];
+            uv[j] = i < H ? yv[j] * (1.0f + w_post[i]) : 0.0f;
+            s4.x += yv[j] * yv[j];
+            s4.z += xv[j] * uv[j];
+            s4.w += uv[j] * uv[j];
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const uint32_t i = threadIdx.x + j * BK_THREADS;
-            r[j] = i < H ? xb[i] : 0.0f;
-        }
+        for (int j = 0; j < J; ++j) uv[j] = 0.0f;
     }
-    float ss2 = 0.0f;
 #pragma unroll
-    for (int j = 0; j < J; ++j) ss2 += r[j] * r[j];
-    ss2 = block_sum(ss2, red);
-    const float sc2 = rsqrtf(ss2 / (float)H + eps);
+    for (int j = 0; j < J; ++j) s4.y += xv[j] * xv[j];
+    s4.x = warp_sum(s4.x);
+    s4.y = warp_sum(s4.y);
+    s4.z = warp_sum(s4.z);
+    s4.w = warp_sum(s4.w);
+    if (lane == 0) red4[warp] = s4;
+    __syncthreads();
+    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < BK_THREADS / 32; ++w) {
+        const float4 q = red4[w];
+        t.x += q.x;
+        t.y += q.y;
+        t.z += q.z;
+        t.w += q.w;
+    }
+    const float s1 = mode == 1 ? rsqrtf(t.x / (float)H + eps) : 0.0f;
+    const float sc2 = rsqrtf((t.y + 2.0f * s1 * t.z + s1 * s1 * t.w) / (float)H + eps);
     float o[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const uint32_t i = threadIdx.x + j * BK_THREADS;
-        o[j] = i < H ? r[j] * sc2 * (1.0f + w_pre[i]) : 0.0f;
+        const float r = xv[j] + s1 * uv[j];
+        if (mode == 1 && i < H) xb[i] = r;
+        o[j] = i < H ? r * sc2 * (1.0f + w_pre[i]) : 0.0f;
     }
     bmm_put_seq(o, H, b, xn.Npad, xn.xs, xn.xb);
 }
