@@ -330,7 +330,9 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
     if (a.mode == 1) return;
     const uint32_t pnew = a.mode == 0 ? pos : 0xFFFFFFFFu;  // mode 2 reads row pos from the cache
     __syncthreads();
-    // scores: one key per warp, lane holds 8 dims of every head
+    // scores: one key per warp, lane holds 8 dims of every head; four keys'
+    // loads in flight per warp
+#pragma unroll 4
     for (uint32_t jj = warp; jj < span; jj += BK_THREADS / 32) {
         const uint32_t j = kv_start + jj;
         const uint4 raw = j == pnew ? *reinterpret_cast<const uint4*>(knew + 8 * lane)
@@ -373,6 +375,7 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
     {
         const uint32_t dp = tid & 127, qr = tid >> 7;
         float acc[4][2] = {};
+#pragma unroll 8
         for (uint32_t jj = qr; jj < span; jj += 4) {
             const uint32_t j = kv_start + jj;
             const __half2 hv = j == pnew ? reinterpret_cast<const __half2*>(vnew)[dp]
