@@ -226,7 +226,12 @@ struct BkAttnArgs {
     // back from the cache and clears the sums.
     size_t seq_stride;
     int mode;
+    // CTAs per sequence (1, or 2 as a cluster): with 2, each CTA attends to
+    // half of the keys and the cluster's rank 0 merges the two partials
+    // (max, sum, unnormalised P.V) from its peer's shared memory
+    uint32_t split;
 };
+constexpr uint32_t BK_ATT_SPLIT = 2;  // CTAs (one cluster) per attending sequence
 __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_constant__ BkAttnArgs a) {
     extern __shared__ __align__(16) float bsm_f[];
     __shared__ float qs[4 * 256];
@@ -235,7 +240,8 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
     __shared__ float cs[256];           // cos | sin for this position
     pdl_launch_dependents();
     pdl_wait();
-    const uint32_t b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t split = a.split, b = blockIdx.x / split, rk = blockIdx.x % split;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t pos = a.pos[b];
     const uint32_t seq = pos + 1;
     const uint32_t kv_start = (a.window == 0 || seq <= a.window) ? 0 : seq - a.window;
@@ -322,18 +328,23 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
                 const __half lo = __float2half_rn(v[i]), hi = __float2half_rn(v[4 + i]);
                 dst[4 * lane + i] = lo;
                 dst[128 + 4 * lane + i] = hi;
-                cache[(size_t)pos * 256 + 4 * lane + i] = lo;
-                cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
+                if (rk == 0) {
+                    cache[(size_t)pos * 256 + 4 * lane + i] = lo;
+                    cache[(size_t)pos * 256 + 128 + 4 * lane + i] = hi;
+                }
             }
         }
     }
     if (a.mode == 1) return;
     const uint32_t pnew = a.mode == 0 ? pos : 0xFFFFFFFFu;  // mode 2 reads row pos from the cache
     __syncthreads();
+    // this CTA's keys: [k_lo, k_hi) of the window
+    const uint32_t half = (span + split - 1) / split;
+    const uint32_t k_lo = min(span, rk * half), k_hi = min(span, k_lo + half);
     // scores: one key per warp, lane holds 8 dims of every head; four keys'
     // loads in flight per warp
 #pragma unroll 4
-    for (uint32_t jj = warp; jj < span; jj += BK_THREADS / 32) {
+    for (uint32_t jj = k_lo + warp; jj < k_hi; jj += BK_THREADS / 32) {
         const uint32_t j = kv_start + jj;
         const uint4 raw = j == pnew ? *reinterpret_cast<const uint4*>(knew + 8 * lane)
                                    : *reinterpret_cast<const uint4*>(kcb + (size_t)j * 256 + 8 * lane);
@@ -357,26 +368,29 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
         if ((lane & 7) == 0) sc[(((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * ms + jj] = tot;
     }
     __syncthreads();
-    __shared__ float sums[4];
+    __shared__ float sums[4], mh[4];
     if (warp < 4) {
         float m = -INFINITY;
-        for (uint32_t jj = lane; jj < span; jj += 32) m = fmaxf(m, sc[warp * ms + jj]);
+        for (uint32_t jj = k_lo + lane; jj < k_hi; jj += 32) m = fmaxf(m, sc[warp * ms + jj]);
         m = warp_max(m);
         float sum = 0.0f;
-        for (uint32_t jj = lane; jj < span; jj += 32) {
+        for (uint32_t jj = k_lo + lane; jj < k_hi; jj += 32) {
             const float p = expf(sc[warp * ms + jj] - m);
             sc[warp * ms + jj] = p;
             sum += p;
         }
         sum = warp_sum(sum);
-        if (lane == 0) sums[warp] = sum;
+        if (lane == 0) {
+            sums[warp] = sum;
+            mh[warp] = m;
+        }
     }
     __syncthreads();
     {
         const uint32_t dp = tid & 127, qr = tid >> 7;
         float acc[4][2] = {};
 #pragma unroll 8
-        for (uint32_t jj = qr; jj < span; jj += 4) {
+        for (uint32_t jj = k_lo + qr; jj < k_hi; jj += 4) {
             const uint32_t j = kv_start + jj;
             const __half2 hv = j == pnew ? reinterpret_cast<const __half2*>(vnew)[dp]
                                         : reinterpret_cast<const __half2*>(vcb + (size_t)j * 256)[dp];
@@ -399,8 +413,35 @@ __global__ void __launch_bounds__(BK_THREADS) bk_attn_kernel(const __grid_consta
 #pragma unroll
     for (int j = 0; j < 1024 / BK_THREADS; ++j) {
         const uint32_t i = tid + j * BK_THREADS;
-        const float t = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
-        o[j] = t / sums[i >> 8];
+        o[j] = red[i] + red[1024 + i] + red[2048 + i] + red[3072 + i];
+    }
+    if (split == 1) {
+#pragma unroll
+        for (int j = 0; j < 1024 / BK_THREADS; ++j) o[j] /= sums[(tid + j * BK_THREADS) >> 8];
+    } else {
+        // flash merge of the two halves: weights e^(m_r - M) per head (a half
+        // with no keys has m = -inf and weight 0)
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        float* part = qs;  // the scaled q is no longer read: this CTA's unnormalised P.V
+#pragma unroll
+        for (int j = 0; j < 1024 / BK_THREADS; ++j) part[tid + j * BK_THREADS] = o[j];
+        cl.sync();
+        if (rk == 0) {
+            const float* ppart = cl.map_shared_rank(part, 1);
+            const float* psums = cl.map_shared_rank(sums, 1);
+            const float* pmh = cl.map_shared_rank(mh, 1);
+#pragma unroll
+            for (int j = 0; j < 1024 / BK_THREADS; ++j) {
+                const uint32_t i = tid + j * BK_THREADS, h = i >> 8;
+                const float m0 = mh[h], m1 = pmh[h], M = fmaxf(m0, m1);
+                const float w0 = m0 == -INFINITY ? 0.0f : expf(m0 - M);
+                const float w1 = m1 == -INFINITY ? 0.0f : expf(m1 - M);
+                o[j] = (o[j] * w0 + ppart[i] * w1) / (sums[h] * w0 + psums[h] * w1);
+            }
+        }
+        cl.sync();  // the peer's shared memory stays until rank 0 has read it
+        if (rk != 0) return;
     }
     bmm_put_seq(o, 1024, b, a.att.Npad, a.att.xs, a.att.xb);
 }

@@ -1153,12 +1153,16 @@ struct xp_bdec {
             const uint32_t ms = aa.window ? std::min(aa.window, max_seq) : max_seq;
             aa.seq_stride = chunk ? 0 : (size_t)max_seq * 256;
             aa.mode = chunk ? 1 : 0;
-            if ((e = launch_ex(bk_attn_kernel, dim3(B), dim3(BK_THREADS), (size_t)4 * ms * 4, st, 1, pdl_k, aa)) != cudaSuccess)
+            aa.split = chunk ? 1 : BK_ATT_SPLIT;  // decode steps only (prefill passes keep one CTA per row)
+            if ((e = launch_ex(bk_attn_kernel, dim3(B * aa.split), dim3(BK_THREADS), (size_t)4 * ms * 4, st, aa.split, pdl_k,
+                               aa)) != cudaSuccess)
                 return e;
             if (chunk) {
                 // every row's k and v are in the cache before any row attends
                 aa.mode = 2;
-                if ((e = launch_ex(bk_attn_kernel, dim3(B), dim3(BK_THREADS), (size_t)4 * ms * 4, st, 1, pdl_k, aa)) != cudaSuccess)
+                aa.split = 1;  // prefill rows: the 2-CTA split measured slower here
+                if ((e = launch_ex(bk_attn_kernel, dim3(B * aa.split), dim3(BK_THREADS), (size_t)4 * ms * 4, st, aa.split,
+                                   pdl_k, aa)) != cudaSuccess)
                     return e;
             }
             if ((e = mm_raw({{o, &W.m[3]}}, op_att)) != cudaSuccess) return e;
